@@ -1,0 +1,271 @@
+/* nncu.h -- C ABI of libllmcpu_b200 (libnncu.so): libnnc's attention hot path
+ * on NVIDIA B200 (sm_100a).
+ *
+ * libnnc (ZacWalk/libllmcpu) runs attention on the CPU inside
+ * attention_forward (src/libnnc/model.cpp:1559-1771), over a K/V cache held
+ * in host vectors (model_kv_cache, src/libnnc/model.h:252-326). This library
+ * replaces the part of attention_forward after the Q/K/V projections -- the
+ * per-head Q/K RMSNorm, RoPE, the K/V append and the blocked attention
+ * (model.cpp:1616-1757) -- and moves the K/V cache to HBM. The projections,
+ * nnc.h and everything else in libnnc stay as they are.
+ *
+ * Conventions, all of them libnnc's:
+ *  - Every entry point returns an int holding an nnc_status value
+ *    (src/libnnc/nnc.h:50-61); NNCU_OK is 0. On failure the detail is kept per
+ *    thread and read with nncu_last_error(), as nnc_last_error() does.
+ *  - Nothing throws across this boundary, and nothing here prints.
+ *  - A cache belongs to one caller thread at a time (nnc.h:27-32).
+ *  - `stream` arguments are cudaStream_t values passed as void* (NULL = the
+ *    legacy default stream); *_dev entry points take device pointers and are
+ *    asynchronous on that stream. Entry points without a stream take host
+ *    pointers and return when the result is in host memory.
+ */
+#ifndef NNCU_H
+#define NNCU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NNCU_ATTN_BLOCK 256           /* MODEL_ATTN_BLOCK, src/libnnc/model.h:229 */
+#define NNCU_ATTN_PART(hd) ((hd) + 2) /* NNC_ATTN_PART, src/libnnc/nn_ops.h:45 */
+
+/* nnc_status values (src/libnnc/nnc.h:50-61), plus two for the device. */
+enum
+{
+	NNCU_OK = 0,
+	NNCU_ERR_INVALID_ARGUMENT = 1,
+	NNCU_ERR_UNSUPPORTED = 2,     /* no usable sm_100 device (nnc: NNC_ERR_UNSUPPORTED_CPU) */
+	NNCU_ERR_OUT_OF_MEMORY = 6,   /* HBM or pinned host memory exhausted */
+	NNCU_ERR_CONTEXT_FULL = 7,
+	NNCU_ERR_DEVICE = 20,         /* a CUDA call failed; nncu_last_error() has its text */
+	NNCU_ERR_TIMEOUT = 21         /* a bounded wait on a peer ran out */
+};
+
+/* nnc_kv_type values (src/libnnc/nnc.h:199-203) plus F16. */
+typedef enum nncu_kv_type
+{
+	NNCU_KV_BF16 = 0,
+	NNCU_KV_F32 = 1,
+	NNCU_KV_F16 = 2
+} nncu_kv_type;
+
+/* nnc_rope_mode (src/libnnc/nn_ops.h:286-290). */
+typedef enum nncu_rope_mode
+{
+	NNCU_ROPE_NEOX = 0,
+	NNCU_ROPE_NORM = 1
+} nncu_rope_mode;
+
+const char* nncu_status_string(int status);
+/* Detail of the most recent failure on the calling thread; never NULL.
+ * Replaces nnc_last_error() (nnc.h:66-69) for this library's calls. */
+const char* nncu_last_error(void);
+int nncu_last_status(void);
+void nncu_clear_error(void);
+/* The library's version string and the device it would use. */
+const char* nncu_version(void);
+int nncu_device_check(int device);
+
+/* ---- spans ----------------------------------------------------------------
+ * The keys [*first, *last] the query at `pos` attends to in a sequence whose
+ * keys fill [0, n_seq). Replaces model_attn_span (model.cpp:2300-2316;
+ * declared model.h:358-364). Host-only. */
+void nncu_attn_span(int causal, int window, int pos, int n_seq, int* first, int* last);
+
+/* ---- unit seam: nn_ops.h:31-61 and :79-81, :283-312, on device pointers ----
+ * Same argument meaning as the reference's; every pointer is a device pointer
+ * and the call is asynchronous on `stream`. */
+
+/* nnc_attn_block (nn_ops.h:53-55): one block of n_keys keys (any count) for
+ * n_heads query heads sharing one KV head. K/V rows are kv_stride elements
+ * apart, of kv_type. No scores scratch: the scores never leave the chip.
+ * softcap > 0 applies cap*tanh(s/cap) to the scaled scores (0 = off). */
+int nncu_attn_block_dev(const float* q, size_t q_stride, const void* K, const void* V, int kv_type, size_t kv_stride,
+                        size_t n_keys, size_t head_dim, size_t n_heads, float scale, float softcap, float* part,
+                        void* stream);
+/* nnc_attn_merge (nn_ops.h:58). */
+int nncu_attn_merge_dev(float* acc, const float* part, size_t head_dim, size_t n_heads, void* stream);
+/* nnc_attn_finish (nn_ops.h:61). */
+int nncu_attn_finish_dev(float* out, size_t out_stride, const float* acc, size_t head_dim, size_t n_heads,
+                         void* stream);
+/* nnc_rmsnorm_gamma_multi_f32 (nn_ops.h:79-81). */
+int nncu_rmsnorm_gamma_multi_dev(float* y, const float* x, size_t n_groups, size_t dim, const float* gamma, float eps,
+                                 void* stream);
+/* nnc_rmsnorm_f32 (nn_ops.h:73) over n_groups rows of dim. */
+int nncu_rmsnorm_dev(float* y, const float* x, size_t n_groups, size_t dim, float eps, void* stream);
+/* nnc_rope_f32 (nn_ops.h:292-294) for n_tok tokens at positions
+ * (pos0 + t) * pos_scale, each token n_heads * head_dim floats. */
+int nncu_rope_dev(float* x, uint32_t n_tok, uint32_t n_heads, uint32_t head_dim, uint32_t n_rot, int32_t pos0,
+                  float pos_scale, float freq_base, int mode, const float* freq_factors, void* stream);
+/* nnc_softcap_f32 (nn_ops.h:312). */
+int nncu_softcap_dev(float* y, const float* x, size_t n, float cap, void* stream);
+
+/* ---- the HBM K/V cache ------------------------------------------------------
+ * Replaces model_kv_buffer / model_kv_cache storage (model.h:231-326),
+ * model_kv_init (model.cpp:1891-2040) and model_kv_rewind (model.cpp:
+ * 2137-2143). Sizing follows model_kv_init exactly: one buffer per
+ * cache-owning layer, a causal sliding layer kept as a ring of
+ * round_up(window + n_batch, 256) rows when that is smaller than n_ctx and
+ * no global layer reads it, max_rewind = min over rings of rows - window, and
+ * a bidirectional model shares one n_ctx-row buffer among all layers.
+ *
+ * Device layout (per buffer): [n_seq][n_kv][rows][head_dim] elements of the
+ * cache type -- head-major, so one KV head's keys are one contiguous stream
+ * -- K and V in separate 256-byte-aligned allocations. Position p of a
+ * sequence is row p % rows. */
+
+typedef struct nncu_kv nncu_kv;
+
+typedef struct nncu_layer_desc
+{
+	int32_t n_kv;     /* KV heads */
+	int32_t head_dim;
+	int32_t window;   /* sliding window in keys; 0 = global */
+	int32_t kv_layer; /* layer whose cache it reads; == its own index when it owns one */
+} nncu_layer_desc;
+
+typedef struct nncu_kv_params
+{
+	int32_t n_ctx;   /* most positions (model_kv_init n_ctx) */
+	int32_t n_batch; /* most tokens one call appends (model_kv_init n_batch) */
+	int32_t n_seq;   /* independent sequences held side by side (1 for a session) */
+	int32_t kv_type; /* nncu_kv_type */
+	int32_t causal;  /* 0: a bidirectional (embedding) model */
+	int32_t device;  /* CUDA device ordinal */
+} nncu_kv_params;
+
+typedef struct nncu_kv_layer_info
+{
+	int32_t buffer;   /* the layer buffer it reads (its kv_layer) */
+	int32_t rows;
+	int32_t window;   /* a ring's window; 0 for a full buffer */
+	int32_t n_kv, head_dim, kv_type;
+	size_t head_bytes; /* bytes between KV heads: rows * head_dim * esize */
+	size_t seq_bytes;  /* bytes between sequences: n_kv * head_bytes */
+	void* k;           /* device pointers */
+	void* v;
+} nncu_kv_layer_info;
+
+typedef struct nncu_kv_state
+{
+	int32_t cur_pos;    /* next position to fill (model_kv_cache::cur_pos) */
+	int32_t kv_written; /* highest position written since 0, plus one */
+	int32_t max_rewind; /* INT32_MAX without rings */
+	int32_t n_ctx;
+	size_t bytes;       /* K/V storage in HBM, all sequences */
+} nncu_kv_state;
+
+/* Per-layer sizing, as nncu_kv_create would allocate it (rows, window,
+ * buffer per layer; max_rewind; total HBM bytes), without touching a device:
+ * model_kv_init's rules (model.cpp:1929-1962) on their own. `per_layer` has
+ * n_layer entries; its k and v pointers are left NULL. */
+int nncu_kv_plan(const nncu_layer_desc* layers, int32_t n_layer, const nncu_kv_params* params,
+                 nncu_kv_layer_info* per_layer, int32_t* max_rewind, size_t* bytes);
+int nncu_kv_create(const nncu_layer_desc* layers, int32_t n_layer, const nncu_kv_params* params, nncu_kv** out);
+void nncu_kv_free(nncu_kv* kv);
+int nncu_kv_layer(const nncu_kv* kv, int32_t layer, nncu_kv_layer_info* out);
+int nncu_kv_get_state(const nncu_kv* kv, int32_t seq, nncu_kv_state* out);
+/* model_kv_rewind: pos in [0, cur_pos]; refused (NNCU_ERR_INVALID_ARGUMENT,
+ * nothing changed) when pos > 0 and kv_written - pos > max_rewind. */
+int nncu_kv_rewind(nncu_kv* kv, int32_t seq, int32_t pos);
+/* The bookkeeping model_forward does after its layers (model.cpp:2130-2133):
+ * cur_pos = pos0 + n_tok; kv_written = max(pos0 == 0 ? 0 : kv_written, cur_pos). */
+int nncu_kv_commit(nncu_kv* kv, int32_t seq, int32_t pos0, int32_t n_tok);
+/* Copy host rows into / out of a layer's cache (reference row layout
+ * [n][n_kv * head_dim] of the cache type's bits), at positions pos0 .. pos0+n-1
+ * (row p % rows). For loading or inspecting a cache; synchronous. */
+int nncu_kv_write_rows(nncu_kv* kv, int32_t layer, int32_t seq, int32_t pos0, int32_t n, const void* k_rows,
+                       const void* v_rows);
+int nncu_kv_read_rows(const nncu_kv* kv, int32_t layer, int32_t seq, int32_t pos0, int32_t n, void* k_rows,
+                      void* v_rows);
+
+/* ---- the attention op --------------------------------------------------------
+ * One layer's attention for a batch of n_tok query tokens at positions
+ * pos0 .. pos0+n_tok-1: the body of attention_forward from the per-head norms
+ * to the attention output (model.cpp:1616-1757). The parameters are what
+ * attention_forward reads from the model and the cache. */
+typedef struct nncu_attn_params
+{
+	int32_t n_tok, pos0, n_seq; /* n_seq: keys visible in [0, n_seq); pos0 + n_tok normally */
+	int32_t n_head, n_kv, head_dim, n_rot, rope_mode;
+	float freq_base, rope_scale;  /* rope position = (pos0 + t) * rope_scale */
+	const float* freq_factors;    /* n_rot/2 floats or NULL (Llama 3 / Gemma 4 scaling) */
+	const float* q_gamma;         /* head_dim floats, or NULL: no Q norm */
+	const float* k_gamma;         /* head_dim floats, or NULL: no K norm */
+	int32_t v_rmsnorm;            /* Gemma 4: RMS-normalise V rows, no gamma */
+	float eps, scale, softcap;    /* softcap > 0: cap*tanh(s/cap) on scaled scores */
+	int32_t causal, window, reuse_kv; /* reuse_kv: read another layer's cache, append nothing */
+} nncu_attn_params;
+
+/* The drop-in call for attention_forward: q [n_tok][n_head*head_dim] and
+ * k, v [n_tok][n_kv*head_dim] are host fp32 rows straight from the
+ * projections (k, v ignored when reuse_kv); out [n_tok][n_head*head_dim] host.
+ * The pointer fields of `p` are host pointers. Synchronous. */
+int nncu_attention(nncu_kv* kv, int32_t layer, int32_t seq, const nncu_attn_params* p, const float* q,
+                   const float* k, const float* v, float* out);
+
+/* Many layers and/or sequences in one submission. Each job is one
+ * nncu_attention's worth of work. In nncu_attention_batch every pointer is a
+ * host pointer and the call is synchronous (one host->device copy of all
+ * inputs, one device->host copy of all outputs). In nncu_attention_batch_dev
+ * every pointer is a device pointer and the call is asynchronous on `stream`.
+ * Jobs of one submission must not append to a cache another of its jobs
+ * reads. */
+typedef struct nncu_attn_job
+{
+	int32_t layer, seq;
+	nncu_attn_params p;
+	const float* q;
+	const float* k;
+	const float* v;
+	float* out;
+} nncu_attn_job;
+
+int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs);
+int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs, void* stream);
+
+/* Wait for `stream` (the asynchronous calls' completion) and report a kernel
+ * whose bounded wait ran out (NNCU_ERR_TIMEOUT: the outputs are void). The
+ * synchronous calls make this check themselves. No reference counterpart:
+ * libnnc's calls are all synchronous. */
+int nncu_sync(nncu_kv* kv, void* stream);
+
+/* ---- profiling ----------------------------------------------------------------
+ * The phase profiler of nnc_perf_enable / nnc_perf_reset / nnc_perf_report
+ * (nnc.h:404-415; slots NNC_PERF_ATTN_ROPE and NNC_PERF_ATTN_CORE,
+ * runtime.h:147-168) for this path: attn_rope is K1 (per-head norms, RoPE,
+ * append), attn_core is K2+K3 (attention and its merge). Device time comes
+ * from CUDA events recorded around the launches on their stream; bytes are
+ * the algorithmic traffic (K/V of every key attended, q in, output out). Off
+ * by default and free when off; process-wide, meant for one caller at a time. */
+enum
+{
+	NNCU_PERF_ATTN_ROPE = 0,
+	NNCU_PERF_ATTN_CORE = 1,
+	NNCU_PERF_COUNT = 2
+};
+
+typedef struct nncu_perf_phase
+{
+	double ms;      /* device time */
+	int64_t calls;  /* launches */
+	uint64_t bytes; /* algorithmic bytes moved */
+} nncu_perf_phase;
+
+void nncu_perf_enable(int enabled);
+void nncu_perf_reset(void);
+/* Wait for the launches recorded so far and fill out[NNCU_PERF_COUNT]. */
+int nncu_perf_read(nncu_perf_phase* out);
+/* A text table like nnc_perf_report's: ms, share, calls, us/call, GB/s. */
+const char* nncu_perf_report(const char* title, int32_t n_tokens);
+/* Kernels this library has launched since it was loaded (all threads). */
+uint64_t nncu_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

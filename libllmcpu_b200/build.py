@@ -1,0 +1,100 @@
+"""Build libnncu.so (the C-ABI library) in-tree with nvcc for sm_100a.
+
+    python -m libllmcpu_b200.build [-j N] [--force]
+
+Every translation unit is compiled separately (in parallel) and linked into
+``libllmcpu_b200/libnncu.so``; an object is rebuilt when its source or any
+header under csrc/ or include/ is newer. The CUDA runtime is linked
+statically, so the library needs only the driver at run time.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+BUILD = os.path.join(PKG, "_build")
+LIB = os.path.join(PKG, "libnncu.so")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+                     "--expt-relaxed-constexpr", f"-I{INCLUDE}", f"-I{CSRC}"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def sources() -> list[str]:
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
+
+
+def headers() -> list[str]:
+    return (glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh"))
+            + glob.glob(os.path.join(INCLUDE, "*.h")))
+
+
+def _compile(src: str, force: bool, extra: list[str]) -> str:
+    obj = os.path.join(BUILD, os.path.basename(src) + ".o")
+    newest_dep = max([os.path.getmtime(src)] + [os.path.getmtime(h) for h in headers()])
+    if not force and os.path.exists(obj) and os.path.getmtime(obj) >= newest_dep:
+        return obj
+    cmd = [nvcc()] + NVCC_FLAGS + extra + ["-c", src, "-o", obj]
+    if src.endswith(".cpp"):
+        cmd = [nvcc(), "-x", "cu"] + NVCC_FLAGS + extra + ["-c", src, "-o", obj]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {os.path.basename(src)}:\n{r.stdout}\n{r.stderr}")
+    return obj
+
+
+def build(force: bool = False, jobs: int | None = None, extra: list[str] | None = None, verbose: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    srcs = sources()
+    extra = extra or []
+    with cf.ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as ex:
+        objs = list(ex.map(lambda s: _compile(s, force, extra), srcs))
+    if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
+        tmp = LIB + ".tmp"
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", tmp] + objs + ["-lcuda"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, LIB)
+    if verbose:
+        print(LIB)
+    return LIB
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("-j", type=int, default=None)
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--ptxas-v", action="store_true", help="print register/shared-memory use per kernel")
+    a = ap.parse_args(argv)
+    extra = ["-Xptxas", "-v"] if a.ptxas_v else []
+    if a.ptxas_v:
+        for s in sources():
+            cmd = [nvcc()] + NVCC_FLAGS + extra + ["-c", s, "-o", os.devnull]
+            if s.endswith(".cpp"):
+                continue
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            sys.stdout.write(r.stdout + r.stderr)
+        return 0
+    build(force=a.force, jobs=a.j, verbose=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,1192 @@
+// api.cpp -- the host side of libnncu: the C ABI declared in include/nncu.h.
+//
+//  * errors: libnnc's convention (a status return plus a per-thread message,
+//    runtime.h:29-46 / nnc.h:62-69), never an exception across the ABI;
+//  * the HBM K/V cache: model_kv_init's sizing rules (model.cpp:1891-2040)
+//    and model_kv_rewind (model.cpp:2137-2143) over device buffers laid out
+//    [n_seq][n_kv][rows][head_dim];
+//  * the attention op: validation, the decode work plan (stream-K over
+//    256-aligned key tiles), pinned staging for the host-pointer calls, and
+//    the launches of K1 (k_prep.cu) and K2+K3 (k_decode.cu).
+#include "nncu.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <climits>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <new>
+#include <tuple>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+
+using namespace nncu;
+
+// ---- errors -------------------------------------------------------------------
+
+namespace
+{
+thread_local int t_status = NNCU_OK;
+thread_local char t_msg[512] = "";
+
+int fail(int status, const char* fmt, ...)
+{
+	t_status = status;
+	va_list ap;
+	va_start(ap, fmt);
+	std::vsnprintf(t_msg, sizeof t_msg, fmt, ap);
+	va_end(ap);
+	return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what)
+{
+	if (e == cudaErrorMemoryAllocation)
+		return fail(NNCU_ERR_OUT_OF_MEMORY, "%s: out of device memory", what);
+	return fail(NNCU_ERR_DEVICE, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+#define CU(call, what)                                                                                                \
+	do                                                                                                                \
+	{                                                                                                                 \
+		cudaError_t e_ = (call);                                                                                      \
+		if (e_ != cudaSuccess) return cuda_fail(e_, what);                                                             \
+	} while (0)
+
+struct DeviceGuard
+{
+	int prev = -1;
+	explicit DeviceGuard(int dev)
+	{
+		cudaGetDevice(&prev);
+		if (prev != dev) cudaSetDevice(dev);
+	}
+	~DeviceGuard()
+	{
+		if (prev >= 0) cudaSetDevice(prev);
+	}
+};
+
+// A device allocation that grows on demand.
+struct DevBuf
+{
+	void* p = nullptr;
+	size_t cap = 0;
+	cudaError_t reserve(size_t bytes)
+	{
+		if (bytes <= cap) return cudaSuccess;
+		if (p) cudaFree(p);
+		p = nullptr;
+		cap = 0;
+		const size_t want = std::max(bytes, (size_t)4096);
+		cudaError_t e = cudaMalloc(&p, want);
+		if (e == cudaSuccess) cap = want;
+		return e;
+	}
+	void release()
+	{
+		if (p) cudaFree(p);
+		p = nullptr;
+		cap = 0;
+	}
+};
+
+struct HostBuf
+{
+	void* p = nullptr;
+	size_t cap = 0;
+	cudaError_t reserve(size_t bytes)
+	{
+		if (bytes <= cap) return cudaSuccess;
+		if (p) cudaFreeHost(p);
+		p = nullptr;
+		cap = 0;
+		const size_t want = std::max(bytes, (size_t)4096);
+		cudaError_t e = cudaMallocHost(&p, want);
+		if (e == cudaSuccess) cap = want;
+		return e;
+	}
+	void release()
+	{
+		if (p) cudaFreeHost(p);
+		p = nullptr;
+		cap = 0;
+	}
+};
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// ---- the phase profiler (nnc_perf_*, runtime.h:147-195, on CUDA events) ----
+std::atomic<uint64_t> g_launches{0};
+std::atomic<bool> g_perf_on{false};
+std::mutex g_perf_mu;
+struct PerfPending
+{
+	int slot;
+	cudaEvent_t a, b;
+	uint64_t bytes;
+};
+std::vector<PerfPending> g_perf_pending;
+std::vector<cudaEvent_t> g_perf_free;
+nncu_perf_phase g_perf[NNCU_PERF_COUNT];
+std::string g_perf_text;
+
+cudaEvent_t perf_event()
+{
+	if (!g_perf_free.empty())
+	{
+		cudaEvent_t e = g_perf_free.back();
+		g_perf_free.pop_back();
+		return e;
+	}
+	cudaEvent_t e = nullptr;
+	cudaEventCreate(&e);
+	return e;
+}
+
+// Brackets one launch: records an event before and after it on `st` when the
+// profiler is on, and counts the launch either way.
+struct PerfScope
+{
+	int slot;
+	uint64_t bytes;
+	cudaStream_t st;
+	cudaEvent_t a = nullptr;
+	PerfScope(int slot_, uint64_t bytes_, cudaStream_t st_) : slot(slot_), bytes(bytes_), st(st_)
+	{
+		if (g_perf_on.load(std::memory_order_relaxed))
+		{
+			std::lock_guard<std::mutex> lk(g_perf_mu);
+			a = perf_event();
+			if (a) cudaEventRecord(a, st);
+		}
+	}
+	~PerfScope()
+	{
+		g_launches.fetch_add(1, std::memory_order_relaxed);
+		if (!a) return;
+		std::lock_guard<std::mutex> lk(g_perf_mu);
+		cudaEvent_t b = perf_event();
+		if (!b) return;
+		cudaEventRecord(b, st);
+		g_perf_pending.push_back({slot, a, b, bytes});
+	}
+};
+} // namespace
+
+// ---- the cache object ---------------------------------------------------------------
+
+struct Buffer
+{
+	int rows = 0;       // logical rows (model_kv_buffer::rows)
+	int rows_alloc = 0; // allocated rows: a multiple of 256 (rings already are)
+	int window = 0;     // a ring's window; 0 for a full buffer
+	size_t seq_bytes = 0;
+	void* k = nullptr;
+	void* v = nullptr;
+};
+
+struct nncu_kv
+{
+	int device = 0;
+	int n_layer = 0, n_seq = 1, n_ctx = 0, n_batch = 1, kv_type = KV_BF16;
+	bool causal = true;
+	int num_sms = 148;
+	std::vector<nncu_layer_desc> layers;
+	std::vector<int> kv_buf; // layer -> buffer index
+	std::vector<Buffer> bufs;
+	std::vector<int> cur_pos, kv_written; // per sequence
+	int max_rewind = INT_MAX;
+	size_t bytes = 0;
+
+	cudaStream_t stream = nullptr; // the host-pointer calls' stream
+	int* err_dev = nullptr;        // device error word (bounded waits)
+	DevBuf jobs_dev, stage_dev, qrot, parts, counters;
+	HostBuf stage_host, jobs_host;
+	cudaEvent_t jobs_uploaded = nullptr; // the last upload from jobs_host has been read
+	std::map<std::pair<uint32_t, int>, float*> rope_tables;
+	std::vector<DevJob> jobs_tmp;
+	int counters_n = 0;
+
+	~nncu_kv()
+	{
+		DeviceGuard g(device);
+		if (stream) cudaStreamSynchronize(stream);
+		for (auto& b : bufs)
+		{
+			if (b.k) cudaFree(b.k);
+			if (b.v) cudaFree(b.v);
+		}
+		for (auto& kv : rope_tables) cudaFree(kv.second);
+		if (err_dev) cudaFree(err_dev);
+		jobs_dev.release();
+		stage_dev.release();
+		qrot.release();
+		parts.release();
+		counters.release();
+		stage_host.release();
+		jobs_host.release();
+		if (jobs_uploaded) cudaEventDestroy(jobs_uploaded);
+		if (stream) cudaStreamDestroy(stream);
+	}
+};
+
+// ---- small host functions --------------------------------------------------------
+
+extern "C" {
+
+const char* nncu_status_string(int status)
+{
+	switch (status)
+	{
+	case NNCU_OK: return "ok";
+	case NNCU_ERR_INVALID_ARGUMENT: return "invalid argument";
+	case NNCU_ERR_UNSUPPORTED: return "no usable sm_100 device";
+	case NNCU_ERR_OUT_OF_MEMORY: return "out of memory";
+	case NNCU_ERR_CONTEXT_FULL: return "context full";
+	case NNCU_ERR_DEVICE: return "CUDA error";
+	case NNCU_ERR_TIMEOUT: return "a bounded wait timed out";
+	default: return "unknown status";
+	}
+}
+
+const char* nncu_last_error(void) { return t_msg; }
+int nncu_last_status(void) { return t_status; }
+void nncu_clear_error(void)
+{
+	t_status = NNCU_OK;
+	t_msg[0] = 0;
+}
+
+const char* nncu_version(void) { return "libnncu 0.1 (sm_100a)"; }
+
+int nncu_device_check(int device)
+{
+	int n = 0;
+	cudaError_t e = cudaGetDeviceCount(&n);
+	if (e != cudaSuccess || n == 0) return fail(NNCU_ERR_UNSUPPORTED, "no CUDA device is visible");
+	if (device < 0 || device >= n) return fail(NNCU_ERR_INVALID_ARGUMENT, "device %d does not exist (%d visible)", device, n);
+	cudaDeviceProp prop;
+	CU(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+	if (prop.major != 10)
+		return fail(NNCU_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build is for sm_100a (B200)", device, prop.major,
+		            prop.minor);
+	return NNCU_OK;
+}
+
+void nncu_attn_span(int causal, int window, int pos, int n_seq, int* first, int* last)
+{
+	// model.cpp:2300-2316
+	if (causal)
+	{
+		*first = (window > 0 && pos + 1 > window) ? pos + 1 - window : 0;
+		*last = std::min(pos, n_seq - 1);
+		return;
+	}
+	*first = 0;
+	*last = n_seq - 1;
+	if (window > 0)
+	{
+		const int half = window / 2;
+		*first = std::max(0, pos - half);
+		*last = std::min(n_seq - 1, pos + half);
+	}
+}
+
+} // extern "C"
+
+// ---- rope tables ----------------------------------------------------------------------
+
+namespace
+{
+// The inverse frequencies of nnc_rope_f32 (nn_ops.cpp:1844-1856): the fp32
+// recurrence inv *= base^(-2/n_rot), formed on the host with the same libm
+// and the same fp32 operations, so the device multiplies exactly these values.
+void rope_inv_table(float base, int n_rot, std::vector<float>& out)
+{
+	const int half = n_rot / 2;
+	out.resize(half);
+	const float ratio = std::pow(base, -2.0f / static_cast<float>(n_rot));
+	float inv = 1.0f;
+	for (int i = 0; i < half; ++i)
+	{
+		out[i] = inv;
+		inv *= ratio;
+	}
+}
+
+int rope_table(nncu_kv* kv, float base, int n_rot, const float** out)
+{
+	*out = nullptr;
+	if (n_rot <= 0) return NNCU_OK;
+	uint32_t bits;
+	std::memcpy(&bits, &base, 4);
+	auto key = std::make_pair(bits, n_rot);
+	auto it = kv->rope_tables.find(key);
+	if (it != kv->rope_tables.end())
+	{
+		*out = it->second;
+		return NNCU_OK;
+	}
+	std::vector<float> tab;
+	rope_inv_table(base, n_rot, tab);
+	float* d = nullptr;
+	CU(cudaMalloc(&d, tab.size() * sizeof(float)), "rope table");
+	cudaError_t e = cudaMemcpy(d, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice);
+	if (e != cudaSuccess)
+	{
+		cudaFree(d);
+		return cuda_fail(e, "rope table upload");
+	}
+	kv->rope_tables[key] = d;
+	*out = d;
+	return NNCU_OK;
+}
+} // namespace
+
+// ---- the cache ----------------------------------------------------------------------------
+
+namespace
+{
+// model_kv_init's checks and sizing (model.cpp:1891-1962), device-free.
+int kv_layout(const nncu_layer_desc* layers, int32_t n_layer, const nncu_kv_params* p, std::vector<int>& kv_buf,
+              std::vector<Buffer>& bufs, int& max_rewind)
+{
+	if (!layers || !p || n_layer <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "no layers");
+	if (p->n_ctx <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "the context size must be positive");
+	if (p->n_seq <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "n_seq must be positive");
+	if (p->kv_type != KV_BF16 && p->kv_type != KV_F32 && p->kv_type != KV_F16)
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "unknown K/V type %d", p->kv_type);
+	for (int li = 0; li < n_layer; ++li)
+	{
+		const nncu_layer_desc& L = layers[li];
+		if (L.n_kv <= 0 || L.head_dim <= 0 || L.head_dim > 512 || L.window < 0)
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d: bad shape (n_kv %d, head_dim %d, window %d)", li, L.n_kv,
+			            L.head_dim, L.window);
+		if (L.kv_layer < 0 || L.kv_layer >= n_layer)
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d: kv_layer %d out of range", li, L.kv_layer);
+		const nncu_layer_desc& O = layers[L.kv_layer];
+		if (O.kv_layer != L.kv_layer)
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d reads layer %d, which owns no cache", li, L.kv_layer);
+		if (p->causal && (O.n_kv != L.n_kv || O.head_dim != L.head_dim))
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d reads a cache of another shape", li);
+	}
+	const size_t es = kv_esize(p->kv_type);
+	const int nb = p->n_batch > 0 ? p->n_batch : 1;
+	kv_buf.assign(n_layer, 0);
+	max_rewind = INT_MAX;
+	if (!p->causal)
+	{
+		// a bidirectional model: one n_ctx-row buffer that every layer rewrites
+		bufs.assign(1, Buffer{});
+		Buffer& b = bufs[0];
+		b.rows = p->n_ctx;
+		b.rows_alloc = (int)align_up((size_t)p->n_ctx, ATTN_BLOCK);
+		size_t max_head = 0;
+		for (int li = 0; li < n_layer; ++li) max_head = std::max(max_head, (size_t)layers[li].n_kv * layers[li].head_dim);
+		b.seq_bytes = max_head * b.rows_alloc * es;
+		return NNCU_OK;
+	}
+	// a sliding layer's buffer becomes a ring when that saves memory and every
+	// layer reading it slides the same way
+	std::vector<int> ring_window(n_layer, 0);
+	std::vector<bool> can_ring(n_layer, true);
+	for (int li = 0; li < n_layer; ++li)
+	{
+		const nncu_layer_desc& L = layers[li];
+		const int owner = L.kv_layer;
+		if (L.window == 0) can_ring[owner] = false;
+		else if (ring_window[owner] == 0) ring_window[owner] = L.window;
+		else if (ring_window[owner] != L.window) can_ring[owner] = false;
+	}
+	bufs.assign(n_layer, Buffer{});
+	for (int li = 0; li < n_layer; ++li)
+	{
+		const nncu_layer_desc& L = layers[li];
+		kv_buf[li] = L.kv_layer;
+		if (L.kv_layer != li) continue;
+		Buffer& b = bufs[li];
+		const int w = ring_window[li];
+		const int ring = (int)align_up((size_t)w + nb, ATTN_BLOCK);
+		const bool is_ring = can_ring[li] && w > 0 && ring < p->n_ctx;
+		b.rows = is_ring ? ring : p->n_ctx;
+		b.rows_alloc = (int)align_up((size_t)b.rows, ATTN_BLOCK);
+		b.window = is_ring ? w : 0;
+		if (b.window) max_rewind = std::min(max_rewind, b.rows - b.window);
+		b.seq_bytes = (size_t)L.n_kv * L.head_dim * b.rows_alloc * es;
+	}
+	return NNCU_OK;
+}
+} // namespace
+
+extern "C" int nncu_kv_plan(const nncu_layer_desc* layers, int32_t n_layer, const nncu_kv_params* p,
+                            nncu_kv_layer_info* per_layer, int32_t* max_rewind, size_t* bytes)
+{
+	std::vector<int> kv_buf;
+	std::vector<Buffer> bufs;
+	int mr = INT_MAX;
+	int rc = kv_layout(layers, n_layer, p, kv_buf, bufs, mr);
+	if (rc != NNCU_OK) return rc;
+	const size_t es = kv_esize(p->kv_type);
+	size_t total = 0;
+	for (const auto& b : bufs)
+		if (b.rows) total += 2 * b.seq_bytes * p->n_seq;
+	if (per_layer)
+		for (int li = 0; li < n_layer; ++li)
+		{
+			const Buffer& b = bufs[kv_buf[li]];
+			nncu_kv_layer_info& o = per_layer[li];
+			o.buffer = kv_buf[li];
+			o.rows = b.rows;
+			o.window = b.window;
+			o.n_kv = layers[li].n_kv;
+			o.head_dim = layers[li].head_dim;
+			o.kv_type = p->kv_type;
+			o.head_bytes = (size_t)b.rows_alloc * layers[li].head_dim * es;
+			o.seq_bytes = b.seq_bytes;
+			o.k = nullptr;
+			o.v = nullptr;
+		}
+	if (max_rewind) *max_rewind = mr;
+	if (bytes) *bytes = total;
+	return NNCU_OK;
+}
+
+extern "C" int nncu_kv_create(const nncu_layer_desc* layers, int32_t n_layer, const nncu_kv_params* p, nncu_kv** out)
+{
+	if (!out) return fail(NNCU_ERR_INVALID_ARGUMENT, "out is NULL");
+	*out = nullptr;
+	std::vector<int> kv_buf;
+	std::vector<Buffer> bufs;
+	int max_rewind = INT_MAX;
+	int rc = kv_layout(layers, n_layer, p, kv_buf, bufs, max_rewind);
+	if (rc != NNCU_OK) return rc;
+	rc = nncu_device_check(p->device);
+	if (rc != NNCU_OK) return rc;
+
+	nncu_kv* kv = new (std::nothrow) nncu_kv();
+	if (!kv) return fail(NNCU_ERR_OUT_OF_MEMORY, "out of host memory");
+	DeviceGuard guard(p->device);
+	kv->device = p->device;
+	kv->n_layer = n_layer;
+	kv->n_seq = p->n_seq;
+	kv->n_ctx = p->n_ctx;
+	kv->n_batch = p->n_batch > 0 ? p->n_batch : 1;
+	kv->kv_type = p->kv_type;
+	kv->causal = p->causal != 0;
+	kv->layers.assign(layers, layers + n_layer);
+	kv->kv_buf = kv_buf;
+	kv->bufs = bufs;
+	kv->max_rewind = max_rewind;
+	kv->cur_pos.assign(p->n_seq, 0);
+	kv->kv_written.assign(p->n_seq, 0);
+	cudaDeviceGetAttribute(&kv->num_sms, cudaDevAttrMultiProcessorCount, p->device);
+
+	auto fail_free = [&](int status) {
+		delete kv;
+		return status;
+	};
+	for (auto& b : kv->bufs)
+	{
+		if (b.rows == 0) continue;
+		const size_t n = b.seq_bytes * kv->n_seq;
+		cudaError_t e = cudaMalloc(&b.k, n);
+		if (e == cudaSuccess) e = cudaMalloc(&b.v, n);
+		if (e == cudaSuccess) e = cudaMemset(b.k, 0, n);
+		if (e == cudaSuccess) e = cudaMemset(b.v, 0, n);
+		if (e != cudaSuccess)
+		{
+			cudaGetLastError();
+			const int st = e == cudaErrorMemoryAllocation
+			                   ? fail(NNCU_ERR_OUT_OF_MEMORY, "out of memory allocating a %d-token context", p->n_ctx)
+			                   : cuda_fail(e, "K/V allocation");
+			return fail_free(st);
+		}
+		kv->bytes += 2 * n;
+	}
+	cudaError_t e = cudaStreamCreateWithFlags(&kv->stream, cudaStreamNonBlocking);
+	if (e == cudaSuccess) e = cudaMalloc(&kv->err_dev, sizeof(int));
+	if (e == cudaSuccess) e = cudaMemset(kv->err_dev, 0, sizeof(int));
+	if (e == cudaSuccess) e = cudaEventCreateWithFlags(&kv->jobs_uploaded, cudaEventDisableTiming);
+	if (e != cudaSuccess) return fail_free(cuda_fail(e, "cache set-up"));
+	*out = kv;
+	return NNCU_OK;
+}
+
+extern "C" void nncu_kv_free(nncu_kv* kv) { delete kv; }
+
+extern "C" int nncu_kv_layer(const nncu_kv* kv, int32_t layer, nncu_kv_layer_info* out)
+{
+	if (!kv || !out) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL argument");
+	if (layer < 0 || layer >= kv->n_layer) return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d out of range", layer);
+	const nncu_layer_desc& L = kv->layers[layer];
+	const int bi = kv->kv_buf[layer];
+	const Buffer& b = kv->bufs[bi];
+	const size_t es = kv_esize(kv->kv_type);
+	out->buffer = bi;
+	out->rows = b.rows;
+	out->window = b.window;
+	out->n_kv = L.n_kv;
+	out->head_dim = L.head_dim;
+	out->kv_type = kv->kv_type;
+	out->head_bytes = (size_t)b.rows_alloc * L.head_dim * es;
+	out->seq_bytes = b.seq_bytes;
+	out->k = b.k;
+	out->v = b.v;
+	return NNCU_OK;
+}
+
+extern "C" int nncu_kv_get_state(const nncu_kv* kv, int32_t seq, nncu_kv_state* out)
+{
+	if (!kv || !out) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL argument");
+	if (seq < 0 || seq >= kv->n_seq) return fail(NNCU_ERR_INVALID_ARGUMENT, "sequence %d out of range", seq);
+	out->cur_pos = kv->cur_pos[seq];
+	out->kv_written = kv->kv_written[seq];
+	out->max_rewind = kv->max_rewind;
+	out->n_ctx = kv->n_ctx;
+	out->bytes = kv->bytes;
+	return NNCU_OK;
+}
+
+extern "C" int nncu_kv_rewind(nncu_kv* kv, int32_t seq, int32_t pos)
+{
+	// model_kv_rewind (model.cpp:2137-2143)
+	if (!kv) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL cache");
+	if (seq < 0 || seq >= kv->n_seq) return fail(NNCU_ERR_INVALID_ARGUMENT, "sequence %d out of range", seq);
+	if (pos < 0 || pos > kv->cur_pos[seq])
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "cannot rewind to %d: the cache is at %d", pos, kv->cur_pos[seq]);
+	if (pos > 0 && kv->kv_written[seq] - pos > kv->max_rewind)
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "cannot rewind to %d: a ring holds only %d positions below %d", pos,
+		            kv->max_rewind, kv->kv_written[seq]);
+	kv->cur_pos[seq] = pos;
+	return NNCU_OK;
+}
+
+extern "C" int nncu_kv_commit(nncu_kv* kv, int32_t seq, int32_t pos0, int32_t n_tok)
+{
+	// the end of model_forward (model.cpp:2130-2133)
+	if (!kv) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL cache");
+	if (seq < 0 || seq >= kv->n_seq) return fail(NNCU_ERR_INVALID_ARGUMENT, "sequence %d out of range", seq);
+	if (pos0 < 0 || n_tok < 0 || pos0 + n_tok > kv->n_ctx)
+		return fail(NNCU_ERR_CONTEXT_FULL, "positions %d..%d exceed the context of %d", pos0, pos0 + n_tok, kv->n_ctx);
+	kv->cur_pos[seq] = pos0 + n_tok;
+	kv->kv_written[seq] = std::max(pos0 == 0 ? 0 : kv->kv_written[seq], kv->cur_pos[seq]);
+	return NNCU_OK;
+}
+
+namespace
+{
+int kv_rows_copy(const nncu_kv* kv, int32_t layer, int32_t seq, int32_t pos0, int32_t n, const void* k_src,
+                 const void* v_src, void* k_dst, void* v_dst, bool to_device)
+{
+	if (!kv) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL cache");
+	if (layer < 0 || layer >= kv->n_layer) return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d out of range", layer);
+	if (seq < 0 || seq >= kv->n_seq) return fail(NNCU_ERR_INVALID_ARGUMENT, "sequence %d out of range", seq);
+	if (pos0 < 0 || n < 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "negative position or count");
+	const nncu_layer_desc& L = kv->layers[layer];
+	const Buffer& b = kv->bufs[kv->kv_buf[layer]];
+	if (n > b.rows) return fail(NNCU_ERR_INVALID_ARGUMENT, "%d rows do not fit a buffer of %d", n, b.rows);
+	if (!b.window && pos0 + n > b.rows)
+		return fail(NNCU_ERR_CONTEXT_FULL, "positions up to %d exceed the buffer's %d rows", pos0 + n, b.rows);
+	DeviceGuard g(kv->device);
+	const size_t es = kv_esize(kv->kv_type);
+	const size_t D = L.head_dim, row_bytes = D * es, host_pitch = (size_t)L.n_kv * row_bytes;
+	const size_t head_bytes = (size_t)b.rows_alloc * row_bytes;
+	int done = 0;
+	while (done < n)
+	{
+		const int p = pos0 + done;
+		const int row = p % b.rows_alloc;
+		const int run = std::min(n - done, b.rows_alloc - row); // rows up to the ring's end
+		for (int h = 0; h < L.n_kv; ++h)
+		{
+			const size_t dev_off = (size_t)seq * b.seq_bytes + (size_t)h * head_bytes + (size_t)row * row_bytes;
+			const size_t host_off = (size_t)done * host_pitch + (size_t)h * row_bytes;
+			for (int which = 0; which < 2; ++which)
+			{
+				if (to_device)
+				{
+					const char* src = static_cast<const char*>(which ? v_src : k_src);
+					char* dst = static_cast<char*>(which ? b.v : b.k);
+					if (!src) continue;
+					CU(cudaMemcpy2D(dst + dev_off, row_bytes, src + host_off, host_pitch, row_bytes, run,
+					                cudaMemcpyHostToDevice),
+					   "cache write");
+				}
+				else
+				{
+					const char* src = static_cast<const char*>(which ? b.v : b.k);
+					char* dst = static_cast<char*>(which ? v_dst : k_dst);
+					if (!dst) continue;
+					CU(cudaMemcpy2D(dst + host_off, host_pitch, src + dev_off, row_bytes, row_bytes, run,
+					                cudaMemcpyDeviceToHost),
+					   "cache read");
+				}
+			}
+		}
+		done += run;
+	}
+	return NNCU_OK;
+}
+} // namespace
+
+extern "C" int nncu_kv_write_rows(nncu_kv* kv, int32_t layer, int32_t seq, int32_t pos0, int32_t n, const void* k_rows,
+                                  const void* v_rows)
+{
+	return kv_rows_copy(kv, layer, seq, pos0, n, k_rows, v_rows, nullptr, nullptr, true);
+}
+
+extern "C" int nncu_kv_read_rows(const nncu_kv* kv, int32_t layer, int32_t seq, int32_t pos0, int32_t n, void* k_rows,
+                                 void* v_rows)
+{
+	return kv_rows_copy(kv, layer, seq, pos0, n, nullptr, nullptr, k_rows, v_rows, false);
+}
+
+// ---- the attention op ----------------------------------------------------------------------
+
+namespace
+{
+
+int validate_job(const nncu_kv* kv, const nncu_attn_job& j)
+{
+	const nncu_attn_params& p = j.p;
+	if (j.layer < 0 || j.layer >= kv->n_layer) return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d out of range", j.layer);
+	if (j.seq < 0 || j.seq >= kv->n_seq) return fail(NNCU_ERR_INVALID_ARGUMENT, "sequence %d out of range", j.seq);
+	const nncu_layer_desc& L = kv->layers[j.layer];
+	const Buffer& b = kv->bufs[kv->kv_buf[j.layer]];
+	if (p.n_kv != L.n_kv || p.head_dim != L.head_dim)
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d: n_kv %d / head_dim %d do not match the cache's %d / %d",
+		            j.layer, p.n_kv, p.head_dim, L.n_kv, L.head_dim);
+	if (p.n_head <= 0 || p.n_head % p.n_kv != 0)
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "n_head %d is not a multiple of n_kv %d", p.n_head, p.n_kv);
+	if (!decode_supported(p.head_dim, kv->kv_type))
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "head_dim %d: the device path takes 64, 128, 256 or 512", p.head_dim);
+	if (p.n_tok <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "n_tok must be positive");
+	if (p.n_tok > kv->n_batch)
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "%d tokens exceed the cache's batch of %d", p.n_tok, kv->n_batch);
+	if (p.pos0 < 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "negative position");
+	if (p.pos0 + p.n_tok > kv->n_ctx)
+		return fail(NNCU_ERR_CONTEXT_FULL, "positions %d..%d exceed the context of %d", p.pos0, p.pos0 + p.n_tok - 1,
+		            kv->n_ctx);
+	if (p.n_seq <= 0 || p.n_seq > kv->n_ctx) return fail(NNCU_ERR_INVALID_ARGUMENT, "n_seq %d out of range", p.n_seq);
+	if (p.n_rot < 0 || p.n_rot > p.head_dim || (p.n_rot & 1))
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "n_rot %d must be even and at most head_dim", p.n_rot);
+	if (p.rope_mode != NNCU_ROPE_NEOX && p.rope_mode != NNCU_ROPE_NORM)
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "unknown rope mode %d", p.rope_mode);
+	if (p.window < 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "negative window");
+	if ((p.reuse_kv != 0) != (L.kv_layer != j.layer))
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d: reuse_kv %d disagrees with the cache (it reads layer %d)",
+		            j.layer, p.reuse_kv, L.kv_layer);
+	if (b.window && (!p.causal || p.window != b.window))
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d: a ring of window %d cannot serve window %d", j.layer, b.window,
+		            p.window);
+	if (!p.causal && p.pos0 + p.n_tok > p.n_seq)
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "bidirectional: queries beyond the %d keys", p.n_seq);
+	if (p.softcap < 0.0f || !(p.scale == p.scale)) return fail(NNCU_ERR_INVALID_ARGUMENT, "bad scale or softcap");
+	return NNCU_OK;
+}
+
+// Jobs of one submission run concurrently: none may read a (buffer,
+// sequence) another of them appends to, and no two may append to the same one.
+int check_conflicts(const nncu_kv* kv, const nncu_attn_job* jobs, int n)
+{
+	if (n < 2) return NNCU_OK;
+	std::map<std::pair<int, int>, std::pair<int, int>> use; // (buffer, seq) -> (jobs, appenders)
+	for (int i = 0; i < n; ++i)
+	{
+		auto& u = use[{kv->kv_buf[jobs[i].layer], jobs[i].seq}];
+		u.first += 1;
+		u.second += jobs[i].p.reuse_kv ? 0 : 1;
+	}
+	for (const auto& kvp : use)
+		if (kvp.second.second > 0 && kvp.second.first > 1)
+			return fail(NNCU_ERR_INVALID_ARGUMENT,
+			            "jobs of one call share buffer %d of sequence %d while one of them appends to it; "
+			            "submit them in separate calls",
+			            kvp.first.first, kvp.first.second);
+	return NNCU_OK;
+}
+
+// Fill the decode plan fields of each DevJob and size the launch.
+void plan_decode(nncu_kv* kv, std::vector<DevJob>& jobs, DecodePlan& P)
+{
+	const int D = jobs[0].D;
+	const int T = decode_tile_keys(D, kv->kv_type);
+	int rows_needed = 1;
+	for (auto& j : jobs) rows_needed = std::max(rows_needed, (j.n_head / j.n_kv) * j.n_tok);
+	int RM = 1;
+	while (RM < rows_needed && RM < decode_rows_max(D)) RM *= 2;
+	long long total = 0;
+	int seg = 0;
+	for (auto& j : jobs)
+	{
+		int first_min = INT_MAX, last_max = -1;
+		for (int t = 0; t < j.n_tok; ++t)
+		{
+			int f, l;
+			nncu_attn_span(j.causal, j.window, j.pos0 + t, j.n_seq, &f, &l);
+			if (l < f) continue;
+			first_min = std::min(first_min, f);
+			last_max = std::max(last_max, l);
+		}
+		const int G = j.n_head / j.n_kv;
+		j.n_rowgroups = (G * j.n_tok + RM - 1) / RM;
+		if (last_max < 0)
+		{
+			j.tile_lo = 0;
+			j.n_tiles = 0;
+		}
+		else
+		{
+			j.tile_lo = first_min / T;
+			j.n_tiles = last_max / T - j.tile_lo + 1;
+		}
+		j.seg0 = seg;
+		j.gtile0 = total;
+		seg += j.n_kv * j.n_rowgroups;
+		total += (long long)j.n_kv * j.n_rowgroups * j.n_tiles;
+	}
+	P.n_jobs = (int)jobs.size();
+	P.D = D;
+	P.kv_type = kv->kv_type;
+	P.RM = RM;
+	P.T = T;
+	P.total_tiles = total;
+	P.n_segments = seg;
+	const long long ctas = std::min<long long>(total, (long long)kv->num_sms);
+	P.tiles_per_cta = ctas > 0 ? (total + ctas - 1) / ctas : 1;
+	P.n_ctas = ctas > 0 ? (int)((total + P.tiles_per_cta - 1) / P.tiles_per_cta) : 0;
+	P.err = kv->err_dev;
+}
+
+// Turn one public job into a DevJob (device pointers already resolved).
+void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
+{
+	const nncu_attn_params& p = j.p;
+	const Buffer& b = kv->bufs[kv->kv_buf[j.layer]];
+	const size_t es = kv_esize(kv->kv_type);
+	std::memset(&d, 0, sizeof d);
+	d.q = j.q;
+	d.k = j.k;
+	d.v = j.v;
+	d.out = j.out;
+	d.q_gamma = p.q_gamma;
+	d.k_gamma = p.k_gamma;
+	d.freq_factors = p.freq_factors;
+	d.K = static_cast<char*>(b.k) + (size_t)j.seq * b.seq_bytes;
+	d.V = static_cast<char*>(b.v) + (size_t)j.seq * b.seq_bytes;
+	d.head_bytes = (long long)b.rows_alloc * p.head_dim * es;
+	d.rows = b.rows_alloc;
+	d.n_tok = p.n_tok;
+	d.pos0 = p.pos0;
+	d.n_seq = p.n_seq;
+	d.n_head = p.n_head;
+	d.n_kv = p.n_kv;
+	d.D = p.head_dim;
+	d.n_rot = p.n_rot;
+	d.rope_mode = p.rope_mode;
+	d.causal = p.causal != 0;
+	d.window = p.window;
+	d.reuse_kv = p.reuse_kv != 0;
+	d.v_rmsnorm = p.v_rmsnorm != 0;
+	d.rope_scale = p.rope_scale;
+	d.eps = p.eps;
+	d.scale = p.scale;
+	d.softcap = p.softcap;
+}
+
+// Launch K1 and K2 for jobs whose DevJob pointers are all device pointers;
+// assigns q_rot scratch, plans, uploads the job table and launches on `st`.
+int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn_job>& pub, cudaStream_t st)
+{
+	const int n = (int)jobs.size();
+	// rope tables and q_rot scratch
+	size_t qrot_floats = 0;
+	int tok = 0;
+	for (int i = 0; i < n; ++i)
+	{
+		const nncu_attn_params& p = pub[i].p;
+		int rc = rope_table(kv, p.freq_base, p.n_rot, &jobs[i].rope_inv);
+		if (rc != NNCU_OK) return rc;
+		jobs[i].tok0 = tok;
+		tok += p.n_tok;
+		qrot_floats += align_up((size_t)p.n_tok * p.n_head * p.head_dim, 64);
+	}
+	CU(kv->qrot.reserve(qrot_floats * sizeof(float)), "q scratch");
+	size_t off = 0;
+	for (int i = 0; i < n; ++i)
+	{
+		jobs[i].q_rot = static_cast<float*>(kv->qrot.p) + off;
+		off += align_up((size_t)jobs[i].n_tok * jobs[i].n_head * jobs[i].D, 64);
+	}
+	// Every job of one launch shares head_dim (the kernels are specialised on it).
+	for (int i = 1; i < n; ++i)
+		if (jobs[i].D != jobs[0].D)
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "jobs of one call must share head_dim (%d vs %d)", jobs[i].D,
+			            jobs[0].D);
+	DecodePlan P{};
+	plan_decode(kv, jobs, P);
+	// scratch for partials and the per-segment counters
+	const size_t part_floats = (size_t)(P.n_segments + P.n_ctas) * P.RM * (P.D + 2);
+	CU(kv->parts.reserve(part_floats * sizeof(float)), "partials scratch");
+	if (P.n_segments > kv->counters_n)
+	{
+		CU(kv->counters.reserve((size_t)P.n_segments * sizeof(int)), "counters");
+		CU(cudaMemsetAsync(kv->counters.p, 0, kv->counters.cap, st), "counters clear");
+		kv->counters_n = (int)(kv->counters.cap / sizeof(int));
+	}
+	P.parts = static_cast<float*>(kv->parts.p);
+	P.counters = static_cast<int*>(kv->counters.p);
+	// the job table: pinned -> device on the stream; the pinned copy is reused
+	// only after the previous upload has been read
+	const size_t jb = (size_t)n * sizeof(DevJob);
+	CU(cudaEventSynchronize(kv->jobs_uploaded), "job table reuse");
+	CU(kv->jobs_host.reserve(jb), "job table (host)");
+	CU(kv->jobs_dev.reserve(jb), "job table (device)");
+	std::memcpy(kv->jobs_host.p, jobs.data(), jb);
+	CU(cudaMemcpyAsync(kv->jobs_dev.p, kv->jobs_host.p, jb, cudaMemcpyHostToDevice, st), "job table upload");
+	CU(cudaEventRecord(kv->jobs_uploaded, st), "job table event");
+	P.jobs = static_cast<const DevJob*>(kv->jobs_dev.p);
+	// jobs whose queries see no key at all produce zeros, as nnc_attn_finish does for l = 0
+	for (int i = 0; i < n; ++i)
+		if (jobs[i].n_tiles == 0)
+			CU(cudaMemsetAsync(jobs[i].out, 0, (size_t)jobs[i].n_tok * jobs[i].n_head * jobs[i].D * sizeof(float), st),
+			   "empty output");
+	// algorithmic bytes: K1 reads q, k, v and writes rotated q and the appended rows;
+	// K2 reads the K/V rows of every key attended (once per KV head) and q, and writes the output
+	uint64_t rope_bytes = 0, core_bytes = 0;
+	const size_t es = kv_esize(kv->kv_type);
+	for (const auto& j : jobs)
+	{
+		const uint64_t qb = (uint64_t)j.n_tok * j.n_head * j.D * 4;
+		const uint64_t kvb = j.reuse_kv ? 0 : (uint64_t)j.n_tok * j.n_kv * j.D;
+		rope_bytes += 2 * qb + kvb * 4 * 2 + kvb * es * 2;
+		int first_min = INT_MAX, last_max = -1;
+		for (int t = 0; t < j.n_tok; ++t)
+		{
+			int f, l;
+			nncu_attn_span(j.causal, j.window, j.pos0 + t, j.n_seq, &f, &l);
+			if (l < f) continue;
+			first_min = std::min(first_min, f);
+			last_max = std::max(last_max, l);
+		}
+		const uint64_t keys = last_max >= first_min ? (uint64_t)(last_max - first_min + 1) : 0;
+		core_bytes += keys * j.n_kv * j.D * es * 2 + 2 * qb;
+	}
+	int e;
+	{
+		PerfScope ps(NNCU_PERF_ATTN_ROPE, rope_bytes, st);
+		e = launch_prep(P.jobs, n, tok, 0, P.D, kv->kv_type, st);
+	}
+	if (e) return cuda_fail((cudaError_t)e, "K1 (norm, RoPE, append) launch");
+	{
+		PerfScope ps(NNCU_PERF_ATTN_CORE, core_bytes, st);
+		e = launch_decode(P, st);
+	}
+	if (e) return cuda_fail((cudaError_t)e, "K2 (attention) launch");
+	return NNCU_OK;
+}
+
+int check_device_error(nncu_kv* kv)
+{
+	int h = 0;
+	CU(cudaMemcpy(&h, kv->err_dev, sizeof(int), cudaMemcpyDeviceToHost), "error word");
+	if (h != 0)
+	{
+		cudaMemset(kv->err_dev, 0, sizeof(int));
+		return fail(NNCU_ERR_TIMEOUT, "a kernel's bounded wait timed out (code %d); the output is void", h);
+	}
+	return NNCU_OK;
+}
+
+size_t fbytes(size_t n) { return align_up(n * sizeof(float), 256); }
+
+} // namespace
+
+extern "C" int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs, void* stream)
+{
+	if (!kv || !jobs || n_jobs <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "no jobs");
+	for (int i = 0; i < n_jobs; ++i)
+	{
+		int rc = validate_job(kv, jobs[i]);
+		if (rc != NNCU_OK) return rc;
+		if (!jobs[i].q || !jobs[i].out || (!jobs[i].p.reuse_kv && (!jobs[i].k || !jobs[i].v)))
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: NULL input or output", i);
+	}
+	int rc = check_conflicts(kv, jobs, n_jobs);
+	if (rc != NNCU_OK) return rc;
+	DeviceGuard g(kv->device);
+	std::vector<nncu_attn_job> pub(jobs, jobs + n_jobs);
+	kv->jobs_tmp.resize(n_jobs);
+	for (int i = 0; i < n_jobs; ++i) fill_devjob(kv, pub[i], kv->jobs_tmp[i]);
+	return run_jobs(kv, kv->jobs_tmp, pub, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs)
+{
+	if (!kv || !jobs || n_jobs <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "no jobs");
+	// Stage every input in one pinned block, copy it up in one transfer, run,
+	// and bring every output back in one transfer.
+	std::vector<size_t> in_off(n_jobs * 6), out_off(n_jobs);
+	size_t in_bytes = 0, out_bytes = 0;
+	for (int i = 0; i < n_jobs; ++i)
+	{
+		int rc = validate_job(kv, jobs[i]);
+		if (rc != NNCU_OK) return rc;
+		const nncu_attn_params& p = jobs[i].p;
+		if (!jobs[i].q || !jobs[i].out || (!p.reuse_kv && (!jobs[i].k || !jobs[i].v)))
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: NULL input or output", i);
+		const size_t qn = (size_t)p.n_tok * p.n_head * p.head_dim, kn = (size_t)p.n_tok * p.n_kv * p.head_dim;
+		const size_t sizes[6] = {qn, p.reuse_kv ? 0 : kn, p.reuse_kv ? 0 : kn, p.q_gamma ? (size_t)p.head_dim : 0,
+		                         p.k_gamma ? (size_t)p.head_dim : 0, p.freq_factors ? (size_t)p.n_rot / 2 : 0};
+		for (int s = 0; s < 6; ++s)
+		{
+			in_off[i * 6 + s] = in_bytes;
+			in_bytes += fbytes(sizes[s]);
+		}
+		out_off[i] = out_bytes;
+		out_bytes += fbytes(qn);
+	}
+	int rc0 = check_conflicts(kv, jobs, n_jobs);
+	if (rc0 != NNCU_OK) return rc0;
+	DeviceGuard g(kv->device);
+	CU(kv->stage_host.reserve(in_bytes + out_bytes), "pinned staging");
+	CU(kv->stage_dev.reserve(in_bytes + out_bytes), "device staging");
+	CU(cudaStreamSynchronize(kv->stream), "staging reuse");
+	char* hs = static_cast<char*>(kv->stage_host.p);
+	char* ds = static_cast<char*>(kv->stage_dev.p);
+	std::vector<nncu_attn_job> dj(jobs, jobs + n_jobs);
+	for (int i = 0; i < n_jobs; ++i)
+	{
+		const nncu_attn_params& p = jobs[i].p;
+		const size_t qn = (size_t)p.n_tok * p.n_head * p.head_dim, kn = (size_t)p.n_tok * p.n_kv * p.head_dim;
+		const float* srcs[6] = {jobs[i].q, jobs[i].k, jobs[i].v, p.q_gamma, p.k_gamma, p.freq_factors};
+		const size_t sizes[6] = {qn, p.reuse_kv ? 0 : kn, p.reuse_kv ? 0 : kn, p.q_gamma ? (size_t)p.head_dim : 0,
+		                         p.k_gamma ? (size_t)p.head_dim : 0, p.freq_factors ? (size_t)p.n_rot / 2 : 0};
+		const float* dptr[6];
+		for (int s = 0; s < 6; ++s)
+		{
+			dptr[s] = sizes[s] ? reinterpret_cast<const float*>(ds + in_off[i * 6 + s]) : nullptr;
+			if (sizes[s]) std::memcpy(hs + in_off[i * 6 + s], srcs[s], sizes[s] * sizeof(float));
+		}
+		dj[i].q = dptr[0];
+		dj[i].k = dptr[1];
+		dj[i].v = dptr[2];
+		dj[i].p.q_gamma = dptr[3];
+		dj[i].p.k_gamma = dptr[4];
+		dj[i].p.freq_factors = dptr[5];
+		dj[i].out = reinterpret_cast<float*>(ds + in_bytes + out_off[i]);
+	}
+	CU(cudaMemcpyAsync(ds, hs, in_bytes, cudaMemcpyHostToDevice, kv->stream), "input upload");
+	kv->jobs_tmp.resize(n_jobs);
+	for (int i = 0; i < n_jobs; ++i) fill_devjob(kv, dj[i], kv->jobs_tmp[i]);
+	int rc = run_jobs(kv, kv->jobs_tmp, dj, kv->stream);
+	if (rc != NNCU_OK) return rc;
+	CU(cudaMemcpyAsync(hs + in_bytes, ds + in_bytes, out_bytes, cudaMemcpyDeviceToHost, kv->stream), "output download");
+	CU(cudaStreamSynchronize(kv->stream), "attention");
+	rc = check_device_error(kv);
+	if (rc != NNCU_OK) return rc;
+	for (int i = 0; i < n_jobs; ++i)
+	{
+		const nncu_attn_params& p = jobs[i].p;
+		std::memcpy(jobs[i].out, hs + in_bytes + out_off[i], (size_t)p.n_tok * p.n_head * p.head_dim * sizeof(float));
+	}
+	return NNCU_OK;
+}
+
+extern "C" int nncu_sync(nncu_kv* kv, void* stream)
+{
+	if (!kv) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL cache");
+	DeviceGuard g(kv->device);
+	CU(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "stream");
+	return check_device_error(kv);
+}
+
+extern "C" int nncu_attention(nncu_kv* kv, int32_t layer, int32_t seq, const nncu_attn_params* p, const float* q,
+                              const float* k, const float* v, float* out)
+{
+	if (!p) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL parameters");
+	nncu_attn_job j{};
+	j.layer = layer;
+	j.seq = seq;
+	j.p = *p;
+	j.q = q;
+	j.k = k;
+	j.v = v;
+	j.out = out;
+	return nncu_attention_batch(kv, &j, 1);
+}
+
+// ---- unit seam on device pointers ----------------------------------------------------------------
+
+namespace
+{
+int launched(int e, const char* what)
+{
+	if (e) return cuda_fail((cudaError_t)e, what);
+	g_launches.fetch_add(1, std::memory_order_relaxed);
+	return NNCU_OK;
+}
+} // namespace
+
+extern "C" int nncu_attn_block_dev(const float* q, size_t q_stride, const void* K, const void* V, int kv_type,
+                                   size_t kv_stride, size_t n_keys, size_t head_dim, size_t n_heads, float scale,
+                                   float softcap, float* part, void* stream)
+{
+	if (kv_type != KV_F32 && kv_type != KV_BF16 && kv_type != KV_F16)
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "unknown K/V type %d", kv_type);
+	if (head_dim == 0 || head_dim > 512) return fail(NNCU_ERR_INVALID_ARGUMENT, "head_dim %zu out of range", head_dim);
+	if (n_keys == 0 || n_heads == 0) return NNCU_OK; // nnc_attn_block returns without writing
+	if (!q || !K || !V || !part) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL pointer");
+	return launched(launch_attn_block(q, q_stride, K, V, kv_type, kv_stride, n_keys, head_dim, n_heads, scale, softcap,
+	                                  part, stream),
+	                "attn_block");
+}
+
+extern "C" int nncu_attn_merge_dev(float* acc, const float* part, size_t head_dim, size_t n_heads, void* stream)
+{
+	if (!acc || !part) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL pointer");
+	return launched(launch_attn_merge(acc, part, head_dim, n_heads, stream), "attn_merge");
+}
+
+extern "C" int nncu_attn_finish_dev(float* out, size_t out_stride, const float* acc, size_t head_dim, size_t n_heads,
+                                    void* stream)
+{
+	if (!out || !acc) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL pointer");
+	return launched(launch_attn_finish(out, out_stride, acc, head_dim, n_heads, stream), "attn_finish");
+}
+
+extern "C" int nncu_rmsnorm_gamma_multi_dev(float* y, const float* x, size_t n_groups, size_t dim, const float* gamma,
+                                            float eps, void* stream)
+{
+	if (!y || !x || !gamma) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL pointer");
+	return launched(launch_rmsnorm(y, x, n_groups, dim, gamma, eps, stream), "rmsnorm_gamma_multi");
+}
+
+extern "C" int nncu_rmsnorm_dev(float* y, const float* x, size_t n_groups, size_t dim, float eps, void* stream)
+{
+	if (!y || !x) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL pointer");
+	return launched(launch_rmsnorm(y, x, n_groups, dim, nullptr, eps, stream), "rmsnorm");
+}
+
+namespace
+{
+std::mutex g_rope_mu;
+std::map<std::tuple<int, uint32_t, int>, float*> g_rope_unit; // (device, base bits, n_rot) -> table
+} // namespace
+
+extern "C" int nncu_rope_dev(float* x, uint32_t n_tok, uint32_t n_heads, uint32_t head_dim, uint32_t n_rot,
+                             int32_t pos0, float pos_scale, float freq_base, int mode, const float* freq_factors,
+                             void* stream)
+{
+	if (!x) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL pointer");
+	if (n_rot & 1u) return fail(NNCU_ERR_INVALID_ARGUMENT, "nnc_rope_f32: n_rot must be even");
+	if (n_rot > head_dim || n_rot / 2 > 256) return fail(NNCU_ERR_INVALID_ARGUMENT, "n_rot %u out of range", n_rot);
+	if (mode != NNCU_ROPE_NEOX && mode != NNCU_ROPE_NORM) return fail(NNCU_ERR_INVALID_ARGUMENT, "unknown rope mode");
+	if (n_rot == 0) return NNCU_OK;
+	int dev = 0;
+	cudaGetDevice(&dev);
+	uint32_t bits;
+	std::memcpy(&bits, &freq_base, 4);
+	float* tab = nullptr;
+	{
+		std::lock_guard<std::mutex> lk(g_rope_mu);
+		auto key = std::make_tuple(dev, bits, (int)n_rot);
+		auto it = g_rope_unit.find(key);
+		if (it == g_rope_unit.end())
+		{
+			std::vector<float> h;
+			rope_inv_table(freq_base, (int)n_rot, h);
+			CU(cudaMalloc(&tab, h.size() * sizeof(float)), "rope table");
+			CU(cudaMemcpy(tab, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice), "rope table upload");
+			g_rope_unit[key] = tab;
+		}
+		else
+			tab = it->second;
+	}
+	return launched(launch_rope(x, n_tok, n_heads, head_dim, n_rot, pos0, pos_scale, tab, mode, freq_factors, stream),
+	                "rope");
+}
+
+extern "C" int nncu_softcap_dev(float* y, const float* x, size_t n, float cap, void* stream)
+{
+	if (!y || !x) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL pointer");
+	if (!(cap > 0.0f)) return fail(NNCU_ERR_INVALID_ARGUMENT, "the cap must be positive");
+	return launched(launch_softcap(y, x, n, cap, stream), "softcap");
+}
+
+// ---- profiling ---------------------------------------------------------------------------------
+
+extern "C" void nncu_perf_enable(int enabled) { g_perf_on.store(enabled != 0); }
+
+extern "C" void nncu_perf_reset(void)
+{
+	std::lock_guard<std::mutex> lk(g_perf_mu);
+	for (auto& p : g_perf_pending)
+	{
+		cudaEventSynchronize(p.b);
+		g_perf_free.push_back(p.a);
+		g_perf_free.push_back(p.b);
+	}
+	g_perf_pending.clear();
+	for (auto& ph : g_perf) ph = nncu_perf_phase{0.0, 0, 0};
+}
+
+extern "C" int nncu_perf_read(nncu_perf_phase* out)
+{
+	std::lock_guard<std::mutex> lk(g_perf_mu);
+	for (auto& p : g_perf_pending)
+	{
+		float ms = 0.0f;
+		cudaError_t e = cudaEventSynchronize(p.b);
+		if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, p.a, p.b);
+		if (e != cudaSuccess) return cuda_fail(e, "profiler events");
+		g_perf[p.slot].ms += ms;
+		g_perf[p.slot].calls += 1;
+		g_perf[p.slot].bytes += p.bytes;
+		g_perf_free.push_back(p.a);
+		g_perf_free.push_back(p.b);
+	}
+	g_perf_pending.clear();
+	if (out)
+		for (int i = 0; i < NNCU_PERF_COUNT; ++i) out[i] = g_perf[i];
+	return NNCU_OK;
+}
+
+extern "C" const char* nncu_perf_report(const char* title, int32_t n_tokens)
+{
+	nncu_perf_phase ph[NNCU_PERF_COUNT];
+	if (nncu_perf_read(ph) != NNCU_OK) return "profiler unavailable";
+	static const char* names[NNCU_PERF_COUNT] = {"attn_rope", "attn_core"};
+	double total = 0.0;
+	for (const auto& p : ph) total += p.ms;
+	char line[256];
+	std::lock_guard<std::mutex> lk(g_perf_mu);
+	g_perf_text = std::string(title ? title : "nncu") + "\n";
+	g_perf_text += "phase           ms       %     calls    us/call     GB/s\n";
+	for (int i = 0; i < NNCU_PERF_COUNT; ++i)
+	{
+		const nncu_perf_phase& p = ph[i];
+		const double us = p.calls ? 1000.0 * p.ms / (double)p.calls : 0.0;
+		const double gbs = p.ms > 0.0 ? (double)p.bytes / (p.ms * 1e-3) / 1e9 : 0.0;
+		std::snprintf(line, sizeof line, "%-10s %9.3f %7.1f %9lld %10.2f %8.1f\n", names[i], p.ms,
+		              total > 0 ? 100.0 * p.ms / total : 0.0, (long long)p.calls, us, gbs);
+		g_perf_text += line;
+	}
+	if (n_tokens > 0)
+	{
+		std::snprintf(line, sizeof line, "per token: %.3f ms\n", total / n_tokens);
+		g_perf_text += line;
+	}
+	return g_perf_text.c_str();
+}
+
+extern "C" uint64_t nncu_launch_count(void) { return g_launches.load(); }

@@ -1,0 +1,348 @@
+// common.cuh -- device helpers shared by the kernels: element types, warp
+// reductions, and the sm_90+/sm_100 asynchronous-copy primitives (mbarrier,
+// cp.async.bulk) written as inline PTX.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "internal.h"
+
+namespace nncu
+{
+
+// ---- element types --------------------------------------------------------
+
+struct kv_f32
+{
+	using T = float;
+	static constexpr int esize = 4;
+	static constexpr int id = KV_F32;
+};
+struct kv_bf16
+{
+	using T = __nv_bfloat16;
+	static constexpr int esize = 2;
+	static constexpr int id = KV_BF16;
+};
+struct kv_f16
+{
+	using T = __half;
+	static constexpr int esize = 2;
+	static constexpr int id = KV_F16;
+};
+
+// fp32 -> stored element, round to nearest even (libnnc's nnc_f32_to_bf16,
+// runtime.h:106-113, is RNE on the upper 16 bits, as __float2bfloat16_rn is).
+__device__ __forceinline__ void store_elem(float* p, float x) { *p = x; }
+__device__ __forceinline__ void store_elem(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
+__device__ __forceinline__ void store_elem(__half* p, float x) { *p = __float2half_rn(x); }
+
+__device__ __forceinline__ float load_elem(const float* p) { return *p; }
+__device__ __forceinline__ float load_elem(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ float load_elem(const __half* p) { return __half2float(*p); }
+
+// A lane's share of a D-element row: E = D/32 elements, taken as chunks of
+// VEC consecutive elements (16 bytes, or all E if fewer) with the lanes'
+// chunks side by side, so each load instruction of a warp reads one
+// contiguous run of shared memory (no bank conflicts). Element e of lane
+// `lane` is row[lane_elem<E, VEC>(lane, e)].
+template <int E, int ESIZE>
+struct LaneVec
+{
+	static constexpr int VEC = (16 / ESIZE) < E ? (16 / ESIZE) : E;
+	static_assert(E % VEC == 0, "chunking");
+};
+
+template <int E, int VEC>
+__device__ __forceinline__ int lane_elem(int lane, int e)
+{
+	return (e / VEC) * 32 * VEC + lane * VEC + (e % VEC);
+}
+
+__device__ __forceinline__ float2 widen2(uint32_t w, const __half*)
+{
+	return __half22float2(*reinterpret_cast<const __half2*>(&w));
+}
+__device__ __forceinline__ float2 widen2(uint32_t w, const __nv_bfloat16*)
+{
+	return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w));
+}
+
+// Load lane `lane`'s E elements of `row` (shared or global) as floats.
+template <int E>
+__device__ __forceinline__ void load_lane(const float* row, int lane, float (&v)[E])
+{
+	constexpr int VEC = LaneVec<E, 4>::VEC;
+#pragma unroll
+	for (int c = 0; c < E / VEC; ++c)
+	{
+		const float* p = row + c * 32 * VEC + lane * VEC;
+		if constexpr (VEC == 4)
+		{
+			const float4 x = *reinterpret_cast<const float4*>(p);
+			v[c * 4] = x.x, v[c * 4 + 1] = x.y, v[c * 4 + 2] = x.z, v[c * 4 + 3] = x.w;
+		}
+		else if constexpr (VEC == 2)
+		{
+			const float2 x = *reinterpret_cast<const float2*>(p);
+			v[c * 2] = x.x, v[c * 2 + 1] = x.y;
+		}
+		else
+		{
+#pragma unroll
+			for (int j = 0; j < VEC; ++j) v[c * VEC + j] = p[j];
+		}
+	}
+}
+
+// fp32 rows read with another element type's lane mapping (VEC per chunk).
+template <int E, int VEC>
+__device__ __forceinline__ void load_lane_f(const float* row, int lane, float (&v)[E])
+{
+#pragma unroll
+	for (int c = 0; c < E / VEC; ++c)
+	{
+		const float* p = row + c * 32 * VEC + lane * VEC;
+		if constexpr (VEC % 4 == 0)
+		{
+#pragma unroll
+			for (int j = 0; j < VEC; j += 4)
+			{
+				const float4 x = *reinterpret_cast<const float4*>(p + j);
+				v[c * VEC + j] = x.x, v[c * VEC + j + 1] = x.y, v[c * VEC + j + 2] = x.z, v[c * VEC + j + 3] = x.w;
+			}
+		}
+		else if constexpr (VEC % 2 == 0)
+		{
+#pragma unroll
+			for (int j = 0; j < VEC; j += 2)
+			{
+				const float2 x = *reinterpret_cast<const float2*>(p + j);
+				v[c * VEC + j] = x.x, v[c * VEC + j + 1] = x.y;
+			}
+		}
+		else
+		{
+#pragma unroll
+			for (int j = 0; j < VEC; ++j) v[c * VEC + j] = p[j];
+		}
+	}
+}
+
+template <int E, typename H>
+__device__ __forceinline__ void load_lane_h(const H* row, int lane, float (&v)[E])
+{
+	constexpr int VEC = LaneVec<E, 2>::VEC;
+#pragma unroll
+	for (int c = 0; c < E / VEC; ++c)
+	{
+		const H* p = row + c * 32 * VEC + lane * VEC;
+		if constexpr (VEC == 8)
+		{
+			const uint4 x = *reinterpret_cast<const uint4*>(p);
+			const uint32_t w[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+			for (int j = 0; j < 4; ++j)
+			{
+				const float2 f = widen2(w[j], p);
+				v[c * 8 + 2 * j] = f.x, v[c * 8 + 2 * j + 1] = f.y;
+			}
+		}
+		else if constexpr (VEC == 4)
+		{
+			const uint2 x = *reinterpret_cast<const uint2*>(p);
+			const float2 f0 = widen2(x.x, p), f1 = widen2(x.y, p);
+			v[c * 4] = f0.x, v[c * 4 + 1] = f0.y, v[c * 4 + 2] = f1.x, v[c * 4 + 3] = f1.y;
+		}
+		else if constexpr (VEC == 2)
+		{
+			const float2 f = widen2(*reinterpret_cast<const uint32_t*>(p), p);
+			v[c * 2] = f.x, v[c * 2 + 1] = f.y;
+		}
+		else
+		{
+#pragma unroll
+			for (int j = 0; j < VEC; ++j) v[c * VEC + j] = load_elem(p + j);
+		}
+	}
+}
+
+template <int E>
+__device__ __forceinline__ void load_lane(const __half* row, int lane, float (&v)[E]) { load_lane_h<E>(row, lane, v); }
+template <int E>
+__device__ __forceinline__ void load_lane(const __nv_bfloat16* row, int lane, float (&v)[E])
+{
+	load_lane_h<E>(row, lane, v);
+}
+
+// ---- warp helpers ---------------------------------------------------------
+
+__device__ __forceinline__ float warp_sum(float x)
+{
+#pragma unroll
+	for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+	return x;
+}
+
+__device__ __forceinline__ float warp_max(float x)
+{
+#pragma unroll
+	for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+	return x;
+}
+
+// One exchange round of transpose_reduce: lanes whose MASK bit is set keep
+// the upper half of their values and send the lower half to the partner,
+// the others the reverse; each kept value gains the partner's copy.
+template <int N, int MASK>
+__device__ __forceinline__ float transpose_reduce_step(const float (&v)[N], int lane)
+{
+	if constexpr (N == 1)
+	{
+		float x = v[0];
+#pragma unroll
+		for (int o = MASK; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+		return x;
+	}
+	else
+	{
+		constexpr int H = N / 2;
+		const bool upper = (lane & MASK) != 0;
+		float keep[H];
+#pragma unroll
+		for (int i = 0; i < H; ++i)
+		{
+			const float send = upper ? v[i] : v[i + H];
+			const float mine = upper ? v[i + H] : v[i];
+			keep[i] = mine + __shfl_xor_sync(0xffffffffu, send, MASK);
+		}
+		return transpose_reduce_step<H, MASK / 2>(keep, lane);
+	}
+}
+
+// Sum N per-lane values over the warp, leaving each lane with ONE full sum:
+// lane l holds the sum of value index (l >> (5 - log2 N)). Each exchange
+// round hands half of the remaining values to the partner lane and keeps the
+// other half, so N values cost about N shuffles instead of 5 per value.
+template <int N>
+__device__ __forceinline__ float transpose_reduce(const float (&v)[N], int lane)
+{
+	static_assert(N >= 1 && N <= 32 && (N & (N - 1)) == 0, "N: power of two up to 32");
+	return transpose_reduce_step<N, 16>(v, lane);
+}
+
+// ---- asynchronous copies and barriers (PTX ISA 8.x, sm_90+) ----------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p)
+{
+	return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
+{
+	asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init()
+{
+	asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
+{
+	asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+	             : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar)
+{
+	asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
+{
+	uint32_t ok;
+	asm volatile(
+		"{\n\t.reg .pred p;\n\t"
+		"mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+		"selp.u32 %0, 1, 0, p;\n\t}"
+		: "=r"(ok)
+		: "r"(smem_u32(bar)), "r"(parity)
+		: "memory");
+	return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns()
+{
+	uint64_t t;
+	asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+	return t;
+}
+
+// Wait for phase `parity` of `bar`, giving up after WAIT_LIMIT_NS. Returns
+// false on timeout, after recording `code` in the device error word.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err, int code)
+{
+	if (mbar_try_wait(bar, parity)) return true;
+	const uint64_t t0 = globaltimer_ns();
+	for (uint32_t it = 0;; ++it)
+	{
+		if (mbar_try_wait(bar, parity)) return true;
+		if ((it & 255u) == 255u && globaltimer_ns() - t0 > WAIT_LIMIT_NS)
+		{
+			if (err) atomicCAS(err, 0, code);
+			return false;
+		}
+	}
+}
+
+// One contiguous global -> shared copy, completing on `bar` (bytes counted
+// against its expect_tx). Addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar)
+{
+	asm volatile(
+		"cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+			smem_u32(smem_dst)),
+		"l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+		: "memory");
+}
+
+// Named barrier over `count` threads (ids 1..15; 0 is __syncthreads).
+__device__ __forceinline__ void named_sync(int id, int count)
+{
+	asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ float ex2(float x)
+{
+	float y;
+	asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+	return y;
+}
+
+// The keys [first, last] the query at `pos` sees (model.cpp:2300-2316).
+__device__ __forceinline__ void span_of(int causal, int window, int pos, int n_seq, int& first, int& last)
+{
+	if (causal)
+	{
+		first = (window > 0 && pos + 1 > window) ? pos + 1 - window : 0;
+		last = min(pos, n_seq - 1);
+	}
+	else
+	{
+		first = 0;
+		last = n_seq - 1;
+		if (window > 0)
+		{
+			const int half = window / 2;
+			first = max(0, pos - half);
+			last = min(n_seq - 1, pos + half);
+		}
+	}
+}
+
+} // namespace nncu

@@ -1,0 +1,100 @@
+// internal.h -- what the host side (api.cpp) and the kernels (*.cu) share:
+// the per-job device descriptor, the work plan of the decode kernel, and the
+// launchers. Plain C++: no CUDA headers are needed to include it.
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+namespace nncu
+{
+
+enum
+{
+	KV_BF16 = 0,
+	KV_F32 = 1,
+	KV_F16 = 2
+};
+
+constexpr int ATTN_BLOCK = 256;                      // MODEL_ATTN_BLOCK (model.h:229)
+constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull; // bounded waits give up after 2 s
+
+// Device error codes written by kernels into the per-cache error word.
+enum
+{
+	DEVERR_NONE = 0,
+	DEVERR_WAIT_FULL = 1,  // a consumer's wait for a K/V tile ran out
+	DEVERR_WAIT_EMPTY = 2, // the producer's wait for a free stage ran out
+	DEVERR_PLAN = 3        // a tile fell outside every job (a planning bug)
+};
+
+inline int kv_esize(int kv_type) { return kv_type == KV_F32 ? 4 : 2; }
+
+// One attention job (one layer of one sequence) as the kernels see it.
+// All pointers are device pointers.
+struct DevJob
+{
+	const float* q;           // [n_tok][n_head*D] projections, fp32
+	const float* k;           // [n_tok][n_kv*D]
+	const float* v;
+	float* q_rot;             // [n_tok][n_head*D] normed + rotated q (scratch)
+	float* out;               // [n_tok][n_head*D]
+	const float* q_gamma;     // D or null
+	const float* k_gamma;     // D or null
+	const float* freq_factors; // n_rot/2 or null
+	const float* rope_inv;    // n_rot/2: the fp32 inverse-frequency recurrence
+	char* K;                  // this sequence's K slab: [n_kv][rows][D]
+	char* V;
+	long long head_bytes;     // rows * D * esize
+	int rows;                 // allocated rows (a multiple of 256); position p -> row p % rows
+	int n_tok, pos0, n_seq;
+	int n_head, n_kv, D, n_rot, rope_mode;
+	int causal, window, reuse_kv, v_rmsnorm;
+	float rope_scale, eps, scale, softcap;
+	// the decode plan (filled by plan_decode on the host)
+	int tile_lo;          // first tile (absolute, units of T keys) of the union of the tokens' spans
+	int n_tiles;          // tiles per segment
+	int n_rowgroups;      // segments per KV head (query rows split into groups of RM)
+	int seg0;             // this job's first segment
+	long long gtile0;     // this job's first tile in the launch's global tile order
+	int tok0;             // this job's first token in the launch's global token order
+	int pad_;
+};
+
+// The decode launch: stream-K over the concatenated tiles of every segment.
+struct DecodePlan
+{
+	const DevJob* jobs; // device array
+	int n_jobs;
+	int D, kv_type, RM, T; // head_dim, element type, query rows per segment, keys per tile
+	long long total_tiles;
+	int n_ctas;
+	long long tiles_per_cta;
+	int n_segments;
+	float* parts;   // (n_segments + n_ctas) slots of RM * (D + 2) floats
+	int* counters;  // n_segments, zero between launches
+	int* err;       // device error word
+};
+
+// Launchers (implemented in the .cu files). Each returns a cudaError_t value.
+int launch_prep(const DevJob* jobs_dev, int n_jobs, int total_tok, int max_heads, int D, int kv_type, void* stream);
+int launch_decode(const DecodePlan& plan, void* stream);
+bool decode_supported(int D, int kv_type);
+int decode_tile_keys(int D, int kv_type);
+int decode_rows_max(int D);
+int decode_smem_bytes(int D, int kv_type, int RM);
+
+// Unit-seam kernels (nn_ops.h equivalents).
+int launch_attn_block(const float* q, size_t q_stride, const void* K, const void* V, int kv_type, size_t kv_stride,
+                      size_t n_keys, size_t head_dim, size_t n_heads, float scale, float softcap, float* part,
+                      void* stream);
+int launch_attn_merge(float* acc, const float* part, size_t head_dim, size_t n_heads, void* stream);
+int launch_attn_finish(float* out, size_t out_stride, const float* acc, size_t head_dim, size_t n_heads,
+                       void* stream);
+int launch_rmsnorm(float* y, const float* x, size_t n_groups, size_t dim, const float* gamma, float eps,
+                   void* stream);
+int launch_rope(float* x, uint32_t n_tok, uint32_t n_heads, uint32_t head_dim, uint32_t n_rot, int32_t pos0,
+                float pos_scale, const float* rope_inv, int mode, const float* freq_factors, void* stream);
+int launch_softcap(float* y, const float* x, size_t n, float cap, void* stream);
+
+} // namespace nncu

@@ -1,0 +1,207 @@
+// k_prep.cu -- K1: the per-head work attention_forward does between the
+// projections and the attention proper (src/libnnc/model.cpp:1616-1694):
+// Q/K RMSNorm with gamma (nnc_rmsnorm_gamma_multi_f32, nn_ops.cpp:590-632),
+// Gemma 4's plain V RMSNorm (nn_ops.cpp:558-588), RoPE on q and on fresh k
+// (nnc_rope_f32, nn_ops.cpp:1830-1873), and the append of k, v at row
+// pos % rows in the cache's element type. One launch covers every token of
+// every job; a warp takes one (token, head) vector at a time.
+//
+// Also the unit-seam kernels for nnc_rmsnorm*, nnc_rope_f32 and
+// nnc_softcap_f32 on device pointers.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace nncu
+{
+namespace
+{
+
+constexpr int PREP_WARPS = 8;
+constexpr int PREP_MAX_D = 512;
+
+// RMS scale of a D-vector held in `buf` (lane-strided), the reference's form:
+// 1 / sqrt(sum(x^2) * (1/D) + eps) evaluated in double.
+__device__ __forceinline__ float rms_scale(const float* buf, int D, float eps, bool gamma_form)
+{
+	float ss = 0.0f;
+	for (int i = threadIdx.x & 31; i < D; i += 32) ss = fmaf(buf[i], buf[i], ss);
+	ss = warp_sum(ss);
+	// nnc_rmsnorm_gamma_multi_f32 multiplies by a float 1/dim; nnc_rmsnorm_f32 divides by n.
+	const double mean = gamma_form ? (double)ss * (double)(1.0f / (float)D) : (double)ss / (double)D;
+	return (float)(1.0 / sqrt(mean + (double)eps));
+}
+
+// Rotate the first n_rot lanes of the vector in `buf` for position rpos.
+__device__ __forceinline__ void rope_vec(float* buf, int n_rot, int mode, float rpos, const float* inv,
+                                         const float* ff)
+{
+	const int half = n_rot / 2;
+	const int step = mode == 0 ? 1 : 2;     // NEOX pairs i, i + half; NORM pairs 2i, 2i + 1
+	const int other = mode == 0 ? half : 1;
+	for (int i = threadIdx.x & 31; i < half; i += 32)
+	{
+		float theta = rpos * inv[i];
+		if (ff) theta = __fdiv_rn(theta, ff[i]);
+		float sn, cs;
+		sincosf(theta, &sn, &cs);
+		float* p = buf + i * step;
+		const float a = p[0], b = p[other];
+		p[0] = cs * a - sn * b;
+		p[other] = sn * a + cs * b;
+	}
+}
+
+template <typename KV>
+__global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __restrict__ jobs, int n_jobs)
+{
+	using T = typename KV::T;
+	__shared__ float bufs[PREP_WARPS][PREP_MAX_D];
+	__shared__ int s_job;
+	if (threadIdx.x == 0)
+	{
+		// the job holding global token blockIdx.x (jobs are ordered by tok0)
+		int lo = 0, hi = n_jobs - 1;
+		while (lo < hi)
+		{
+			const int mid = (lo + hi + 1) >> 1;
+			if (jobs[mid].tok0 <= (int)blockIdx.x) lo = mid;
+			else hi = mid - 1;
+		}
+		s_job = lo;
+	}
+	__syncthreads();
+	const DevJob& j = jobs[s_job];
+	const int t = blockIdx.x - j.tok0;
+	if (t < 0 || t >= j.n_tok) return;
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const int D = j.D;
+	float* buf = bufs[warp];
+	const int n_q = j.n_head, n_kv = j.reuse_kv ? 0 : j.n_kv;
+	const int n_tasks = n_q + 2 * n_kv;
+	const float rpos = (float)(j.pos0 + t) * j.rope_scale;
+	const int row = (j.pos0 + t) % j.rows;
+	for (int task = warp; task < n_tasks; task += PREP_WARPS)
+	{
+		const int kind = task < n_q ? 0 : (task < n_q + n_kv ? 1 : 2); // q, k, v
+		const int h = kind == 0 ? task : (kind == 1 ? task - n_q : task - n_q - n_kv);
+		const float* src = kind == 0 ? j.q + ((size_t)t * n_q + h) * D
+		                             : (kind == 1 ? j.k : j.v) + ((size_t)t * j.n_kv + h) * D;
+		for (int i = lane; i < D; i += 32) buf[i] = src[i];
+		__syncwarp();
+		const float* gamma = kind == 0 ? j.q_gamma : (kind == 1 ? j.k_gamma : nullptr);
+		if (gamma)
+		{
+			const float sc = rms_scale(buf, D, j.eps, true);
+			for (int i = lane; i < D; i += 32) buf[i] = buf[i] * sc * gamma[i];
+		}
+		else if (kind == 2 && j.v_rmsnorm)
+		{
+			const float sc = rms_scale(buf, D, j.eps, false);
+			for (int i = lane; i < D; i += 32) buf[i] = buf[i] * sc;
+		}
+		__syncwarp();
+		if (kind != 2 && j.n_rot > 0) rope_vec(buf, j.n_rot, j.rope_mode, rpos, j.rope_inv, j.freq_factors);
+		__syncwarp();
+		if (kind == 0)
+		{
+			float* dst = j.q_rot + ((size_t)t * n_q + h) * D;
+			for (int i = lane; i < D; i += 32) dst[i] = buf[i];
+		}
+		else
+		{
+			char* base = (kind == 1 ? j.K : j.V) + (size_t)h * j.head_bytes;
+			T* dst = reinterpret_cast<T*>(base) + (size_t)row * D;
+			for (int i = lane; i < D; i += 32) store_elem(dst + i, buf[i]);
+		}
+		__syncwarp();
+	}
+}
+
+// ---- unit seam ---------------------------------------------------------------
+
+__global__ void rmsnorm_kernel(float* y, const float* x, size_t n_groups, size_t dim, const float* gamma, float eps)
+{
+	const size_t g = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+	if (g >= n_groups) return;
+	const int lane = threadIdx.x & 31;
+	const float* xg = x + g * dim;
+	float ss = 0.0f;
+	for (size_t i = lane; i < dim; i += 32) ss = fmaf(xg[i], xg[i], ss);
+	ss = warp_sum(ss);
+	const double mean = gamma ? (double)ss * (double)(1.0f / (float)dim) : (double)ss / (double)dim;
+	const float sc = (float)(1.0 / sqrt(mean + (double)eps));
+	float* yg = y + g * dim;
+	for (size_t i = lane; i < dim; i += 32) yg[i] = gamma ? xg[i] * sc * gamma[i] : xg[i] * sc;
+}
+
+__global__ void rope_kernel(float* x, uint32_t n_tok, uint32_t n_heads, uint32_t head_dim, uint32_t n_rot,
+                            int32_t pos0, float pos_scale, const float* inv, int mode, const float* ff)
+{
+	extern __shared__ float sbuf[];
+	const uint32_t w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+	if (w >= n_tok * n_heads) return;
+	const uint32_t t = w / n_heads;
+	float* xh = x + (size_t)w * head_dim;
+	float* buf = sbuf + (threadIdx.x >> 5) * head_dim;
+	for (uint32_t i = threadIdx.x & 31; i < head_dim; i += 32) buf[i] = xh[i];
+	__syncwarp();
+	rope_vec(buf, (int)n_rot, mode, (float)(pos0 + (int32_t)t) * pos_scale, inv, ff);
+	__syncwarp();
+	for (uint32_t i = threadIdx.x & 31; i < head_dim; i += 32) xh[i] = buf[i];
+}
+
+__global__ void softcap_kernel(float* y, const float* x, size_t n, float cap)
+{
+	const float inv = 1.0f / cap;
+	for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+		y[i] = tanhf(x[i] * inv) * cap;
+}
+
+} // namespace
+
+int launch_prep(const DevJob* jobs_dev, int n_jobs, int total_tok, int max_heads, int D, int kv_type, void* stream)
+{
+	(void)max_heads;
+	if (D > PREP_MAX_D) return (int)cudaErrorInvalidValue;
+	if (total_tok == 0) return 0;
+	auto st = static_cast<cudaStream_t>(stream);
+	switch (kv_type)
+	{
+	case KV_F32: prep_kernel<kv_f32><<<total_tok, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
+	case KV_BF16: prep_kernel<kv_bf16><<<total_tok, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
+	default: prep_kernel<kv_f16><<<total_tok, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
+	}
+	return (int)cudaGetLastError();
+}
+
+int launch_rmsnorm(float* y, const float* x, size_t n_groups, size_t dim, const float* gamma, float eps,
+                   void* stream)
+{
+	if (n_groups == 0 || dim == 0) return 0;
+	const unsigned blocks = (unsigned)((n_groups + 7) / 8);
+	rmsnorm_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, x, n_groups, dim, gamma, eps);
+	return (int)cudaGetLastError();
+}
+
+int launch_rope(float* x, uint32_t n_tok, uint32_t n_heads, uint32_t head_dim, uint32_t n_rot, int32_t pos0,
+                float pos_scale, const float* rope_inv, int mode, const float* freq_factors, void* stream)
+{
+	if (n_rot == 0 || n_tok == 0 || n_heads == 0) return 0;
+	const uint32_t warps = n_tok * n_heads;
+	const unsigned blocks = (warps + 7) / 8;
+	const size_t smem = (size_t)8 * head_dim * sizeof(float);
+	rope_kernel<<<blocks, 256, smem, static_cast<cudaStream_t>(stream)>>>(x, n_tok, n_heads, head_dim, n_rot, pos0,
+	                                                                      pos_scale, rope_inv, mode, freq_factors);
+	return (int)cudaGetLastError();
+}
+
+int launch_softcap(float* y, const float* x, size_t n, float cap, void* stream)
+{
+	if (n == 0) return 0;
+	const unsigned blocks = (unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+	softcap_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(y, x, n, cap);
+	return (int)cudaGetLastError();
+}
+
+} // namespace nncu

@@ -1,0 +1,258 @@
+"""Parity of the CUDA attention path (norm + RoPE + append: K1; split-KV
+attention with its in-kernel merge: K2+K3) with the checker, through the
+C ABI. Tolerance (north_star): max-abs 2e-3 and relative-L2 1e-3 for fp32 and
+fp16 caches; fp32 caches are also held to 1e-5, which any indexing or
+masking mistake would break."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import oracle as O
+from oracle import scenarios as S
+from oracle.scenarios import LayerSpec
+
+from golden import cases as G
+from gpu_helpers import assert_close, make_cache, run_product
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "golden.npz"))
+
+
+def check_case(N, case, tight=None, batch=False):
+    want, caches = S.run_checker(case, "oracle")
+    got, kv = run_product(N, case, batch=batch)
+    if tight is None:
+        tight = case.kv_type == O.KV_F32
+    for s in range(case.n_seqs):
+        for li in range(len(case.layers)):
+            assert_close(got[s][li], want[s][li], f"seq {s} layer {li}")
+            if tight:
+                assert_close(got[s][li], want[s][li], f"seq {s} layer {li} (fp32, tight)", 1e-5, 1e-5)
+    # the appended rows: V is a plain rounding (bit-exact), K went through norm + RoPE
+    for s in range(case.n_seqs):
+        for owner, (Kc, Vc) in caches[s].items():
+            if case.layers[owner].kv_layer not in (None, owner):
+                continue
+            p0 = case.pos0[s]
+            rows = case.rows[owner]
+            k_dev, v_dev = kv.read_rows(owner, p0, case.n_tok, seq=s) if case.causal else kv.read_rows(owner, 0, case.n_tok, seq=s)
+            idx = [(p0 + t) % rows for t in range(case.n_tok)] if case.causal else list(range(case.n_tok))
+            if not case.causal and owner != len(case.layers) - 1:
+                continue  # a bidirectional model's shared buffer holds the last layer's rows
+            if not case.layers[owner].v_rmsnorm:
+                assert np.array_equal(v_dev, Vc[idx]), f"appended V rows differ (seq {s}, layer {owner})"
+            kd = O.widen(k_dev, case.kv_type).astype(np.float64)
+            kw = O.widen(Kc[idx], case.kv_type).astype(np.float64)
+            step, floor = {O.KV_F32: (2.0 ** -20, 1.0), O.KV_BF16: (2.0 ** -7, 1e-2), O.KV_F16: (2.0 ** -10, 1e-2)}[
+                case.kv_type]
+            assert np.all(np.abs(kd - kw) <= step * np.maximum(np.abs(kw), floor)), f"appended K rows (seq {s})"
+    kv.close()
+    return got
+
+
+@pytest.mark.parametrize("name", sorted(G.all_cases().keys()))
+def test_golden_cases(nncu, name):
+    case = G.all_cases()[name]
+    got = check_case(nncu, case)
+    # and straight against the reference's own outputs
+    for s in range(case.n_seqs):
+        for li in range(len(case.layers)):
+            key = f"{name}.out.{s}.{li}"
+            if key in GOLDEN.files:
+                assert_close(got[s][li], GOLDEN[key], f"{key} vs the reference")
+
+
+@pytest.mark.parametrize("name", ["cfg2_stack_f32", "cfg4_verify_bf16", "window_partial_rope_f32"])
+def test_batch_call_matches(nncu, name):
+    check_case(nncu, G.all_cases()[name], batch=True)
+
+
+def test_cfg4_verify_f16(nncu):
+    g34 = [LayerSpec(8, 4, 256, window=1024, freq_base=1e4, qk_norm=True),
+           LayerSpec(8, 4, 256, window=0, freq_base=1e6, qk_norm=True)]
+    case = S.build_case(3, g34, n_ctx=4096, n_tok=4, pos0=[2000, 3100, 4092], kv_type=O.KV_F16)
+    check_case(nncu, case)
+
+
+def test_cfg5_long_f16_reduced(nncu):
+    case = S.build_case(4, [LayerSpec(32, 8, 64, freq_base=5e5, rope_mode=O.ROPE_NORM)], n_ctx=16384 + 16,
+                        n_tok=1, pos0=16384, kv_type=O.KV_F16)
+    check_case(nncu, case)
+
+
+@pytest.mark.parametrize("D", [64, 128, 256, 512])
+@pytest.mark.parametrize("kv_type", [O.KV_F32, O.KV_BF16, O.KV_F16])
+@pytest.mark.parametrize("G_,n_tok", [(1, 1), (4, 1), (2, 3), (8, 2)])
+def test_shapes_and_types(nncu, D, kv_type, G_, n_tok):
+    # spans that start and end inside tiles and blocks, two KV heads
+    n_kv = 2
+    L = [LayerSpec(G_ * n_kv, n_kv, D, freq_base=1e4, qk_norm=(D != 512))]
+    case = S.build_case(100 + D + G_, L, n_ctx=700, n_tok=n_tok, pos0=[257, 3], kv_type=kv_type)
+    check_case(nncu, case)
+
+
+@pytest.mark.parametrize("pos0", [0, 1, 15, 16, 255, 256, 511])
+def test_span_edges(nncu, pos0):
+    L = [LayerSpec(8, 2, 128, freq_base=1e6), LayerSpec(8, 2, 128, window=100, freq_base=1e4)]
+    case = S.build_case(200 + pos0, L, n_ctx=1024, n_tok=2, pos0=pos0, kv_type=O.KV_F32)
+    check_case(nncu, case)
+
+
+def test_softcap_and_norm_rope(nncu):
+    L = [LayerSpec(8, 2, 256, freq_base=1e4, rope_mode=O.ROPE_NORM, softcap=50.0, qk_norm=True),
+         LayerSpec(8, 2, 256, freq_base=1e4, softcap=20.0, n_rot=128, v_rmsnorm=True, scale=1.0)]
+    case = S.build_case(300, L, n_ctx=900, n_tok=3, pos0=800, kv_type=O.KV_BF16)
+    check_case(nncu, case)
+
+
+def test_config1_full(nncu):
+    case = S.build_case(0, [LayerSpec(32, 8, 64, freq_base=5e5, rope_mode=O.ROPE_NORM)], n_ctx=1025, n_tok=1,
+                        pos0=1024, kv_type=O.KV_F32, rotate_past=True)
+    check_case(nncu, case)
+
+
+def test_config2_full(nncu):
+    layers = [LayerSpec(4, 1, 256, window=0 if (li + 1) % 6 == 0 else 512, freq_base=1e6 if (li + 1) % 6 == 0 else 1e4,
+                        qk_norm=True) for li in range(26)]
+    case = S.build_case(1, layers, n_ctx=4097, n_tok=1, pos0=4096, kv_type=O.KV_F32, n_batch=1)
+    check_case(nncu, case, batch=True)
+
+
+def test_config5_full_f16(nncu):
+    case = S.build_case(4, [LayerSpec(32, 8, 64, freq_base=5e5, rope_mode=O.ROPE_NORM)], n_ctx=131073, n_tok=1,
+                        pos0=131072, kv_type=O.KV_F16)
+    check_case(nncu, case)
+
+
+def test_verify_rows_match_single_decodes(nncu):
+    """tests.cpp:2634-2663 (decode == batch) on the device: 3 tokens in one call
+    give what 3 one-token calls give, to within float rounding."""
+    L = [LayerSpec(8, 2, 128, freq_base=1e6, qk_norm=True)]
+    case = S.build_case(400, L, n_ctx=1200, n_tok=3, pos0=1100, kv_type=O.KV_F32)
+    got_batch, kv = run_product(nncu, case)
+    kv.close()
+    kv = make_cache(nncu, case)
+    inp = case.inputs[0][0]
+    rows = []
+    for t in range(3):
+        d = case.params_dict(0, 0)
+        d.update(n_tok=1, pos0=1100 + t, n_seq=1101 + t)
+        p = nncu.params(**d)
+        rows.append(kv.attention(0, p, inp.q[t:t + 1], inp.k[t:t + 1], inp.v[t:t + 1])[0])
+    kv.close()
+    assert np.abs(np.stack(rows) - got_batch[0][0]).max() <= 1e-6
+
+
+def test_repeatable_bits(nncu):
+    L = [LayerSpec(4, 1, 256, freq_base=1e6, qk_norm=True)]
+    case = S.build_case(500, L, n_ctx=5000, n_tok=1, pos0=4000, kv_type=O.KV_F32)
+    a, kv = run_product(nncu, case)
+    kv.close()
+    b, kv = run_product(nncu, case)
+    kv.close()
+    assert np.array_equal(a[0][0], b[0][0])
+
+
+def test_sliding_ring_through_wraps_and_rewind(nncu):
+    """tests.cpp:2598-2630 on the device: a sliding layer kept as a ring of 256
+    rows (window 40, batch 16) attends exactly as over a full buffer, through
+    many wraps, a step back, and a refused step back."""
+    N = nncu
+    layers = [LayerSpec(4, 2, 64, window=40, freq_base=1e4, qk_norm=True),
+              LayerSpec(4, 2, 64, window=0, freq_base=1e6, qk_norm=True)]
+    kv = N.KVCache([(2, 64, 40, 0), (2, 64, 0, 1)], n_ctx=1200, n_batch=16, kv_type=O.KV_BF16)
+    assert kv.layer_info(0).rows == 256 and kv.layer_info(0).window == 40 and kv.state().max_rewind == 216
+    full = {li: (np.zeros((1200, 128), np.uint16), np.zeros((1200, 128), np.uint16)) for li in (0, 1)}
+    rng = O.Rng(600)
+    gam = {li: (rng.normal(64, 1.0, 0.1), rng.normal(64, 1.0, 0.1)) for li in (0, 1)}
+
+    def forward(p0, p1, step):
+        for pos in range(p0, p1, step):
+            n = min(step, p1 - pos)
+            for li, L in enumerate(layers):
+                q, k, v = rng.normal(n * 256).reshape(n, 256), rng.normal(n * 128).reshape(n, 128), \
+                    rng.normal(n * 128).reshape(n, 128)
+                d = dict(n_tok=n, pos0=pos, n_seq=pos + n, n_head=4, n_kv=2, head_dim=64, freq_base=L.freq_base,
+                         q_gamma=gam[li][0], k_gamma=gam[li][1], window=L.window)
+                got = kv.attention(li, N.params(**d), q, k, v)
+                Kc, Vc = full[li]
+                want, _, _ = O.attention_forward(O.params(**d), q, k, v, Kc, Vc, O.KV_BF16, 1200)
+                assert_close(got, want, f"positions {pos}..{pos + n - 1}, layer {li}")
+            kv.commit(pos, n)
+
+    forward(0, 700, 16)
+    forward(700, 720, 1)
+    assert kv.rewind(705)
+    forward(705, 760, 16)
+    assert not kv.rewind(760 - 217) and kv.state().cur_pos == 760
+    assert kv.rewind(760 - 216) and kv.rewind(0)
+    forward(0, 300, 16)
+    kv.close()
+
+
+def test_device_pointer_batch_matches_host(nncu, torch_cuda):
+    torch = torch_cuda
+    N = nncu
+    layers = [LayerSpec(4, 1, 256, window=512, freq_base=1e4, qk_norm=True),
+              LayerSpec(4, 1, 256, window=0, freq_base=1e6, qk_norm=True)]
+    case = S.build_case(700, layers, n_ctx=2048, n_tok=1, pos0=1500, kv_type=O.KV_F32, n_batch=1)
+    want, kv_h = run_product(N, case)
+    kv_h.close()
+    kv = make_cache(N, case)
+    st = torch.cuda.Stream()
+    keep, outs, jobs = [], [], []
+    for li in range(2):
+        inp = case.inputs[0][li]
+        t = {k: torch.from_numpy(np.ascontiguousarray(getattr(inp, k))).cuda() for k in ("q", "k", "v", "q_gamma", "k_gamma")}
+        d = case.params_dict(li, 0)
+        d.update(q_gamma=t["q_gamma"].data_ptr(), k_gamma=t["k_gamma"].data_ptr())
+        out = torch.empty(1, 4 * 256, device="cuda")
+        jobs.append(N.job(li, N.params(**d), t["q"], t["k"], t["v"], out))
+        keep.append(t)
+        outs.append(out)
+    torch.cuda.synchronize()
+    kv.attention_batch_dev(jobs, st)
+    kv.sync(st)
+    for li in range(2):
+        assert np.array_equal(outs[li].cpu().numpy(), want[0][li])
+    kv.close()
+
+
+def test_errors_are_statuses(nncu):
+    N = nncu
+    kv = N.KVCache([(2, 64, 40, 0), (2, 64, 0, 1)], n_ctx=300, n_batch=4, kv_type=O.KV_F32)
+    q = np.zeros((1, 256), np.float32)
+    k = np.zeros((1, 128), np.float32)
+
+    def call(layer=1, **kw):
+        d = dict(n_tok=1, pos0=0, n_head=4, n_kv=2, head_dim=64, window=0)
+        d.update(kw)
+        n = d["n_tok"]
+        return kv.attention(layer, N.params(**d), np.zeros((n, 4 * d["head_dim"]), np.float32),
+                            np.zeros((n, 2 * d["head_dim"]), np.float32), np.zeros((n, 2 * d["head_dim"]), np.float32))
+
+    with pytest.raises(N.NnncError) as e:
+        call(pos0=300)
+    assert e.value.status == N.ERR_CONTEXT_FULL
+    with pytest.raises(N.NnncError) as e:
+        call(n_tok=5)
+    assert e.value.status == N.ERR_INVALID_ARGUMENT
+    with pytest.raises(N.NnncError) as e:
+        call(head_dim=32)
+    assert e.value.status == N.ERR_INVALID_ARGUMENT
+    with pytest.raises(N.NnncError) as e:
+        call(layer=0, window=64)  # a ring of window 40 cannot serve window 64
+    assert e.value.status == N.ERR_INVALID_ARGUMENT
+    with pytest.raises(N.NnncError) as e:
+        call(layer=1, reuse_kv=1)
+    assert e.value.status == N.ERR_INVALID_ARGUMENT
+    with pytest.raises(N.NnncError) as e:
+        call(n_head=3)
+    assert e.value.status == N.ERR_INVALID_ARGUMENT
+    assert not kv.rewind(5)  # beyond cur_pos
+    out = call(layer=1)  # and the cache still works
+    assert out.shape == (1, 256) and np.all(out == 0.0)
+    del q, k
+    kv.close()
