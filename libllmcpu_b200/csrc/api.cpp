@@ -11,6 +11,7 @@
 #include "nncu.h"
 
 #include <cuda_runtime.h>
+#include <vector_functions.h>
 
 #include <algorithm>
 #include <atomic>
@@ -124,6 +125,7 @@ struct HostBuf
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+
 // ---- the phase profiler (nnc_perf_*, runtime.h:147-195, on CUDA events) ----
 std::atomic<uint64_t> g_launches{0};
 std::atomic<bool> g_perf_on{false};
@@ -212,6 +214,8 @@ struct nncu_kv
 	DevBuf jobs_dev, stage_dev, qrot, parts, counters;
 	HostBuf stage_host, jobs_host;
 	cudaEvent_t jobs_uploaded = nullptr; // the last upload from jobs_host has been read
+	cudaEvent_t done = nullptr;          // the last submission's kernels have finished: calls on one
+	                                     // cache are ordered on the device whatever their streams
 	std::map<std::pair<uint32_t, int>, float*> rope_tables;
 	std::vector<DevJob> jobs_tmp;
 	int counters_n = 0;
@@ -235,6 +239,7 @@ struct nncu_kv
 		stage_host.release();
 		jobs_host.release();
 		if (jobs_uploaded) cudaEventDestroy(jobs_uploaded);
+		if (done) cudaEventDestroy(done);
 		if (stream) cudaStreamDestroy(stream);
 	}
 };
@@ -516,6 +521,7 @@ extern "C" int nncu_kv_create(const nncu_layer_desc* layers, int32_t n_layer, co
 	if (e == cudaSuccess) e = cudaMalloc(&kv->err_dev, sizeof(int));
 	if (e == cudaSuccess) e = cudaMemset(kv->err_dev, 0, sizeof(int));
 	if (e == cudaSuccess) e = cudaEventCreateWithFlags(&kv->jobs_uploaded, cudaEventDisableTiming);
+	if (e == cudaSuccess) e = cudaEventCreateWithFlags(&kv->done, cudaEventDisableTiming);
 	if (e != cudaSuccess) return fail_free(cuda_fail(e, "cache set-up"));
 	*out = kv;
 	return NNCU_OK;
@@ -761,7 +767,9 @@ void plan_decode(nncu_kv* kv, std::vector<DevJob>& jobs, DecodePlan& P)
 	P.T = T;
 	P.total_tiles = total;
 	P.n_segments = seg;
-	const long long ctas = std::min<long long>(total, (long long)kv->num_sms);
+	// one CTA per SM (the kernel's shared memory allows no more); at most 256, so
+	// the in-kernel fold's per-piece weights fit its merge area
+	const long long ctas = std::min<long long>(std::min<long long>(total, (long long)kv->num_sms), 256);
 	P.tiles_per_cta = ctas > 0 ? (total + ctas - 1) / ctas : 1;
 	P.n_ctas = ctas > 0 ? (int)((total + P.tiles_per_cta - 1) / P.tiles_per_cta) : 0;
 	P.err = kv->err_dev;
@@ -808,9 +816,11 @@ void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn_job>& pub, cudaStream_t st)
 {
 	const int n = (int)jobs.size();
+	// the job table, q scratch and partials are the cache's: wait for the previous submission
+	CU(cudaStreamWaitEvent(st, kv->done, 0), "order after the previous call");
 	// rope tables and q_rot scratch
 	size_t qrot_floats = 0;
-	int tok = 0;
+	int tok = 0, max_tok = 0;
 	for (int i = 0; i < n; ++i)
 	{
 		const nncu_attn_params& p = pub[i].p;
@@ -818,6 +828,7 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn
 		if (rc != NNCU_OK) return rc;
 		jobs[i].tok0 = tok;
 		tok += p.n_tok;
+		max_tok = std::max(max_tok, p.n_tok);
 		qrot_floats += align_up((size_t)p.n_tok * p.n_head * p.head_dim, 64);
 	}
 	CU(kv->qrot.reserve(qrot_floats * sizeof(float)), "q scratch");
@@ -835,7 +846,7 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn
 	DecodePlan P{};
 	plan_decode(kv, jobs, P);
 	// scratch for partials and the per-segment counters
-	const size_t part_floats = (size_t)(P.n_segments + P.n_ctas) * P.RM * (P.D + 2);
+	const size_t part_floats = (size_t)(P.n_segments + P.n_ctas) * P.RM * (P.D + 4);
 	CU(kv->parts.reserve(part_floats * sizeof(float)), "partials scratch");
 	if (P.n_segments > kv->counters_n)
 	{
@@ -845,16 +856,33 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn
 	}
 	P.parts = static_cast<float*>(kv->parts.p);
 	P.counters = static_cast<int*>(kv->counters.p);
-	// the job table: pinned -> device on the stream; the pinned copy is reused
-	// only after the previous upload has been read
-	const size_t jb = (size_t)n * sizeof(DevJob);
+	P.fused = 0;
+	// Each CTA's first tile, walked out here once instead of searched for by every CTA.
+	std::vector<int4> starts((size_t)std::max(P.n_ctas, 1));
+	{
+		int j = 0;
+		for (int c = 0; c < P.n_ctas; ++c)
+		{
+			const long long g = (long long)c * P.tiles_per_cta;
+			while (j + 1 < n && jobs[j + 1].gtile0 <= g) ++j;
+			while (jobs[j].n_tiles == 0 && j + 1 < n) ++j; // defensive: a job without tiles owns none
+			const long long local = g - jobs[j].gtile0;
+			starts[c] = make_int4(j, (int)(local / jobs[j].n_tiles), (int)(local % jobs[j].n_tiles), 0);
+		}
+	}
+	// the job table and the starts: pinned -> device on the stream; the pinned
+	// copy is reused only after the previous upload has been read
+	const size_t jb = align_up((size_t)n * sizeof(DevJob), 16);
+	const size_t sb = (size_t)P.n_ctas * sizeof(int4);
 	CU(cudaEventSynchronize(kv->jobs_uploaded), "job table reuse");
-	CU(kv->jobs_host.reserve(jb), "job table (host)");
-	CU(kv->jobs_dev.reserve(jb), "job table (device)");
-	std::memcpy(kv->jobs_host.p, jobs.data(), jb);
-	CU(cudaMemcpyAsync(kv->jobs_dev.p, kv->jobs_host.p, jb, cudaMemcpyHostToDevice, st), "job table upload");
+	CU(kv->jobs_host.reserve(jb + sb), "job table (host)");
+	CU(kv->jobs_dev.reserve(jb + sb), "job table (device)");
+	std::memcpy(kv->jobs_host.p, jobs.data(), (size_t)n * sizeof(DevJob));
+	std::memcpy(static_cast<char*>(kv->jobs_host.p) + jb, starts.data(), sb);
+	CU(cudaMemcpyAsync(kv->jobs_dev.p, kv->jobs_host.p, jb + sb, cudaMemcpyHostToDevice, st), "job table upload");
 	CU(cudaEventRecord(kv->jobs_uploaded, st), "job table event");
 	P.jobs = static_cast<const DevJob*>(kv->jobs_dev.p);
+	P.cta_start = reinterpret_cast<const int4*>(static_cast<const char*>(kv->jobs_dev.p) + jb);
 	// jobs whose queries see no key at all produce zeros, as nnc_attn_finish does for l = 0
 	for (int i = 0; i < n; ++i)
 		if (jobs[i].n_tiles == 0)
@@ -881,10 +909,12 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn
 		const uint64_t keys = last_max >= first_min ? (uint64_t)(last_max - first_min + 1) : 0;
 		core_bytes += keys * j.n_kv * j.D * es * 2 + 2 * qb;
 	}
-	int e;
+	// K1 then K2. K2 is a programmatic dependent of K1: its CTAs become
+	// resident while K1 runs and start streaming the moment K1 completes.
+	int e = 0;
 	{
 		PerfScope ps(NNCU_PERF_ATTN_ROPE, rope_bytes, st);
-		e = launch_prep(P.jobs, n, tok, 0, P.D, kv->kv_type, st);
+		e = launch_prep(P.jobs, n, max_tok, 0, P.D, kv->kv_type, st);
 	}
 	if (e) return cuda_fail((cudaError_t)e, "K1 (norm, RoPE, append) launch");
 	{
@@ -892,6 +922,7 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn
 		e = launch_decode(P, st);
 	}
 	if (e) return cuda_fail((cudaError_t)e, "K2 (attention) launch");
+	CU(cudaEventRecord(kv->done, st), "completion event");
 	return NNCU_OK;
 }
 

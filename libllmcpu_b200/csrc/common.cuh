@@ -311,6 +311,15 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
 		: "memory");
 }
 
+// Programmatic dependent launch (sm_90+): a primary kernel lets its dependent
+// grid start early; the dependent waits, where it needs the primary's
+// results, for the primary grid to complete and its writes to be visible.
+__device__ __forceinline__ void griddep_launch_dependents()
+{
+	asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Named barrier over `count` threads (ids 1..15; 0 is __syncthreads).
 __device__ __forceinline__ void named_sync(int id, int count)
 {
@@ -343,6 +352,67 @@ __device__ __forceinline__ void span_of(int causal, int window, int pos, int n_s
 			last = min(n_seq - 1, pos + half);
 		}
 	}
+}
+
+// ---- per-head preparation (norms and RoPE) on a warp ------------------------
+
+// RMS scale of a D-vector held in shared `buf`, the reference's form:
+// 1 / sqrt(sum(x^2) * (1/D) + eps) in double (nnc_rmsnorm_gamma_multi_f32,
+// nn_ops.cpp:590-632), or sum / D for the plain nnc_rmsnorm_f32 (:558-588).
+__device__ __forceinline__ float rms_scale(const float* buf, int D, float eps, bool gamma_form)
+{
+	float ss = 0.0f;
+	for (int i = threadIdx.x & 31; i < D; i += 32) ss = fmaf(buf[i], buf[i], ss);
+	ss = warp_sum(ss);
+	const double mean = gamma_form ? (double)ss * (double)(1.0f / (float)D) : (double)ss / (double)D;
+	return (float)(1.0 / sqrt(mean + (double)eps));
+}
+
+// Rotate the first n_rot lanes of the vector in shared `buf` for position
+// rpos (nnc_rope_f32, nn_ops.cpp:1830-1873): theta_i = rpos * inv[i]
+// (/ freq_factors[i]); NEOX pairs i and i + n_rot/2, NORM pairs 2i and 2i+1.
+__device__ __forceinline__ void rope_vec(float* buf, int n_rot, int mode, float rpos, const float* inv, const float* ff)
+{
+	const int half = n_rot / 2;
+	const int step = mode == 0 ? 1 : 2;
+	const int other = mode == 0 ? half : 1;
+	for (int i = threadIdx.x & 31; i < half; i += 32)
+	{
+		float theta = rpos * inv[i];
+		if (ff) theta = __fdiv_rn(theta, ff[i]);
+		float sn, cs;
+		sincosf(theta, &sn, &cs);
+		float* p = buf + i * step;
+		const float a = p[0], b = p[other];
+		p[0] = cs * a - sn * b;
+		p[other] = sn * a + cs * b;
+	}
+}
+
+// One head vector through attention_forward's per-head steps (model.cpp:
+// 1616-1660): load src into shared `buf`, RMSNorm with `gamma` (or the plain
+// norm when plain_norm), then RoPE when rpos is given. Warp-cooperative; buf
+// holds the result, visible to the whole warp, on return.
+__device__ __forceinline__ void prep_head(float* buf, const float* src, int D, const float* gamma, bool plain_norm,
+                                          float eps, bool rotate, int n_rot, int mode, float rpos, const float* inv,
+                                          const float* ff)
+{
+	const int lane = threadIdx.x & 31;
+	for (int i = lane; i < D; i += 32) buf[i] = src[i];
+	__syncwarp();
+	if (gamma)
+	{
+		const float sc = rms_scale(buf, D, eps, true);
+		for (int i = lane; i < D; i += 32) buf[i] = buf[i] * sc * gamma[i];
+	}
+	else if (plain_norm)
+	{
+		const float sc = rms_scale(buf, D, eps, false);
+		for (int i = lane; i < D; i += 32) buf[i] = buf[i] * sc;
+	}
+	__syncwarp();
+	if (rotate && n_rot > 0) rope_vec(buf, n_rot, mode, rpos, inv, ff);
+	__syncwarp();
 }
 
 } // namespace nncu

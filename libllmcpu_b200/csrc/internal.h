@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <vector_types.h>
+
 namespace nncu
 {
 
@@ -71,13 +73,15 @@ struct DecodePlan
 	int n_ctas;
 	long long tiles_per_cta;
 	int n_segments;
-	float* parts;   // (n_segments + n_ctas) slots of RM * (D + 2) floats
+	int fused;      // reserved, 0: K1 runs as its own grid before this one
+	const int4* cta_start; // per CTA: (job, segment, tile) of its first tile
+	float* parts;   // (n_segments + n_ctas) slots of RM * (D + 4) floats
 	int* counters;  // n_segments, zero between launches
 	int* err;       // device error word
 };
 
 // Launchers (implemented in the .cu files). Each returns a cudaError_t value.
-int launch_prep(const DevJob* jobs_dev, int n_jobs, int total_tok, int max_heads, int D, int kv_type, void* stream);
+int launch_prep(const DevJob* jobs_dev, int n_jobs, int max_tok, int max_heads, int D, int kv_type, void* stream);
 int launch_decode(const DecodePlan& plan, void* stream);
 bool decode_supported(int D, int kv_type);
 int decode_tile_keys(int D, int kv_type);

@@ -19,9 +19,14 @@
 //    segment's last piece merges the pieces in key order (nnc_attn_merge)
 //    and divides by l (nnc_attn_finish). No second launch.
 //  * Memory. One producer warp streams each tile's K rows and V rows (one
-//    contiguous run each in the head-major cache) into a 4-stage shared
+//    contiguous 32 KB run each in the head-major cache) into a 3-stage shared
 //    memory ring with cp.async.bulk, completing on mbarriers; 8 consumer
-//    warps compute while the next tiles are in flight.
+//    warps compute while the next tiles are in flight. Each piece's q rows
+//    come the same way, into one of two q slots, ahead of the piece's tiles,
+//    so no consumer ever waits on a plain global load behind the tile stream.
+//  * Order. The kernel is a programmatic dependent of K1 (k_prep.cu): its
+//    CTAs become resident while K1 runs, and the producer starts streaming as
+//    soon as K1's q rows and appended K/V rows are complete.
 //  * Math. fp32 throughout. A warp owns T/8 keys of each tile; its lanes
 //    split head_dim (D/32 elements each). The q.k partial sums of a batch of
 //    keys x rows are summed across lanes with a transposing reduction, the
@@ -31,6 +36,8 @@
 
 #include <math_constants.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace nncu
@@ -38,9 +45,10 @@ namespace nncu
 namespace
 {
 
-constexpr int NW = 8;          // consumer warps
-constexpr int STAGES = 4;      // K/V tiles in flight per CTA
-constexpr int TILE_BYTES = 16384;
+constexpr int NW = 8;              // consumer warps
+constexpr int MAX_STAGES = 4;      // K/V tiles in flight per CTA, as shared memory allows
+constexpr int SMEM_LIMIT = 232448; // 227 KB of shared memory per CTA
+constexpr int TILE_BYTES = 32768;  // one tile's K (or V) rows
 constexpr float LOG2E = 1.4426950408889634f;
 
 template <int D, typename KV, int RM>
@@ -58,53 +66,72 @@ struct Cfg
 	static constexpr int SHIFT = 5 - LOG2N;                // lane >> SHIFT = value index after the reduction
 	static constexpr int LOG2RMW = RMW >= 32 ? 5 : RMW >= 16 ? 4 : RMW >= 8 ? 3 : RMW >= 4 ? 2 : RMW >= 2 ? 1 : 0;
 	static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-	static constexpr int MERGE_FLOATS = NW * RMW * D + 2 * NW * RMW;
-	static constexpr int SMEM = STAGES * STAGE_BYTES + MERGE_FLOATS * 4 + 2 * STAGES * 8 + 64;
+	// the warps' (o, m, l) at a piece's end, merged in two rounds of half the
+	// warps each; the fold's weights reuse the same area
+	static constexpr int AREA_FLOATS = (NW / 2) * RMW * D;
+	static constexpr int QSLOT_FLOATS = RM * D; // one piece's q rows
+	static constexpr int FIXED_BYTES = (AREA_FLOATS + 2 * NW * RMW + 2 * QSLOT_FLOATS) * 4 + 256;
+	static constexpr int FIT = (SMEM_LIMIT - FIXED_BYTES) / STAGE_BYTES;
+	static constexpr int STAGES = FIT < MAX_STAGES ? FIT : MAX_STAGES;
+	static constexpr int SMEM = STAGES * STAGE_BYTES + FIXED_BYTES;
+	static_assert(STAGES >= 3, "shared memory for at least three stages");
 	static_assert(D % 32 == 0, "D: a multiple of 32");
-	static_assert(RM % RS == 0 && NW % RS == 0, "row slices");
+	static_assert(RM % RS == 0 && NW % RS == 0 && (NW / 2) % RS == 0, "row slices");
 	static_assert(T >= NKG && T <= ATTN_BLOCK && ATTN_BLOCK % T == 0 && T % NKG == 0, "tile keys");
 	static_assert(KB % KS == 0, "batches per warp");
 	static_assert(RMW * E <= 32, "accumulator registers");
 };
 
-// Where global tile g of the launch lies.
-struct TileLoc
+// The CTA's walk over its run of the launch's tiles: (job, segment within
+// the job, tile within the segment), advanced one tile at a time.
+struct Cursor
 {
-	int job;
-	int seg_local;   // segment within the job: h * n_rowgroups + rg
-	int tis;         // tile within the segment
+	int job = 0, seg = 0, tis = 0;
+	int n_tiles = 1, n_segs = 1;
 };
 
-struct JobCursor
+__device__ __forceinline__ void cursor_load(const DecodePlan& P, Cursor& c)
 {
-	int j = -1;
-	long long g0 = 0, g1 = 0; // global tiles of job j: [g0, g1)
-	int n_tiles = 1;
-};
+	const DevJob& J = P.jobs[c.job];
+	c.n_tiles = J.n_tiles;
+	c.n_segs = J.n_kv * J.n_rowgroups;
+}
 
-__device__ __forceinline__ void locate(const DecodePlan& P, JobCursor& c, long long g, TileLoc& loc)
+__device__ __forceinline__ void cursor_start(const DecodePlan& P, Cursor& c)
 {
-	if (c.j < 0 || g < c.g0 || g >= c.g1)
-	{
-		int lo = 0, hi = P.n_jobs - 1;
-		while (lo < hi)
-		{
-			const int mid = (lo + hi + 1) >> 1;
-			if (P.jobs[mid].gtile0 <= g) lo = mid;
-			else hi = mid - 1;
-		}
-		// skip jobs with no tiles that share the same gtile0
-		while (lo + 1 < P.n_jobs && P.jobs[lo + 1].gtile0 <= g) ++lo;
-		const DevJob& J = P.jobs[lo];
-		c.j = lo;
-		c.g0 = J.gtile0;
-		c.n_tiles = J.n_tiles;
-		c.g1 = J.gtile0 + (long long)J.n_kv * J.n_rowgroups * J.n_tiles;
-	}
-	const long long local = g - c.g0;
-	loc.job = c.j;
-	loc.seg_local = (int)(local / c.n_tiles);
-	loc.tis = (int)(local % c.n_tiles);
+	const int4 st = P.cta_start[blockIdx.x]; // placed by the host: (job, segment, tile)
+	c.job = st.x;
+	c.seg = st.y;
+	c.tis = st.z;
+	cursor_load(P, c);
+}
+
+__device__ __forceinline__ void cursor_next(const DecodePlan& P, Cursor& c)
+{
+	if (++c.tis < c.n_tiles) return;
+	c.tis = 0;
+	if (++c.seg < c.n_segs) return;
+	c.seg = 0;
+	do
+		++c.job;
+	while (c.job < P.n_jobs && P.jobs[c.job].n_tiles == 0);
+	if (c.job < P.n_jobs) cursor_load(P, c);
+}
+
+// atom.add with acquire-release semantics at GPU scope: the arriving CTA's
+// partial (written before it, ordered by the CTA barrier) is visible to the
+// CTA that sees the final count.
+__device__ __forceinline__ int atomic_add_acq_rel(int* p, int v)
+{
+	int old;
+	asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+	return old;
+}
+
+// The rows of a segment that exist (the last row group may be short).
+__device__ __forceinline__ int seg_rows(const DevJob& J, int rg, int RM)
+{
+	return min(RM, (J.n_head / J.n_kv) * J.n_tok - rg * RM);
 }
 
 template <int D, typename KV, int RM>
@@ -114,19 +141,26 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	using T_ = typename KV::T;
 	constexpr int E = C::E, T = C::T, KB = C::KB, KS = C::KS, N = C::N, SHIFT = C::SHIFT;
 	constexpr int VEC = LaneVec<E, KV::esize>::VEC; // lane <-> element mapping of K, V, q and o
+	constexpr int RS = C::RS, RMW = C::RMW;
+	constexpr int PW = D + 4; // a partial row: o[D], m, l, two pad floats (16-byte rows)
+	constexpr int STAGES = C::STAGES;
 
 	extern __shared__ __align__(1024) unsigned char smem[];
 	unsigned char* stages = smem;
-	float* m_s = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES); // [NW][RMW]
-	float* l_s = m_s + NW * C::RMW;                                        // [NW][RMW]
-	float* o_s = l_s + NW * C::RMW;                                        // [NW][RMW][D]
-	uint64_t* full = reinterpret_cast<uint64_t*>(o_s + NW * C::RMW * D);
+	float* area = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES); // [NW/2][RMW][D]
+	float* m_s = area + C::AREA_FLOATS;                                      // [NW][RMW]
+	float* l_s = m_s + NW * RMW;                                             // [NW][RMW]
+	float* qslot = l_s + NW * RMW;                                           // [2][RM][D]
+	uint64_t* full = reinterpret_cast<uint64_t*>(qslot + 2 * C::QSLOT_FLOATS);
 	uint64_t* empty = full + STAGES;
-	volatile int* s_flags = reinterpret_cast<volatile int*>(empty + STAGES); // [0] abort, [1] last-piece vote
+	uint64_t* qfull = empty + STAGES;  // [2]
+	uint64_t* qempty = qfull + 2;      // [2]
+	volatile int* s_flags = reinterpret_cast<volatile int*>(qempty + 2); // [0] abort, [1] last-piece vote
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const long long g_begin = (long long)blockIdx.x * P.tiles_per_cta;
 	const long long g_end = min(g_begin + P.tiles_per_cta, P.total_tiles);
+	const int n_mine = (int)(g_end - g_begin);
 
 	if (threadIdx.x == 0)
 	{
@@ -134,6 +168,11 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		{
 			mbar_init(&full[s], 1);
 			mbar_init(&empty[s], NW);
+		}
+		for (int s = 0; s < 2; ++s)
+		{
+			mbar_init(&qfull[s], 1);
+			mbar_init(&qempty[s], NW);
 		}
 		s_flags[0] = 0;
 		s_flags[1] = 0;
@@ -143,23 +182,49 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 
 	if (warp == NW)
 	{
-		// ---- producer: one lane streams the CTA's tiles into the stage ring ----
-		if (lane == 0)
+		// ---- producer: one lane streams each piece's q rows and the CTA's tiles ----
+		if (lane == 0 && n_mine > 0)
 		{
-			JobCursor cur;
-			TileLoc loc;
-			long long i = 0;
-			for (long long g = g_begin; g < g_end; ++g, ++i)
+			griddep_wait(); // K1's q rows and appended K/V rows are complete and visible
+			Cursor cur;
+			cursor_start(P, cur);
+			int pj = -1, ps = -1, piece = 0;
+			for (int i = 0; i < n_mine; ++i)
 			{
-				locate(P, cur, g, loc);
-				const DevJob& J = P.jobs[loc.job];
-				const int h = loc.seg_local / J.n_rowgroups;
-				const long long key0 = (long long)(J.tile_lo + loc.tis) * T;
-				const size_t row0 = (size_t)(key0 % J.rows);
-				const size_t off = (size_t)h * J.head_bytes + row0 * D * KV::esize;
-				const int s = (int)(i % STAGES);
-				if (i >= STAGES && !mbar_wait_bounded(&empty[s], (uint32_t)(((i / STAGES) - 1) & 1), P.err,
-				                                      DEVERR_WAIT_EMPTY))
+				const DevJob& J = P.jobs[cur.job];
+				const int h = cur.seg / J.n_rowgroups, rg = cur.seg % J.n_rowgroups;
+				if (cur.job != pj || cur.seg != ps)
+				{
+					// a new piece: its q rows into slot piece % 2, once the consumers are done with it
+					const int sl = piece & 1;
+					if (piece >= 2 &&
+					    !mbar_wait_bounded(&qempty[sl], (uint32_t)(((piece >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
+					{
+						s_flags[0] = 1;
+						break;
+					}
+					const int G = J.n_head / J.n_kv;
+					const int rows = seg_rows(J, rg, RM);
+					mbar_arrive_expect_tx(&qfull[sl], (uint32_t)(rows * D * 4));
+					// rows (t, g) of the segment: per token, its G heads are contiguous
+					for (int r = 0; r < rows;)
+					{
+						const int gr = rg * RM + r, t = gr / G, g = gr % G;
+						const int run = min(G - g, rows - r);
+						bulk_g2s(qslot + sl * C::QSLOT_FLOATS + r * D,
+						         J.q_rot + ((size_t)t * J.n_head + (size_t)h * G + g) * D, (uint32_t)(run * D * 4),
+						         &qfull[sl]);
+						r += run;
+					}
+					pj = cur.job;
+					ps = cur.seg;
+					++piece;
+				}
+				const int key0 = (J.tile_lo + cur.tis) * T;
+				const size_t off = (size_t)h * J.head_bytes + (size_t)(key0 % J.rows) * D * KV::esize;
+				const int s = i % STAGES;
+				if (i >= STAGES &&
+				    !mbar_wait_bounded(&empty[s], (uint32_t)(((i / STAGES) - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
 				{
 					s_flags[0] = 1;
 					break;
@@ -169,6 +234,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 				mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
 				bulk_g2s(st, J.K + off, TILE_BYTES, &full[s]);
 				bulk_g2s(st + TILE_BYTES, J.V + off, TILE_BYTES, &full[s]);
+				cursor_next(P, cur);
 			}
 		}
 		return;
@@ -177,7 +243,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	// ---- consumers ----
 	// Warp w takes rows [rs*RMW, rs*RMW + RMW) of the segment (rs = w % RS)
 	// for the keys [kg*KB, kg*KB + KB) of every tile (kg = w / RS).
-	constexpr int RS = C::RS, RMW = C::RMW;
 	const int ctid = threadIdx.x; // 0 .. NW*32-1
 	const int rs = warp % RS, kg = warp / RS;
 	const int r_v = (lane >> SHIFT) % RMW;  // the row (within the warp's rows) of this lane's reduced value
@@ -190,27 +255,27 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	int first_v = 0, last_v = -1; // this lane's row span
 	bool softcap = false;
 	float cap = 0.0f;
+	int piece = 0;
 
-	JobCursor cur;
-	TileLoc loc;
-	int cur_job = -1, cur_seg = -1;
-	long long piece_g0 = 0; // first global tile of the current segment
-
+	// Piece start: the piece's q rows from their slot into registers.
 	auto start_piece = [&](const DevJob& J, int seg_local) {
 		const int G = J.n_head / J.n_kv;
-		const int h = seg_local / J.n_rowgroups, rg = seg_local % J.n_rowgroups;
+		const int rg = seg_local % J.n_rowgroups;
+		const int rows = seg_rows(J, rg, RM);
+		const int sl = piece & 1;
 		softcap = J.softcap > 0.0f;
 		cap = J.softcap;
+		if (!s_flags[0] && !mbar_wait_bounded(&qfull[sl], (uint32_t)((piece >> 1) & 1), P.err, DEVERR_WAIT_FULL))
+			s_flags[0] = 1;
 		const float qmul = softcap ? J.scale : J.scale * LOG2E;
+		const float* qs = qslot + sl * C::QSLOT_FLOATS;
 #pragma unroll
 		for (int r = 0; r < RMW; ++r)
 		{
-			const int gr = rg * RM + rs * RMW + r;
-			const bool ok = gr < G * J.n_tok;
-			const int t = ok ? gr / G : 0, g = ok ? gr % G : 0;
-			const float* src = J.q_rot + ((size_t)t * J.n_head + (size_t)h * G + g) * D;
+			const int R = rs * RMW + r;
+			const bool ok = R < rows; // warp-uniform
 			float tmp[E];
-			if (ok) load_lane_f<E, VEC>(src, lane, tmp);
+			if (ok) load_lane_f<E, VEC>(qs + R * D, lane, tmp);
 #pragma unroll
 			for (int e = 0; e < E; ++e)
 			{
@@ -219,6 +284,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			}
 			m[r] = -CUDART_INF_F;
 		}
+		__syncwarp();
+		if (lane == 0) mbar_arrive(&qempty[sl]); // this warp is done with the slot
+		++piece;
 		l_lane = 0.0f;
 		const int gr_v = rg * RM + rs * RMW + r_v;
 		if (gr_v < G * J.n_tok)
@@ -227,24 +295,61 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			first_v = 0, last_v = -1; // a padding row sees nothing
 	};
 
-	// Merge the warps' states of the finished piece; write the output (whole
+	// Merge the warps' states of the finished piece (two rounds: the upper half
+	// of the warps hands its state to the lower half, which folds it in
+	// registers and leaves the result for the CTA); write the output (whole
 	// segment in this CTA) or a partial, and fold the partials if this CTA
 	// completes the segment.
-	auto finish_piece = [&](const DevJob& J, int seg_local, long long seg_gstart) {
+	auto finish_piece = [&](const DevJob& J, int seg_local) {
 		// l of row r: sum over the batch's key slots (lanes differing in the key bits)
 		float lsum = l_lane;
 #pragma unroll
 		for (int off = 1 << (SHIFT + C::LOG2RMW); off < 32; off <<= 1)
 			lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
-#pragma unroll
-		for (int r = 0; r < RMW; ++r)
+		constexpr int HW = NW / 2;
+		if (warp >= HW)
 		{
 #pragma unroll
-			for (int e = 0; e < E; ++e) o_s[(warp * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
-			if (lane == (r << SHIFT))
+			for (int r = 0; r < RMW; ++r)
 			{
-				m_s[warp * RMW + r] = m[r];
-				l_s[warp * RMW + r] = lsum;
+#pragma unroll
+				for (int e = 0; e < E; ++e)
+					area[((warp - HW) * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
+				if (lane == (r << SHIFT))
+				{
+					m_s[warp * RMW + r] = m[r];
+					l_s[warp * RMW + r] = lsum;
+				}
+			}
+		}
+		named_sync(1, NW * 32);
+		if (warp < HW)
+		{
+			// warp w + HW has the same row slice (HW is a multiple of RS)
+#pragma unroll
+			for (int r = 0; r < RMW; ++r)
+			{
+				const float mo = m_s[(warp + HW) * RMW + r], lo = l_s[(warp + HW) * RMW + r];
+				const float M = fmaxf(m[r], mo);
+				const float ca = m[r] == -CUDART_INF_F ? 0.0f : ex2(m[r] - M);
+				const float cb = mo == -CUDART_INF_F ? 0.0f : ex2(mo - M);
+#pragma unroll
+				for (int e = 0; e < E; ++e)
+				{
+					const float ob = area[(warp * RMW + r) * D + lane_elem<E, VEC>(lane, e)];
+					o[r][e] = fmaf(o[r][e], ca, ob * cb);
+				}
+				m[r] = M;
+				const float lr = __shfl_sync(0xffffffffu, lsum, r << SHIFT);
+				const float lsum_r = fmaf(lr, ca, lo * cb);
+				__syncwarp();
+#pragma unroll
+				for (int e = 0; e < E; ++e) area[(warp * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
+				if (lane == 0)
+				{
+					m_s[warp * RMW + r] = M;
+					l_s[warp * RMW + r] = lsum_r;
+				}
 			}
 		}
 		named_sync(1, NW * 32);
@@ -252,11 +357,12 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		const int G = J.n_head / J.n_kv;
 		const int h = seg_local / J.n_rowgroups, rg = seg_local % J.n_rowgroups;
 		const long long W = P.tiles_per_cta;
+		const long long seg_gstart = J.gtile0 + (long long)seg_local * J.n_tiles;
 		const long long seg_gend = seg_gstart + J.n_tiles;
 		const int c_first = (int)(seg_gstart / W), c_last = (int)((seg_gend - 1) / W);
 		const bool single = c_first == c_last;
 		const int seg = J.seg0 + seg_local;
-		float* part = P.parts + (size_t)(seg + (int)blockIdx.x) * RM * (D + 2);
+		float* part = P.parts + (size_t)(seg + (int)blockIdx.x) * RM * PW;
 
 		for (int idx = ctid; idx < RM * D; idx += NW * 32)
 		{
@@ -264,15 +370,15 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			const int sl = R / RMW, r = R % RMW; // the row's slice and its row within the slice
 			float M = -CUDART_INF_F;
 #pragma unroll
-			for (int k = 0; k < C::NKG; ++k) M = fmaxf(M, m_s[(k * RS + sl) * RMW + r]);
+			for (int k = 0; k < HW / RS; ++k) M = fmaxf(M, m_s[(k * RS + sl) * RMW + r]);
 			float acc = 0.0f, L = 0.0f;
 #pragma unroll
-			for (int k = 0; k < C::NKG; ++k)
+			for (int k = 0; k < HW / RS; ++k)
 			{
 				const int w = k * RS + sl;
 				const float mw = m_s[w * RMW + r];
 				const float c = mw == -CUDART_INF_F ? 0.0f : ex2(mw - M);
-				acc = fmaf(o_s[(w * RMW + r) * D + d], c, acc);
+				acc = fmaf(area[(w * RMW + r) * D + d], c, acc);
 				L = fmaf(l_s[w * RMW + r], c, L);
 			}
 			if (single)
@@ -286,48 +392,103 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			}
 			else
 			{
-				part[R * (D + 2) + d] = acc;
+				part[R * PW + d] = acc;
 				if (d == 0)
 				{
-					part[R * (D + 2) + D] = M;
-					part[R * (D + 2) + D + 1] = L;
+					part[R * PW + D] = M;
+					part[R * PW + D + 1] = L;
 				}
 			}
 		}
 		if (!single)
 		{
-			__threadfence();
 			named_sync(1, NW * 32);
 			if (ctid == 0)
 			{
 				const int n_pieces = c_last - c_first + 1;
-				const int prev = atomicAdd(&P.counters[seg], 1);
+				const int prev = atomic_add_acq_rel(&P.counters[seg], 1);
 				s_flags[1] = prev == n_pieces - 1;
 			}
 			named_sync(1, NW * 32);
 			if (s_flags[1])
 			{
-				__threadfence();
-				// fold the pieces in key order: merge (o, m, l), then o / l
-				for (int idx = ctid; idx < RM * D; idx += NW * 32)
+				// Fold the pieces (nnc_attn_merge in key order, then
+				// nnc_attn_finish) in two rounds of independent loads: a warp
+				// per row takes every piece's (m, l) at once and leaves the
+				// weights exp2(m_c - M) / L in the area; then each thread sums
+				// its 4 output columns over the pieces with 16-byte loads.
+				const int np = c_last - c_first + 1;
+				const float* base = P.parts + (size_t)(seg + c_first) * RM * PW;
+				float* wgt = area; // [np][RM]
+				for (int R = warp; R < RM; R += NW)
 				{
-					const int R = idx / D, d = idx % D;
+					float2 ml[4];
+#pragma unroll
+					for (int k = 0; k < 4; ++k)
+					{
+						const int c = lane + 32 * k;
+						ml[k] = c < np ? __ldcg(reinterpret_cast<const float2*>(base + (size_t)c * RM * PW + R * PW + D))
+						               : make_float2(-CUDART_INF_F, 0.0f);
+					}
+					float mx = fmaxf(fmaxf(ml[0].x, ml[1].x), fmaxf(ml[2].x, ml[3].x));
+					for (int c = lane + 128; c < np; c += 32)
+						mx = fmaxf(mx, __ldcg(base + (size_t)c * RM * PW + R * PW + D));
+					mx = warp_max(mx);
+					float L = 0.0f;
+#pragma unroll
+					for (int k = 0; k < 4; ++k)
+					{
+						const int c = lane + 32 * k;
+						const float w = ml[k].x == -CUDART_INF_F ? 0.0f : ex2(ml[k].x - mx);
+						if (c < np) wgt[c * RM + R] = w;
+						L = fmaf(ml[k].y, w, L);
+					}
+					for (int c = lane + 128; c < np; c += 32)
+					{
+						const float2 v = __ldcg(reinterpret_cast<const float2*>(base + (size_t)c * RM * PW + R * PW + D));
+						const float w = v.x == -CUDART_INF_F ? 0.0f : ex2(v.x - mx);
+						wgt[c * RM + R] = w;
+						L = fmaf(v.y, w, L);
+					}
+					L = warp_sum(L);
+					const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+					for (int c = lane; c < np; c += 32) wgt[c * RM + R] *= inv;
+				}
+				named_sync(1, NW * 32);
+				for (int idx = ctid; idx < RM * (D / 4); idx += NW * 32)
+				{
+					const int R = idx / (D / 4), d = 4 * (idx % (D / 4));
 					const int gr = rg * RM + R;
 					if (gr >= G * J.n_tok) continue;
-					float M = -CUDART_INF_F;
-					for (int c = c_first; c <= c_last; ++c)
-						M = fmaxf(M, __ldcg(P.parts + (size_t)(seg + c) * RM * (D + 2) + R * (D + 2) + D));
-					float acc = 0.0f, L = 0.0f;
-					for (int c = c_first; c <= c_last; ++c)
+					const float* col = base + R * PW + d;
+					float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+					int c = 0;
+					for (; c + 4 <= np; c += 4)
 					{
-						const float* pc = P.parts + (size_t)(seg + c) * RM * (D + 2) + R * (D + 2);
-						const float mc = __ldcg(pc + D);
-						const float w = mc == -CUDART_INF_F ? 0.0f : ex2(mc - M);
-						acc = fmaf(__ldcg(pc + d), w, acc);
-						L = fmaf(__ldcg(pc + D + 1), w, L);
+						float4 v[4];
+#pragma unroll
+						for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(col + (size_t)(c + u) * RM * PW));
+#pragma unroll
+						for (int u = 0; u < 4; ++u)
+						{
+							const float w = wgt[(c + u) * RM + R];
+							acc.x = fmaf(v[u].x, w, acc.x);
+							acc.y = fmaf(v[u].y, w, acc.y);
+							acc.z = fmaf(v[u].z, w, acc.z);
+							acc.w = fmaf(v[u].w, w, acc.w);
+						}
+					}
+					for (; c < np; ++c)
+					{
+						const float4 v = __ldcg(reinterpret_cast<const float4*>(col + (size_t)c * RM * PW));
+						const float w = wgt[c * RM + R];
+						acc.x = fmaf(v.x, w, acc.x);
+						acc.y = fmaf(v.y, w, acc.y);
+						acc.z = fmaf(v.z, w, acc.z);
+						acc.w = fmaf(v.w, w, acc.w);
 					}
 					const int t = gr / G, g = gr % G;
-					J.out[((size_t)t * J.n_head + (size_t)h * G + g) * D + d] = L > 0.0f ? acc / L : 0.0f;
+					*reinterpret_cast<float4*>(J.out + ((size_t)t * J.n_head + (size_t)h * G + g) * D + d) = acc;
 				}
 				if (ctid == 0) P.counters[seg] = 0; // ready for the next launch
 			}
@@ -335,102 +496,114 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		named_sync(1, NW * 32); // the merge area is free again
 	};
 
-	long long i = 0;
-	for (long long g = g_begin; g < g_end; ++g, ++i)
+	if (n_mine > 0)
 	{
-		locate(P, cur, g, loc);
-		const DevJob& J = P.jobs[loc.job];
-		if (loc.job != cur_job || loc.seg_local != cur_seg)
+		Cursor cur;
+		cursor_start(P, cur);
+		int cur_job = -1, cur_seg = -1, key_base = 0;
+		for (int i = 0; i < n_mine; ++i)
 		{
-			if (cur_job >= 0) finish_piece(P.jobs[cur_job], cur_seg, piece_g0);
-			cur_job = loc.job;
-			cur_seg = loc.seg_local;
-			piece_g0 = J.gtile0 + (long long)loc.seg_local * J.n_tiles;
-			start_piece(J, loc.seg_local);
-		}
-		const int s = (int)(i % STAGES);
-		// After a timed-out wait the CTA stops waiting (fail fast) but keeps
-		// stepping through its tiles, so every consumer warp still meets the
-		// same named barriers; the error word tells the host the result is void.
-		if (!s_flags[0] && !mbar_wait_bounded(&full[s], (uint32_t)((i / STAGES) & 1), P.err, DEVERR_WAIT_FULL))
-			s_flags[0] = 1;
-		if (s_flags[0])
-		{
+			const DevJob& J = P.jobs[cur.job];
+			if (cur.job != cur_job || cur.seg != cur_seg)
+			{
+				if (cur_job >= 0) finish_piece(P.jobs[cur_job], cur_seg);
+				cur_job = cur.job;
+				cur_seg = cur.seg;
+				key_base = (J.tile_lo + cur.tis) * T;
+				start_piece(J, cur.seg);
+			}
+			const int s = i % STAGES;
+			// After a timed-out wait the CTA stops waiting (fail fast) but keeps
+			// stepping through its tiles, so every consumer warp still meets the
+			// same named barriers; the error word tells the host the result is void.
+			if (!s_flags[0] && !mbar_wait_bounded(&full[s], (uint32_t)((i / STAGES) & 1), P.err, DEVERR_WAIT_FULL))
+				s_flags[0] = 1;
+			const T_* Kt = reinterpret_cast<const T_*>(stages + s * C::STAGE_BYTES);
+			const T_* Vt = reinterpret_cast<const T_*>(stages + s * C::STAGE_BYTES + TILE_BYTES);
+			if (!s_flags[0])
+			{
+#pragma unroll
+				for (int b = 0; b < KB / KS; ++b)
+				{
+					const int k0 = kg * KB + b * KS; // key index within the tile
+					// scores of KS keys x RMW rows: lane-partial dot products, then reduced
+					float part[N];
+#pragma unroll
+					for (int kk = 0; kk < KS; ++kk)
+					{
+						float kv[E];
+						load_lane<E>(Kt + (size_t)(k0 + kk) * D, lane, kv);
+#pragma unroll
+						for (int r = 0; r < RMW; ++r)
+						{
+							float acc = 0.0f;
+#pragma unroll
+							for (int e = 0; e < E; ++e) acc = fmaf(q[r][e], kv[e], acc);
+							part[kk * RMW + r] = acc;
+						}
+					}
+					float sv = transpose_reduce<N>(part, lane);
+					const int pos = key_base + k0 + kk_v;
+					if (softcap) sv = cap * tanhf(sv / cap) * LOG2E;
+					if (pos < first_v || pos > last_v) sv = -CUDART_INF_F;
+					// the batch's max of each row, then the new running max of every row
+					float mx = sv;
+#pragma unroll
+					for (int off = 1 << (SHIFT + C::LOG2RMW); off < 32; off <<= 1)
+						mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+					float alpha[RMW];
+					bool moved = false;
+					float m_v = 0.0f, alpha_v = 1.0f; // this lane's row's, picked without dynamic indexing
+#pragma unroll
+					for (int r = 0; r < RMW; ++r)
+					{
+						const float mn = fmaxf(m[r], __shfl_sync(0xffffffffu, mx, r << SHIFT));
+						moved |= mn != m[r];
+						alpha[r] = mn == -CUDART_INF_F ? 1.0f : ex2(m[r] - mn);
+						m[r] = mn;
+						if (r == r_v)
+						{
+							m_v = mn;
+							alpha_v = alpha[r];
+						}
+					}
+					const float pv = sv == -CUDART_INF_F ? 0.0f : ex2(sv - m_v);
+					l_lane = fmaf(l_lane, alpha_v, pv);
+					if (moved) // warp-uniform: m is the same in every lane
+					{
+#pragma unroll
+						for (int r = 0; r < RMW; ++r)
+#pragma unroll
+							for (int e = 0; e < E; ++e) o[r][e] *= alpha[r];
+					}
+					// o += p v over the batch's keys
+#pragma unroll
+					for (int kk = 0; kk < KS; ++kk)
+					{
+						float vv[E];
+						load_lane<E>(Vt + (size_t)(k0 + kk) * D, lane, vv);
+#pragma unroll
+						for (int r = 0; r < RMW; ++r)
+						{
+							const float p = __shfl_sync(0xffffffffu, pv, (kk * RMW + r) << SHIFT);
+#pragma unroll
+							for (int e = 0; e < E; ++e) o[r][e] = fmaf(p, vv[e], o[r][e]);
+						}
+					}
+				}
+			}
 			__syncwarp();
-			continue;
+			if (lane == 0) mbar_arrive(&empty[s]);
+			key_base += T;
+			cursor_next(P, cur);
 		}
-		const T_* Kt = reinterpret_cast<const T_*>(stages + s * C::STAGE_BYTES);
-		const T_* Vt = reinterpret_cast<const T_*>(stages + s * C::STAGE_BYTES + TILE_BYTES);
-		const int key_base = (J.tile_lo + loc.tis) * T; // absolute position of the tile's first key
-
-#pragma unroll
-		for (int b = 0; b < KB / KS; ++b)
-		{
-			const int k0 = kg * KB + b * KS; // key index within the tile
-			// scores of KS keys x RMW rows: lane-partial dot products, then reduced
-			float part[N];
-#pragma unroll
-			for (int kk = 0; kk < KS; ++kk)
-			{
-				float kv[E];
-				load_lane<E>(Kt + (size_t)(k0 + kk) * D, lane, kv);
-#pragma unroll
-				for (int r = 0; r < RMW; ++r)
-				{
-					float acc = 0.0f;
-#pragma unroll
-					for (int e = 0; e < E; ++e) acc = fmaf(q[r][e], kv[e], acc);
-					part[kk * RMW + r] = acc;
-				}
-			}
-			float sv = transpose_reduce<N>(part, lane);
-			const int pos = key_base + k0 + kk_v;
-			if (softcap) sv = cap * tanhf(sv / cap) * LOG2E;
-			if (pos < first_v || pos > last_v) sv = -CUDART_INF_F;
-			// the batch's max of each row, then the new running max of every row
-			float mx = sv;
-#pragma unroll
-			for (int off = 1 << (SHIFT + C::LOG2RMW); off < 32; off <<= 1)
-				mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-			float alpha[RMW];
-#pragma unroll
-			for (int r = 0; r < RMW; ++r)
-			{
-				const float mn = fmaxf(m[r], __shfl_sync(0xffffffffu, mx, r << SHIFT));
-				alpha[r] = mn == -CUDART_INF_F ? 1.0f : ex2(m[r] - mn);
-				m[r] = mn;
-			}
-			const float pv = sv == -CUDART_INF_F ? 0.0f : ex2(sv - m[r_v]);
-			l_lane = fmaf(l_lane, alpha[r_v], pv);
-#pragma unroll
-			for (int r = 0; r < RMW; ++r)
-#pragma unroll
-				for (int e = 0; e < E; ++e) o[r][e] *= alpha[r];
-			// o += p v over the batch's keys
-#pragma unroll
-			for (int kk = 0; kk < KS; ++kk)
-			{
-				float vv[E];
-				load_lane<E>(Vt + (size_t)(k0 + kk) * D, lane, vv);
-#pragma unroll
-				for (int r = 0; r < RMW; ++r)
-				{
-					const float p = __shfl_sync(0xffffffffu, pv, (kk * RMW + r) << SHIFT);
-#pragma unroll
-					for (int e = 0; e < E; ++e) o[r][e] = fmaf(p, vv[e], o[r][e]);
-				}
-			}
-		}
-		__syncwarp();
-		if (lane == 0) mbar_arrive(&empty[s]);
+		finish_piece(P.jobs[cur_job], cur_seg);
 	}
-	if (cur_job >= 0) finish_piece(P.jobs[cur_job], cur_seg, piece_g0);
 	if (s_flags[0] && ctid == 0)
 	{
 		// Do not leave while a copy issued into this CTA's shared memory may
 		// still land: wait (bounded again) for every stage's last phase.
-		const long long n = g_end - g_begin;
-		for (long long k = n > STAGES ? n - STAGES : 0; k < n; ++k)
+		for (int k = n_mine > STAGES ? n_mine - STAGES : 0; k < n_mine; ++k)
 			mbar_wait_bounded(&full[k % STAGES], (uint32_t)((k / STAGES) & 1), nullptr, 0);
 	}
 }
@@ -549,16 +722,30 @@ template <int D, typename KV, int RM>
 int launch_one(const DecodePlan& P, cudaStream_t st)
 {
 	using C = Cfg<D, KV, RM>;
-	static bool configured = false;
-	if (!configured)
+	static bool configured[64] = {};
+	int dev = 0;
+	cudaGetDevice(&dev);
+	if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+	if (!configured[dev])
 	{
 		cudaError_t e = cudaFuncSetAttribute(decode_kernel<D, KV, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
 		                                     C::SMEM);
 		if (e != cudaSuccess) return (int)e;
-		configured = true;
+		configured[dev] = true;
 	}
-	decode_kernel<D, KV, RM><<<P.n_ctas, (NW + 1) * 32, C::SMEM, st>>>(P);
-	return (int)cudaGetLastError();
+	// launched as a programmatic dependent of the K1 grid before it (when there
+	// is one): it starts while K1 runs and waits for it where it must
+	cudaLaunchConfig_t cfg = {};
+	cfg.gridDim = dim3((unsigned)P.n_ctas);
+	cfg.blockDim = dim3((NW + 1) * 32);
+	cfg.dynamicSmemBytes = C::SMEM;
+	cfg.stream = st;
+	cudaLaunchAttribute attr[1];
+	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+	attr[0].val.programmaticStreamSerializationAllowed = 1;
+	cfg.attrs = attr;
+	cfg.numAttrs = 1;
+	return (int)cudaLaunchKernelEx(&cfg, decode_kernel<D, KV, RM>, P);
 }
 
 template <int D, typename KV>
@@ -613,7 +800,9 @@ int decode_smem_bytes(int D, int kv_type, int RM)
 {
 	(void)kv_type;
 	const int E = D / 32, RS = RM * E > 32 ? RM * E / 32 : 1, RMW = RM / RS;
-	return STAGES * 2 * TILE_BYTES + (NW * RMW * D + 2 * NW * RMW) * 4 + 2 * STAGES * 8 + 64;
+	const int fixed = ((NW / 2) * RMW * D + 2 * NW * RMW + 2 * RM * D) * 4 + 256;
+	const int stages = std::min(MAX_STAGES, (SMEM_LIMIT - fixed) / (2 * TILE_BYTES));
+	return stages * 2 * TILE_BYTES + fixed;
 }
 
 int launch_decode(const DecodePlan& P, void* stream)

@@ -20,62 +20,37 @@ namespace
 constexpr int PREP_WARPS = 8;
 constexpr int PREP_MAX_D = 512;
 
-// RMS scale of a D-vector held in `buf` (lane-strided), the reference's form:
-// 1 / sqrt(sum(x^2) * (1/D) + eps) evaluated in double.
-__device__ __forceinline__ float rms_scale(const float* buf, int D, float eps, bool gamma_form)
-{
-	float ss = 0.0f;
-	for (int i = threadIdx.x & 31; i < D; i += 32) ss = fmaf(buf[i], buf[i], ss);
-	ss = warp_sum(ss);
-	// nnc_rmsnorm_gamma_multi_f32 multiplies by a float 1/dim; nnc_rmsnorm_f32 divides by n.
-	const double mean = gamma_form ? (double)ss * (double)(1.0f / (float)D) : (double)ss / (double)D;
-	return (float)(1.0 / sqrt(mean + (double)eps));
-}
-
-// Rotate the first n_rot lanes of the vector in `buf` for position rpos.
-__device__ __forceinline__ void rope_vec(float* buf, int n_rot, int mode, float rpos, const float* inv,
-                                         const float* ff)
-{
-	const int half = n_rot / 2;
-	const int step = mode == 0 ? 1 : 2;     // NEOX pairs i, i + half; NORM pairs 2i, 2i + 1
-	const int other = mode == 0 ? half : 1;
-	for (int i = threadIdx.x & 31; i < half; i += 32)
-	{
-		float theta = rpos * inv[i];
-		if (ff) theta = __fdiv_rn(theta, ff[i]);
-		float sn, cs;
-		sincosf(theta, &sn, &cs);
-		float* p = buf + i * step;
-		const float a = p[0], b = p[other];
-		p[0] = cs * a - sn * b;
-		p[other] = sn * a + cs * b;
-	}
-}
-
 template <typename KV>
 __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __restrict__ jobs, int n_jobs)
 {
 	using T = typename KV::T;
+	// The attention kernel that follows may start now: it streams K/V tiles
+	// that do not depend on this kernel and waits for it only where it does.
+	griddep_launch_dependents();
 	__shared__ float bufs[PREP_WARPS][PREP_MAX_D];
-	__shared__ int s_job;
-	if (threadIdx.x == 0)
+	__shared__ float s_qg[PREP_MAX_D], s_kg[PREP_MAX_D], s_inv[PREP_MAX_D / 2], s_ff[PREP_MAX_D / 2];
+	// block (t, job): token t of job blockIdx.y
+	const DevJob& j = jobs[blockIdx.y];
+	const int t = blockIdx.x;
+	if (t >= j.n_tok) return;
+	(void)n_jobs;
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const int D = j.D, half = j.n_rot / 2;
+	// the gains and the RoPE tables, staged once for every head of the token
+	const float* qg = j.q_gamma;
+	const float* kg = j.k_gamma;
+	const float* ff = j.freq_factors;
+	for (int i = threadIdx.x; i < D; i += blockDim.x)
 	{
-		// the job holding global token blockIdx.x (jobs are ordered by tok0)
-		int lo = 0, hi = n_jobs - 1;
-		while (lo < hi)
+		if (qg) s_qg[i] = qg[i];
+		if (kg) s_kg[i] = kg[i];
+		if (i < half)
 		{
-			const int mid = (lo + hi + 1) >> 1;
-			if (jobs[mid].tok0 <= (int)blockIdx.x) lo = mid;
-			else hi = mid - 1;
+			s_inv[i] = j.rope_inv[i];
+			if (ff) s_ff[i] = ff[i];
 		}
-		s_job = lo;
 	}
 	__syncthreads();
-	const DevJob& j = jobs[s_job];
-	const int t = blockIdx.x - j.tok0;
-	if (t < 0 || t >= j.n_tok) return;
-	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	const int D = j.D;
 	float* buf = bufs[warp];
 	const int n_q = j.n_head, n_kv = j.reuse_kv ? 0 : j.n_kv;
 	const int n_tasks = n_q + 2 * n_kv;
@@ -87,22 +62,9 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __r
 		const int h = kind == 0 ? task : (kind == 1 ? task - n_q : task - n_q - n_kv);
 		const float* src = kind == 0 ? j.q + ((size_t)t * n_q + h) * D
 		                             : (kind == 1 ? j.k : j.v) + ((size_t)t * j.n_kv + h) * D;
-		for (int i = lane; i < D; i += 32) buf[i] = src[i];
-		__syncwarp();
-		const float* gamma = kind == 0 ? j.q_gamma : (kind == 1 ? j.k_gamma : nullptr);
-		if (gamma)
-		{
-			const float sc = rms_scale(buf, D, j.eps, true);
-			for (int i = lane; i < D; i += 32) buf[i] = buf[i] * sc * gamma[i];
-		}
-		else if (kind == 2 && j.v_rmsnorm)
-		{
-			const float sc = rms_scale(buf, D, j.eps, false);
-			for (int i = lane; i < D; i += 32) buf[i] = buf[i] * sc;
-		}
-		__syncwarp();
-		if (kind != 2 && j.n_rot > 0) rope_vec(buf, j.n_rot, j.rope_mode, rpos, j.rope_inv, j.freq_factors);
-		__syncwarp();
+		const float* gamma = kind == 0 ? (qg ? s_qg : nullptr) : (kind == 1 ? (kg ? s_kg : nullptr) : nullptr);
+		prep_head(buf, src, D, gamma, kind == 2 && j.v_rmsnorm, j.eps, kind != 2, j.n_rot, j.rope_mode, rpos, s_inv,
+		          ff ? s_ff : nullptr);
 		if (kind == 0)
 		{
 			float* dst = j.q_rot + ((size_t)t * n_q + h) * D;
@@ -160,17 +122,18 @@ __global__ void softcap_kernel(float* y, const float* x, size_t n, float cap)
 
 } // namespace
 
-int launch_prep(const DevJob* jobs_dev, int n_jobs, int total_tok, int max_heads, int D, int kv_type, void* stream)
+int launch_prep(const DevJob* jobs_dev, int n_jobs, int max_tok, int max_heads, int D, int kv_type, void* stream)
 {
 	(void)max_heads;
-	if (D > PREP_MAX_D) return (int)cudaErrorInvalidValue;
-	if (total_tok == 0) return 0;
+	if (D > PREP_MAX_D || n_jobs > 65535) return (int)cudaErrorInvalidValue;
+	if (max_tok == 0 || n_jobs == 0) return 0;
 	auto st = static_cast<cudaStream_t>(stream);
+	const dim3 grid((unsigned)max_tok, (unsigned)n_jobs);
 	switch (kv_type)
 	{
-	case KV_F32: prep_kernel<kv_f32><<<total_tok, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
-	case KV_BF16: prep_kernel<kv_bf16><<<total_tok, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
-	default: prep_kernel<kv_f16><<<total_tok, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
+	case KV_F32: prep_kernel<kv_f32><<<grid, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
+	case KV_BF16: prep_kernel<kv_bf16><<<grid, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
+	default: prep_kernel<kv_f16><<<grid, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
 	}
 	return (int)cudaGetLastError();
 }
