@@ -228,6 +228,26 @@ typedef struct nncu_attn_job
 int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs);
 int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs, void* stream);
 
+/* One layer's decode / verify attention that allocates nothing: the same
+ * K1 + K2 kernels as nncu_attention_batch_dev for one job, with every buffer
+ * the caller's. No counterpart in the reference, whose CPU path never
+ * allocates device memory: this is for callers that cannot let a library call
+ * cudaMalloc -- hosts whose device memory all belongs to their own arena or
+ * caching allocator, and latency-critical loops that must not stall on the
+ * allocator's device synchronisation.
+ *
+ * q, k, v, out and the pointer fields of `p` are device pointers; k_cache and
+ * v_cache are the caller's cache for this layer and sequence, laid out
+ * [n_kv][rows][head_dim] of kv_type, position p at row p % rows, rows a
+ * multiple of 256. Asynchronous on `stream`. The kernels' scratch is one
+ * 4 MiB device array inside the library, shared by every call: calls that
+ * overlap on the GPU race on it (order them on one stream); a call that would
+ * need more fails with NNCU_ERR_INVALID_ARGUMENT and a message. The first call
+ * on each device looks the array's device address up (cudaGetSymbolAddress)
+ * with that device current; make that first call during set-up. */
+int nncu_attention_noalloc(const nncu_attn_params* p, const float* q, const float* k, const float* v, float* out,
+                           void* k_cache, void* v_cache, int32_t kv_type, int32_t rows, void* stream);
+
 /* Wait for `stream` (the asynchronous calls' completion) and report a kernel
  * whose bounded wait ran out (NNCU_ERR_TIMEOUT: the outputs are void). The
  * synchronous calls make this check themselves. No reference counterpart:

@@ -52,7 +52,7 @@ EXPORTS = [
     "nncu_softcap_dev", "nncu_kv_plan", "nncu_kv_create", "nncu_kv_free", "nncu_kv_layer", "nncu_kv_get_state",
     "nncu_kv_rewind", "nncu_kv_commit", "nncu_kv_write_rows", "nncu_kv_read_rows", "nncu_attention",
     "nncu_attention_batch", "nncu_attention_batch_dev", "nncu_sync", "nncu_perf_enable", "nncu_perf_reset",
-    "nncu_perf_read", "nncu_perf_report", "nncu_launch_count",
+    "nncu_perf_read", "nncu_perf_report", "nncu_launch_count", "nncu_attention_noalloc",
 ]
 
 
@@ -187,6 +187,7 @@ def lib() -> C.CDLL:
     L.nncu_perf_report.argtypes = [C.c_char_p, i32]
     L.nncu_perf_report.restype = C.c_char_p
     L.nncu_launch_count.restype = C.c_uint64
+    L.nncu_attention_noalloc.argtypes = [C.POINTER(AttnParams), vp, vp, vp, vp, vp, vp, i32, i32, vp]
     _lib = L
     return L
 
@@ -340,6 +341,13 @@ class KVCache:
     def sync(self, stream=None) -> None:
         """Wait for `stream` and report a kernel's timed-out wait."""
         _check(lib().nncu_sync(self._h, _stream(stream)))
+
+
+def attention_noalloc(p: AttnParams, q, k, v, out, k_cache, v_cache, kv_type: int, rows: int, stream=None) -> None:
+    """nncu_attention_noalloc: one layer's attention on caller-owned device
+    buffers (the cache laid out [n_kv][rows][head_dim]), with no allocation."""
+    _check(lib().nncu_attention_noalloc(C.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(out), _ptr(k_cache),
+                                        _ptr(v_cache), int(kv_type), int(rows), _stream(stream)))
 
 
 def job(layer: int, p: AttnParams, q, k, v, out, seq: int = 0) -> AttnJob:

@@ -36,6 +36,7 @@ using namespace nncu;
 namespace
 {
 thread_local int t_status = NNCU_OK;
+int cuda_fail(cudaError_t e, const char* what);
 thread_local char t_msg[512] = "";
 
 int fail(int status, const char* fmt, ...)
@@ -48,6 +49,21 @@ int fail(int status, const char* fmt, ...)
 	return status;
 }
 
+} // namespace
+
+// The same per-thread status and message for the library's other files.
+int nncu::set_error(int status, const char* msg)
+{
+	return fail(status, "%s", msg);
+}
+
+int nncu::set_cuda_error(int cuda_status, const char* what)
+{
+	return cuda_fail(static_cast<cudaError_t>(cuda_status), what);
+}
+
+namespace
+{
 int cuda_fail(cudaError_t e, const char* what)
 {
 	if (e == cudaErrorMemoryAllocation)

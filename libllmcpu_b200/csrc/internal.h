@@ -80,6 +80,10 @@ struct DecodePlan
 	int* err;       // device error word
 };
 
+// Record a failure for nncu_last_error() (api.cpp); return `status`.
+int set_error(int status, const char* msg);
+int set_cuda_error(int cuda_status, const char* what);
+
 // Launchers (implemented in the .cu files). Each returns a cudaError_t value.
 int launch_prep(const DevJob* jobs_dev, int n_jobs, int max_tok, int max_heads, int D, int kv_type, void* stream);
 int launch_decode(const DecodePlan& plan, void* stream);

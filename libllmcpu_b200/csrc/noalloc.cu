@@ -1,0 +1,262 @@
+// noalloc.cu -- one layer's decode / verify attention without any allocation.
+//
+// Who needs this. The allocating entry points (nncu_kv_create and the
+// attention calls on its cache) grow their scratch with cudaMalloc on first
+// use. Some callers cannot have that: a host whose device memory is all
+// handed out by its own arena or by a framework's caching allocator (an
+// allocation behind its back breaks its accounting and can fail when the
+// arena owns the whole device), and a latency-critical decode loop that must
+// not stall on cudaMalloc / cudaFree, which may synchronise the whole device.
+// nncu_attention_noalloc serves them: the caller passes every input, the
+// output and its own K/V cache (allocated up front, by whatever means it
+// uses), and the kernels' scratch -- the job descriptor and per-CTA starts,
+// the RoPE table, the normed and rotated q rows, the per-piece partials and
+// their counters -- lives in one file-scope device array of fixed size.
+//
+// What sharing one array means:
+//  * every GPU that loads the library holds the array (NOALLOC_SCRATCH_BYTES)
+//    until the process exits;
+//  * all calls use the same array: two calls whose kernels overlap on the GPU
+//    (different streams, or different host threads, without ordering between
+//    them) race on it and give wrong results; order them on one stream;
+//  * a call leaves its scratch behind for the next one, which clears the
+//    parts that must start at zero (the piece counters, the error word);
+//  * the first call on each device looks up the array's device address
+//    (cudaGetSymbolAddress) with that device current; make that first call
+//    before any use where even such a lookup is unwelcome.
+//
+// The kernels are the allocating path's own K1 (k_prep.cu) and K2 (the
+// decode kernel, k_decode.cu), planned here for a single job.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "internal.h"
+#include "nncu.h"
+
+namespace nncu
+{
+namespace
+{
+
+// The scratch of every no-allocation call on a device: 4 MiB, enough for one
+// layer's decode or verify at the shapes of the benchmark configurations
+// (e.g. 32 query heads of 64 or 8 of 256, a few tokens, 148 CTAs of partials).
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(4) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+constexpr int MAX_DEVICES = 64;
+std::mutex g_setup_mu;
+void* g_scratch_addr[MAX_DEVICES];
+
+// Once per device, with that device current: the array's device address
+// (host code cannot use the symbol itself as a device pointer).
+int scratch_on_device(int dev, unsigned char** out)
+{
+	if (dev < 0 || dev >= MAX_DEVICES) return set_error(NNCU_ERR_INVALID_ARGUMENT, "device ordinal out of range");
+	std::lock_guard<std::mutex> lk(g_setup_mu);
+	if (!g_scratch_addr[dev])
+	{
+		void* p = nullptr;
+		const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+		if (e != cudaSuccess) return set_cuda_error((int)e, "no-allocation scratch: cudaGetSymbolAddress");
+		g_scratch_addr[dev] = p;
+	}
+	*out = static_cast<unsigned char*>(g_scratch_addr[dev]);
+	return NNCU_OK;
+}
+
+size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Host staging for the job descriptor, the CTA starts and the RoPE table:
+// static storage, so building them allocates nothing either.
+constexpr int MAX_CTAS = 256;
+struct alignas(16) HostHead
+{
+	DevJob job;
+	int4 starts[MAX_CTAS];
+	float rope[256];
+};
+thread_local HostHead t_head;
+
+} // namespace
+} // namespace nncu
+
+using namespace nncu;
+
+extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q, const float* k, const float* v,
+                                      float* out, void* k_cache, void* v_cache, int32_t kv_type, int32_t rows,
+                                      void* stream)
+{
+	// ---- arguments (the allocating path's rules, for a caller-owned cache) ----
+	if (!p || !q || !out || !k_cache || !v_cache) return set_error(NNCU_ERR_INVALID_ARGUMENT, "NULL argument");
+	if (!p->reuse_kv && (!k || !v)) return set_error(NNCU_ERR_INVALID_ARGUMENT, "NULL k or v projections");
+	if (kv_type != KV_F32 && kv_type != KV_BF16 && kv_type != KV_F16)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "unknown K/V type");
+	const int D = p->head_dim;
+	if (!decode_supported(D, kv_type))
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "head_dim must be 64, 128, 256 or 512");
+	if (p->n_kv <= 0 || p->n_head <= 0 || p->n_head % p->n_kv)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "n_head must be a positive multiple of n_kv");
+	if (p->n_tok <= 0 || p->pos0 < 0 || p->n_seq <= 0)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "n_tok, pos0 and n_seq must be positive");
+	if (rows <= 0 || rows % ATTN_BLOCK)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "the cache's rows must be a positive multiple of 256");
+	if (p->n_rot < 0 || p->n_rot > D || (p->n_rot & 1) || p->n_rot > 512)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "n_rot must be even and at most head_dim");
+	if (p->rope_mode != NNCU_ROPE_NEOX && p->rope_mode != NNCU_ROPE_NORM)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "unknown rope mode");
+	if (p->window < 0 || p->softcap < 0.0f) return set_error(NNCU_ERR_INVALID_ARGUMENT, "negative window or softcap");
+	// every key a query sees must still be in the caller's `rows` rows
+	const bool windowed = p->causal && p->window > 0;
+	if (windowed ? p->window + p->n_tok > rows : (p->pos0 + p->n_tok > rows || p->n_seq > rows))
+		return set_error(NNCU_ERR_CONTEXT_FULL, "the cache's rows cannot hold every key these queries see");
+
+	int dev = 0;
+	cudaError_t ce = cudaGetDevice(&dev);
+	if (ce != cudaSuccess) return set_cuda_error((int)ce, "cudaGetDevice");
+	unsigned char* scratch = nullptr;
+	int rc = scratch_on_device(dev, &scratch);
+	if (rc != NNCU_OK) return rc;
+	int n_sms = 148;
+	cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev);
+
+	// ---- the plan: one job, stream-K over its tiles ----
+	const size_t es = kv_esize(kv_type);
+	const int T = decode_tile_keys(D, kv_type);
+	const int G = p->n_head / p->n_kv;
+	int RM = 1;
+	while (RM < G * p->n_tok && RM < decode_rows_max(D)) RM *= 2;
+	int first_min = INT_MAX, last_max = -1;
+	for (int t = 0; t < p->n_tok; ++t)
+	{
+		int f, l;
+		nncu_attn_span(p->causal, p->window, p->pos0 + t, p->n_seq, &f, &l);
+		if (l < f) continue;
+		first_min = std::min(first_min, f);
+		last_max = std::max(last_max, l);
+	}
+	const int n_rowgroups = (G * p->n_tok + RM - 1) / RM;
+	const int n_tiles = last_max < 0 ? 0 : last_max / T - first_min / T + 1;
+	const int n_seg = p->n_kv * n_rowgroups;
+	const long long total = (long long)n_seg * n_tiles;
+	const int ctas0 = (int)std::min<long long>(std::min<long long>(total, n_sms), MAX_CTAS);
+	const long long W = ctas0 > 0 ? (total + ctas0 - 1) / ctas0 : 1;
+	const int n_ctas = ctas0 > 0 ? (int)((total + W - 1) / W) : 0;
+
+	// ---- the scratch: [job | starts | rope | q rows | partials | counters | error] ----
+	const size_t off_job = 0;
+	const size_t off_starts = up256(sizeof(DevJob));
+	const size_t off_rope = off_starts + up256((size_t)MAX_CTAS * sizeof(int4));
+	const size_t off_qrot = off_rope + up256(256 * sizeof(float));
+	const size_t off_parts = off_qrot + up256((size_t)p->n_tok * p->n_head * D * sizeof(float));
+	const size_t off_count = off_parts + up256((size_t)(n_seg + n_ctas) * RM * (D + 4) * sizeof(float));
+	const size_t off_err = off_count + up256((size_t)n_seg * sizeof(int));
+	const size_t need = off_err + 256;
+	if (need > NOALLOC_SCRATCH_BYTES)
+	{
+		char msg[200];
+		std::snprintf(msg, sizeof msg,
+		              "this call needs %zu bytes of scratch; the no-allocation entry point has %zu (fewer tokens or "
+		              "heads per call, or use nncu_attention)",
+		              need, NOALLOC_SCRATCH_BYTES);
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, msg);
+	}
+
+	HostHead& hh = t_head;
+	std::memset(&hh.job, 0, sizeof hh.job);
+	DevJob& j = hh.job;
+	j.q = q;
+	j.k = k;
+	j.v = v;
+	j.q_rot = reinterpret_cast<float*>(scratch + off_qrot);
+	j.out = out;
+	j.q_gamma = p->q_gamma;
+	j.k_gamma = p->k_gamma;
+	j.freq_factors = p->freq_factors;
+	j.rope_inv = reinterpret_cast<const float*>(scratch + off_rope);
+	j.K = static_cast<char*>(k_cache);
+	j.V = static_cast<char*>(v_cache);
+	j.head_bytes = (long long)rows * D * (long long)es;
+	j.rows = rows;
+	j.n_tok = p->n_tok;
+	j.pos0 = p->pos0;
+	j.n_seq = p->n_seq;
+	j.n_head = p->n_head;
+	j.n_kv = p->n_kv;
+	j.D = D;
+	j.n_rot = p->n_rot;
+	j.rope_mode = p->rope_mode;
+	j.causal = p->causal != 0;
+	j.window = p->window;
+	j.reuse_kv = p->reuse_kv != 0;
+	j.v_rmsnorm = p->v_rmsnorm != 0;
+	j.rope_scale = p->rope_scale;
+	j.eps = p->eps;
+	j.scale = p->scale;
+	j.softcap = p->softcap;
+	j.tile_lo = last_max < 0 ? 0 : first_min / T;
+	j.n_tiles = n_tiles;
+	j.n_rowgroups = n_rowgroups;
+	for (int c = 0; c < n_ctas; ++c)
+	{
+		const long long g = (long long)c * W;
+		hh.starts[c] = make_int4(0, (int)(g / n_tiles), (int)(g % n_tiles), 0);
+	}
+	// nnc_rope_f32's inverse frequencies (nn_ops.cpp:1844-1856), the fp32 recurrence
+	const int half = p->n_rot / 2;
+	if (half > 0)
+	{
+		const float ratio = std::pow(p->freq_base, -2.0f / static_cast<float>(p->n_rot));
+		float inv = 1.0f;
+		for (int i = 0; i < half; ++i)
+		{
+			hh.rope[i] = inv;
+			inv *= ratio;
+		}
+	}
+
+	// ---- upload the head, clear what must start at zero, run K1 and K2 ----
+	auto st = static_cast<cudaStream_t>(stream);
+	// copies from pageable host memory: each returns once its source is consumed
+	ce = cudaMemcpyAsync(scratch + off_job, &hh.job, sizeof(DevJob), cudaMemcpyHostToDevice, st);
+	if (ce == cudaSuccess && n_ctas > 0)
+		ce = cudaMemcpyAsync(scratch + off_starts, hh.starts, (size_t)n_ctas * sizeof(int4), cudaMemcpyHostToDevice,
+		                     st);
+	if (ce == cudaSuccess && half > 0)
+		ce = cudaMemcpyAsync(scratch + off_rope, hh.rope, (size_t)half * sizeof(float), cudaMemcpyHostToDevice, st);
+	if (ce == cudaSuccess) ce = cudaMemsetAsync(scratch + off_count, 0, off_err + 256 - off_count, st);
+	if (ce == cudaSuccess && n_tiles == 0)
+		ce = cudaMemsetAsync(out, 0, (size_t)p->n_tok * p->n_head * D * sizeof(float), st);
+	if (ce != cudaSuccess) return set_cuda_error((int)ce, "no-allocation call: staging");
+
+	int e = launch_prep(reinterpret_cast<const DevJob*>(scratch + off_job), 1, p->n_tok, 0, D, kv_type, st);
+	if (e) return set_cuda_error(e, "K1 (norm, RoPE, append) launch");
+	if (n_tiles > 0)
+	{
+		DecodePlan P{};
+		P.jobs = reinterpret_cast<const DevJob*>(scratch + off_job);
+		P.n_jobs = 1;
+		P.D = D;
+		P.kv_type = kv_type;
+		P.RM = RM;
+		P.T = T;
+		P.total_tiles = total;
+		P.n_ctas = n_ctas;
+		P.tiles_per_cta = W;
+		P.n_segments = n_seg;
+		P.fused = 0;
+		P.cta_start = reinterpret_cast<const int4*>(scratch + off_starts);
+		P.parts = reinterpret_cast<float*>(scratch + off_parts);
+		P.counters = reinterpret_cast<int*>(scratch + off_count);
+		P.err = reinterpret_cast<int*>(scratch + off_err);
+		e = launch_decode(P, st);
+		if (e) return set_cuda_error(e, "K2 (attention) launch");
+	}
+	return NNCU_OK;
+}
