@@ -389,16 +389,41 @@ __device__ __forceinline__ void rope_vec(float* buf, int n_rot, int mode, float 
 	}
 }
 
+// A head vector of up to 512 floats held by a warp, lane-strided: element
+// lane + 32 k in slot k. Loading all of it into registers before writing any
+// of it to shared memory lets the loads overlap (through generic pointers the
+// compiler could not otherwise move a load past the previous store).
+struct HeadRegs
+{
+	float x[16];
+};
+
+__device__ __forceinline__ void load_head(HeadRegs& r, const float* __restrict__ src, int D)
+{
+	const int lane = threadIdx.x & 31;
+#pragma unroll
+	for (int k = 0; k < 16; ++k)
+	{
+		const int i = lane + 32 * k;
+		r.x[k] = i < D ? src[i] : 0.0f;
+	}
+}
+
 // One head vector through attention_forward's per-head steps (model.cpp:
-// 1616-1660): load src into shared `buf`, RMSNorm with `gamma` (or the plain
-// norm when plain_norm), then RoPE when rpos is given. Warp-cooperative; buf
+// 1616-1660): from registers into shared `buf`, RMSNorm with `gamma` (or the
+// plain norm when plain_norm), then RoPE when rotate. Warp-cooperative; buf
 // holds the result, visible to the whole warp, on return.
-__device__ __forceinline__ void prep_head(float* buf, const float* src, int D, const float* gamma, bool plain_norm,
+__device__ __forceinline__ void prep_head(float* buf, const HeadRegs& r, int D, const float* gamma, bool plain_norm,
                                           float eps, bool rotate, int n_rot, int mode, float rpos, const float* inv,
                                           const float* ff)
 {
 	const int lane = threadIdx.x & 31;
-	for (int i = lane; i < D; i += 32) buf[i] = src[i];
+#pragma unroll
+	for (int k = 0; k < 16; ++k)
+	{
+		const int i = lane + 32 * k;
+		if (i < D) buf[i] = r.x[k];
+	}
 	__syncwarp();
 	if (gamma)
 	{

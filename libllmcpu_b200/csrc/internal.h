@@ -33,8 +33,9 @@ enum
 inline int kv_esize(int kv_type) { return kv_type == KV_F32 ? 4 : 2; }
 
 // One attention job (one layer of one sequence) as the kernels see it.
-// All pointers are device pointers.
-struct DevJob
+// All pointers are device pointers. The decode kernel bulk-copies it into
+// shared memory, hence the 16-byte alignment and size.
+struct alignas(16) DevJob
 {
 	const float* q;           // [n_tok][n_head*D] projections, fp32
 	const float* k;           // [n_tok][n_kv*D]
@@ -62,6 +63,7 @@ struct DevJob
 	int tok0;             // this job's first token in the launch's global token order
 	int pad_;
 };
+static_assert(sizeof(DevJob) % 16 == 0, "DevJob is bulk-copied");
 
 // The decode launch: stream-K over the concatenated tiles of every segment.
 struct DecodePlan

@@ -69,7 +69,10 @@ struct Cfg
 	// the warps' (o, m, l) at a piece's end, merged in two rounds of half the
 	// warps each; the fold's weights reuse the same area
 	static constexpr int AREA_FLOATS = (NW / 2) * RMW * D;
-	static constexpr int QSLOT_FLOATS = RM * D; // one piece's q rows
+	// one piece's slot: its job descriptor, its tile count / first tile /
+	// segment, then its q rows
+	static constexpr int QHEAD_FLOATS = (int)(sizeof(DevJob) / 4) + 4;
+	static constexpr int QSLOT_FLOATS = QHEAD_FLOATS + RM * D;
 	static constexpr int FIXED_BYTES = (AREA_FLOATS + 2 * NW * RMW + 2 * QSLOT_FLOATS) * 4 + 256;
 	static constexpr int FIT = (SMEM_LIMIT - FIXED_BYTES) / STAGE_BYTES;
 	static constexpr int STAGES = FIT < MAX_STAGES ? FIT : MAX_STAGES;
@@ -95,6 +98,12 @@ __device__ __forceinline__ void cursor_load(const DecodePlan& P, Cursor& c)
 	const DevJob& J = P.jobs[c.job];
 	c.n_tiles = J.n_tiles;
 	c.n_segs = J.n_kv * J.n_rowgroups;
+	if (c.job + 1 < P.n_jobs)
+	{
+		// the next job's descriptor into L1 ahead of the job change
+		const char* nx = reinterpret_cast<const char*>(P.jobs + c.job + 1);
+		for (int b = 0; b < (int)sizeof(DevJob); b += 128) asm volatile("prefetch.global.L1 [%0];" ::"l"(nx + b));
+	}
 }
 
 __device__ __forceinline__ void cursor_start(const DecodePlan& P, Cursor& c)
@@ -195,7 +204,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 				const int h = cur.seg / J.n_rowgroups, rg = cur.seg % J.n_rowgroups;
 				if (cur.job != pj || cur.seg != ps)
 				{
-					// a new piece: its q rows into slot piece % 2, once the consumers are done with it
+					// a new piece: its descriptor, tile count and q rows into slot piece % 2,
+					// once the consumers are done with what that slot held
 					const int sl = piece & 1;
 					if (piece >= 2 &&
 					    !mbar_wait_bounded(&qempty[sl], (uint32_t)(((piece >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
@@ -205,13 +215,19 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					}
 					const int G = J.n_head / J.n_kv;
 					const int rows = seg_rows(J, rg, RM);
-					mbar_arrive_expect_tx(&qfull[sl], (uint32_t)(rows * D * 4));
+					float* slot = qslot + sl * C::QSLOT_FLOATS;
+					int* info = reinterpret_cast<int*>(slot + C::QHEAD_FLOATS - 4);
+					info[0] = min(cur.n_tiles - cur.tis, n_mine - i); // tiles of this piece in this CTA
+					info[1] = cur.tis;
+					info[2] = cur.seg;
+					mbar_arrive_expect_tx(&qfull[sl], (uint32_t)(sizeof(DevJob) + rows * D * 4));
+					bulk_g2s(slot, P.jobs + cur.job, (uint32_t)sizeof(DevJob), &qfull[sl]);
 					// rows (t, g) of the segment: per token, its G heads are contiguous
 					for (int r = 0; r < rows;)
 					{
 						const int gr = rg * RM + r, t = gr / G, g = gr % G;
 						const int run = min(G - g, rows - r);
-						bulk_g2s(qslot + sl * C::QSLOT_FLOATS + r * D,
+						bulk_g2s(slot + C::QHEAD_FLOATS + r * D,
 						         J.q_rot + ((size_t)t * J.n_head + (size_t)h * G + g) * D, (uint32_t)(run * D * 4),
 						         &qfull[sl]);
 						r += run;
@@ -255,20 +271,25 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	int first_v = 0, last_v = -1; // this lane's row span
 	bool softcap = false;
 	float cap = 0.0f;
-	int piece = 0;
 
-	// Piece start: the piece's q rows from their slot into registers.
-	auto start_piece = [&](const DevJob& J, int seg_local) {
+	// What the end of a piece needs from its job, kept in registers (the slot
+	// it came in may be refilled before the piece ends).
+	struct PieceEnd
+	{
+		float* out;
+		int n_head, G, h, rg, n_tok, seg, c_first, c_last;
+	} pe;
+
+	// Piece start: the piece's q rows from its slot into registers, and what
+	// its end will need; then the slot goes back to the producer.
+	auto start_piece = [&](const DevJob& J, int seg_local, int sl) {
 		const int G = J.n_head / J.n_kv;
-		const int rg = seg_local % J.n_rowgroups;
+		const int h = seg_local / J.n_rowgroups, rg = seg_local % J.n_rowgroups;
 		const int rows = seg_rows(J, rg, RM);
-		const int sl = piece & 1;
 		softcap = J.softcap > 0.0f;
 		cap = J.softcap;
-		if (!s_flags[0] && !mbar_wait_bounded(&qfull[sl], (uint32_t)((piece >> 1) & 1), P.err, DEVERR_WAIT_FULL))
-			s_flags[0] = 1;
 		const float qmul = softcap ? J.scale : J.scale * LOG2E;
-		const float* qs = qslot + sl * C::QSLOT_FLOATS;
+		const float* qs = qslot + sl * C::QSLOT_FLOATS + C::QHEAD_FLOATS;
 #pragma unroll
 		for (int r = 0; r < RMW; ++r)
 		{
@@ -284,15 +305,25 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			}
 			m[r] = -CUDART_INF_F;
 		}
-		__syncwarp();
-		if (lane == 0) mbar_arrive(&qempty[sl]); // this warp is done with the slot
-		++piece;
 		l_lane = 0.0f;
 		const int gr_v = rg * RM + rs * RMW + r_v;
 		if (gr_v < G * J.n_tok)
 			span_of(J.causal, J.window, J.pos0 + gr_v / G, J.n_seq, first_v, last_v);
 		else
 			first_v = 0, last_v = -1; // a padding row sees nothing
+		const long long W = P.tiles_per_cta;
+		const long long seg_gstart = J.gtile0 + (long long)seg_local * J.n_tiles;
+		pe.out = J.out;
+		pe.n_head = J.n_head;
+		pe.G = G;
+		pe.h = h;
+		pe.rg = rg;
+		pe.n_tok = J.n_tok;
+		pe.seg = J.seg0 + seg_local;
+		pe.c_first = (int)(seg_gstart / W);
+		pe.c_last = (int)((seg_gstart + J.n_tiles - 1) / W);
+		__syncwarp();
+		if (lane == 0) mbar_arrive(&qempty[sl]); // this warp is done with the slot
 	};
 
 	// Merge the warps' states of the finished piece (two rounds: the upper half
@@ -300,7 +331,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	// registers and leaves the result for the CTA); write the output (whole
 	// segment in this CTA) or a partial, and fold the partials if this CTA
 	// completes the segment.
-	auto finish_piece = [&](const DevJob& J, int seg_local) {
+	auto finish_piece = [&]() {
 		// l of row r: sum over the batch's key slots (lanes differing in the key bits)
 		float lsum = l_lane;
 #pragma unroll
@@ -354,14 +385,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		}
 		named_sync(1, NW * 32);
 
-		const int G = J.n_head / J.n_kv;
-		const int h = seg_local / J.n_rowgroups, rg = seg_local % J.n_rowgroups;
-		const long long W = P.tiles_per_cta;
-		const long long seg_gstart = J.gtile0 + (long long)seg_local * J.n_tiles;
-		const long long seg_gend = seg_gstart + J.n_tiles;
-		const int c_first = (int)(seg_gstart / W), c_last = (int)((seg_gend - 1) / W);
+		const int G = pe.G, h = pe.h, rg = pe.rg, n_tok = pe.n_tok, n_head = pe.n_head;
+		const int c_first = pe.c_first, c_last = pe.c_last, seg = pe.seg;
 		const bool single = c_first == c_last;
-		const int seg = J.seg0 + seg_local;
 		float* part = P.parts + (size_t)(seg + (int)blockIdx.x) * RM * PW;
 
 		for (int idx = ctid; idx < RM * D; idx += NW * 32)
@@ -384,10 +410,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			if (single)
 			{
 				const int gr = rg * RM + R;
-				if (gr < G * J.n_tok)
+				if (gr < G * n_tok)
 				{
 					const int t = gr / G, g = gr % G;
-					J.out[((size_t)t * J.n_head + (size_t)h * G + g) * D + d] = L > 0.0f ? acc / L : 0.0f;
+					pe.out[((size_t)t * n_head + (size_t)h * G + g) * D + d] = L > 0.0f ? acc / L : 0.0f;
 				}
 			}
 			else
@@ -459,7 +485,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 				{
 					const int R = idx / (D / 4), d = 4 * (idx % (D / 4));
 					const int gr = rg * RM + R;
-					if (gr >= G * J.n_tok) continue;
+					if (gr >= G * n_tok) continue;
 					const float* col = base + R * PW + d;
 					float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 					int c = 0;
@@ -488,7 +514,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 						acc.w = fmaf(v.w, w, acc.w);
 					}
 					const int t = gr / G, g = gr % G;
-					*reinterpret_cast<float4*>(J.out + ((size_t)t * J.n_head + (size_t)h * G + g) * D + d) = acc;
+					*reinterpret_cast<float4*>(pe.out + ((size_t)t * n_head + (size_t)h * G + g) * D + d) = acc;
 				}
 				if (ctid == 0) P.counters[seg] = 0; // ready for the next launch
 			}
@@ -496,25 +522,26 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		named_sync(1, NW * 32); // the merge area is free again
 	};
 
-	if (n_mine > 0)
+	// Pieces as the producer announces them in the q slots: start, tiles, end.
+	int i = 0;
+	for (int piece = 0; i < n_mine; ++piece)
 	{
-		Cursor cur;
-		cursor_start(P, cur);
-		int cur_job = -1, cur_seg = -1, key_base = 0;
-		for (int i = 0; i < n_mine; ++i)
+		const int sl = piece & 1;
+		if (!s_flags[0] && !mbar_wait_bounded(&qfull[sl], (uint32_t)((piece >> 1) & 1), P.err, DEVERR_WAIT_FULL))
+			s_flags[0] = 1;
+		named_sync(1, NW * 32); // every warp has its answer: the decision below is uniform
+		if (s_flags[0]) break;
+		const float* slot = qslot + sl * C::QSLOT_FLOATS;
+		const DevJob& J = *reinterpret_cast<const DevJob*>(slot);
+		const int* info = reinterpret_cast<const int*>(slot + C::QHEAD_FLOATS - 4);
+		const int n_piece = info[0], tis0 = info[1], seg_local = info[2];
+		int key_base = (J.tile_lo + tis0) * T;
+		start_piece(J, seg_local, sl);
+		for (int k = 0; k < n_piece; ++k, ++i)
 		{
-			const DevJob& J = P.jobs[cur.job];
-			if (cur.job != cur_job || cur.seg != cur_seg)
-			{
-				if (cur_job >= 0) finish_piece(P.jobs[cur_job], cur_seg);
-				cur_job = cur.job;
-				cur_seg = cur.seg;
-				key_base = (J.tile_lo + cur.tis) * T;
-				start_piece(J, cur.seg);
-			}
 			const int s = i % STAGES;
 			// After a timed-out wait the CTA stops waiting (fail fast) but keeps
-			// stepping through its tiles, so every consumer warp still meets the
+			// stepping through the piece, so every consumer warp still meets the
 			// same named barriers; the error word tells the host the result is void.
 			if (!s_flags[0] && !mbar_wait_bounded(&full[s], (uint32_t)((i / STAGES) & 1), P.err, DEVERR_WAIT_FULL))
 				s_flags[0] = 1;
@@ -595,15 +622,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			__syncwarp();
 			if (lane == 0) mbar_arrive(&empty[s]);
 			key_base += T;
-			cursor_next(P, cur);
 		}
-		finish_piece(P.jobs[cur_job], cur_seg);
+		finish_piece();
 	}
+	const int n_done = i;
 	if (s_flags[0] && ctid == 0)
 	{
 		// Do not leave while a copy issued into this CTA's shared memory may
-		// still land: wait (bounded again) for every stage's last phase.
-		for (int k = n_mine > STAGES ? n_mine - STAGES : 0; k < n_mine; ++k)
+		// still land: wait (bounded again) for the stages the producer may
+		// have filled beyond the last consumed tile.
+		for (int k = n_done; k < n_mine && k < n_done + STAGES; ++k)
 			mbar_wait_bounded(&full[k % STAGES], (uint32_t)((k / STAGES) & 1), nullptr, 0);
 	}
 }

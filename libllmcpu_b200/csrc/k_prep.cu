@@ -36,34 +36,43 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __r
 	(void)n_jobs;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int D = j.D, half = j.n_rot / 2;
-	// the gains and the RoPE tables, staged once for every head of the token
-	const float* qg = j.q_gamma;
-	const float* kg = j.k_gamma;
-	const float* ff = j.freq_factors;
-	for (int i = threadIdx.x; i < D; i += blockDim.x)
-	{
-		if (qg) s_qg[i] = qg[i];
-		if (kg) s_kg[i] = kg[i];
-		if (i < half)
-		{
-			s_inv[i] = j.rope_inv[i];
-			if (ff) s_ff[i] = ff[i];
-		}
-	}
-	__syncthreads();
 	float* buf = bufs[warp];
 	const int n_q = j.n_head, n_kv = j.reuse_kv ? 0 : j.n_kv;
 	const int n_tasks = n_q + 2 * n_kv;
 	const float rpos = (float)(j.pos0 + t) * j.rope_scale;
 	const int row = (j.pos0 + t) % j.rows;
-	for (int task = warp; task < n_tasks; task += PREP_WARPS)
-	{
+	auto task_src = [&](int task) {
 		const int kind = task < n_q ? 0 : (task < n_q + n_kv ? 1 : 2); // q, k, v
 		const int h = kind == 0 ? task : (kind == 1 ? task - n_q : task - n_q - n_kv);
-		const float* src = kind == 0 ? j.q + ((size_t)t * n_q + h) * D
-		                             : (kind == 1 ? j.k : j.v) + ((size_t)t * j.n_kv + h) * D;
+		return kind == 0 ? j.q + ((size_t)t * n_q + h) * D : (kind == 1 ? j.k : j.v) + ((size_t)t * j.n_kv + h) * D;
+	};
+	// one round of loads: this warp's first head vector, and the gains and
+	// RoPE tables staged once for every head of the token
+	HeadRegs x;
+	if (warp < n_tasks) load_head(x, task_src(warp), D);
+	const float* qg = j.q_gamma;
+	const float* kg = j.k_gamma;
+	const float* ff = j.freq_factors;
+	for (int i = threadIdx.x; i < D; i += blockDim.x)
+	{
+		const float a = qg ? qg[i] : 0.0f, b = kg ? kg[i] : 0.0f;
+		const float c = i < half ? j.rope_inv[i] : 0.0f, d = (ff && i < half) ? ff[i] : 0.0f;
+		s_qg[i] = a;
+		s_kg[i] = b;
+		if (i < half)
+		{
+			s_inv[i] = c;
+			s_ff[i] = d;
+		}
+	}
+	__syncthreads();
+	for (int task = warp; task < n_tasks; task += PREP_WARPS)
+	{
+		if (task != warp) load_head(x, task_src(task), D);
+		const int kind = task < n_q ? 0 : (task < n_q + n_kv ? 1 : 2); // q, k, v
+		const int h = kind == 0 ? task : (kind == 1 ? task - n_q : task - n_q - n_kv);
 		const float* gamma = kind == 0 ? (qg ? s_qg : nullptr) : (kind == 1 ? (kg ? s_kg : nullptr) : nullptr);
-		prep_head(buf, src, D, gamma, kind == 2 && j.v_rmsnorm, j.eps, kind != 2, j.n_rot, j.rope_mode, rpos, s_inv,
+		prep_head(buf, x, D, gamma, kind == 2 && j.v_rmsnorm, j.eps, kind != 2, j.n_rot, j.rope_mode, rpos, s_inv,
 		          ff ? s_ff : nullptr);
 		if (kind == 0)
 		{
