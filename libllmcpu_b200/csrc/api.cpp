@@ -227,7 +227,7 @@ struct nncu_kv
 
 	cudaStream_t stream = nullptr; // the host-pointer calls' stream
 	int* err_dev = nullptr;        // device error word (bounded waits)
-	DevBuf jobs_dev, stage_dev, qrot, parts, counters;
+	DevBuf jobs_dev, stage_dev, parts, counters;
 	HostBuf stage_host, jobs_host;
 	cudaEvent_t jobs_uploaded = nullptr; // the last upload from jobs_host has been read
 	cudaEvent_t done = nullptr;          // the last submission's kernels have finished: calls on one
@@ -249,7 +249,6 @@ struct nncu_kv
 		if (err_dev) cudaFree(err_dev);
 		jobs_dev.release();
 		stage_dev.release();
-		qrot.release();
 		parts.release();
 		counters.release();
 		stage_host.release();
@@ -359,6 +358,7 @@ int rope_table(nncu_kv* kv, float base, int n_rot, const float** out)
 	}
 	std::vector<float> tab;
 	rope_inv_table(base, n_rot, tab);
+	tab.resize((tab.size() + 3) & ~size_t(3), 0.0f); // whole 16-byte pieces: the decode kernel bulk-copies it
 	float* d = nullptr;
 	CU(cudaMalloc(&d, tab.size() * sizeof(float)), "rope table");
 	cudaError_t e = cudaMemcpy(d, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice);
@@ -703,6 +703,8 @@ int validate_job(const nncu_kv* kv, const nncu_attn_job& j)
 		return fail(NNCU_ERR_INVALID_ARGUMENT, "n_rot %d must be even and at most head_dim", p.n_rot);
 	if (p.rope_mode != NNCU_ROPE_NEOX && p.rope_mode != NNCU_ROPE_NORM)
 		return fail(NNCU_ERR_INVALID_ARGUMENT, "unknown rope mode %d", p.rope_mode);
+	if (p.freq_factors && p.n_rot % 8)
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "freq_factors need n_rot to be a multiple of 8 (it is %d)", p.n_rot);
 	if (p.window < 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "negative window");
 	if ((p.reuse_kv != 0) != (L.kv_layer != j.layer))
 		return fail(NNCU_ERR_INVALID_ARGUMENT, "layer %d: reuse_kv %d disagrees with the cache (it reads layer %d)",
@@ -786,8 +788,14 @@ void plan_decode(nncu_kv* kv, std::vector<DevJob>& jobs, DecodePlan& P)
 	// one CTA per SM (the kernel's shared memory allows no more); at most 256, so
 	// the in-kernel fold's per-piece weights fit its merge area
 	const long long ctas = std::min<long long>(std::min<long long>(total, (long long)kv->num_sms), 256);
-	P.tiles_per_cta = ctas > 0 ? (total + ctas - 1) / ctas : 1;
-	P.n_ctas = ctas > 0 ? (int)((total + P.tiles_per_cta - 1) / P.tiles_per_cta) : 0;
+	long long W = ctas > 0 ? (total + ctas - 1) / ctas : 1;
+	// the in-kernel fold keeps one weight per (piece, row) in the merge area:
+	// no segment may be cut into more pieces than that holds
+	int max_tiles = 1;
+	for (const auto& j : jobs) max_tiles = std::max(max_tiles, j.n_tiles);
+	W = std::max(W, (long long)((max_tiles + decode_fold_pieces(D, RM) - 2) / (decode_fold_pieces(D, RM) - 1)));
+	P.tiles_per_cta = W;
+	P.n_ctas = ctas > 0 ? (int)((total + W - 1) / W) : 0;
 	P.err = kv->err_dev;
 }
 
@@ -827,15 +835,13 @@ void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 	d.softcap = p.softcap;
 }
 
-// Launch K1 and K2 for jobs whose DevJob pointers are all device pointers;
-// assigns q_rot scratch, plans, uploads the job table and launches on `st`.
+// Launch K1 and K2 for jobs whose DevJob pointers are all device pointers:
+// plans, uploads the job table and launches on `st`.
 int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn_job>& pub, cudaStream_t st)
 {
 	const int n = (int)jobs.size();
-	// the job table, q scratch and partials are the cache's: wait for the previous submission
+	// the job table and the partials are the cache's: wait for the previous submission
 	CU(cudaStreamWaitEvent(st, kv->done, 0), "order after the previous call");
-	// rope tables and q_rot scratch
-	size_t qrot_floats = 0;
 	int tok = 0, max_tok = 0;
 	for (int i = 0; i < n; ++i)
 	{
@@ -845,14 +851,6 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn
 		jobs[i].tok0 = tok;
 		tok += p.n_tok;
 		max_tok = std::max(max_tok, p.n_tok);
-		qrot_floats += align_up((size_t)p.n_tok * p.n_head * p.head_dim, 64);
-	}
-	CU(kv->qrot.reserve(qrot_floats * sizeof(float)), "q scratch");
-	size_t off = 0;
-	for (int i = 0; i < n; ++i)
-	{
-		jobs[i].q_rot = static_cast<float*>(kv->qrot.p) + off;
-		off += align_up((size_t)jobs[i].n_tok * jobs[i].n_head * jobs[i].D, 64);
 	}
 	// Every job of one launch shares head_dim (the kernels are specialised on it).
 	for (int i = 1; i < n; ++i)
@@ -967,6 +965,10 @@ extern "C" int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, 
 		if (rc != NNCU_OK) return rc;
 		if (!jobs[i].q || !jobs[i].out || (!jobs[i].p.reuse_kv && (!jobs[i].k || !jobs[i].v)))
 			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: NULL input or output", i);
+		// q rows, the q gains and the frequency factors are bulk-copied into shared memory
+		auto misaligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; };
+		if (misaligned(jobs[i].q) || misaligned(jobs[i].p.q_gamma) || misaligned(jobs[i].p.freq_factors))
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: q, q_gamma and freq_factors must be 16-byte aligned", i);
 	}
 	int rc = check_conflicts(kv, jobs, n_jobs);
 	if (rc != NNCU_OK) return rc;

@@ -40,12 +40,11 @@ struct alignas(16) DevJob
 	const float* q;           // [n_tok][n_head*D] projections, fp32
 	const float* k;           // [n_tok][n_kv*D]
 	const float* v;
-	float* q_rot;             // [n_tok][n_head*D] normed + rotated q (scratch)
 	float* out;               // [n_tok][n_head*D]
 	const float* q_gamma;     // D or null
 	const float* k_gamma;     // D or null
 	const float* freq_factors; // n_rot/2 or null
-	const float* rope_inv;    // n_rot/2: the fp32 inverse-frequency recurrence
+	const float* rope_inv;    // n_rot/2, padded to 16 bytes: the fp32 inverse-frequency recurrence
 	char* K;                  // this sequence's K slab: [n_kv][rows][D]
 	char* V;
 	long long head_bytes;     // rows * D * esize
@@ -61,7 +60,7 @@ struct alignas(16) DevJob
 	int seg0;             // this job's first segment
 	long long gtile0;     // this job's first tile in the launch's global tile order
 	int tok0;             // this job's first token in the launch's global token order
-	int pad_;
+	int pad_[3];
 };
 static_assert(sizeof(DevJob) % 16 == 0, "DevJob is bulk-copied");
 
@@ -93,6 +92,7 @@ bool decode_supported(int D, int kv_type);
 int decode_tile_keys(int D, int kv_type);
 int decode_rows_max(int D);
 int decode_smem_bytes(int D, int kv_type, int RM);
+int decode_fold_pieces(int D, int RM); // the most pieces one segment may be cut into
 
 // Unit-seam kernels (nn_ops.h equivalents).
 int launch_attn_block(const float* q, size_t q_stride, const void* K, const void* V, int kv_type, size_t kv_stride,

@@ -66,20 +66,24 @@ struct Cfg
 	static constexpr int SHIFT = 5 - LOG2N;                // lane >> SHIFT = value index after the reduction
 	static constexpr int LOG2RMW = RMW >= 32 ? 5 : RMW >= 16 ? 4 : RMW >= 8 ? 3 : RMW >= 4 ? 2 : RMW >= 2 ? 1 : 0;
 	static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-	// the warps' (o, m, l) at a piece's end, merged in two rounds of half the
-	// warps each; the fold's weights reuse the same area
-	static constexpr int AREA_FLOATS = (NW / 2) * RMW * D;
+	// the warps' (o, m, l) at a piece's end pass through two warps' worth of
+	// area in a pairwise tree; the fold's weights reuse the same area
+	static constexpr int AREA_FLOATS = 2 * RMW * D;
 	// one piece's slot: its job descriptor, its tile count / first tile /
-	// segment, then its q rows
+	// segment, its raw q rows, the q gains and the RoPE tables
 	static constexpr int QHEAD_FLOATS = (int)(sizeof(DevJob) / 4) + 4;
-	static constexpr int QSLOT_FLOATS = QHEAD_FLOATS + RM * D;
+	static constexpr int QROWS = QHEAD_FLOATS;             // RM * D
+	static constexpr int QGAIN = QROWS + RM * D;           // D
+	static constexpr int QINV = QGAIN + D;                 // D / 2
+	static constexpr int QFF = QINV + D / 2;               // D / 2
+	static constexpr int QSLOT_FLOATS = QFF + D / 2;
 	static constexpr int FIXED_BYTES = (AREA_FLOATS + 2 * NW * RMW + 2 * QSLOT_FLOATS) * 4 + 256;
 	static constexpr int FIT = (SMEM_LIMIT - FIXED_BYTES) / STAGE_BYTES;
 	static constexpr int STAGES = FIT < MAX_STAGES ? FIT : MAX_STAGES;
 	static constexpr int SMEM = STAGES * STAGE_BYTES + FIXED_BYTES;
 	static_assert(STAGES >= 3, "shared memory for at least three stages");
 	static_assert(D % 32 == 0, "D: a multiple of 32");
-	static_assert(RM % RS == 0 && NW % RS == 0 && (NW / 2) % RS == 0, "row slices");
+	static_assert(RM % RS == 0 && NW == 8 && RS <= 2, "row slices");
 	static_assert(T >= NKG && T <= ATTN_BLOCK && ATTN_BLOCK % T == 0 && T % NKG == 0, "tile keys");
 	static_assert(KB % KS == 0, "batches per warp");
 	static_assert(RMW * E <= 32, "accumulator registers");
@@ -194,10 +198,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		// ---- producer: one lane streams each piece's q rows and the CTA's tiles ----
 		if (lane == 0 && n_mine > 0)
 		{
-			griddep_wait(); // K1's q rows and appended K/V rows are complete and visible
 			Cursor cur;
 			cursor_start(P, cur);
 			int pj = -1, ps = -1, piece = 0;
+			bool waited = false;
 			for (int i = 0; i < n_mine; ++i)
 			{
 				const DevJob& J = P.jobs[cur.job];
@@ -220,16 +224,22 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					info[0] = min(cur.n_tiles - cur.tis, n_mine - i); // tiles of this piece in this CTA
 					info[1] = cur.tis;
 					info[2] = cur.seg;
-					mbar_arrive_expect_tx(&qfull[sl], (uint32_t)(sizeof(DevJob) + rows * D * 4));
+					const int half = J.n_rot / 2;
+					const uint32_t inv_bytes = (uint32_t)((half * 4 + 15) & ~15); // the table is padded
+					const uint32_t bytes = (uint32_t)(sizeof(DevJob) + rows * D * 4 + (J.q_gamma ? D * 4 : 0) +
+					                                  inv_bytes + (J.freq_factors ? half * 4 : 0));
+					mbar_arrive_expect_tx(&qfull[sl], bytes);
 					bulk_g2s(slot, P.jobs + cur.job, (uint32_t)sizeof(DevJob), &qfull[sl]);
+					if (J.q_gamma) bulk_g2s(slot + C::QGAIN, J.q_gamma, (uint32_t)(D * 4), &qfull[sl]);
+					if (inv_bytes) bulk_g2s(slot + C::QINV, J.rope_inv, inv_bytes, &qfull[sl]);
+					if (J.freq_factors) bulk_g2s(slot + C::QFF, J.freq_factors, (uint32_t)(half * 4), &qfull[sl]);
 					// rows (t, g) of the segment: per token, its G heads are contiguous
 					for (int r = 0; r < rows;)
 					{
 						const int gr = rg * RM + r, t = gr / G, g = gr % G;
 						const int run = min(G - g, rows - r);
-						bulk_g2s(slot + C::QHEAD_FLOATS + r * D,
-						         J.q_rot + ((size_t)t * J.n_head + (size_t)h * G + g) * D, (uint32_t)(run * D * 4),
-						         &qfull[sl]);
+						bulk_g2s(slot + C::QROWS + r * D, J.q + ((size_t)t * J.n_head + (size_t)h * G + g) * D,
+						         (uint32_t)(run * D * 4), &qfull[sl]);
 						r += run;
 					}
 					pj = cur.job;
@@ -237,6 +247,13 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					++piece;
 				}
 				const int key0 = (J.tile_lo + cur.tis) * T;
+				// the rows K1 appends come from the preceding grid: wait for it
+				// before streaming a tile that holds them (earlier tiles need not)
+				if (!waited && !J.reuse_kv && key0 <= J.pos0 + J.n_tok - 1 && key0 + T - 1 >= J.pos0)
+				{
+					griddep_wait();
+					waited = true;
+				}
 				const size_t off = (size_t)h * J.head_bytes + (size_t)(key0 % J.rows) * D * KV::esize;
 				const int s = i % STAGES;
 				if (i >= STAGES &&
@@ -289,7 +306,24 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		softcap = J.softcap > 0.0f;
 		cap = J.softcap;
 		const float qmul = softcap ? J.scale : J.scale * LOG2E;
-		const float* qs = qslot + sl * C::QSLOT_FLOATS + C::QHEAD_FLOATS;
+		float* slot = qslot + sl * C::QSLOT_FLOATS;
+		float* qs = slot + C::QROWS;
+		// attention_forward's q work (model.cpp:1616-1660), a warp per row:
+		// RMSNorm with the gains, then RoPE at the row's token position
+		for (int r = warp; r < rows; r += NW)
+		{
+			float* buf = qs + r * D;
+			if (J.q_gamma)
+			{
+				const float sc = rms_scale(buf, D, J.eps, true);
+				for (int i2 = lane; i2 < D; i2 += 32) buf[i2] = buf[i2] * sc * slot[C::QGAIN + i2];
+				__syncwarp();
+			}
+			rope_vec(buf, J.n_rot, J.rope_mode, (float)(J.pos0 + (rg * RM + r) / G) * J.rope_scale, slot + C::QINV,
+			         J.freq_factors ? slot + C::QFF : nullptr);
+			__syncwarp();
+		}
+		named_sync(1, NW * 32);
 #pragma unroll
 		for (int r = 0; r < RMW; ++r)
 		{
@@ -322,8 +356,11 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		pe.seg = J.seg0 + seg_local;
 		pe.c_first = (int)(seg_gstart / W);
 		pe.c_last = (int)((seg_gstart + J.n_tiles - 1) / W);
+		// the slot is refilled by bulk copies (the async proxy): order this warp's
+		// writes to it first, then hand it back
+		asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 		__syncwarp();
-		if (lane == 0) mbar_arrive(&qempty[sl]); // this warp is done with the slot
+		if (lane == 0) mbar_arrive(&qempty[sl]);
 	};
 
 	// Merge the warps' states of the finished piece (two rounds: the upper half
@@ -332,58 +369,61 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	// segment in this CTA) or a partial, and fold the partials if this CTA
 	// completes the segment.
 	auto finish_piece = [&]() {
-		// l of row r: sum over the batch's key slots (lanes differing in the key bits)
+		// l of each row: sum over the batch's key slots (lanes differing in the
+		// key bits), then every row's l in every lane
 		float lsum = l_lane;
 #pragma unroll
 		for (int off = 1 << (SHIFT + C::LOG2RMW); off < 32; off <<= 1)
 			lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
-		constexpr int HW = NW / 2;
-		if (warp >= HW)
-		{
+		float lrow[RMW];
+#pragma unroll
+		for (int r = 0; r < RMW; ++r) lrow[r] = __shfl_sync(0xffffffffu, lsum, r << SHIFT);
+		// Pairwise tree over the warps through two warps' worth of area: 6,7 into
+		// 2,3; 4,5 into 0,1; 2,3 into 0,1. Partners have the same row slice.
+		auto put = [&](int slot_i) {
 #pragma unroll
 			for (int r = 0; r < RMW; ++r)
 			{
 #pragma unroll
-				for (int e = 0; e < E; ++e)
-					area[((warp - HW) * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
-				if (lane == (r << SHIFT))
+				for (int e = 0; e < E; ++e) area[(slot_i * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
+				if (lane == 0)
 				{
-					m_s[warp * RMW + r] = m[r];
-					l_s[warp * RMW + r] = lsum;
+					m_s[slot_i * RMW + r] = m[r];
+					l_s[slot_i * RMW + r] = lrow[r];
 				}
 			}
-		}
-		named_sync(1, NW * 32);
-		if (warp < HW)
-		{
-			// warp w + HW has the same row slice (HW is a multiple of RS)
+		};
+		auto take = [&](int slot_i) {
 #pragma unroll
 			for (int r = 0; r < RMW; ++r)
 			{
-				const float mo = m_s[(warp + HW) * RMW + r], lo = l_s[(warp + HW) * RMW + r];
+				const float mo = m_s[slot_i * RMW + r], lo = l_s[slot_i * RMW + r];
 				const float M = fmaxf(m[r], mo);
 				const float ca = m[r] == -CUDART_INF_F ? 0.0f : ex2(m[r] - M);
 				const float cb = mo == -CUDART_INF_F ? 0.0f : ex2(mo - M);
 #pragma unroll
 				for (int e = 0; e < E; ++e)
-				{
-					const float ob = area[(warp * RMW + r) * D + lane_elem<E, VEC>(lane, e)];
-					o[r][e] = fmaf(o[r][e], ca, ob * cb);
-				}
+					o[r][e] = fmaf(o[r][e], ca, area[(slot_i * RMW + r) * D + lane_elem<E, VEC>(lane, e)] * cb);
 				m[r] = M;
-				const float lr = __shfl_sync(0xffffffffu, lsum, r << SHIFT);
-				const float lsum_r = fmaf(lr, ca, lo * cb);
-				__syncwarp();
-#pragma unroll
-				for (int e = 0; e < E; ++e) area[(warp * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
-				if (lane == 0)
-				{
-					m_s[warp * RMW + r] = M;
-					l_s[warp * RMW + r] = lsum_r;
-				}
+				lrow[r] = fmaf(lrow[r], ca, lo * cb);
 			}
-		}
+		};
+		if (warp >= 6) put(warp - 6);
 		named_sync(1, NW * 32);
+		if (warp == 2 || warp == 3) take(warp - 2);
+		named_sync(1, NW * 32);
+		if (warp == 4 || warp == 5) put(warp - 4);
+		named_sync(1, NW * 32);
+		if (warp < 2) take(warp);
+		named_sync(1, NW * 32);
+		if (warp == 2 || warp == 3) put(warp - 2);
+		named_sync(1, NW * 32);
+		if (warp < 2) take(warp);
+		named_sync(1, NW * 32);
+		if (warp < 2) put(warp);
+		named_sync(1, NW * 32);
+		// area slot 0 holds warp 0's merged state, slot 1 warp 1's: the same rows
+		// (one row slice) or the two slices
 
 		const int G = pe.G, h = pe.h, rg = pe.rg, n_tok = pe.n_tok, n_head = pe.n_head;
 		const int c_first = pe.c_first, c_last = pe.c_last, seg = pe.seg;
@@ -396,10 +436,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			const int sl = R / RMW, r = R % RMW; // the row's slice and its row within the slice
 			float M = -CUDART_INF_F;
 #pragma unroll
-			for (int k = 0; k < HW / RS; ++k) M = fmaxf(M, m_s[(k * RS + sl) * RMW + r]);
+			for (int k = 0; k < 2 / RS; ++k) M = fmaxf(M, m_s[(k * RS + sl) * RMW + r]);
 			float acc = 0.0f, L = 0.0f;
 #pragma unroll
-			for (int k = 0; k < HW / RS; ++k)
+			for (int k = 0; k < 2 / RS; ++k)
 			{
 				const int w = k * RS + sl;
 				const float mw = m_s[w * RMW + r];
@@ -443,7 +483,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 				// per row takes every piece's (m, l) at once and leaves the
 				// weights exp2(m_c - M) / L in the area; then each thread sums
 				// its 4 output columns over the pieces with 16-byte loads.
-				const int np = c_last - c_first + 1;
+				const int np = c_last - c_first + 1; // the planner keeps np * RM within the area
 				const float* base = P.parts + (size_t)(seg + c_first) * RM * PW;
 				float* wgt = area; // [np][RM]
 				for (int R = warp; R < RM; R += NW)
@@ -824,14 +864,22 @@ int decode_tile_keys(int D, int kv_type) { return TILE_BYTES / (D * kv_esize(kv_
 
 int decode_rows_max(int D) { return 64 / (D / 32) < 32 ? 64 / (D / 32) : 32; }
 
+namespace
+{
+constexpr int slices(int D, int RM) { return RM * (D / 32) > 32 ? RM * (D / 32) / 32 : 1; }
+} // namespace
+
 int decode_smem_bytes(int D, int kv_type, int RM)
 {
 	(void)kv_type;
-	const int E = D / 32, RS = RM * E > 32 ? RM * E / 32 : 1, RMW = RM / RS;
-	const int fixed = ((NW / 2) * RMW * D + 2 * NW * RMW + 2 * RM * D) * 4 + 256;
+	const int RMW = RM / slices(D, RM);
+	const int qslot = (int)(sizeof(DevJob) / 4) + 4 + RM * D + 2 * D;
+	const int fixed = (2 * RMW * D + 2 * NW * RMW + 2 * qslot) * 4 + 256;
 	const int stages = std::min(MAX_STAGES, (SMEM_LIMIT - fixed) / (2 * TILE_BYTES));
 	return stages * 2 * TILE_BYTES + fixed;
 }
+
+int decode_fold_pieces(int D, int RM) { return 2 * (RM / slices(D, RM)) * D / RM; }
 
 int launch_decode(const DecodePlan& P, void* stream)
 {

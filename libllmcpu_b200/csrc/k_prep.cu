@@ -1,10 +1,11 @@
-// k_prep.cu -- K1: the per-head work attention_forward does between the
-// projections and the attention proper (src/libnnc/model.cpp:1616-1694):
-// Q/K RMSNorm with gamma (nnc_rmsnorm_gamma_multi_f32, nn_ops.cpp:590-632),
-// Gemma 4's plain V RMSNorm (nn_ops.cpp:558-588), RoPE on q and on fresh k
-// (nnc_rope_f32, nn_ops.cpp:1830-1873), and the append of k, v at row
-// pos % rows in the cache's element type. One launch covers every token of
-// every job; a warp takes one (token, head) vector at a time.
+// k_prep.cu -- K1: the K/V half of the per-head work attention_forward does
+// between the projections and the attention proper (src/libnnc/model.cpp:
+// 1616-1694): K RMSNorm with gamma (nnc_rmsnorm_gamma_multi_f32, nn_ops.cpp:
+// 590-632), Gemma 4's plain V RMSNorm (nn_ops.cpp:558-588), RoPE on the fresh
+// k (nnc_rope_f32, nn_ops.cpp:1830-1873), and the append of k, v at row
+// pos % rows in the cache's element type. The q half runs inside the decode
+// kernel. One launch covers every token of every job; a warp takes one
+// (token, head) vector at a time.
 //
 // Also the unit-seam kernels for nnc_rmsnorm*, nnc_rope_f32 and
 // nnc_softcap_f32 on device pointers.
@@ -24,11 +25,12 @@ template <typename KV>
 __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __restrict__ jobs, int n_jobs)
 {
 	using T = typename KV::T;
-	// The attention kernel that follows may start now: it streams K/V tiles
-	// that do not depend on this kernel and waits for it only where it does.
+	// The attention kernel that follows may start now: it streams the K/V
+	// tiles that do not hold this kernel's rows and waits for it only before
+	// the ones that do.
 	griddep_launch_dependents();
 	__shared__ float bufs[PREP_WARPS][PREP_MAX_D];
-	__shared__ float s_qg[PREP_MAX_D], s_kg[PREP_MAX_D], s_inv[PREP_MAX_D / 2], s_ff[PREP_MAX_D / 2];
+	__shared__ float s_kg[PREP_MAX_D], s_inv[PREP_MAX_D / 2], s_ff[PREP_MAX_D / 2];
 	// block (t, job): token t of job blockIdx.y
 	const DevJob& j = jobs[blockIdx.y];
 	const int t = blockIdx.x;
@@ -37,27 +39,26 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __r
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int D = j.D, half = j.n_rot / 2;
 	float* buf = bufs[warp];
-	const int n_q = j.n_head, n_kv = j.reuse_kv ? 0 : j.n_kv;
-	const int n_tasks = n_q + 2 * n_kv;
+	const int n_q = 0, n_kv = j.reuse_kv ? 0 : j.n_kv; // k heads, then v heads
+	const int n_tasks = 2 * n_kv;
+	if (n_tasks == 0) return;
 	const float rpos = (float)(j.pos0 + t) * j.rope_scale;
 	const int row = (j.pos0 + t) % j.rows;
 	auto task_src = [&](int task) {
 		const int kind = task < n_q ? 0 : (task < n_q + n_kv ? 1 : 2); // q, k, v
 		const int h = kind == 0 ? task : (kind == 1 ? task - n_q : task - n_q - n_kv);
-		return kind == 0 ? j.q + ((size_t)t * n_q + h) * D : (kind == 1 ? j.k : j.v) + ((size_t)t * j.n_kv + h) * D;
+		return (kind == 1 ? j.k : j.v) + ((size_t)t * j.n_kv + h) * D;
 	};
 	// one round of loads: this warp's first head vector, and the gains and
 	// RoPE tables staged once for every head of the token
 	HeadRegs x;
 	if (warp < n_tasks) load_head(x, task_src(warp), D);
-	const float* qg = j.q_gamma;
 	const float* kg = j.k_gamma;
 	const float* ff = j.freq_factors;
 	for (int i = threadIdx.x; i < D; i += blockDim.x)
 	{
-		const float a = qg ? qg[i] : 0.0f, b = kg ? kg[i] : 0.0f;
+		const float b = kg ? kg[i] : 0.0f;
 		const float c = i < half ? j.rope_inv[i] : 0.0f, d = (ff && i < half) ? ff[i] : 0.0f;
-		s_qg[i] = a;
 		s_kg[i] = b;
 		if (i < half)
 		{
@@ -71,20 +72,12 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __r
 		if (task != warp) load_head(x, task_src(task), D);
 		const int kind = task < n_q ? 0 : (task < n_q + n_kv ? 1 : 2); // q, k, v
 		const int h = kind == 0 ? task : (kind == 1 ? task - n_q : task - n_q - n_kv);
-		const float* gamma = kind == 0 ? (qg ? s_qg : nullptr) : (kind == 1 ? (kg ? s_kg : nullptr) : nullptr);
+		const float* gamma = kind == 1 && kg ? s_kg : nullptr;
 		prep_head(buf, x, D, gamma, kind == 2 && j.v_rmsnorm, j.eps, kind != 2, j.n_rot, j.rope_mode, rpos, s_inv,
 		          ff ? s_ff : nullptr);
-		if (kind == 0)
-		{
-			float* dst = j.q_rot + ((size_t)t * n_q + h) * D;
-			for (int i = lane; i < D; i += 32) dst[i] = buf[i];
-		}
-		else
-		{
-			char* base = (kind == 1 ? j.K : j.V) + (size_t)h * j.head_bytes;
-			T* dst = reinterpret_cast<T*>(base) + (size_t)row * D;
-			for (int i = lane; i < D; i += 32) store_elem(dst + i, buf[i]);
-		}
+		char* base = (kind == 1 ? j.K : j.V) + (size_t)h * j.head_bytes;
+		T* dst = reinterpret_cast<T*>(base) + (size_t)row * D;
+		for (int i = lane; i < D; i += 32) store_elem(dst + i, buf[i]);
 		__syncwarp();
 	}
 }

@@ -10,8 +10,8 @@
 // nncu_attention_noalloc serves them: the caller passes every input, the
 // output and its own K/V cache (allocated up front, by whatever means it
 // uses), and the kernels' scratch -- the job descriptor and per-CTA starts,
-// the RoPE table, the normed and rotated q rows, the per-piece partials and
-// their counters -- lives in one file-scope device array of fixed size.
+// the RoPE table, the per-piece partials and their counters -- lives in one
+// file-scope device array of fixed size.
 //
 // What sharing one array means:
 //  * every GPU that loads the library holds the array (NOALLOC_SCRATCH_BYTES)
@@ -112,6 +112,11 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	if (p->rope_mode != NNCU_ROPE_NEOX && p->rope_mode != NNCU_ROPE_NORM)
 		return set_error(NNCU_ERR_INVALID_ARGUMENT, "unknown rope mode");
 	if (p->window < 0 || p->softcap < 0.0f) return set_error(NNCU_ERR_INVALID_ARGUMENT, "negative window or softcap");
+	if (p->freq_factors && p->n_rot % 8)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "freq_factors need n_rot to be a multiple of 8");
+	const auto misaligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; };
+	if (misaligned(q) || misaligned(p->q_gamma) || misaligned(p->freq_factors))
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "q, q_gamma and freq_factors must be 16-byte aligned");
 	// every key a query sees must still be in the caller's `rows` rows
 	const bool windowed = p->causal && p->window > 0;
 	if (windowed ? p->window + p->n_tok > rows : (p->pos0 + p->n_tok > rows || p->n_seq > rows))
@@ -146,15 +151,16 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	const int n_seg = p->n_kv * n_rowgroups;
 	const long long total = (long long)n_seg * n_tiles;
 	const int ctas0 = (int)std::min<long long>(std::min<long long>(total, n_sms), MAX_CTAS);
-	const long long W = ctas0 > 0 ? (total + ctas0 - 1) / ctas0 : 1;
+	const int fold = decode_fold_pieces(D, RM); // pieces one segment may be cut into
+	const long long W =
+		std::max<long long>(ctas0 > 0 ? (total + ctas0 - 1) / ctas0 : 1, (n_tiles + fold - 2) / (fold - 1));
 	const int n_ctas = ctas0 > 0 ? (int)((total + W - 1) / W) : 0;
 
-	// ---- the scratch: [job | starts | rope | q rows | partials | counters | error] ----
+	// ---- the scratch: [job | starts | rope | partials | counters | error] ----
 	const size_t off_job = 0;
 	const size_t off_starts = up256(sizeof(DevJob));
 	const size_t off_rope = off_starts + up256((size_t)MAX_CTAS * sizeof(int4));
-	const size_t off_qrot = off_rope + up256(256 * sizeof(float));
-	const size_t off_parts = off_qrot + up256((size_t)p->n_tok * p->n_head * D * sizeof(float));
+	const size_t off_parts = off_rope + up256(256 * sizeof(float));
 	const size_t off_count = off_parts + up256((size_t)(n_seg + n_ctas) * RM * (D + 4) * sizeof(float));
 	const size_t off_err = off_count + up256((size_t)n_seg * sizeof(int));
 	const size_t need = off_err + 256;
@@ -174,7 +180,6 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	j.q = q;
 	j.k = k;
 	j.v = v;
-	j.q_rot = reinterpret_cast<float*>(scratch + off_qrot);
 	j.out = out;
 	j.q_gamma = p->q_gamma;
 	j.k_gamma = p->k_gamma;
@@ -229,7 +234,11 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 		ce = cudaMemcpyAsync(scratch + off_starts, hh.starts, (size_t)n_ctas * sizeof(int4), cudaMemcpyHostToDevice,
 		                     st);
 	if (ce == cudaSuccess && half > 0)
-		ce = cudaMemcpyAsync(scratch + off_rope, hh.rope, (size_t)half * sizeof(float), cudaMemcpyHostToDevice, st);
+	{
+		for (int i = half; i < ((half + 3) & ~3); ++i) hh.rope[i] = 0.0f; // whole 16-byte pieces
+		ce = cudaMemcpyAsync(scratch + off_rope, hh.rope, (size_t)((half + 3) & ~3) * sizeof(float),
+		                     cudaMemcpyHostToDevice, st);
+	}
 	if (ce == cudaSuccess) ce = cudaMemsetAsync(scratch + off_count, 0, off_err + 256 - off_count, st);
 	if (ce == cudaSuccess && n_tiles == 0)
 		ce = cudaMemsetAsync(out, 0, (size_t)p->n_tok * p->n_head * D * sizeof(float), st);
