@@ -239,12 +239,15 @@ int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_j
  * q, k, v, out and the pointer fields of `p` are device pointers; k_cache and
  * v_cache are the caller's cache for this layer and sequence, laid out
  * [n_kv][rows][head_dim] of kv_type, position p at row p % rows, rows a
- * multiple of 256. Asynchronous on `stream`. The kernels' scratch is one
+ * multiple of 256. Asynchronous on `stream`. It serves decode and verify:
+ * n_tok is at most NNCU_NOALLOC_MAX_TOKENS, and a larger call fails with
+ * NNCU_ERR_INVALID_ARGUMENT before anything runs. The kernels' scratch is one
  * 4 MiB device array inside the library, shared by every call: calls that
  * overlap on the GPU race on it (order them on one stream); a call that would
  * need more fails with NNCU_ERR_INVALID_ARGUMENT and a message. The first call
  * on each device looks the array's device address up (cudaGetSymbolAddress)
  * with that device current; make that first call during set-up. */
+#define NNCU_NOALLOC_MAX_TOKENS 64
 int nncu_attention_noalloc(const nncu_attn_params* p, const float* q, const float* k, const float* v, float* out,
                            void* k_cache, void* v_cache, int32_t kv_type, int32_t rows, void* stream);
 

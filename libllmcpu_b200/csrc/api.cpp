@@ -227,13 +227,30 @@ struct nncu_kv
 
 	cudaStream_t stream = nullptr; // the host-pointer calls' stream
 	int* err_dev = nullptr;        // device error word (bounded waits)
-	DevBuf jobs_dev, stage_dev, parts, counters;
-	HostBuf stage_host, jobs_host;
-	cudaEvent_t jobs_uploaded = nullptr; // the last upload from jobs_host has been read
+	DevBuf stage_dev, parts, counters;
+	HostBuf stage_host;
+	// The job tables go up on their own stream through a ring of slots, so
+	// the upload of one call's table overlaps the previous call's kernels
+	// instead of sitting between them in the launching stream.
+	struct JobSlot
+	{
+		DevBuf dev;
+		HostBuf host;
+		cudaEvent_t up = nullptr;   // the upload from `host` into `dev` is done
+		cudaEvent_t used = nullptr; // the kernels that read `dev` are done
+		bool ever = false;
+	};
+	static constexpr int JOB_SLOTS = 4;
+	JobSlot slots[JOB_SLOTS];
+	int slot_next = 0;
+	cudaStream_t up = nullptr; // the upload stream
 	cudaEvent_t done = nullptr;          // the last submission's kernels have finished: calls on one
 	                                     // cache are ordered on the device whatever their streams
+	cudaStream_t last_stream = nullptr;  // the stream `done` was recorded on
+	bool any_call = false;
 	std::map<std::pair<uint32_t, int>, float*> rope_tables;
 	std::vector<DevJob> jobs_tmp;
+	std::vector<CtaStart> starts_tmp;
 	int counters_n = 0;
 
 	~nncu_kv()
@@ -247,15 +264,20 @@ struct nncu_kv
 		}
 		for (auto& kv : rope_tables) cudaFree(kv.second);
 		if (err_dev) cudaFree(err_dev);
-		jobs_dev.release();
+		for (auto& sl : slots)
+		{
+			sl.dev.release();
+			sl.host.release();
+			if (sl.up) cudaEventDestroy(sl.up);
+			if (sl.used) cudaEventDestroy(sl.used);
+		}
 		stage_dev.release();
 		parts.release();
 		counters.release();
 		stage_host.release();
-		jobs_host.release();
-		if (jobs_uploaded) cudaEventDestroy(jobs_uploaded);
 		if (done) cudaEventDestroy(done);
 		if (stream) cudaStreamDestroy(stream);
+		if (up) cudaStreamDestroy(up);
 	}
 };
 
@@ -534,9 +556,14 @@ extern "C" int nncu_kv_create(const nncu_layer_desc* layers, int32_t n_layer, co
 		kv->bytes += 2 * n;
 	}
 	cudaError_t e = cudaStreamCreateWithFlags(&kv->stream, cudaStreamNonBlocking);
+	if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&kv->up, cudaStreamNonBlocking);
+	for (auto& sl : kv->slots)
+	{
+		if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.up, cudaEventDisableTiming);
+		if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.used, cudaEventDisableTiming);
+	}
 	if (e == cudaSuccess) e = cudaMalloc(&kv->err_dev, sizeof(int));
 	if (e == cudaSuccess) e = cudaMemset(kv->err_dev, 0, sizeof(int));
-	if (e == cudaSuccess) e = cudaEventCreateWithFlags(&kv->jobs_uploaded, cudaEventDisableTiming);
 	if (e == cudaSuccess) e = cudaEventCreateWithFlags(&kv->done, cudaEventDisableTiming);
 	if (e != cudaSuccess) return fail_free(cuda_fail(e, "cache set-up"));
 	*out = kv;
@@ -739,66 +766,6 @@ int check_conflicts(const nncu_kv* kv, const nncu_attn_job* jobs, int n)
 	return NNCU_OK;
 }
 
-// Fill the decode plan fields of each DevJob and size the launch.
-void plan_decode(nncu_kv* kv, std::vector<DevJob>& jobs, DecodePlan& P)
-{
-	const int D = jobs[0].D;
-	const int T = decode_tile_keys(D, kv->kv_type);
-	int rows_needed = 1;
-	for (auto& j : jobs) rows_needed = std::max(rows_needed, (j.n_head / j.n_kv) * j.n_tok);
-	int RM = 1;
-	while (RM < rows_needed && RM < decode_rows_max(D)) RM *= 2;
-	long long total = 0;
-	int seg = 0;
-	for (auto& j : jobs)
-	{
-		int first_min = INT_MAX, last_max = -1;
-		for (int t = 0; t < j.n_tok; ++t)
-		{
-			int f, l;
-			nncu_attn_span(j.causal, j.window, j.pos0 + t, j.n_seq, &f, &l);
-			if (l < f) continue;
-			first_min = std::min(first_min, f);
-			last_max = std::max(last_max, l);
-		}
-		const int G = j.n_head / j.n_kv;
-		j.n_rowgroups = (G * j.n_tok + RM - 1) / RM;
-		if (last_max < 0)
-		{
-			j.tile_lo = 0;
-			j.n_tiles = 0;
-		}
-		else
-		{
-			j.tile_lo = first_min / T;
-			j.n_tiles = last_max / T - j.tile_lo + 1;
-		}
-		j.seg0 = seg;
-		j.gtile0 = total;
-		seg += j.n_kv * j.n_rowgroups;
-		total += (long long)j.n_kv * j.n_rowgroups * j.n_tiles;
-	}
-	P.n_jobs = (int)jobs.size();
-	P.D = D;
-	P.kv_type = kv->kv_type;
-	P.RM = RM;
-	P.T = T;
-	P.total_tiles = total;
-	P.n_segments = seg;
-	// one CTA per SM (the kernel's shared memory allows no more); at most 256, so
-	// the in-kernel fold's per-piece weights fit its merge area
-	const long long ctas = std::min<long long>(std::min<long long>(total, (long long)kv->num_sms), 256);
-	long long W = ctas > 0 ? (total + ctas - 1) / ctas : 1;
-	// the in-kernel fold keeps one weight per (piece, row) in the merge area:
-	// no segment may be cut into more pieces than that holds
-	int max_tiles = 1;
-	for (const auto& j : jobs) max_tiles = std::max(max_tiles, j.n_tiles);
-	W = std::max(W, (long long)((max_tiles + decode_fold_pieces(D, RM) - 2) / (decode_fold_pieces(D, RM) - 1)));
-	P.tiles_per_cta = W;
-	P.n_ctas = ctas > 0 ? (int)((total + W - 1) / W) : 0;
-	P.err = kv->err_dev;
-}
-
 // Turn one public job into a DevJob (device pointers already resolved).
 void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 {
@@ -835,32 +802,32 @@ void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 	d.softcap = p.softcap;
 }
 
-// Launch K1 and K2 for jobs whose DevJob pointers are all device pointers:
-// plans, uploads the job table and launches on `st`.
-int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn_job>& pub, cudaStream_t st)
+// Launch K1 and K2 for jobs whose DevJob pointers are all device pointers,
+// on `st`.
+int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, cudaStream_t st)
 {
 	const int n = (int)jobs.size();
-	// the job table and the partials are the cache's: wait for the previous submission
-	CU(cudaStreamWaitEvent(st, kv->done, 0), "order after the previous call");
-	int tok = 0, max_tok = 0;
 	for (int i = 0; i < n; ++i)
 	{
-		const nncu_attn_params& p = pub[i].p;
-		int rc = rope_table(kv, p.freq_base, p.n_rot, &jobs[i].rope_inv);
+		int rc = rope_table(kv, pub[i].p.freq_base, pub[i].p.n_rot, &jobs[i].rope_inv);
 		if (rc != NNCU_OK) return rc;
-		jobs[i].tok0 = tok;
-		tok += p.n_tok;
-		max_tok = std::max(max_tok, p.n_tok);
 	}
 	// Every job of one launch shares head_dim (the kernels are specialised on it).
 	for (int i = 1; i < n; ++i)
 		if (jobs[i].D != jobs[0].D)
 			return fail(NNCU_ERR_INVALID_ARGUMENT, "jobs of one call must share head_dim (%d vs %d)", jobs[i].D,
 			            jobs[0].D);
+	// the partials and counters are the cache's: a call on another stream than
+	// the previous one waits for it on the device
+	if (kv->any_call && kv->last_stream != st)
+		CU(cudaStreamWaitEvent(st, kv->done, 0), "order after the previous call");
 	DecodePlan P{};
-	plan_decode(kv, jobs, P);
+	kv->starts_tmp.resize((size_t)kv->num_sms);
+	int rc = plan_launch(jobs.data(), n, kv->kv_type, kv->num_sms, P, kv->starts_tmp.data(), kv->num_sms);
+	if (rc != NNCU_OK) return rc;
+	P.err = kv->err_dev;
 	// scratch for partials and the per-segment counters
-	const size_t part_floats = (size_t)(P.n_segments + P.n_ctas) * P.RM * (P.D + 4);
+	const size_t part_floats = (size_t)std::max<long long>(P.n_parts, 1) * P.RM * (P.D + 4);
 	CU(kv->parts.reserve(part_floats * sizeof(float)), "partials scratch");
 	if (P.n_segments > kv->counters_n)
 	{
@@ -870,47 +837,43 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn
 	}
 	P.parts = static_cast<float*>(kv->parts.p);
 	P.counters = static_cast<int*>(kv->counters.p);
-	P.fused = 0;
-	// Each CTA's first tile, walked out here once instead of searched for by every CTA.
-	std::vector<int4> starts((size_t)std::max(P.n_ctas, 1));
-	{
-		int j = 0;
-		for (int c = 0; c < P.n_ctas; ++c)
-		{
-			const long long g = (long long)c * P.tiles_per_cta;
-			while (j + 1 < n && jobs[j + 1].gtile0 <= g) ++j;
-			while (jobs[j].n_tiles == 0 && j + 1 < n) ++j; // defensive: a job without tiles owns none
-			const long long local = g - jobs[j].gtile0;
-			starts[c] = make_int4(j, (int)(local / jobs[j].n_tiles), (int)(local % jobs[j].n_tiles), 0);
-		}
-	}
-	// the job table and the starts: pinned -> device on the stream; the pinned
-	// copy is reused only after the previous upload has been read
 	const size_t jb = align_up((size_t)n * sizeof(DevJob), 16);
-	const size_t sb = (size_t)P.n_ctas * sizeof(int4);
-	CU(cudaEventSynchronize(kv->jobs_uploaded), "job table reuse");
-	CU(kv->jobs_host.reserve(jb + sb), "job table (host)");
-	CU(kv->jobs_dev.reserve(jb + sb), "job table (device)");
-	std::memcpy(kv->jobs_host.p, jobs.data(), (size_t)n * sizeof(DevJob));
-	std::memcpy(static_cast<char*>(kv->jobs_host.p) + jb, starts.data(), sb);
-	CU(cudaMemcpyAsync(kv->jobs_dev.p, kv->jobs_host.p, jb + sb, cudaMemcpyHostToDevice, st), "job table upload");
-	CU(cudaEventRecord(kv->jobs_uploaded, st), "job table event");
-	P.jobs = static_cast<const DevJob*>(kv->jobs_dev.p);
-	P.cta_start = reinterpret_cast<const int4*>(static_cast<const char*>(kv->jobs_dev.p) + jb);
-	// jobs whose queries see no key at all produce zeros, as nnc_attn_finish does for l = 0
-	for (int i = 0; i < n; ++i)
-		if (jobs[i].n_tiles == 0)
-			CU(cudaMemsetAsync(jobs[i].out, 0, (size_t)jobs[i].n_tok * jobs[i].n_head * jobs[i].D * sizeof(float), st),
-			   "empty output");
-	// algorithmic bytes: K1 reads q, k, v and writes rotated q and the appended rows;
-	// K2 reads the K/V rows of every key attended (once per KV head) and q, and writes the output
+	const size_t sb = (size_t)P.n_ctas * sizeof(CtaStart);
+	auto& slot = kv->slots[kv->slot_next];
+	kv->slot_next = (kv->slot_next + 1) % nncu_kv::JOB_SLOTS;
+	CU(cudaEventSynchronize(slot.up), "job table reuse"); // its pinned copy was read
+	CU(slot.host.reserve(jb + sb), "job table (host)");
+	if (slot.dev.cap < jb + sb)
+	{
+		CU(cudaStreamSynchronize(kv->up), "job table growth");
+		CU(slot.dev.reserve(jb + sb), "job table (device)");
+	}
+	std::memcpy(slot.host.p, jobs.data(), (size_t)n * sizeof(DevJob));
+	std::memcpy(static_cast<char*>(slot.host.p) + jb, kv->starts_tmp.data(), sb);
+	// upload on the side stream once the kernels that last read this slot are
+	// done; the launching stream waits only for the upload itself
+	if (slot.ever) CU(cudaStreamWaitEvent(kv->up, slot.used, 0), "job table slot reuse");
+	CU(cudaMemcpyAsync(slot.dev.p, slot.host.p, jb + sb, cudaMemcpyHostToDevice, kv->up), "job table upload");
+	CU(cudaEventRecord(slot.up, kv->up), "job table event");
+	CU(cudaStreamWaitEvent(st, slot.up, 0), "job table ready");
+	P.jobs = static_cast<const DevJob*>(slot.dev.p);
+	P.cta_start = reinterpret_cast<const CtaStart*>(static_cast<const char*>(slot.dev.p) + jb);
+	// algorithmic bytes: K1 reads k, v and writes the appended rows; K2 reads
+	// the K/V rows of every key attended (once per KV head), q, and writes the output.
+	// Jobs whose queries see no key at all produce zeros, as nnc_attn_finish does for l = 0.
 	uint64_t rope_bytes = 0, core_bytes = 0;
 	const size_t es = kv_esize(kv->kv_type);
-	for (const auto& j : jobs)
+	for (int i = 0; i < n; ++i)
 	{
+		const DevJob& j = jobs[i];
 		const uint64_t qb = (uint64_t)j.n_tok * j.n_head * j.D * 4;
 		const uint64_t kvb = j.reuse_kv ? 0 : (uint64_t)j.n_tok * j.n_kv * j.D;
-		rope_bytes += 2 * qb + kvb * 4 * 2 + kvb * es * 2;
+		rope_bytes += kvb * 4 * 2 + kvb * es * 2;
+		if (j.n_tiles == 0)
+		{
+			CU(cudaMemsetAsync(j.out, 0, qb, st), "empty output");
+			continue;
+		}
 		int first_min = INT_MAX, last_max = -1;
 		for (int t = 0; t < j.n_tok; ++t)
 		{
@@ -920,15 +883,16 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn
 			first_min = std::min(first_min, f);
 			last_max = std::max(last_max, l);
 		}
-		const uint64_t keys = last_max >= first_min ? (uint64_t)(last_max - first_min + 1) : 0;
-		core_bytes += keys * j.n_kv * j.D * es * 2 + 2 * qb;
+		core_bytes += (uint64_t)(last_max - first_min + 1) * j.n_kv * j.D * es * 2 + 2 * qb;
 	}
-	// K1 then K2. K2 is a programmatic dependent of K1: its CTAs become
-	// resident while K1 runs and start streaming the moment K1 completes.
+	// K1 then K2, or K2 alone when it appends the new rows itself. After K1,
+	// K2 is a programmatic dependent of it: its CTAs become resident while K1
+	// runs and start streaming at once.
 	int e = 0;
+	if (!P.fused)
 	{
 		PerfScope ps(NNCU_PERF_ATTN_ROPE, rope_bytes, st);
-		e = launch_prep(P.jobs, n, max_tok, 0, P.D, kv->kv_type, st);
+		e = launch_prep(P, st);
 	}
 	if (e) return cuda_fail((cudaError_t)e, "K1 (norm, RoPE, append) launch");
 	{
@@ -936,7 +900,11 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const std::vector<nncu_attn
 		e = launch_decode(P, st);
 	}
 	if (e) return cuda_fail((cudaError_t)e, "K2 (attention) launch");
+	CU(cudaEventRecord(slot.used, st), "job table slot event");
+	slot.ever = true;
 	CU(cudaEventRecord(kv->done, st), "completion event");
+	kv->last_stream = st;
+	kv->any_call = true;
 	return NNCU_OK;
 }
 
@@ -973,10 +941,9 @@ extern "C" int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, 
 	int rc = check_conflicts(kv, jobs, n_jobs);
 	if (rc != NNCU_OK) return rc;
 	DeviceGuard g(kv->device);
-	std::vector<nncu_attn_job> pub(jobs, jobs + n_jobs);
 	kv->jobs_tmp.resize(n_jobs);
-	for (int i = 0; i < n_jobs; ++i) fill_devjob(kv, pub[i], kv->jobs_tmp[i]);
-	return run_jobs(kv, kv->jobs_tmp, pub, static_cast<cudaStream_t>(stream));
+	for (int i = 0; i < n_jobs; ++i) fill_devjob(kv, jobs[i], kv->jobs_tmp[i]);
+	return run_jobs(kv, kv->jobs_tmp, jobs, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs)
@@ -1037,7 +1004,7 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 	CU(cudaMemcpyAsync(ds, hs, in_bytes, cudaMemcpyHostToDevice, kv->stream), "input upload");
 	kv->jobs_tmp.resize(n_jobs);
 	for (int i = 0; i < n_jobs; ++i) fill_devjob(kv, dj[i], kv->jobs_tmp[i]);
-	int rc = run_jobs(kv, kv->jobs_tmp, dj, kv->stream);
+	int rc = run_jobs(kv, kv->jobs_tmp, dj.data(), kv->stream);
 	if (rc != NNCU_OK) return rc;
 	CU(cudaMemcpyAsync(hs + in_bytes, ds + in_bytes, out_bytes, cudaMemcpyDeviceToHost, kv->stream), "output download");
 	CU(cudaStreamSynchronize(kv->stream), "attention");

@@ -409,22 +409,15 @@ __device__ __forceinline__ void load_head(HeadRegs& r, const float* __restrict__
 	}
 }
 
-// One head vector through attention_forward's per-head steps (model.cpp:
-// 1616-1660): from registers into shared `buf`, RMSNorm with `gamma` (or the
-// plain norm when plain_norm), then RoPE when rotate. Warp-cooperative; buf
-// holds the result, visible to the whole warp, on return.
-__device__ __forceinline__ void prep_head(float* buf, const HeadRegs& r, int D, const float* gamma, bool plain_norm,
-                                          float eps, bool rotate, int n_rot, int mode, float rpos, const float* inv,
-                                          const float* ff)
+// One head vector in shared `buf` through attention_forward's per-head steps
+// (model.cpp:1616-1660), in place: RMSNorm with `gamma` (or the plain norm
+// when plain_norm), then RoPE when rotate. Warp-cooperative; buf holds the
+// result, visible to the whole warp, on return.
+__device__ __forceinline__ void prep_buf(float* buf, int D, const float* gamma, bool plain_norm, float eps,
+                                         bool rotate, int n_rot, int mode, float rpos, const float* inv,
+                                         const float* ff)
 {
 	const int lane = threadIdx.x & 31;
-#pragma unroll
-	for (int k = 0; k < 16; ++k)
-	{
-		const int i = lane + 32 * k;
-		if (i < D) buf[i] = r.x[k];
-	}
-	__syncwarp();
 	if (gamma)
 	{
 		const float sc = rms_scale(buf, D, eps, true);
@@ -437,6 +430,48 @@ __device__ __forceinline__ void prep_head(float* buf, const HeadRegs& r, int D, 
 	}
 	__syncwarp();
 	if (rotate && n_rot > 0) rope_vec(buf, n_rot, mode, rpos, inv, ff);
+	__syncwarp();
+}
+
+// The same from registers: the vector goes into `buf` first.
+__device__ __forceinline__ void prep_head(float* buf, const HeadRegs& r, int D, const float* gamma, bool plain_norm,
+                                          float eps, bool rotate, int n_rot, int mode, float rpos, const float* inv,
+                                          const float* ff)
+{
+	const int lane = threadIdx.x & 31;
+#pragma unroll
+	for (int k = 0; k < 16; ++k)
+	{
+		const int i = lane + 32 * k;
+		if (i < D) buf[i] = r.x[k];
+	}
+	__syncwarp();
+	prep_buf(buf, D, gamma, plain_norm, eps, rotate, n_rot, mode, rpos, inv, ff);
+}
+
+// Narrow a D-vector of floats in shared `buf` to the cache's element type in
+// place (element i at ((T*)buf)[i]); warp-cooperative, D <= 512.
+template <typename KV>
+__device__ __forceinline__ void narrow_buf(float* buf, int D)
+{
+	using T = typename KV::T;
+	if constexpr (KV::esize == 4) return;
+	const int lane = threadIdx.x & 31;
+	float x[16];
+#pragma unroll
+	for (int k = 0; k < 16; ++k)
+	{
+		const int i = lane + 32 * k;
+		x[k] = i < D ? buf[i] : 0.0f;
+	}
+	__syncwarp();
+	T* out = reinterpret_cast<T*>(buf);
+#pragma unroll
+	for (int k = 0; k < 16; ++k)
+	{
+		const int i = lane + 32 * k;
+		if (i < D) store_elem(out + i, x[k]);
+	}
 	__syncwarp();
 }
 

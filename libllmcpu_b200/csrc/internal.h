@@ -53,46 +53,65 @@ struct alignas(16) DevJob
 	int n_head, n_kv, D, n_rot, rope_mode;
 	int causal, window, reuse_kv, v_rmsnorm;
 	float rope_scale, eps, scale, softcap;
-	// the decode plan (filled by plan_decode on the host)
+	// the decode plan (filled by plan_launch on the host)
 	int tile_lo;          // first tile (absolute, units of T keys) of the union of the tokens' spans
 	int n_tiles;          // tiles per segment
 	int n_rowgroups;      // segments per KV head (query rows split into groups of RM)
-	int seg0;             // this job's first segment
-	long long gtile0;     // this job's first tile in the launch's global tile order
-	int tok0;             // this job's first token in the launch's global token order
-	int pad_[3];
+	int seg0;             // this job's first segment (its counters)
+	int chunk;            // tiles per chunk: a segment is cut into n_chunks chunks of this many
+	int n_chunks;         // (the last may be short); each chunk is one piece with its own partial
+	int part0;            // this job's first partial slot: segment s, chunk c at part0 + s * n_chunks + c
 };
 static_assert(sizeof(DevJob) % 16 == 0, "DevJob is bulk-copied");
 
-// The decode launch: stream-K over the concatenated tiles of every segment.
+// Where one CTA starts: its first tile (job, segment, tile within the
+// segment), how many tiles it streams, and the addresses of the first `pre`
+// tiles' K and V rows (contiguous runs), which it issues before reading the job.
+struct alignas(16) CtaStart
+{
+	int job, seg, tis, n_tiles;
+	const char* k0;
+	const char* v0;
+	int pre;
+	int pad_[3];
+};
+static_assert(sizeof(CtaStart) == 48, "CtaStart layout");
+
+// One launch of K1 and K2: each CTA streams a run of whole chunks (of one or
+// more segments) given by its CtaStart.
 struct DecodePlan
 {
-	const DevJob* jobs; // device array
+	const DevJob* jobs;        // device copy of the job table
+	const CtaStart* cta_start; // per CTA
 	int n_jobs;
 	int D, kv_type, RM, T; // head_dim, element type, query rows per segment, keys per tile
-	long long total_tiles;
 	int n_ctas;
-	long long tiles_per_cta;
 	int n_segments;
-	int fused;      // reserved, 0: K1 runs as its own grid before this one
-	const int4* cta_start; // per CTA: (job, segment, tile) of its first tile
-	float* parts;   // (n_segments + n_ctas) slots of RM * (D + 4) floats
+	int max_tok;            // K1's grid: tokens of the longest job
+	int fused;              // 1: K2 appends the new K/V rows itself and K1 does not run
+	long long n_parts;      // partial slots in use
+	float* parts;   // n_parts slots of RM * (D + 4) floats
 	int* counters;  // n_segments, zero between launches
 	int* err;       // device error word
 };
+
+// Plan one launch over jobs[0, n) (their D, kv geometry, positions and
+// pointers filled): the row group size, every job's tiles, chunks and
+// partial slots, whether K2 appends itself, and the per-CTA starts (at most
+// max_starts, at most num_sms). Host code; allocates nothing.
+int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, CtaStart* starts, int max_starts);
 
 // Record a failure for nncu_last_error() (api.cpp); return `status`.
 int set_error(int status, const char* msg);
 int set_cuda_error(int cuda_status, const char* what);
 
 // Launchers (implemented in the .cu files). Each returns a cudaError_t value.
-int launch_prep(const DevJob* jobs_dev, int n_jobs, int max_tok, int max_heads, int D, int kv_type, void* stream);
+int launch_prep(const DecodePlan& plan, void* stream);
 int launch_decode(const DecodePlan& plan, void* stream);
 bool decode_supported(int D, int kv_type);
 int decode_tile_keys(int D, int kv_type);
 int decode_rows_max(int D);
-int decode_smem_bytes(int D, int kv_type, int RM);
-int decode_fold_pieces(int D, int RM); // the most pieces one segment may be cut into
+int decode_fuse_tokens(int D, int kv_type, int RM); // new tokens K2 can append itself (0: K1 must)
 
 // Unit-seam kernels (nn_ops.h equivalents).
 int launch_attn_block(const float* q, size_t q_stride, const void* K, const void* V, int kv_type, size_t kv_stride,

@@ -12,21 +12,28 @@
 //    are the union of the rows' spans, cut into tiles of T keys aligned to
 //    absolute positions (T divides 256, so a tile never straddles a ring's
 //    end); a row ignores the keys outside its own span.
-//  * Split. The tiles of all segments of the launch are concatenated and cut
-//    into equal runs, one per CTA (stream-K). A segment that falls into
-//    several runs is computed as several pieces, each giving a partial
-//    (o, m, l) exactly like nnc_attn_block's; the CTA that finishes a
-//    segment's last piece merges the pieces in key order (nnc_attn_merge)
-//    and divides by l (nnc_attn_finish). No second launch.
+//  * Split. Each segment is cut into a few equal chunks of whole tiles and
+//    each CTA streams a run of consecutive chunks (plan.cpp), most CTAs a
+//    single one. A chunk is computed as one piece giving a partial (o, m, l)
+//    like nnc_attn_block's; the CTA that finishes a segment's last piece
+//    merges the pieces (nnc_attn_merge) and divides by l (nnc_attn_finish).
+//    A segment of one chunk writes the output directly. No second launch.
 //  * Memory. One producer warp streams each tile's K rows and V rows (one
 //    contiguous 32 KB run each in the head-major cache) into a 3-stage shared
 //    memory ring with cp.async.bulk, completing on mbarriers; 8 consumer
-//    warps compute while the next tiles are in flight. Each piece's q rows
-//    come the same way, into one of two q slots, ahead of the piece's tiles,
-//    so no consumer ever waits on a plain global load behind the tile stream.
-//  * Order. The kernel is a programmatic dependent of K1 (k_prep.cu): its
-//    CTAs become resident while K1 runs, and the producer starts streaming as
-//    soon as K1's q rows and appended K/V rows are complete.
+//    warps compute while the next tiles are in flight. The first tile goes
+//    out before the job is even read (its address is in the CTA's start).
+//    Each piece's job descriptor, raw q rows, gains and RoPE tables come the
+//    same way, into one of two q slots, ahead of the piece's tiles, so no
+//    consumer ever waits on a plain global load behind the tile stream.
+//  * Per-head work. The consumers give the q rows their RMSNorm and RoPE in
+//    the slot. For decode and short verify the kernel also appends the new
+//    tokens' K/V rows itself: the piece holding them normalises, rotates and
+//    narrows the raw k, v rows from its slot, reads them from there in place
+//    of the cache rows, and (first row group only) stores them to the cache.
+//    Longer batches have K1 (k_prep.cu) append first; the kernel is then its
+//    programmatic dependent, starts while K1 runs, and waits for K1 only
+//    before the tiles that hold the new rows, which it streams last.
 //  * Math. fp32 throughout. A warp owns T/8 keys of each tile; its lanes
 //    split head_dim (D/32 elements each). The q.k partial sums of a batch of
 //    keys x rows are summed across lanes with a transposing reduction, the
@@ -70,17 +77,26 @@ struct Cfg
 	// area in a pairwise tree; the fold's weights reuse the same area
 	static constexpr int AREA_FLOATS = 2 * RMW * D;
 	// one piece's slot: its job descriptor, its tile count / first tile /
-	// segment, its raw q rows, the q gains and the RoPE tables
+	// segment / whether it appends, its raw q rows, the q and k gains, the RoPE
+	// tables, and (when this kernel appends the new rows itself) the new
+	// tokens' k rows and v rows of its KV head
 	static constexpr int QHEAD_FLOATS = (int)(sizeof(DevJob) / 4) + 4;
 	static constexpr int QROWS = QHEAD_FLOATS;             // RM * D
 	static constexpr int QGAIN = QROWS + RM * D;           // D
 	static constexpr int QINV = QGAIN + D;                 // D / 2
 	static constexpr int QFF = QINV + D / 2;               // D / 2
-	static constexpr int QSLOT_FLOATS = QFF + D / 2;
-	static constexpr int FIXED_BYTES = (AREA_FLOATS + 2 * NW * RMW + 2 * QSLOT_FLOATS) * 4 + 256;
-	static constexpr int FIT = (SMEM_LIMIT - FIXED_BYTES) / STAGE_BYTES;
+	static constexpr int QKG = QFF + D / 2;                // D (only with NT > 0)
+	static constexpr int QNEW = QKG + D;                   // NT * D k rows, then NT * D v rows
+	static constexpr int FIXED0 = (AREA_FLOATS + 2 * NW * RMW + 2 * QKG) * 4 + 256;
+	static constexpr int FIT = (SMEM_LIMIT - FIXED0) / STAGE_BYTES;
 	static constexpr int STAGES = FIT < MAX_STAGES ? FIT : MAX_STAGES;
+	// new tokens per launch this kernel can append itself, in what the stages leave
+	static constexpr int NT_FIT = (SMEM_LIMIT - FIXED0 - STAGES * STAGE_BYTES - 2 * D * 4) / (2 * 2 * D * 4);
+	static constexpr int NT = NT_FIT < 0 ? 0 : NT_FIT < 16 ? NT_FIT : 16;
+	static constexpr int QSLOT_FLOATS = NT > 0 ? QNEW + 2 * NT * D : QKG;
+	static constexpr int FIXED_BYTES = (AREA_FLOATS + 2 * NW * RMW + 2 * QSLOT_FLOATS) * 4 + 256;
 	static constexpr int SMEM = STAGES * STAGE_BYTES + FIXED_BYTES;
+	static_assert(SMEM <= SMEM_LIMIT, "shared memory");
 	static_assert(STAGES >= 3, "shared memory for at least three stages");
 	static_assert(D % 32 == 0, "D: a multiple of 32");
 	static_assert(RM % RS == 0 && NW == 8 && RS <= 2, "row slices");
@@ -110,18 +126,9 @@ __device__ __forceinline__ void cursor_load(const DecodePlan& P, Cursor& c)
 	}
 }
 
-__device__ __forceinline__ void cursor_start(const DecodePlan& P, Cursor& c)
+// On to the first tile of the next segment.
+__device__ __forceinline__ void cursor_next_segment(const DecodePlan& P, Cursor& c)
 {
-	const int4 st = P.cta_start[blockIdx.x]; // placed by the host: (job, segment, tile)
-	c.job = st.x;
-	c.seg = st.y;
-	c.tis = st.z;
-	cursor_load(P, c);
-}
-
-__device__ __forceinline__ void cursor_next(const DecodePlan& P, Cursor& c)
-{
-	if (++c.tis < c.n_tiles) return;
 	c.tis = 0;
 	if (++c.seg < c.n_segs) return;
 	c.seg = 0;
@@ -129,6 +136,13 @@ __device__ __forceinline__ void cursor_next(const DecodePlan& P, Cursor& c)
 		++c.job;
 	while (c.job < P.n_jobs && P.jobs[c.job].n_tiles == 0);
 	if (c.job < P.n_jobs) cursor_load(P, c);
+}
+
+// Whether tiles [tis, tis + n) of a job's segment hold keys K1 appends in
+// this launch (they must wait for K1; earlier keys need not).
+__device__ __forceinline__ bool holds_new_rows(const DevJob& J, int tis, int n, int T)
+{
+	return !J.reuse_kv && (J.tile_lo + tis) * T <= J.pos0 + J.n_tok - 1 && (J.tile_lo + tis + n) * T - 1 >= J.pos0;
 }
 
 // atom.add with acquire-release semantics at GPU scope: the arriving CTA's
@@ -169,14 +183,13 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	uint64_t* qfull = empty + STAGES;  // [2]
 	uint64_t* qempty = qfull + 2;      // [2]
 	volatile int* s_flags = reinterpret_cast<volatile int*>(qempty + 2); // [0] abort, [1] last-piece vote
+	CtaStart* s_start = reinterpret_cast<CtaStart*>(qempty + 4);          // this CTA's start (16-byte aligned)
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	const long long g_begin = (long long)blockIdx.x * P.tiles_per_cta;
-	const long long g_end = min(g_begin + P.tiles_per_cta, P.total_tiles);
-	const int n_mine = (int)(g_end - g_begin);
 
 	if (threadIdx.x == 0)
 	{
+		*s_start = P.cta_start[blockIdx.x];
 		for (int s = 0; s < STAGES; ++s)
 		{
 			mbar_init(&full[s], 1);
@@ -192,82 +205,126 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		fence_barrier_init();
 	}
 	__syncthreads();
+	const int n_mine = s_start->n_tiles;
 
 	if (warp == NW)
 	{
 		// ---- producer: one lane streams each piece's q rows and the CTA's tiles ----
+		// A piece is one chunk of a segment (or the part of it in this CTA). The
+		// first tiles go out before anything else, from addresses the plan
+		// gives. While K1 appends, the pieces go in two passes: first those
+		// without any key K1 appends, then those with them, so that the wait for
+		// K1 comes as late in the CTA's stream as it can (a piece's own tiles
+		// stay in key order; so do its new keys, last).
 		if (lane == 0 && n_mine > 0)
 		{
-			Cursor cur;
-			cursor_start(P, cur);
-			int pj = -1, ps = -1, piece = 0;
-			bool waited = false;
-			for (int i = 0; i < n_mine; ++i)
+			const CtaStart S = *s_start;
+			for (int t = 0; t < S.pre; ++t)
 			{
-				const DevJob& J = P.jobs[cur.job];
-				const int h = cur.seg / J.n_rowgroups, rg = cur.seg % J.n_rowgroups;
-				if (cur.job != pj || cur.seg != ps)
+				unsigned char* st = stages + t * C::STAGE_BYTES;
+				mbar_arrive_expect_tx(&full[t], 2 * TILE_BYTES);
+				bulk_g2s(st, S.k0 + (size_t)t * TILE_BYTES, TILE_BYTES, &full[t]);
+				bulk_g2s(st + TILE_BYTES, S.v0 + (size_t)t * TILE_BYTES, TILE_BYTES, &full[t]);
+			}
+			Cursor c0;
+			c0.job = S.job;
+			c0.seg = S.seg;
+			c0.tis = S.tis;
+			cursor_load(P, c0);
+			int piece = 0, i = 0;
+			bool waited = false;
+			for (int pass = 0; pass < (P.fused ? 1 : 2) && !s_flags[0]; ++pass)
+			{
+				Cursor cur = c0;
+				for (int left = n_mine; left > 0 && !s_flags[0];)
 				{
-					// a new piece: its descriptor, tile count and q rows into slot piece % 2,
-					// once the consumers are done with what that slot held
-					const int sl = piece & 1;
-					if (piece >= 2 &&
-					    !mbar_wait_bounded(&qempty[sl], (uint32_t)(((piece >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
+					const DevJob& J = P.jobs[cur.job];
+					const int n = min(min(cur.n_tiles - cur.tis, J.chunk - cur.tis % J.chunk), left);
+					const bool fresh = holds_new_rows(J, cur.tis, n, T);
+					if (P.fused || (int)fresh == pass)
 					{
-						s_flags[0] = 1;
-						break;
+						// a piece holding new keys appends them itself when K1 does not run
+						const bool append = P.fused && fresh;
+						const int h = cur.seg / J.n_rowgroups, rg = cur.seg % J.n_rowgroups;
+						// the piece's descriptor, tile count and q rows into slot piece % 2,
+						// once the consumers are done with what that slot held
+						const int sl = piece & 1;
+						if (piece >= 2 && !mbar_wait_bounded(&qempty[sl], (uint32_t)(((piece >> 1) - 1) & 1), P.err,
+						                                     DEVERR_WAIT_EMPTY))
+						{
+							s_flags[0] = 1;
+							break;
+						}
+						const int G = J.n_head / J.n_kv;
+						const int rows = seg_rows(J, rg, RM);
+						float* slot = qslot + sl * C::QSLOT_FLOATS;
+						int* info = reinterpret_cast<int*>(slot + C::QHEAD_FLOATS - 4);
+						info[0] = n;       // tiles of this piece in this CTA
+						info[1] = cur.tis; // its first tile within the segment
+						info[2] = cur.seg;
+						info[3] = append;
+						const int half = J.n_rot / 2;
+						const uint32_t inv_bytes = (uint32_t)((half * 4 + 15) & ~15); // the table is padded
+						const uint32_t bytes =
+							(uint32_t)(sizeof(DevJob) + rows * D * 4 + (J.q_gamma ? D * 4 : 0) + inv_bytes +
+						               (J.freq_factors ? half * 4 : 0) +
+						               (append ? (J.k_gamma ? D * 4 : 0) + 2 * J.n_tok * D * 4 : 0));
+						mbar_arrive_expect_tx(&qfull[sl], bytes); // also releases the stores above
+						bulk_g2s(slot, &J, (uint32_t)sizeof(DevJob), &qfull[sl]);
+						if (J.q_gamma) bulk_g2s(slot + C::QGAIN, J.q_gamma, (uint32_t)(D * 4), &qfull[sl]);
+						if (inv_bytes) bulk_g2s(slot + C::QINV, J.rope_inv, inv_bytes, &qfull[sl]);
+						if (J.freq_factors) bulk_g2s(slot + C::QFF, J.freq_factors, (uint32_t)(half * 4), &qfull[sl]);
+						// rows (t, g) of the segment: per token, its G heads are contiguous
+						for (int r = 0; r < rows;)
+						{
+							const int gr = rg * RM + r, t = gr / G, g = gr % G;
+							const int run = min(G - g, rows - r);
+							bulk_g2s(slot + C::QROWS + r * D, J.q + ((size_t)t * J.n_head + (size_t)h * G + g) * D,
+							         (uint32_t)(run * D * 4), &qfull[sl]);
+							r += run;
+						}
+						if (append)
+						{
+							// the new tokens' raw k and v rows of this KV head, and the k gains
+							if (J.k_gamma) bulk_g2s(slot + C::QKG, J.k_gamma, (uint32_t)(D * 4), &qfull[sl]);
+							for (int t = 0; t < J.n_tok; ++t)
+							{
+								const size_t src = ((size_t)t * J.n_kv + h) * D;
+								bulk_g2s(slot + C::QNEW + t * D, J.k + src, (uint32_t)(D * 4), &qfull[sl]);
+								bulk_g2s(slot + C::QNEW + (C::NT + t) * D, J.v + src, (uint32_t)(D * 4), &qfull[sl]);
+							}
+						}
+						++piece;
+						for (int k = 0; k < n; ++k, ++i)
+						{
+							const int key0 = (J.tile_lo + cur.tis + k) * T;
+							// the rows K1 appends come from the preceding grid: wait for it
+							// before streaming a tile that holds them
+							if (!P.fused && !waited && fresh && holds_new_rows(J, cur.tis + k, 1, T))
+							{
+								griddep_wait();
+								waited = true;
+							}
+							if (i < S.pre) continue; // issued at the start
+							const size_t off = (size_t)h * J.head_bytes + (size_t)(key0 % J.rows) * D * KV::esize;
+							const int s = i % STAGES;
+							if (i >= STAGES && !mbar_wait_bounded(&empty[s], (uint32_t)(((i / STAGES) - 1) & 1), P.err,
+							                                      DEVERR_WAIT_EMPTY))
+							{
+								s_flags[0] = 1;
+								break;
+							}
+							if (s_flags[0]) break;
+							unsigned char* st = stages + s * C::STAGE_BYTES;
+							mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
+							bulk_g2s(st, J.K + off, TILE_BYTES, &full[s]);
+							bulk_g2s(st + TILE_BYTES, J.V + off, TILE_BYTES, &full[s]);
+						}
 					}
-					const int G = J.n_head / J.n_kv;
-					const int rows = seg_rows(J, rg, RM);
-					float* slot = qslot + sl * C::QSLOT_FLOATS;
-					int* info = reinterpret_cast<int*>(slot + C::QHEAD_FLOATS - 4);
-					info[0] = min(cur.n_tiles - cur.tis, n_mine - i); // tiles of this piece in this CTA
-					info[1] = cur.tis;
-					info[2] = cur.seg;
-					const int half = J.n_rot / 2;
-					const uint32_t inv_bytes = (uint32_t)((half * 4 + 15) & ~15); // the table is padded
-					const uint32_t bytes = (uint32_t)(sizeof(DevJob) + rows * D * 4 + (J.q_gamma ? D * 4 : 0) +
-					                                  inv_bytes + (J.freq_factors ? half * 4 : 0));
-					mbar_arrive_expect_tx(&qfull[sl], bytes);
-					bulk_g2s(slot, P.jobs + cur.job, (uint32_t)sizeof(DevJob), &qfull[sl]);
-					if (J.q_gamma) bulk_g2s(slot + C::QGAIN, J.q_gamma, (uint32_t)(D * 4), &qfull[sl]);
-					if (inv_bytes) bulk_g2s(slot + C::QINV, J.rope_inv, inv_bytes, &qfull[sl]);
-					if (J.freq_factors) bulk_g2s(slot + C::QFF, J.freq_factors, (uint32_t)(half * 4), &qfull[sl]);
-					// rows (t, g) of the segment: per token, its G heads are contiguous
-					for (int r = 0; r < rows;)
-					{
-						const int gr = rg * RM + r, t = gr / G, g = gr % G;
-						const int run = min(G - g, rows - r);
-						bulk_g2s(slot + C::QROWS + r * D, J.q + ((size_t)t * J.n_head + (size_t)h * G + g) * D,
-						         (uint32_t)(run * D * 4), &qfull[sl]);
-						r += run;
-					}
-					pj = cur.job;
-					ps = cur.seg;
-					++piece;
+					left -= n;
+					cur.tis += n;
+					if (cur.tis >= cur.n_tiles) cursor_next_segment(P, cur);
 				}
-				const int key0 = (J.tile_lo + cur.tis) * T;
-				// the rows K1 appends come from the preceding grid: wait for it
-				// before streaming a tile that holds them (earlier tiles need not)
-				if (!waited && !J.reuse_kv && key0 <= J.pos0 + J.n_tok - 1 && key0 + T - 1 >= J.pos0)
-				{
-					griddep_wait();
-					waited = true;
-				}
-				const size_t off = (size_t)h * J.head_bytes + (size_t)(key0 % J.rows) * D * KV::esize;
-				const int s = i % STAGES;
-				if (i >= STAGES &&
-				    !mbar_wait_bounded(&empty[s], (uint32_t)(((i / STAGES) - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
-				{
-					s_flags[0] = 1;
-					break;
-				}
-				if (s_flags[0]) break;
-				unsigned char* st = stages + s * C::STAGE_BYTES;
-				mbar_arrive_expect_tx(&full[s], 2 * TILE_BYTES);
-				bulk_g2s(st, J.K + off, TILE_BYTES, &full[s]);
-				bulk_g2s(st + TILE_BYTES, J.V + off, TILE_BYTES, &full[s]);
-				cursor_next(P, cur);
 			}
 		}
 		return;
@@ -294,12 +351,21 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	struct PieceEnd
 	{
 		float* out;
-		int n_head, G, h, rg, n_tok, seg, c_first, c_last;
+		int n_head, G, h, rg, n_tok, seg, n_pieces, part, chunk;
 	} pe;
 
+	// The new keys a piece appends itself, in its slot in the cache's element
+	// type (row t of the k rows at new_k + t * NSTRIDE), used in place of the
+	// cache rows of positions [new_lo, new_lo + n_new) of its tiles.
+	constexpr int NSTRIDE = D * 4 / KV::esize;
+	int new_lo = 0, n_new = 0;
+	const T_* new_k = nullptr;
+	const T_* new_v = nullptr;
+
 	// Piece start: the piece's q rows from its slot into registers, and what
-	// its end will need; then the slot goes back to the producer.
-	auto start_piece = [&](const DevJob& J, int seg_local, int sl) {
+	// its end will need; then the slot goes back to the producer (at the
+	// piece's end instead when the slot holds the new keys it appends).
+	auto start_piece = [&](const DevJob& J, int seg_local, int sl, bool append, int tis0, int n_piece) {
 		const int G = J.n_head / J.n_kv;
 		const int h = seg_local / J.n_rowgroups, rg = seg_local % J.n_rowgroups;
 		const int rows = seg_rows(J, rg, RM);
@@ -308,21 +374,42 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		const float qmul = softcap ? J.scale : J.scale * LOG2E;
 		float* slot = qslot + sl * C::QSLOT_FLOATS;
 		float* qs = slot + C::QROWS;
-		// attention_forward's q work (model.cpp:1616-1660), a warp per row:
-		// RMSNorm with the gains, then RoPE at the row's token position
-		for (int r = warp; r < rows; r += NW)
+		const float* ff = J.freq_factors ? slot + C::QFF : nullptr;
+		// attention_forward's per-head work (model.cpp:1616-1694), a warp per
+		// vector: each q row gets RMSNorm with the gains and RoPE at its token's
+		// position; when the piece appends, each new k row gets RMSNorm with the
+		// k gains and RoPE, each new v row the plain norm if asked, both are
+		// narrowed to the cache's type and, by the first row group's piece,
+		// stored at row pos % rows of the cache (the append loop, :1662-1694)
+		const int n_app = append ? 2 * J.n_tok : 0;
+		for (int task = warp; task < rows + n_app; task += NW)
 		{
-			float* buf = qs + r * D;
-			if (J.q_gamma)
+			if (task < rows)
 			{
-				const float sc = rms_scale(buf, D, J.eps, true);
-				for (int i2 = lane; i2 < D; i2 += 32) buf[i2] = buf[i2] * sc * slot[C::QGAIN + i2];
-				__syncwarp();
+				prep_buf(qs + task * D, D, J.q_gamma ? slot + C::QGAIN : nullptr, false, J.eps, true, J.n_rot,
+				         J.rope_mode, (float)(J.pos0 + (rg * RM + task) / G) * J.rope_scale, slot + C::QINV, ff);
+				continue;
 			}
-			rope_vec(buf, J.n_rot, J.rope_mode, (float)(J.pos0 + (rg * RM + r) / G) * J.rope_scale, slot + C::QINV,
-			         J.freq_factors ? slot + C::QFF : nullptr);
-			__syncwarp();
+			const int u = task - rows;
+			const bool is_k = u < J.n_tok;
+			const int t = is_k ? u : u - J.n_tok;
+			float* buf = slot + C::QNEW + (is_k ? t : C::NT + t) * D;
+			prep_buf(buf, D, is_k && J.k_gamma ? slot + C::QKG : nullptr, !is_k && J.v_rmsnorm, J.eps, is_k, J.n_rot,
+			         J.rope_mode, (float)(J.pos0 + t) * J.rope_scale, slot + C::QINV, ff);
+			narrow_buf<KV>(buf, D);
+			const int pos = J.pos0 + t;
+			const int lo = (J.tile_lo + tis0) * T;
+			if (rg == 0 && pos >= lo && pos < lo + n_piece * T)
+			{
+				const T_* src = reinterpret_cast<const T_*>(buf);
+				T_* dst = reinterpret_cast<T_*>((is_k ? J.K : J.V) + (size_t)h * J.head_bytes) + (size_t)(pos % J.rows) * D;
+				for (int i2 = lane; i2 < D; i2 += 32) dst[i2] = src[i2];
+			}
 		}
+		new_lo = J.pos0;
+		n_new = append ? J.n_tok : 0;
+		new_k = reinterpret_cast<const T_*>(slot + C::QNEW);
+		new_v = reinterpret_cast<const T_*>(slot + C::QNEW + C::NT * D);
 		named_sync(1, NW * 32);
 #pragma unroll
 		for (int r = 0; r < RMW; ++r)
@@ -345,8 +432,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			span_of(J.causal, J.window, J.pos0 + gr_v / G, J.n_seq, first_v, last_v);
 		else
 			first_v = 0, last_v = -1; // a padding row sees nothing
-		const long long W = P.tiles_per_cta;
-		const long long seg_gstart = J.gtile0 + (long long)seg_local * J.n_tiles;
 		pe.out = J.out;
 		pe.n_head = J.n_head;
 		pe.G = G;
@@ -354,13 +439,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		pe.rg = rg;
 		pe.n_tok = J.n_tok;
 		pe.seg = J.seg0 + seg_local;
-		pe.c_first = (int)(seg_gstart / W);
-		pe.c_last = (int)((seg_gstart + J.n_tiles - 1) / W);
+		pe.n_pieces = J.n_chunks;
+		pe.part = J.part0 + seg_local * J.n_chunks; // the segment's first partial slot
+		pe.chunk = tis0 / J.chunk;
 		// the slot is refilled by bulk copies (the async proxy): order this warp's
 		// writes to it first, then hand it back
 		asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 		__syncwarp();
-		if (lane == 0) mbar_arrive(&qempty[sl]);
+		if (lane == 0 && !append) mbar_arrive(&qempty[sl]);
 	};
 
 	// Merge the warps' states of the finished piece (two rounds: the upper half
@@ -426,9 +512,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		// (one row slice) or the two slices
 
 		const int G = pe.G, h = pe.h, rg = pe.rg, n_tok = pe.n_tok, n_head = pe.n_head;
-		const int c_first = pe.c_first, c_last = pe.c_last, seg = pe.seg;
-		const bool single = c_first == c_last;
-		float* part = P.parts + (size_t)(seg + (int)blockIdx.x) * RM * PW;
+		const int seg = pe.seg, n_pieces = pe.n_pieces;
+		const bool single = n_pieces == 1;
+		float* part = P.parts + (size_t)(pe.part + pe.chunk) * RM * PW;
 
 		for (int idx = ctid; idx < RM * D; idx += NW * 32)
 		{
@@ -471,88 +557,68 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			named_sync(1, NW * 32);
 			if (ctid == 0)
 			{
-				const int n_pieces = c_last - c_first + 1;
 				const int prev = atomic_add_acq_rel(&P.counters[seg], 1);
 				s_flags[1] = prev == n_pieces - 1;
 			}
 			named_sync(1, NW * 32);
 			if (s_flags[1])
 			{
-				// Fold the pieces (nnc_attn_merge in key order, then
-				// nnc_attn_finish) in two rounds of independent loads: a warp
-				// per row takes every piece's (m, l) at once and leaves the
-				// weights exp2(m_c - M) / L in the area; then each thread sums
-				// its 4 output columns over the pieces with 16-byte loads.
-				const int np = c_last - c_first + 1; // the planner keeps np * RM within the area
-				const float* base = P.parts + (size_t)(seg + c_first) * RM * PW;
-				float* wgt = area; // [np][RM]
-				for (int R = warp; R < RM; R += NW)
-				{
-					float2 ml[4];
-#pragma unroll
-					for (int k = 0; k < 4; ++k)
-					{
-						const int c = lane + 32 * k;
-						ml[k] = c < np ? __ldcg(reinterpret_cast<const float2*>(base + (size_t)c * RM * PW + R * PW + D))
-						               : make_float2(-CUDART_INF_F, 0.0f);
-					}
-					float mx = fmaxf(fmaxf(ml[0].x, ml[1].x), fmaxf(ml[2].x, ml[3].x));
-					for (int c = lane + 128; c < np; c += 32)
-						mx = fmaxf(mx, __ldcg(base + (size_t)c * RM * PW + R * PW + D));
-					mx = warp_max(mx);
-					float L = 0.0f;
-#pragma unroll
-					for (int k = 0; k < 4; ++k)
-					{
-						const int c = lane + 32 * k;
-						const float w = ml[k].x == -CUDART_INF_F ? 0.0f : ex2(ml[k].x - mx);
-						if (c < np) wgt[c * RM + R] = w;
-						L = fmaf(ml[k].y, w, L);
-					}
-					for (int c = lane + 128; c < np; c += 32)
-					{
-						const float2 v = __ldcg(reinterpret_cast<const float2*>(base + (size_t)c * RM * PW + R * PW + D));
-						const float w = v.x == -CUDART_INF_F ? 0.0f : ex2(v.x - mx);
-						wgt[c * RM + R] = w;
-						L = fmaf(v.y, w, L);
-					}
-					L = warp_sum(L);
-					const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-					for (int c = lane; c < np; c += 32) wgt[c * RM + R] *= inv;
-				}
-				named_sync(1, NW * 32);
+				// Fold the pieces (nnc_attn_merge over the chunks, then
+				// nnc_attn_finish): each thread owns 4 output columns of a row and
+				// merges the pieces' (o, m, l) online, 16 pieces' worth of
+				// independent 16-byte loads at a time.
+				const int np = n_pieces;
+				const float* base = P.parts + (size_t)pe.part * RM * PW;
+				constexpr int FB = 16;
 				for (int idx = ctid; idx < RM * (D / 4); idx += NW * 32)
 				{
 					const int R = idx / (D / 4), d = 4 * (idx % (D / 4));
 					const int gr = rg * RM + R;
 					if (gr >= G * n_tok) continue;
 					const float* col = base + R * PW + d;
+					const float* mlp = base + R * PW + D;
+					float M = -CUDART_INF_F, L = 0.0f;
 					float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-					int c = 0;
-					for (; c + 4 <= np; c += 4)
+					for (int c0 = 0; c0 < np; c0 += FB)
 					{
-						float4 v[4];
+						float4 v[FB];
+						float2 ml[FB];
 #pragma unroll
-						for (int u = 0; u < 4; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(col + (size_t)(c + u) * RM * PW));
-#pragma unroll
-						for (int u = 0; u < 4; ++u)
+						for (int u = 0; u < FB; ++u)
 						{
-							const float w = wgt[(c + u) * RM + R];
+							const bool ok = c0 + u < np;
+							v[u] = ok ? __ldcg(reinterpret_cast<const float4*>(col + (size_t)(c0 + u) * RM * PW))
+							          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+							ml[u] = ok ? __ldcg(reinterpret_cast<const float2*>(mlp + (size_t)(c0 + u) * RM * PW))
+							           : make_float2(-CUDART_INF_F, 0.0f);
+						}
+						float mx = M;
+#pragma unroll
+						for (int u = 0; u < FB; ++u) mx = fmaxf(mx, ml[u].x);
+						if (mx == -CUDART_INF_F) continue; // nothing seen yet
+						const float sc = M == -CUDART_INF_F ? 0.0f : ex2(M - mx);
+						acc.x *= sc;
+						acc.y *= sc;
+						acc.z *= sc;
+						acc.w *= sc;
+						L *= sc;
+#pragma unroll
+						for (int u = 0; u < FB; ++u)
+						{
+							const float w = ml[u].x == -CUDART_INF_F ? 0.0f : ex2(ml[u].x - mx);
 							acc.x = fmaf(v[u].x, w, acc.x);
 							acc.y = fmaf(v[u].y, w, acc.y);
 							acc.z = fmaf(v[u].z, w, acc.z);
 							acc.w = fmaf(v[u].w, w, acc.w);
+							L = fmaf(ml[u].y, w, L);
 						}
+						M = mx;
 					}
-					for (; c < np; ++c)
-					{
-						const float4 v = __ldcg(reinterpret_cast<const float4*>(col + (size_t)c * RM * PW));
-						const float w = wgt[c * RM + R];
-						acc.x = fmaf(v.x, w, acc.x);
-						acc.y = fmaf(v.y, w, acc.y);
-						acc.z = fmaf(v.z, w, acc.z);
-						acc.w = fmaf(v.w, w, acc.w);
-					}
+					const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+					acc.x *= inv;
+					acc.y *= inv;
+					acc.z *= inv;
+					acc.w *= inv;
 					const int t = gr / G, g = gr % G;
 					*reinterpret_cast<float4*>(pe.out + ((size_t)t * n_head + (size_t)h * G + g) * D + d) = acc;
 				}
@@ -575,8 +641,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		const DevJob& J = *reinterpret_cast<const DevJob*>(slot);
 		const int* info = reinterpret_cast<const int*>(slot + C::QHEAD_FLOATS - 4);
 		const int n_piece = info[0], tis0 = info[1], seg_local = info[2];
+		const bool append = info[3] != 0;
 		int key_base = (J.tile_lo + tis0) * T;
-		start_piece(J, seg_local, sl);
+		start_piece(J, seg_local, sl, append, tis0, n_piece);
 		for (int k = 0; k < n_piece; ++k, ++i)
 		{
 			const int s = i % STAGES;
@@ -599,7 +666,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					for (int kk = 0; kk < KS; ++kk)
 					{
 						float kv[E];
-						load_lane<E>(Kt + (size_t)(k0 + kk) * D, lane, kv);
+						const int np = key_base + k0 + kk - new_lo; // a new key: its row from the slot
+						load_lane<E>((unsigned)np < (unsigned)n_new ? new_k + np * NSTRIDE : Kt + (size_t)(k0 + kk) * D,
+						             lane, kv);
 #pragma unroll
 						for (int r = 0; r < RMW; ++r)
 						{
@@ -648,7 +717,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					for (int kk = 0; kk < KS; ++kk)
 					{
 						float vv[E];
-						load_lane<E>(Vt + (size_t)(k0 + kk) * D, lane, vv);
+						const int np = key_base + k0 + kk - new_lo;
+						load_lane<E>((unsigned)np < (unsigned)n_new ? new_v + np * NSTRIDE : Vt + (size_t)(k0 + kk) * D,
+						             lane, vv);
 #pragma unroll
 						for (int r = 0; r < RMW; ++r)
 						{
@@ -663,6 +734,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			if (lane == 0) mbar_arrive(&empty[s]);
 			key_base += T;
 		}
+		if (append && lane == 0) mbar_arrive(&qempty[sl]); // the new keys are no longer needed
+		n_new = 0;
 		finish_piece();
 	}
 	const int n_done = i;
@@ -812,7 +885,7 @@ int launch_one(const DecodePlan& P, cudaStream_t st)
 	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
 	attr[0].val.programmaticStreamSerializationAllowed = 1;
 	cfg.attrs = attr;
-	cfg.numAttrs = 1;
+	cfg.numAttrs = P.fused ? 0 : 1; // appending itself, it follows the stream's previous work in full
 	return (int)cudaLaunchKernelEx(&cfg, decode_kernel<D, KV, RM>, P);
 }
 
@@ -869,21 +942,60 @@ namespace
 constexpr int slices(int D, int RM) { return RM * (D / 32) > 32 ? RM * (D / 32) / 32 : 1; }
 } // namespace
 
-int decode_smem_bytes(int D, int kv_type, int RM)
+namespace
 {
-	(void)kv_type;
-	const int RMW = RM / slices(D, RM);
-	const int qslot = (int)(sizeof(DevJob) / 4) + 4 + RM * D + 2 * D;
-	const int fixed = (2 * RMW * D + 2 * NW * RMW + 2 * qslot) * 4 + 256;
-	const int stages = std::min(MAX_STAGES, (SMEM_LIMIT - fixed) / (2 * TILE_BYTES));
-	return stages * 2 * TILE_BYTES + fixed;
+template <int D, typename KV>
+int fuse_tokens_rows(int RM)
+{
+	constexpr int E = D / 32;
+	switch (RM)
+	{
+	case 1: return Cfg<D, KV, 1>::NT;
+	case 2: return Cfg<D, KV, 2>::NT;
+	case 4: return Cfg<D, KV, 4>::NT;
+	case 8:
+		if constexpr (8 * E <= 64) return Cfg<D, KV, 8>::NT;
+		break;
+	case 16:
+		if constexpr (16 * E <= 64) return Cfg<D, KV, 16>::NT;
+		break;
+	case 32:
+		if constexpr (32 * E <= 64) return Cfg<D, KV, 32>::NT;
+		break;
+	default: break;
+	}
+	return 0;
+}
+
+template <typename KV>
+int fuse_tokens_dims(int D, int RM)
+{
+	switch (D)
+	{
+	case 64: return fuse_tokens_rows<64, KV>(RM);
+	case 128: return fuse_tokens_rows<128, KV>(RM);
+	case 256: return fuse_tokens_rows<256, KV>(RM);
+	case 512: return fuse_tokens_rows<512, KV>(RM);
+	default: return 0;
+	}
+}
+} // namespace
+
+int decode_fuse_tokens(int D, int kv_type, int RM)
+{
+	switch (kv_type)
+	{
+	case KV_F32: return fuse_tokens_dims<kv_f32>(D, RM);
+	case KV_BF16: return fuse_tokens_dims<kv_bf16>(D, RM);
+	default: return fuse_tokens_dims<kv_f16>(D, RM);
+	}
 }
 
 int decode_fold_pieces(int D, int RM) { return 2 * (RM / slices(D, RM)) * D / RM; }
 
 int launch_decode(const DecodePlan& P, void* stream)
 {
-	if (P.total_tiles == 0) return 0;
+	if (P.n_ctas == 0) return 0;
 	auto st = static_cast<cudaStream_t>(stream);
 	switch (P.kv_type)
 	{

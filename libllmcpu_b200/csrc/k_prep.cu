@@ -22,7 +22,7 @@ constexpr int PREP_WARPS = 8;
 constexpr int PREP_MAX_D = 512;
 
 template <typename KV>
-__global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __restrict__ jobs, int n_jobs)
+__global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __restrict__ jobs)
 {
 	using T = typename KV::T;
 	// The attention kernel that follows may start now: it streams the K/V
@@ -35,19 +35,16 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __r
 	const DevJob& j = jobs[blockIdx.y];
 	const int t = blockIdx.x;
 	if (t >= j.n_tok) return;
-	(void)n_jobs;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int D = j.D, half = j.n_rot / 2;
 	float* buf = bufs[warp];
-	const int n_q = 0, n_kv = j.reuse_kv ? 0 : j.n_kv; // k heads, then v heads
+	const int n_kv = j.reuse_kv ? 0 : j.n_kv; // tasks: k heads, then v heads
 	const int n_tasks = 2 * n_kv;
 	if (n_tasks == 0) return;
 	const float rpos = (float)(j.pos0 + t) * j.rope_scale;
 	const int row = (j.pos0 + t) % j.rows;
 	auto task_src = [&](int task) {
-		const int kind = task < n_q ? 0 : (task < n_q + n_kv ? 1 : 2); // q, k, v
-		const int h = kind == 0 ? task : (kind == 1 ? task - n_q : task - n_q - n_kv);
-		return (kind == 1 ? j.k : j.v) + ((size_t)t * j.n_kv + h) * D;
+		return (task < n_kv ? j.k : j.v) + ((size_t)t * j.n_kv + task % n_kv) * D;
 	};
 	// one round of loads: this warp's first head vector, and the gains and
 	// RoPE tables staged once for every head of the token
@@ -70,12 +67,12 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __r
 	for (int task = warp; task < n_tasks; task += PREP_WARPS)
 	{
 		if (task != warp) load_head(x, task_src(task), D);
-		const int kind = task < n_q ? 0 : (task < n_q + n_kv ? 1 : 2); // q, k, v
-		const int h = kind == 0 ? task : (kind == 1 ? task - n_q : task - n_q - n_kv);
-		const float* gamma = kind == 1 && kg ? s_kg : nullptr;
-		prep_head(buf, x, D, gamma, kind == 2 && j.v_rmsnorm, j.eps, kind != 2, j.n_rot, j.rope_mode, rpos, s_inv,
+		const bool is_k = task < n_kv;
+		const int h = task % n_kv;
+		const float* gamma = is_k && kg ? s_kg : nullptr;
+		prep_head(buf, x, D, gamma, !is_k && j.v_rmsnorm, j.eps, is_k, j.n_rot, j.rope_mode, rpos, s_inv,
 		          ff ? s_ff : nullptr);
-		char* base = (kind == 1 ? j.K : j.V) + (size_t)h * j.head_bytes;
+		char* base = (is_k ? j.K : j.V) + (size_t)h * j.head_bytes;
 		T* dst = reinterpret_cast<T*>(base) + (size_t)row * D;
 		for (int i = lane; i < D; i += 32) store_elem(dst + i, buf[i]);
 		__syncwarp();
@@ -124,18 +121,17 @@ __global__ void softcap_kernel(float* y, const float* x, size_t n, float cap)
 
 } // namespace
 
-int launch_prep(const DevJob* jobs_dev, int n_jobs, int max_tok, int max_heads, int D, int kv_type, void* stream)
+int launch_prep(const DecodePlan& P, void* stream)
 {
-	(void)max_heads;
-	if (D > PREP_MAX_D || n_jobs > 65535) return (int)cudaErrorInvalidValue;
-	if (max_tok == 0 || n_jobs == 0) return 0;
+	if (P.D > PREP_MAX_D || P.n_jobs > 65535) return (int)cudaErrorInvalidValue;
+	if (P.max_tok == 0 || P.n_jobs == 0) return 0;
 	auto st = static_cast<cudaStream_t>(stream);
-	const dim3 grid((unsigned)max_tok, (unsigned)n_jobs);
-	switch (kv_type)
+	const dim3 grid((unsigned)P.max_tok, (unsigned)P.n_jobs);
+	switch (P.kv_type)
 	{
-	case KV_F32: prep_kernel<kv_f32><<<grid, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
-	case KV_BF16: prep_kernel<kv_bf16><<<grid, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
-	default: prep_kernel<kv_f16><<<grid, PREP_WARPS * 32, 0, st>>>(jobs_dev, n_jobs); break;
+	case KV_F32: prep_kernel<kv_f32><<<grid, PREP_WARPS * 32, 0, st>>>(P.jobs); break;
+	case KV_BF16: prep_kernel<kv_bf16><<<grid, PREP_WARPS * 32, 0, st>>>(P.jobs); break;
+	default: prep_kernel<kv_f16><<<grid, PREP_WARPS * 32, 0, st>>>(P.jobs); break;
 	}
 	return (int)cudaGetLastError();
 }

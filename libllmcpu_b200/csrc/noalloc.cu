@@ -26,7 +26,8 @@
 //    before any use where even such a lookup is unwelcome.
 //
 // The kernels are the allocating path's own K1 (k_prep.cu) and K2 (the
-// decode kernel, k_decode.cu), planned here for a single job.
+// decode kernel, k_decode.cu), planned by the same planner (plan.cpp) for a
+// single job.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -79,7 +80,7 @@ constexpr int MAX_CTAS = 256;
 struct alignas(16) HostHead
 {
 	DevJob job;
-	int4 starts[MAX_CTAS];
+	CtaStart starts[MAX_CTAS];
 	float rope[256];
 };
 thread_local HostHead t_head;
@@ -105,6 +106,10 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 		return set_error(NNCU_ERR_INVALID_ARGUMENT, "n_head must be a positive multiple of n_kv");
 	if (p->n_tok <= 0 || p->pos0 < 0 || p->n_seq <= 0)
 		return set_error(NNCU_ERR_INVALID_ARGUMENT, "n_tok, pos0 and n_seq must be positive");
+	if (p->n_tok > NNCU_NOALLOC_MAX_TOKENS)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT,
+		                 "the no-allocation entry point takes at most NNCU_NOALLOC_MAX_TOKENS tokens (decode and "
+		                 "verify); use nncu_attention for more");
 	if (rows <= 0 || rows % ATTN_BLOCK)
 		return set_error(NNCU_ERR_INVALID_ARGUMENT, "the cache's rows must be a positive multiple of 256");
 	if (p->n_rot < 0 || p->n_rot > D || (p->n_rot & 1) || p->n_rot > 512)
@@ -131,52 +136,12 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	int n_sms = 148;
 	cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev);
 
-	// ---- the plan: one job, stream-K over its tiles ----
+	// ---- the job, then the plan (the allocating path's planner, for one job) ----
 	const size_t es = kv_esize(kv_type);
-	const int T = decode_tile_keys(D, kv_type);
-	const int G = p->n_head / p->n_kv;
-	int RM = 1;
-	while (RM < G * p->n_tok && RM < decode_rows_max(D)) RM *= 2;
-	int first_min = INT_MAX, last_max = -1;
-	for (int t = 0; t < p->n_tok; ++t)
-	{
-		int f, l;
-		nncu_attn_span(p->causal, p->window, p->pos0 + t, p->n_seq, &f, &l);
-		if (l < f) continue;
-		first_min = std::min(first_min, f);
-		last_max = std::max(last_max, l);
-	}
-	const int n_rowgroups = (G * p->n_tok + RM - 1) / RM;
-	const int n_tiles = last_max < 0 ? 0 : last_max / T - first_min / T + 1;
-	const int n_seg = p->n_kv * n_rowgroups;
-	const long long total = (long long)n_seg * n_tiles;
-	const int ctas0 = (int)std::min<long long>(std::min<long long>(total, n_sms), MAX_CTAS);
-	const int fold = decode_fold_pieces(D, RM); // pieces one segment may be cut into
-	const long long W =
-		std::max<long long>(ctas0 > 0 ? (total + ctas0 - 1) / ctas0 : 1, (n_tiles + fold - 2) / (fold - 1));
-	const int n_ctas = ctas0 > 0 ? (int)((total + W - 1) / W) : 0;
-
-	// ---- the scratch: [job | starts | rope | partials | counters | error] ----
-	const size_t off_job = 0;
-	const size_t off_starts = up256(sizeof(DevJob));
-	const size_t off_rope = off_starts + up256((size_t)MAX_CTAS * sizeof(int4));
-	const size_t off_parts = off_rope + up256(256 * sizeof(float));
-	const size_t off_count = off_parts + up256((size_t)(n_seg + n_ctas) * RM * (D + 4) * sizeof(float));
-	const size_t off_err = off_count + up256((size_t)n_seg * sizeof(int));
-	const size_t need = off_err + 256;
-	if (need > NOALLOC_SCRATCH_BYTES)
-	{
-		char msg[200];
-		std::snprintf(msg, sizeof msg,
-		              "this call needs %zu bytes of scratch; the no-allocation entry point has %zu (fewer tokens or "
-		              "heads per call, or use nncu_attention)",
-		              need, NOALLOC_SCRATCH_BYTES);
-		return set_error(NNCU_ERR_INVALID_ARGUMENT, msg);
-	}
-
 	HostHead& hh = t_head;
 	std::memset(&hh.job, 0, sizeof hh.job);
 	DevJob& j = hh.job;
+	const size_t off_rope = 0; // scratch: [rope | job | starts | partials | counters | error]
 	j.q = q;
 	j.k = k;
 	j.v = v;
@@ -205,13 +170,25 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	j.eps = p->eps;
 	j.scale = p->scale;
 	j.softcap = p->softcap;
-	j.tile_lo = last_max < 0 ? 0 : first_min / T;
-	j.n_tiles = n_tiles;
-	j.n_rowgroups = n_rowgroups;
-	for (int c = 0; c < n_ctas; ++c)
+	DecodePlan P{};
+	rc = plan_launch(&j, 1, kv_type, std::min(n_sms, MAX_CTAS), P, hh.starts, MAX_CTAS);
+	if (rc != NNCU_OK) return rc;
+
+	const size_t off_job = up256(256 * sizeof(float));
+	const size_t off_starts = off_job + up256(sizeof(DevJob));
+	const size_t off_parts = off_starts + up256((size_t)MAX_CTAS * sizeof(CtaStart));
+	const size_t off_count =
+		off_parts + up256((size_t)std::max<long long>(P.n_parts, 1) * P.RM * (D + 4) * sizeof(float));
+	const size_t off_err = off_count + up256((size_t)P.n_segments * sizeof(int));
+	const size_t need = off_err + 256;
+	if (need > NOALLOC_SCRATCH_BYTES)
 	{
-		const long long g = (long long)c * W;
-		hh.starts[c] = make_int4(0, (int)(g / n_tiles), (int)(g % n_tiles), 0);
+		char msg[200];
+		std::snprintf(msg, sizeof msg,
+		              "this call needs %zu bytes of scratch; the no-allocation entry point has %zu (fewer tokens or "
+		              "heads per call, or use nncu_attention)",
+		              need, NOALLOC_SCRATCH_BYTES);
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, msg);
 	}
 	// nnc_rope_f32's inverse frequencies (nn_ops.cpp:1844-1856), the fp32 recurrence
 	const int half = p->n_rot / 2;
@@ -226,13 +203,13 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 		}
 	}
 
-	// ---- upload the head, clear what must start at zero, run K1 and K2 ----
+	// ---- upload the job, the starts and the RoPE table, clear what must start at zero, run K1 and K2 ----
 	auto st = static_cast<cudaStream_t>(stream);
 	// copies from pageable host memory: each returns once its source is consumed
 	ce = cudaMemcpyAsync(scratch + off_job, &hh.job, sizeof(DevJob), cudaMemcpyHostToDevice, st);
-	if (ce == cudaSuccess && n_ctas > 0)
-		ce = cudaMemcpyAsync(scratch + off_starts, hh.starts, (size_t)n_ctas * sizeof(int4), cudaMemcpyHostToDevice,
-		                     st);
+	if (ce == cudaSuccess && P.n_ctas > 0)
+		ce = cudaMemcpyAsync(scratch + off_starts, hh.starts, (size_t)P.n_ctas * sizeof(CtaStart),
+		                     cudaMemcpyHostToDevice, st);
 	if (ce == cudaSuccess && half > 0)
 	{
 		for (int i = half; i < ((half + 3) & ~3); ++i) hh.rope[i] = 0.0f; // whole 16-byte pieces
@@ -240,30 +217,19 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 		                     cudaMemcpyHostToDevice, st);
 	}
 	if (ce == cudaSuccess) ce = cudaMemsetAsync(scratch + off_count, 0, off_err + 256 - off_count, st);
-	if (ce == cudaSuccess && n_tiles == 0)
+	if (ce == cudaSuccess && j.n_tiles == 0)
 		ce = cudaMemsetAsync(out, 0, (size_t)p->n_tok * p->n_head * D * sizeof(float), st);
 	if (ce != cudaSuccess) return set_cuda_error((int)ce, "no-allocation call: staging");
 
-	int e = launch_prep(reinterpret_cast<const DevJob*>(scratch + off_job), 1, p->n_tok, 0, D, kv_type, st);
+	P.jobs = reinterpret_cast<const DevJob*>(scratch + off_job);
+	P.cta_start = reinterpret_cast<const CtaStart*>(scratch + off_starts);
+	P.parts = reinterpret_cast<float*>(scratch + off_parts);
+	P.counters = reinterpret_cast<int*>(scratch + off_count);
+	P.err = reinterpret_cast<int*>(scratch + off_err);
+	int e = P.fused ? 0 : launch_prep(P, st); // K2 appends itself when it can
 	if (e) return set_cuda_error(e, "K1 (norm, RoPE, append) launch");
-	if (n_tiles > 0)
+	if (P.n_ctas > 0)
 	{
-		DecodePlan P{};
-		P.jobs = reinterpret_cast<const DevJob*>(scratch + off_job);
-		P.n_jobs = 1;
-		P.D = D;
-		P.kv_type = kv_type;
-		P.RM = RM;
-		P.T = T;
-		P.total_tiles = total;
-		P.n_ctas = n_ctas;
-		P.tiles_per_cta = W;
-		P.n_segments = n_seg;
-		P.fused = 0;
-		P.cta_start = reinterpret_cast<const int4*>(scratch + off_starts);
-		P.parts = reinterpret_cast<float*>(scratch + off_parts);
-		P.counters = reinterpret_cast<int*>(scratch + off_count);
-		P.err = reinterpret_cast<int*>(scratch + off_err);
 		e = launch_decode(P, st);
 		if (e) return set_cuda_error(e, "K2 (attention) launch");
 	}

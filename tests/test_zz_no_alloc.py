@@ -77,17 +77,23 @@ def test_noalloc_refuses_what_does_not_fit(nncu, torch_cuda):
     D, rows = 256, 4096
     k_cache = torch.zeros(8, rows, D, device="cuda")
     v_cache = torch.zeros_like(k_cache)
-    # 4096 tokens x 64 heads would need far more than the 4 MiB scratch; refused before any
-    # buffer is touched, so small stand-ins do for the inputs and the output
-    q = torch.zeros(16, device="cuda")
+    # 4096 tokens are beyond what the entry point takes (decode and verify). The
+    # buffers have the call's full sizes all the same, so that nothing could be
+    # read or written out of bounds even if the call were accepted.
+    n_tok, n_head, n_kv = 4096, 64, 8
+    q = torch.zeros(n_tok, n_head * D, device="cuda")
     out = torch.zeros_like(q)
-    kvp = torch.zeros_like(q)
-    p = N.params(n_tok=4096, pos0=0, n_head=64, n_kv=8, head_dim=D)
+    kv_new = torch.zeros(n_tok, n_kv * D, device="cuda")
+    p = N.params(n_tok=n_tok, pos0=0, n_head=n_head, n_kv=n_kv, head_dim=D)
     with pytest.raises(N.NnncError) as e:
-        N.attention_noalloc(p, q, kvp, kvp, out, k_cache, v_cache, O.KV_F32, rows)
-    assert e.value.status == N.ERR_INVALID_ARGUMENT and "scratch" in str(e.value)
-    # a cache whose rows are not whole 256-key blocks is refused too
+        N.attention_noalloc(p, q, kv_new, kv_new, out, k_cache, v_cache, O.KV_F32, rows)
+    assert e.value.status == N.ERR_INVALID_ARGUMENT and "tokens" in str(e.value)
+    # a cache whose rows are not whole 256-key blocks is refused too (full-size buffers again)
     p = N.params(n_tok=1, pos0=10, n_head=4, n_kv=1, head_dim=D)
+    q1 = torch.zeros(1, 4 * D, device="cuda")
+    out1 = torch.zeros_like(q1)
+    kv1 = torch.zeros(1, D, device="cuda")
     with pytest.raises(N.NnncError) as e:
-        N.attention_noalloc(p, q, kvp, kvp, out, k_cache, v_cache, O.KV_F32, 1000)
+        N.attention_noalloc(p, q1, kv1, kv1, out1, k_cache, v_cache, O.KV_F32, 1000)
     assert e.value.status == N.ERR_INVALID_ARGUMENT
+    torch.cuda.synchronize()
