@@ -247,6 +247,41 @@ int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_j
  * need more fails with NNCU_ERR_INVALID_ARGUMENT and a message. The first call
  * on each device looks the array's device address up (cudaGetSymbolAddress)
  * with that device current; make that first call during set-up. */
+/* ---- One sequence split over the GPUs of a node ----
+ *
+ * No counterpart in the reference (one CPU, one process). Its equivalent is
+ * attend_blocks (model.cpp:1296-1319) merging 256-key blocks in order with
+ * nnc_attn_merge (nn_ops.cpp:461-482): here GPU r holds and reads keys
+ * [key_lo, key_hi) of the sequence, and the partials of all GPUs are merged
+ * in rank order, on every GPU, inside the attention kernel: each GPU stores
+ * its partial straight into every other GPU's receive buffer over NVLink and
+ * the last to arrive merges. One process per GPU; every rank makes the same
+ * calls in the same order.
+ *
+ * nncu_group_create allocates this GPU's shared block (receive buffers,
+ * counters, and the output: max_rows rows of head_dim floats, the jobs'
+ * n_tok * n_head rows one after another). Exchange the handles out of band
+ * (nncu_group_handle on each rank, nncu_group_open with every peer's) before
+ * the first call. nncu_attention_split_dev runs the jobs over this GPU's keys
+ * [key_lo, key_hi) (key_lo a multiple of 256; the new tokens are appended
+ * only by the GPU whose range holds them) and leaves the merged attention in
+ * nncu_group_output() of every GPU when `stream` reaches the end of the call.
+ * A rank that does not take part makes the others' calls end with
+ * NNCU_ERR_TIMEOUT (reported by nncu_sync) after 2 s instead of hanging. */
+typedef struct nncu_group nncu_group;
+#define NNCU_GROUP_HANDLE_BYTES 64
+int nncu_group_create(int32_t device, int32_t rank, int32_t world, int32_t max_rows, int32_t head_dim,
+                      nncu_group** out);
+int nncu_group_handle(const nncu_group* g, void* handle);
+int nncu_group_open(nncu_group* g, int32_t peer, const void* handle);
+float* nncu_group_output(const nncu_group* g);
+/* Copy the first n_floats of this GPU's merged output to dst (host or device
+ * memory), ordered on `stream` after the split calls before it. */
+int nncu_group_copy_output(const nncu_group* g, float* dst, size_t n_floats, void* stream);
+void nncu_group_free(nncu_group* g);
+int nncu_attention_split_dev(nncu_kv* kv, nncu_group* group, const nncu_attn_job* jobs, int32_t n_jobs,
+                             int32_t key_lo, int32_t key_hi, void* stream);
+
 #define NNCU_NOALLOC_MAX_TOKENS 64
 int nncu_attention_noalloc(const nncu_attn_params* p, const float* q, const float* k, const float* v, float* out,
                            void* k_cache, void* v_cache, int32_t kv_type, int32_t rows, void* stream);

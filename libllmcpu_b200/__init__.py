@@ -52,8 +52,11 @@ EXPORTS = [
     "nncu_softcap_dev", "nncu_kv_plan", "nncu_kv_create", "nncu_kv_free", "nncu_kv_layer", "nncu_kv_get_state",
     "nncu_kv_rewind", "nncu_kv_commit", "nncu_kv_write_rows", "nncu_kv_read_rows", "nncu_attention",
     "nncu_attention_batch", "nncu_attention_batch_dev", "nncu_sync", "nncu_perf_enable", "nncu_perf_reset",
-    "nncu_perf_read", "nncu_perf_report", "nncu_launch_count", "nncu_attention_noalloc",
+    "nncu_perf_read", "nncu_perf_report", "nncu_launch_count", "nncu_attention_noalloc", "nncu_group_create",
+    "nncu_group_handle", "nncu_group_open", "nncu_group_output", "nncu_group_copy_output", "nncu_group_free",
+    "nncu_attention_split_dev",
 ]
+GROUP_HANDLE_BYTES = 64
 
 
 class NnncError(RuntimeError):
@@ -188,6 +191,15 @@ def lib() -> C.CDLL:
     L.nncu_perf_report.restype = C.c_char_p
     L.nncu_launch_count.restype = C.c_uint64
     L.nncu_attention_noalloc.argtypes = [C.POINTER(AttnParams), vp, vp, vp, vp, vp, vp, i32, i32, vp]
+    L.nncu_group_create.argtypes = [i32, i32, i32, i32, i32, C.POINTER(vp)]
+    L.nncu_group_handle.argtypes = [vp, vp]
+    L.nncu_group_open.argtypes = [vp, i32, vp]
+    L.nncu_group_output.argtypes = [vp]
+    L.nncu_group_output.restype = vp
+    L.nncu_group_copy_output.argtypes = [vp, vp, sz, vp]
+    L.nncu_group_free.argtypes = [vp]
+    L.nncu_group_free.restype = None
+    L.nncu_attention_split_dev.argtypes = [vp, vp, C.POINTER(AttnJob), i32, i32, i32, vp]
     _lib = L
     return L
 
@@ -396,3 +408,65 @@ def rope_dev(x, n_tok, n_heads, head_dim, n_rot, pos0, pos_scale, freq_base, mod
 
 def softcap_dev(y, x, n, cap, stream=None):
     _check(lib().nncu_softcap_dev(_ptr(y), _ptr(x), n, cap, _stream(stream)))
+
+
+# ---- one sequence split over the GPUs of a node (nncu_group) ----------------------------------
+
+def split_ranges(n_keys: int, world: int, block: int = 256):
+    """The key range of each rank: equal 256-aligned runs of the n_keys keys
+    (the last one short). Raises if a rank would be left without keys."""
+    per = -(-n_keys // world)
+    chunk = -(-per // block) * block
+    ranges = [(r * chunk, min((r + 1) * chunk, n_keys)) for r in range(world)]
+    if any(hi <= lo for lo, hi in ranges):
+        raise ValueError(f"{n_keys} keys leave a rank of {world} without keys")
+    return ranges
+
+
+def exchange_handles(handle: bytes, world: int):
+    """Every rank's group handle, through the default torch.distributed group
+    (host plumbing only: the handles are a few bytes)."""
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, handle)
+    return out
+
+
+class SplitGroup:
+    """This GPU's part of a sequence split over `world` GPUs (nncu_group):
+    rank r reads keys [key_lo, key_hi) and every GPU ends with the merged
+    attention in its output rows."""
+
+    def __init__(self, rank: int, world: int, max_rows: int, head_dim: int, device: int = 0, exchange=None):
+        L = lib()
+        h = C.c_void_p()
+        _check(L.nncu_group_create(int(device), int(rank), int(world), int(max_rows), int(head_dim), C.byref(h)))
+        self._h, self.rank, self.world, self.head_dim, self.max_rows = h, rank, world, head_dim, max_rows
+        buf = C.create_string_buffer(GROUP_HANDLE_BYTES)
+        _check(L.nncu_group_handle(self._h, buf))
+        handles = (exchange or exchange_handles)(buf.raw, world)
+        for r, hb in enumerate(handles):
+            if r != rank:
+                _check(L.nncu_group_open(self._h, r, C.create_string_buffer(hb, GROUP_HANDLE_BYTES)))
+
+    def output_ptr(self) -> int:
+        """Device address of this GPU's merged output rows (float32, head_dim each)."""
+        return int(lib().nncu_group_output(self._h))
+
+    def read_output(self, n_floats: int, stream=None) -> np.ndarray:
+        """The first n_floats of this GPU's merged output, on the host (waits for `stream`)."""
+        out = np.empty(int(n_floats), np.float32)
+        _check(lib().nncu_group_copy_output(self._h, out.ctypes.data, out.size, _stream(stream)))
+        import torch
+        torch.cuda.synchronize()
+        return out
+
+    def attention(self, kv: "KVCache", jobs, key_lo: int, key_hi: int, stream=None) -> None:
+        arr = jobs if isinstance(jobs, C.Array) else (AttnJob * len(jobs))(*jobs)
+        _check(lib().nncu_attention_split_dev(kv._h, self._h, arr, len(arr), int(key_lo), int(key_hi),
+                                               _stream(stream)))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().nncu_group_free(self._h)
+            self._h = None

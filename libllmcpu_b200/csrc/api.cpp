@@ -800,11 +800,14 @@ void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 	d.eps = p.eps;
 	d.scale = p.scale;
 	d.softcap = p.softcap;
+	d.key_lo = 0;
+	d.key_hi = INT_MAX;
 }
 
 // Launch K1 and K2 for jobs whose DevJob pointers are all device pointers,
 // on `st`.
-int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, cudaStream_t st)
+int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, cudaStream_t st,
+             nncu_group* group = nullptr)
 {
 	const int n = (int)jobs.size();
 	for (int i = 0; i < n; ++i)
@@ -826,6 +829,21 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	int rc = plan_launch(jobs.data(), n, kv->kv_type, kv->num_sms, P, kv->starts_tmp.data(), kv->num_sms);
 	if (rc != NNCU_OK) return rc;
 	P.err = kv->err_dev;
+	P.world = 1;
+	if (group)
+	{
+		// every GPU of the split sends a partial for every segment: each needs keys
+		int n_rows = 0;
+		for (int i = 0; i < n; ++i)
+		{
+			if (jobs[i].n_tiles == 0)
+				return fail(NNCU_ERR_INVALID_ARGUMENT, "split: job %d sees no key in [%d, %d) on this GPU", i,
+				            jobs[i].key_lo, jobs[i].key_hi);
+			n_rows += jobs[i].n_tok * jobs[i].n_head;
+		}
+		rc = group_prepare(group, P, n_rows);
+		if (rc != NNCU_OK) return rc;
+	}
 	// scratch for partials and the per-segment counters
 	const size_t part_floats = (size_t)std::max<long long>(P.n_parts, 1) * P.RM * (P.D + 4);
 	CU(kv->parts.reserve(part_floats * sizeof(float)), "partials scratch");
@@ -879,6 +897,8 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 		{
 			int f, l;
 			nncu_attn_span(j.causal, j.window, j.pos0 + t, j.n_seq, &f, &l);
+			f = std::max(f, j.key_lo);
+			l = std::min(l, j.key_hi - 1);
 			if (l < f) continue;
 			first_min = std::min(first_min, f);
 			last_max = std::max(last_max, l);
@@ -900,6 +920,11 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 		e = launch_decode(P, st);
 	}
 	if (e) return cuda_fail((cudaError_t)e, "K2 (attention) launch");
+	if (group)
+	{
+		e = launch_split_wait(P, st);
+		if (e) return cuda_fail((cudaError_t)e, "split wait launch");
+	}
 	CU(cudaEventRecord(slot.used, st), "job table slot event");
 	slot.ever = true;
 	CU(cudaEventRecord(kv->done, st), "completion event");
@@ -944,6 +969,41 @@ extern "C" int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, 
 	kv->jobs_tmp.resize(n_jobs);
 	for (int i = 0; i < n_jobs; ++i) fill_devjob(kv, jobs[i], kv->jobs_tmp[i]);
 	return run_jobs(kv, kv->jobs_tmp, jobs, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nncu_attention_split_dev(nncu_kv* kv, nncu_group* group, const nncu_attn_job* jobs, int32_t n_jobs,
+                                        int32_t key_lo, int32_t key_hi, void* stream)
+{
+	if (!kv || !group || !jobs || n_jobs <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "no jobs or no group");
+	if (group_device(group) != kv->device) return fail(NNCU_ERR_INVALID_ARGUMENT, "group and cache on different GPUs");
+	if (key_lo < 0 || key_hi <= key_lo || key_lo % ATTN_BLOCK)
+		return fail(NNCU_ERR_INVALID_ARGUMENT, "split: keys [%d, %d) must be a non-empty range from a 256-key block",
+		            key_lo, key_hi);
+	for (int i = 0; i < n_jobs; ++i)
+	{
+		int rc = validate_job(kv, jobs[i]);
+		if (rc != NNCU_OK) return rc;
+		if (!jobs[i].q || (!jobs[i].p.reuse_kv && (!jobs[i].k || !jobs[i].v)))
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: NULL input", i);
+		auto misaligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; };
+		if (misaligned(jobs[i].q) || misaligned(jobs[i].p.q_gamma) || misaligned(jobs[i].p.freq_factors))
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: q, q_gamma and freq_factors must be 16-byte aligned", i);
+	}
+	int rc = check_conflicts(kv, jobs, n_jobs);
+	if (rc != NNCU_OK) return rc;
+	DeviceGuard g(kv->device);
+	kv->jobs_tmp.resize(n_jobs);
+	int row = 0;
+	for (int i = 0; i < n_jobs; ++i)
+	{
+		fill_devjob(kv, jobs[i], kv->jobs_tmp[i]);
+		kv->jobs_tmp[i].key_lo = key_lo;
+		kv->jobs_tmp[i].key_hi = key_hi;
+		kv->jobs_tmp[i].out_row0 = row;
+		kv->jobs_tmp[i].out = nullptr; // the merged rows land in the group's output
+		row += jobs[i].p.n_tok * jobs[i].p.n_head;
+	}
+	return run_jobs(kv, kv->jobs_tmp, jobs, static_cast<cudaStream_t>(stream), group);
 }
 
 extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs)

@@ -8,6 +8,8 @@
 
 #include <vector_types.h>
 
+struct nncu_group; // split.cpp
+
 namespace nncu
 {
 
@@ -27,7 +29,8 @@ enum
 	DEVERR_NONE = 0,
 	DEVERR_WAIT_FULL = 1,  // a consumer's wait for a K/V tile ran out
 	DEVERR_WAIT_EMPTY = 2, // the producer's wait for a free stage ran out
-	DEVERR_PLAN = 3        // a tile fell outside every job (a planning bug)
+	DEVERR_PLAN = 3,       // a tile fell outside every job (a planning bug)
+	DEVERR_SPLIT = 4       // a split call's partials did not all arrive on this GPU in time
 };
 
 inline int kv_esize(int kv_type) { return kv_type == KV_F32 ? 4 : 2; }
@@ -61,6 +64,10 @@ struct alignas(16) DevJob
 	int chunk;            // tiles per chunk: a segment is cut into n_chunks chunks of this many
 	int n_chunks;         // (the last may be short); each chunk is one piece with its own partial
 	int part0;            // this job's first partial slot: segment s, chunk c at part0 + s * n_chunks + c
+	// the keys this launch attends and appends: [key_lo, key_hi) of every
+	// query's span (the whole span unless the sequence is split over GPUs)
+	int key_lo, key_hi;
+	int out_row0;         // split over GPUs: the job's first row in the group's output
 };
 static_assert(sizeof(DevJob) % 16 == 0, "DevJob is bulk-copied");
 
@@ -76,6 +83,8 @@ struct alignas(16) CtaStart
 	int pad_[3];
 };
 static_assert(sizeof(CtaStart) == 48, "CtaStart layout");
+
+constexpr int MAX_WORLD = 8; // GPUs a sequence may be split over (one NVSwitch node)
 
 // One launch of K1 and K2: each CTA streams a run of whole chunks (of one or
 // more segments) given by its CtaStart.
@@ -93,6 +102,17 @@ struct DecodePlan
 	float* parts;   // n_parts slots of RM * (D + 4) floats
 	int* counters;  // n_segments, zero between launches
 	int* err;       // device error word
+	// A sequence split over the GPUs of a group (world > 1; nncu_group, split.cpp):
+	// each segment's result over this GPU's keys goes, as a partial, to every
+	// GPU's receive buffer; on each GPU the last partial to arrive merges them
+	// in rank order into that GPU's output. All pointers are for this call's
+	// parity (calls alternate between two sets), GPU g's at index g.
+	int world, rank;
+	long long recv_stride;       // floats between two ranks' blocks of a receive buffer
+	float* recv[MAX_WORLD];      // [world][segments][RM][D + 4]
+	int* arrive[MAX_WORLD];      // [segments] partials arrived, zero between calls
+	int* done[MAX_WORLD];        // segments merged on GPU g in this call
+	float* out[MAX_WORLD];       // GPU g's output rows (job i from its out_row0)
 };
 
 // Plan one launch over jobs[0, n) (their D, kv geometry, positions and
@@ -108,6 +128,12 @@ int set_cuda_error(int cuda_status, const char* what);
 // Launchers (implemented in the .cu files). Each returns a cudaError_t value.
 int launch_prep(const DecodePlan& plan, void* stream);
 int launch_decode(const DecodePlan& plan, void* stream);
+int launch_split_wait(const DecodePlan& plan, void* stream); // a split call's end: this GPU's rows merged
+
+// Fill the split fields of a plan from a group (split.cpp): its peers'
+// buffers for this call's parity; checks that the call fits the group.
+int group_prepare(nncu_group* g, DecodePlan& P, int n_rows);
+int group_device(const nncu_group* g);
 bool decode_supported(int D, int kv_type);
 int decode_tile_keys(int D, int kv_type);
 int decode_rows_max(int D);

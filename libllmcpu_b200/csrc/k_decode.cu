@@ -138,11 +138,13 @@ __device__ __forceinline__ void cursor_next_segment(const DecodePlan& P, Cursor&
 	if (c.job < P.n_jobs) cursor_load(P, c);
 }
 
-// Whether tiles [tis, tis + n) of a job's segment hold keys K1 appends in
-// this launch (they must wait for K1; earlier keys need not).
+// Whether tiles [tis, tis + n) of a job's segment hold keys appended in this
+// launch: its new tokens within its key range (while K1 appends, they must
+// wait for K1; earlier keys need not).
 __device__ __forceinline__ bool holds_new_rows(const DevJob& J, int tis, int n, int T)
 {
-	return !J.reuse_kv && (J.tile_lo + tis) * T <= J.pos0 + J.n_tok - 1 && (J.tile_lo + tis + n) * T - 1 >= J.pos0;
+	const int lo = max(J.pos0, J.key_lo), hi = min(J.pos0 + J.n_tok, J.key_hi);
+	return !J.reuse_kv && lo < hi && (J.tile_lo + tis) * T <= hi - 1 && (J.tile_lo + tis + n) * T - 1 >= lo;
 }
 
 // atom.add with acquire-release semantics at GPU scope: the arriving CTA's
@@ -153,6 +155,80 @@ __device__ __forceinline__ int atomic_add_acq_rel(int* p, int v)
 	int old;
 	asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
 	return old;
+}
+
+// The same at system scope: partials crossing to other GPUs of a split.
+__device__ __forceinline__ int atomic_add_acq_rel_sys(int* p, int v)
+{
+	int old;
+	asm volatile("atom.acq_rel.sys.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+	return old;
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p)
+{
+	int v;
+	asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+	return v;
+}
+
+// Merge np partials of a segment's rows in order (nnc_attn_merge, piece 0
+// first): piece c of row R is o[D], m, l at base + c * stride + R * PW, m in
+// log2 units. A thread owns 4 columns of a row and merges online, FB pieces'
+// worth of independent 16-byte loads at a time; `emit(R, d, acc, M, L)` gets
+// the merged (o, m, l) of columns d .. d+3 (o relative to 2^M). Rows R >=
+// rows_valid are padding and skipped.
+template <int D, int RM, typename Emit>
+__device__ __forceinline__ void merge_pieces(const float* base, size_t stride, int np, int rows_valid, int tid,
+                                             int nthreads, Emit emit)
+{
+	constexpr int PW = D + 4;
+	constexpr int FB = 16;
+	for (int idx = tid; idx < RM * (D / 4); idx += nthreads)
+	{
+		const int R = idx / (D / 4), d = 4 * (idx % (D / 4));
+		if (R >= rows_valid) continue;
+		const float* col = base + R * PW + d;
+		const float* mlp = base + R * PW + D;
+		float M = -CUDART_INF_F, L = 0.0f;
+		float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+		for (int c0 = 0; c0 < np; c0 += FB)
+		{
+			float4 v[FB];
+			float2 ml[FB];
+#pragma unroll
+			for (int u = 0; u < FB; ++u)
+			{
+				const bool ok = c0 + u < np;
+				v[u] = ok ? __ldcg(reinterpret_cast<const float4*>(col + (size_t)(c0 + u) * stride))
+				          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+				ml[u] = ok ? __ldcg(reinterpret_cast<const float2*>(mlp + (size_t)(c0 + u) * stride))
+				           : make_float2(-CUDART_INF_F, 0.0f);
+			}
+			float mx = M;
+#pragma unroll
+			for (int u = 0; u < FB; ++u) mx = fmaxf(mx, ml[u].x);
+			if (mx == -CUDART_INF_F) continue; // nothing seen yet
+			const float sc = M == -CUDART_INF_F ? 0.0f : ex2(M - mx);
+			acc.x *= sc;
+			acc.y *= sc;
+			acc.z *= sc;
+			acc.w *= sc;
+			L *= sc;
+#pragma unroll
+			for (int u = 0; u < FB; ++u)
+			{
+				const float w = ml[u].x == -CUDART_INF_F ? 0.0f : ex2(ml[u].x - mx);
+				acc.x = fmaf(v[u].x, w, acc.x);
+				acc.y = fmaf(v[u].y, w, acc.y);
+				acc.z = fmaf(v[u].z, w, acc.z);
+				acc.w = fmaf(v[u].w, w, acc.w);
+				L = fmaf(ml[u].y, w, L);
+			}
+			M = mx;
+		}
+		emit(R, d, acc, M, L);
+	}
 }
 
 // The rows of a segment that exist (the last row group may be short).
@@ -182,7 +258,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	uint64_t* empty = full + STAGES;
 	uint64_t* qfull = empty + STAGES;  // [2]
 	uint64_t* qempty = qfull + 2;      // [2]
-	volatile int* s_flags = reinterpret_cast<volatile int*>(qempty + 2); // [0] abort, [1] last-piece vote
+	// [0] abort, [1] last-piece vote, [2] the GPUs whose split merge this CTA does
+	volatile int* s_flags = reinterpret_cast<volatile int*>(qempty + 2);
 	CtaStart* s_start = reinterpret_cast<CtaStart*>(qempty + 4);          // this CTA's start (16-byte aligned)
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -351,7 +428,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	struct PieceEnd
 	{
 		float* out;
-		int n_head, G, h, rg, n_tok, seg, n_pieces, part, chunk;
+		int n_head, G, h, rg, n_tok, seg, n_pieces, part, chunk, out_row0;
 	} pe;
 
 	// The new keys a piece appends itself, in its slot in the cache's element
@@ -399,7 +476,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			narrow_buf<KV>(buf, D);
 			const int pos = J.pos0 + t;
 			const int lo = (J.tile_lo + tis0) * T;
-			if (rg == 0 && pos >= lo && pos < lo + n_piece * T)
+			if (rg == 0 && pos >= lo && pos < lo + n_piece * T && pos >= J.key_lo && pos < J.key_hi)
 			{
 				const T_* src = reinterpret_cast<const T_*>(buf);
 				T_* dst = reinterpret_cast<T_*>((is_k ? J.K : J.V) + (size_t)h * J.head_bytes) + (size_t)(pos % J.rows) * D;
@@ -429,7 +506,11 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		l_lane = 0.0f;
 		const int gr_v = rg * RM + rs * RMW + r_v;
 		if (gr_v < G * J.n_tok)
+		{
 			span_of(J.causal, J.window, J.pos0 + gr_v / G, J.n_seq, first_v, last_v);
+			first_v = max(first_v, J.key_lo);
+			last_v = min(last_v, J.key_hi - 1);
+		}
 		else
 			first_v = 0, last_v = -1; // a padding row sees nothing
 		pe.out = J.out;
@@ -442,6 +523,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		pe.n_pieces = J.n_chunks;
 		pe.part = J.part0 + seg_local * J.n_chunks; // the segment's first partial slot
 		pe.chunk = tis0 / J.chunk;
+		pe.out_row0 = J.out_row0;
 		// the slot is refilled by bulk copies (the async proxy): order this warp's
 		// writes to it first, then hand it back
 		asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -514,7 +596,18 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		const int G = pe.G, h = pe.h, rg = pe.rg, n_tok = pe.n_tok, n_head = pe.n_head;
 		const int seg = pe.seg, n_pieces = pe.n_pieces;
 		const bool single = n_pieces == 1;
+		const bool split = P.world > 1;
 		float* part = P.parts + (size_t)(pe.part + pe.chunk) * RM * PW;
+		const int rows_valid = G * n_tok - rg * RM;
+		// where row R of this segment goes: the output (t, head) row, and, split,
+		// the segment's partial slot in GPU g's receive block of this rank
+		auto out_row = [&](float* base_out, int R) -> float* {
+			const int gr = rg * RM + R;
+			return base_out + ((size_t)(gr / G) * n_head + (size_t)h * G + gr % G) * D;
+		};
+		auto recv_row = [&](int g, int rank, int R) {
+			return P.recv[g] + (size_t)rank * P.recv_stride + ((size_t)seg * RM + R) * PW;
+		};
 
 		for (int idx = ctid; idx < RM * D; idx += NW * 32)
 		{
@@ -533,13 +626,22 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 				acc = fmaf(area[(w * RMW + r) * D + d], c, acc);
 				L = fmaf(l_s[w * RMW + r], c, L);
 			}
-			if (single)
+			if (single && !split)
 			{
-				const int gr = rg * RM + R;
-				if (gr < G * n_tok)
+				if (R < rows_valid) out_row(pe.out, R)[d] = L > 0.0f ? acc / L : 0.0f;
+			}
+			else if (single)
+			{
+				// the segment's result over this GPU's keys, to every GPU of the split
+				for (int g = 0; g < P.world; ++g)
 				{
-					const int t = gr / G, g = gr % G;
-					pe.out[((size_t)t * n_head + (size_t)h * G + g) * D + d] = L > 0.0f ? acc / L : 0.0f;
+					float* dst = recv_row(g, P.rank, R);
+					dst[d] = acc;
+					if (d == 0)
+					{
+						dst[D] = M;
+						dst[D + 1] = L;
+					}
 				}
 			}
 			else
@@ -552,6 +654,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 				}
 			}
 		}
+		bool have = single; // this CTA holds the segment's result over this GPU's keys
 		if (!single)
 		{
 			named_sync(1, NW * 32);
@@ -564,65 +667,68 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			if (s_flags[1])
 			{
 				// Fold the pieces (nnc_attn_merge over the chunks, then
-				// nnc_attn_finish): each thread owns 4 output columns of a row and
-				// merges the pieces' (o, m, l) online, 16 pieces' worth of
-				// independent 16-byte loads at a time.
-				const int np = n_pieces;
+				// nnc_attn_finish), or, split, merge them into the partial this
+				// GPU sends
 				const float* base = P.parts + (size_t)pe.part * RM * PW;
-				constexpr int FB = 16;
-				for (int idx = ctid; idx < RM * (D / 4); idx += NW * 32)
-				{
-					const int R = idx / (D / 4), d = 4 * (idx % (D / 4));
-					const int gr = rg * RM + R;
-					if (gr >= G * n_tok) continue;
-					const float* col = base + R * PW + d;
-					const float* mlp = base + R * PW + D;
-					float M = -CUDART_INF_F, L = 0.0f;
-					float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-					for (int c0 = 0; c0 < np; c0 += FB)
-					{
-						float4 v[FB];
-						float2 ml[FB];
-#pragma unroll
-						for (int u = 0; u < FB; ++u)
-						{
-							const bool ok = c0 + u < np;
-							v[u] = ok ? __ldcg(reinterpret_cast<const float4*>(col + (size_t)(c0 + u) * RM * PW))
-							          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-							ml[u] = ok ? __ldcg(reinterpret_cast<const float2*>(mlp + (size_t)(c0 + u) * RM * PW))
-							           : make_float2(-CUDART_INF_F, 0.0f);
-						}
-						float mx = M;
-#pragma unroll
-						for (int u = 0; u < FB; ++u) mx = fmaxf(mx, ml[u].x);
-						if (mx == -CUDART_INF_F) continue; // nothing seen yet
-						const float sc = M == -CUDART_INF_F ? 0.0f : ex2(M - mx);
-						acc.x *= sc;
-						acc.y *= sc;
-						acc.z *= sc;
-						acc.w *= sc;
-						L *= sc;
-#pragma unroll
-						for (int u = 0; u < FB; ++u)
-						{
-							const float w = ml[u].x == -CUDART_INF_F ? 0.0f : ex2(ml[u].x - mx);
-							acc.x = fmaf(v[u].x, w, acc.x);
-							acc.y = fmaf(v[u].y, w, acc.y);
-							acc.z = fmaf(v[u].z, w, acc.z);
-							acc.w = fmaf(v[u].w, w, acc.w);
-							L = fmaf(ml[u].y, w, L);
-						}
-						M = mx;
-					}
-					const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-					acc.x *= inv;
-					acc.y *= inv;
-					acc.z *= inv;
-					acc.w *= inv;
-					const int t = gr / G, g = gr % G;
-					*reinterpret_cast<float4*>(pe.out + ((size_t)t * n_head + (size_t)h * G + g) * D + d) = acc;
-				}
+				if (!split)
+					merge_pieces<D, RM>(base, (size_t)RM * PW, n_pieces, rows_valid, ctid, NW * 32,
+					                    [&](int R, int d, float4 acc, float M, float L) {
+						                    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+						                    acc.x *= inv;
+						                    acc.y *= inv;
+						                    acc.z *= inv;
+						                    acc.w *= inv;
+						                    *reinterpret_cast<float4*>(out_row(pe.out, R) + d) = acc;
+					                    });
+				else
+					merge_pieces<D, RM>(base, (size_t)RM * PW, n_pieces, rows_valid, ctid, NW * 32,
+					                    [&](int R, int d, float4 acc, float M, float L) {
+						                    for (int g = 0; g < P.world; ++g)
+						                    {
+							                    float* dst = recv_row(g, P.rank, R);
+							                    *reinterpret_cast<float4*>(dst + d) = acc;
+							                    if (d == 0) *reinterpret_cast<float2*>(dst + D) = make_float2(M, L);
+						                    }
+					                    });
 				if (ctid == 0) P.counters[seg] = 0; // ready for the next launch
+				have = true;
+			}
+		}
+		if (split && have)
+		{
+			// Arrive on every GPU's counter for this segment; where this partial
+			// is the last of the split to arrive, merge the ranks' partials in
+			// rank order into that GPU's output rows, then count the segment done
+			// there. Nothing waits: whoever arrives last does the merge.
+			named_sync(1, NW * 32);
+			if (ctid == 0)
+			{
+				int mask = 0;
+				for (int g = 0; g < P.world; ++g)
+					if (atomic_add_acq_rel_sys(P.arrive[g] + seg, 1) == P.world - 1) mask |= 1 << g;
+				s_flags[2] = mask;
+			}
+			named_sync(1, NW * 32);
+			const int mask = s_flags[2];
+			for (int g = 0; g < P.world; ++g)
+			{
+				if (!(mask >> g & 1)) continue;
+				float* out_g = P.out[g] + (size_t)pe.out_row0 * D;
+				merge_pieces<D, RM>(recv_row(g, 0, 0), (size_t)P.recv_stride, P.world, rows_valid, ctid, NW * 32,
+				                    [&](int R, int d, float4 acc, float M, float L) {
+					                    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+					                    acc.x *= inv;
+					                    acc.y *= inv;
+					                    acc.z *= inv;
+					                    acc.w *= inv;
+					                    *reinterpret_cast<float4*>(out_row(out_g, R) + d) = acc;
+				                    });
+				named_sync(1, NW * 32);
+				if (ctid == 0)
+				{
+					atomicExch(P.arrive[g] + seg, 0); // ready for this parity's next call
+					atomic_add_acq_rel_sys(P.done[g], 1);
+				}
 			}
 		}
 		named_sync(1, NW * 32); // the merge area is free again
@@ -747,6 +853,26 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		for (int k = n_done; k < n_mine && k < n_done + STAGES; ++k)
 			mbar_wait_bounded(&full[k % STAGES], (uint32_t)((k / STAGES) & 1), nullptr, 0);
 	}
+}
+
+// The end of a split call on this GPU: wait (bounded) until every segment's
+// merge has landed here, then clear the count for this parity's next call. A
+// rank that never arrives makes this time out with DEVERR_SPLIT instead of
+// hanging; the host reports it as NNCU_ERR_TIMEOUT.
+__global__ void split_wait_kernel(int* done, int target, int* err)
+{
+	if (threadIdx.x != 0) return;
+	const uint64_t t0 = globaltimer_ns();
+	while (ld_acquire_sys(done) < target)
+	{
+		if (globaltimer_ns() - t0 > WAIT_LIMIT_NS)
+		{
+			atomicExch(err, DEVERR_SPLIT);
+			return;
+		}
+		__nanosleep(200);
+	}
+	atomicExch(done, 0);
 }
 
 // ---- unit seam: nnc_attn_block / merge / finish on device pointers ---------------
@@ -1003,6 +1129,12 @@ int launch_decode(const DecodePlan& P, void* stream)
 	case KV_BF16: return launch_dims<kv_bf16>(P, st);
 	default: return launch_dims<kv_f16>(P, st);
 	}
+}
+
+int launch_split_wait(const DecodePlan& P, void* stream)
+{
+	split_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(P.done[P.rank], P.n_segments, P.err);
+	return (int)cudaGetLastError();
 }
 
 int launch_attn_block(const float* q, size_t q_stride, const void* K, const void* V, int kv_type, size_t kv_stride,

@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __r
 	// block (t, job): token t of job blockIdx.y
 	const DevJob& j = jobs[blockIdx.y];
 	const int t = blockIdx.x;
-	if (t >= j.n_tok) return;
+	if (t >= j.n_tok || j.pos0 + t < j.key_lo || j.pos0 + t >= j.key_hi) return; // not this launch's row
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int D = j.D, half = j.n_rot / 2;
 	float* buf = bufs[warp];

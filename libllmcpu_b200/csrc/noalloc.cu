@@ -170,6 +170,8 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	j.eps = p->eps;
 	j.scale = p->scale;
 	j.softcap = p->softcap;
+	j.key_lo = 0;
+	j.key_hi = INT_MAX;
 	DecodePlan P{};
 	rc = plan_launch(&j, 1, kv_type, std::min(n_sms, MAX_CTAS), P, hh.starts, MAX_CTAS);
 	if (rc != NNCU_OK) return rc;

@@ -28,10 +28,14 @@ namespace
 // ring of them, and the consumers can start on the first tile sooner.
 constexpr int PREFETCH_TILES = 1;
 
+// The positions a job appends in this launch: its new tokens within its key range.
+int append_lo(const DevJob& j) { return j.reuse_kv ? 0 : std::max(j.pos0, j.key_lo); }
+int append_hi(const DevJob& j) { return j.reuse_kv ? 0 : std::min(j.pos0 + j.n_tok, j.key_hi); }
+
 bool holds_new_rows(const DevJob& j, int tis, int len, int T)
 {
-	return !j.reuse_kv && (long long)(j.tile_lo + tis) * T <= j.pos0 + j.n_tok - 1 &&
-	       (long long)(j.tile_lo + tis + len) * T - 1 >= j.pos0;
+	const int lo = append_lo(j), hi = append_hi(j);
+	return lo < hi && (long long)(j.tile_lo + tis) * T <= hi - 1 && (long long)(j.tile_lo + tis + len) * T - 1 >= lo;
 }
 
 } // namespace
@@ -50,6 +54,7 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 	while (RM < rows_needed && RM < decode_rows_max(D)) RM *= 2;
 
 	// every job's tiles: the union of its tokens' spans (model_attn_span)
+	// within its key range
 	long long total = 0;
 	int seg = 0;
 	for (int i = 0; i < n; ++i)
@@ -60,6 +65,8 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 		{
 			int f, l;
 			nncu_attn_span(j.causal, j.window, j.pos0 + t, j.n_seq, &f, &l);
+			f = std::max(f, j.key_lo);
+			l = std::min(l, j.key_hi - 1);
 			if (l < f) continue;
 			first_min = std::min(first_min, f);
 			last_max = std::max(last_max, l);
@@ -80,9 +87,10 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 	for (int i = 0; i < n && fused; ++i)
 	{
 		const DevJob& j = jobs[i];
-		if (j.reuse_kv) continue;
-		if (j.n_tiles == 0 || (long long)j.pos0 < (long long)j.tile_lo * T ||
-		    (long long)j.pos0 + j.n_tok > (long long)(j.tile_lo + j.n_tiles) * T || !aligned(j.k) || !aligned(j.v) ||
+		const int lo = append_lo(j), hi = append_hi(j);
+		if (lo >= hi) continue;
+		if (j.n_tiles == 0 || (long long)lo < (long long)j.tile_lo * T ||
+		    (long long)hi > (long long)(j.tile_lo + j.n_tiles) * T || !aligned(j.k) || !aligned(j.v) ||
 		    !aligned(j.k_gamma))
 			fused = 0;
 	}
