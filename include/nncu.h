@@ -175,9 +175,10 @@ int nncu_kv_rewind(nncu_kv* kv, int32_t seq, int32_t pos);
 /* The bookkeeping model_forward does after its layers (model.cpp:2130-2133):
  * cur_pos = pos0 + n_tok; kv_written = max(pos0 == 0 ? 0 : kv_written, cur_pos). */
 int nncu_kv_commit(nncu_kv* kv, int32_t seq, int32_t pos0, int32_t n_tok);
-/* Copy host rows into / out of a layer's cache (reference row layout
- * [n][n_kv * head_dim] of the cache type's bits), at positions pos0 .. pos0+n-1
- * (row p % rows). For loading or inspecting a cache; synchronous. */
+/* Copy rows into / out of a layer's cache (reference row layout
+ * [n][n_kv * head_dim] of the cache type's bits; host or device memory), at
+ * positions pos0 .. pos0+n-1 (row p % rows). For loading or inspecting a
+ * cache; synchronous. */
 int nncu_kv_write_rows(nncu_kv* kv, int32_t layer, int32_t seq, int32_t pos0, int32_t n, const void* k_rows,
                        const void* v_rows);
 int nncu_kv_read_rows(const nncu_kv* kv, int32_t layer, int32_t seq, int32_t pos0, int32_t n, void* k_rows,

@@ -318,10 +318,12 @@ class KVCache:
         _check(lib().nncu_kv_commit(self._h, seq, pos0, n_tok))
 
     def write_rows(self, layer: int, pos0: int, k_rows: np.ndarray, v_rows: np.ndarray, seq: int = 0) -> None:
-        """Load rows [n][n_kv*head_dim] of the cache type's bits at positions pos0.."""
+        """Load rows [n][n_kv*head_dim] of the cache type's bits at positions pos0..
+        (numpy arrays, or contiguous device tensors)."""
         n = k_rows.shape[0]
-        _check(lib().nncu_kv_write_rows(self._h, layer, seq, pos0, n, _ptr(np.ascontiguousarray(k_rows)),
-                                        _ptr(np.ascontiguousarray(v_rows))))
+        if isinstance(k_rows, np.ndarray):
+            k_rows, v_rows = np.ascontiguousarray(k_rows), np.ascontiguousarray(v_rows)
+        _check(lib().nncu_kv_write_rows(self._h, layer, seq, pos0, n, _ptr(k_rows), _ptr(v_rows)))
 
     def read_rows(self, layer: int, pos0: int, n: int, seq: int = 0):
         info = self.layer_info(layer)

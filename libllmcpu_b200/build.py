@@ -67,7 +67,7 @@ def build(force: bool = False, jobs: int | None = None, extra: list[str] | None 
         objs = list(ex.map(lambda s: _compile(s, force, extra), srcs))
     if force or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
         tmp = LIB + ".tmp"
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", tmp] + objs + ["-lcuda"]
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", tmp] + objs
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -227,7 +227,7 @@ struct nncu_kv
 
 	cudaStream_t stream = nullptr; // the host-pointer calls' stream
 	int* err_dev = nullptr;        // device error word (bounded waits)
-	DevBuf stage_dev, parts, counters;
+	DevBuf stage_dev, parts, counters, qbuf;
 	HostBuf stage_host;
 	// The job tables go up on their own stream through a ring of slots, so
 	// the upload of one call's table overlaps the previous call's kernels
@@ -272,6 +272,7 @@ struct nncu_kv
 			if (sl.used) cudaEventDestroy(sl.used);
 		}
 		stage_dev.release();
+		qbuf.release();
 		parts.release();
 		counters.release();
 		stage_host.release();
@@ -667,7 +668,7 @@ int kv_rows_copy(const nncu_kv* kv, int32_t layer, int32_t seq, int32_t pos0, in
 					char* dst = static_cast<char*>(which ? b.v : b.k);
 					if (!src) continue;
 					CU(cudaMemcpy2D(dst + dev_off, row_bytes, src + host_off, host_pitch, row_bytes, run,
-					                cudaMemcpyHostToDevice),
+					                cudaMemcpyDefault),
 					   "cache write");
 				}
 				else
@@ -676,7 +677,7 @@ int kv_rows_copy(const nncu_kv* kv, int32_t layer, int32_t seq, int32_t pos0, in
 					char* dst = static_cast<char*>(which ? v_dst : k_dst);
 					if (!dst) continue;
 					CU(cudaMemcpy2D(dst + host_off, host_pitch, src + dev_off, row_bytes, row_bytes, run,
-					                cudaMemcpyDeviceToHost),
+					                cudaMemcpyDefault),
 					   "cache read");
 				}
 			}
@@ -806,10 +807,41 @@ void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 
 // Launch K1 and K2 for jobs whose DevJob pointers are all device pointers,
 // on `st`.
+// A long causal batch on a bf16 cache of head_dim 128 (a prefill) runs on
+// the tensor cores: K1 appends its rows, then the q rows' norm and RoPE and
+// the attention of every row (k_prefill.cu).
+bool prefill_eligible(const nncu_kv* kv, const DevJob& j, const nncu_attn_job& pub)
+{
+	const Buffer& b = kv->bufs[kv->kv_buf[pub.layer]];
+	return prefill_supported(j.D, kv->kv_type) && j.causal && j.n_tok >= 128 && b.window == 0 && j.key_lo == 0 &&
+	       j.key_hi == INT_MAX;
+}
+
+int run_prefill(nncu_kv* kv, const DevJob& j, cudaStream_t st)
+{
+	CU(kv->qbuf.reserve(prefill_qbuf_bytes(j.n_tok, j.n_head)), "prefill q scratch");
+	const size_t es = kv_esize(kv->kv_type);
+	const uint64_t kvb = j.reuse_kv ? 0 : (uint64_t)j.n_tok * j.n_kv * j.D;
+	const uint64_t keys = (uint64_t)std::min(j.n_seq, j.pos0 + j.n_tok);
+	int e = 0;
+	{
+		PerfScope ps(NNCU_PERF_ATTN_ROPE, kvb * (8 + 2 * es) + (uint64_t)j.n_tok * j.n_head * j.D * 6, st);
+		e = j.reuse_kv ? 0 : launch_prep_one(j, kv->kv_type, st);
+	}
+	if (e) return cuda_fail((cudaError_t)e, "K1 (norm, RoPE, append) launch");
+	{
+		PerfScope ps(NNCU_PERF_ATTN_CORE,
+		             keys * j.n_kv * j.D * es * 2 + (uint64_t)j.n_tok * j.n_head * j.D * (2 + 4), st);
+		e = launch_prefill(j, kv->qbuf.p, kv->err_dev, st);
+	}
+	if (e) return cuda_fail((cudaError_t)e, "prefill attention launch");
+	return NNCU_OK;
+}
+
 int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, cudaStream_t st,
              nncu_group* group = nullptr)
 {
-	const int n = (int)jobs.size();
+	int n = (int)jobs.size();
 	for (int i = 0; i < n; ++i)
 	{
 		int rc = rope_table(kv, pub[i].p.freq_base, pub[i].p.n_rot, &jobs[i].rope_inv);
@@ -824,6 +856,30 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	// the previous one waits for it on the device
 	if (kv->any_call && kv->last_stream != st)
 		CU(cudaStreamWaitEvent(st, kv->done, 0), "order after the previous call");
+	// prefills one by one on the tensor cores; the rest together below
+	if (!group)
+	{
+		int keep = 0;
+		for (int i = 0; i < n; ++i)
+		{
+			if (prefill_eligible(kv, jobs[i], pub[i]))
+			{
+				int rc = run_prefill(kv, jobs[i], st);
+				if (rc != NNCU_OK) return rc;
+			}
+			else
+				jobs[keep++] = jobs[i];
+		}
+		jobs.resize(keep);
+		n = keep;
+		if (n == 0)
+		{
+			CU(cudaEventRecord(kv->done, st), "completion event");
+			kv->last_stream = st;
+			kv->any_call = true;
+			return NNCU_OK;
+		}
+	}
 	DecodePlan P{};
 	kv->starts_tmp.resize((size_t)kv->num_sms);
 	int rc = plan_launch(jobs.data(), n, kv->kv_type, kv->num_sms, P, kv->starts_tmp.data(), kv->num_sms);

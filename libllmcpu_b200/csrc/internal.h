@@ -121,12 +121,28 @@ struct DecodePlan
 // max_starts, at most num_sms). Host code; allocates nothing.
 int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, CtaStart* starts, int max_starts);
 
+// One causal prefill on the tensor cores (k_prefill.cu): bf16 cache, head_dim 128.
+struct PrefillPlan
+{
+	int n_tok, pos0, n_seq, n_head, n_kv, window, q_tiles;
+	float scale, log2e, softcap;
+	float* out; // [n_tok][n_head * 128]
+	int* err;   // device error word
+};
+bool prefill_supported(int D, int kv_type);
+size_t prefill_qbuf_bytes(int n_tok, int n_head);
+// The q rows' norm + RoPE into `qbuf` (bf16, head-major), then the attention
+// of every row over its causal span into j.out; the cache already holds the
+// new rows (K1). j is the host copy of the job.
+int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream);
+
 // Record a failure for nncu_last_error() (api.cpp); return `status`.
 int set_error(int status, const char* msg);
 int set_cuda_error(int cuda_status, const char* what);
 
 // Launchers (implemented in the .cu files). Each returns a cudaError_t value.
 int launch_prep(const DecodePlan& plan, void* stream);
+int launch_prep_one(const DevJob& job, int kv_type, void* stream); // K1 for one job passed by value
 int launch_decode(const DecodePlan& plan, void* stream);
 int launch_split_wait(const DecodePlan& plan, void* stream); // a split call's end: this GPU's rows merged
 

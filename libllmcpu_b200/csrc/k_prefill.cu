@@ -1,0 +1,518 @@
+// k_prefill.cu -- causal prefill attention on the tensor cores (tcgen05).
+//
+// The same attention as the reference's batched path (attend_chunks over
+// nnc_attn_block / nnc_attn_merge / nnc_attn_finish, model.cpp:1251-1319,
+// nn_ops.cpp:351-499): every query row of a long batch attends over its
+// causal span. Here, for bf16 caches and head_dim 128, the two products run
+// on the 5th-generation tensor cores: one CTA takes 128 query rows of one
+// query head and walks the key tiles of its span, 128 keys at a time:
+//
+//   S = Q K^T      tcgen05.mma, M 128 x N 128 x K 128, bf16 in, fp32 in TMEM
+//   P = softmax    4 warps, one query row per thread, read from TMEM
+//   O += P V       tcgen05.mma, P (bf16) from shared memory, O in TMEM
+//
+// Roles: warp 0 issues the TMA loads (Q once, then K and V tiles into a
+// 2-stage ring); warp 1 owns the TMEM allocation and, from one lane, issues
+// the MMAs (S into two TMEM buffers in turn, so the next tile's S is computed
+// while this tile's softmax runs); warps 4-7 do the softmax, keep O in scale
+// and write the output. Online softmax in base 2 with a lazily moved maximum:
+// a row's reference maximum moves (and O and l are rescaled) only when a new
+// score exceeds it by more than 2^8, so O is rarely touched; the result is
+// the same softmax, divided by the same l.
+//
+// Operands in shared memory use the 128-byte swizzled K-major layout TMA
+// writes (8-row atoms of 1 KB), described to tcgen05.mma by shared memory
+// descriptors; V is used as an MN-major operand straight from its tile.
+// Every wait is bounded; on a timeout the CTA records an error and steps
+// through without waiting further.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <math_constants.h>
+
+#include "common.cuh"
+
+namespace nncu
+{
+namespace
+{
+
+constexpr int PF_BM = 128;                      // query rows per CTA
+constexpr int PF_BN = 128;                      // keys per tile
+constexpr int PF_D = 128;                       // head_dim
+constexpr int PF_THREADS = 256;                 // 8 warps
+constexpr int PANEL = 128 * 128;                // 128 rows x 64 bf16: one 128-byte-swizzled panel
+constexpr int TILE = 2 * PANEL;                 // 128 rows x 128 bf16
+constexpr int KV_STAGES = 2;
+constexpr int SM_Q = 0;                         // Q tile
+constexpr int SM_KV = SM_Q + TILE;              // [stage][K tile, V tile]
+constexpr int SM_P = SM_KV + KV_STAGES * 2 * TILE; // P tile
+constexpr int SM_BAR = SM_P + TILE;             // barriers, TMEM address
+constexpr int PF_SMEM = SM_BAR + 256 + 1024;    // + alignment slack
+constexpr int TMEM_COLS = 512;                  // S0, S1, O (128 columns each)
+constexpr float LAZY = 8.0f;                    // log2 headroom before the row maximum moves
+
+// tcgen05 instruction descriptors (kind::f16): fp32 accumulate, bf16 A and
+// B, M = 128, N = 128; A K-major; B K-major (Q K^T) or MN-major (P V).
+constexpr uint32_t idesc(bool b_mn_major)
+{
+	return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((128u >> 3) << 17) |
+	       ((128u >> 4) << 24);
+}
+
+// Shared memory matrix descriptor, 128-byte swizzle (layout type 2),
+// version 1: start address, leading and stride byte offsets (16-byte units).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo)
+{
+	return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+	       ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t id, uint32_t acc)
+{
+	asm volatile(
+		"{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+		"tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+		"l"(adesc), "l"(bdesc), "r"(id), "r"(acc)
+		: "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar)
+{
+	asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+	             : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v)
+{
+	uint32_t r[32];
+	asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+	             "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+	             "[%32];"
+	             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+	               "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+	               "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+	               "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+	               "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+	             : "r"(taddr)
+	             : "memory");
+#pragma unroll
+	for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v)
+{
+	asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+	             "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, "
+	             "%31, %32};" ::"r"(taddr),
+	             "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+	             "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+	             "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+	             "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+	             "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+	             "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+	             "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+	             "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+	             "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+	             "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+	             "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+	             : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// One box of a 3-D tensor map (x along head_dim, y rows, z head) into shared
+// memory, completing on `bar`. x is 0 or 64: 128-byte aligned.
+__device__ __forceinline__ void tma3(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar)
+{
+	asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+	             "%4}], [%5];" ::"r"(smem_u32(dst)),
+	             "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+	             : "memory");
+}
+
+} // namespace
+
+namespace
+{
+
+__global__ void __launch_bounds__(PF_THREADS, 1)
+	prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, const PrefillPlan P)
+{
+	extern __shared__ unsigned char smem_raw[];
+	unsigned char* smem =
+		reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+	uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
+	uint64_t* q_full = bars + 0;
+	uint64_t* kv_full = bars + 1;  // [2]
+	uint64_t* kv_empty = bars + 3; // [2]
+	uint64_t* s_full = bars + 5;   // [2]
+	uint64_t* s_empty = bars + 7;  // [2]
+	uint64_t* p_full = bars + 9;
+	uint64_t* pv_done = bars + 10;
+	uint64_t* mma_done = bars + 11;
+	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+	volatile int* flags = reinterpret_cast<volatile int*>(bars + 13); // [0] abort
+
+	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	// the heaviest query tiles (the longest causal spans) go first
+	const int h = blockIdx.x % P.n_head;
+	const int qt = P.q_tiles - 1 - blockIdx.x / P.n_head;
+	const int q0 = qt * PF_BM;
+	const int qlo = P.pos0 + q0, qhi = P.pos0 + min(P.n_tok, q0 + PF_BM) - 1;
+	const int klo = (P.window > 0 && qlo + 1 > P.window) ? qlo + 1 - P.window : 0;
+	const int khi = min(qhi, P.n_seq - 1);
+	const int j_lo = klo / PF_BN, n_tiles = khi / PF_BN - j_lo + 1;
+	const int hk = h / (P.n_head / P.n_kv);
+
+	if (threadIdx.x == 0)
+	{
+		mbar_init(q_full, 1);
+		for (int s = 0; s < 2; ++s)
+		{
+			mbar_init(&kv_full[s], 1);
+			mbar_init(&kv_empty[s], 1);
+			mbar_init(&s_full[s], 1);
+			mbar_init(&s_empty[s], 128);
+		}
+		mbar_init(p_full, 128);
+		mbar_init(pv_done, 1);
+		mbar_init(mma_done, 1);
+		flags[0] = 0;
+		fence_barrier_init();
+	}
+	if (warp == 1)
+	{
+		asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+		             "r"(TMEM_COLS)
+		             : "memory");
+		asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+	}
+	tc_fence_before();
+	__syncthreads();
+	tc_fence_after();
+	const uint32_t tmem = *tmem_slot;
+	const uint32_t TS[2] = {tmem, tmem + 128};
+	const uint32_t TO = tmem + 256;
+
+	if (warp == 0)
+	{
+		// ---- TMA: Q once, then the K and V tiles through the 2-stage ring ----
+		if (lane == 0)
+		{
+			mbar_arrive_expect_tx(q_full, TILE);
+			tma3(smem + SM_Q, &qmap, 0, q0, h, q_full);
+			tma3(smem + SM_Q + PANEL, &qmap, 64, q0, h, q_full);
+			int issued = 0;
+			for (int jj = 0; jj < n_tiles; ++jj)
+			{
+				const int s = jj & 1;
+				if (jj >= 2 && !mbar_wait_bounded(&kv_empty[s], (uint32_t)(((jj >> 1) - 1) & 1), P.err,
+				                                  DEVERR_WAIT_EMPTY))
+				{
+					flags[0] = 1;
+					break;
+				}
+				if (flags[0]) break;
+				unsigned char* kt = smem + SM_KV + s * 2 * TILE;
+				unsigned char* vt = kt + TILE;
+				const int key0 = (j_lo + jj) * PF_BN;
+				mbar_arrive_expect_tx(&kv_full[s], 2 * TILE);
+				tma3(kt, &kmap, 0, key0, hk, &kv_full[s]);
+				tma3(kt + PANEL, &kmap, 64, key0, hk, &kv_full[s]);
+				tma3(vt, &vmap, 0, key0, hk, &kv_full[s]);
+				tma3(vt + PANEL, &vmap, 64, key0, hk, &kv_full[s]);
+				issued = jj + 1;
+			}
+			// on an abort, do not leave while a copy may still land here
+			mbar_wait_bounded(q_full, 0, nullptr, 0);
+			for (int jj = max(0, issued - 2); jj < issued; ++jj)
+				mbar_wait_bounded(&kv_full[jj & 1], (uint32_t)((jj >> 1) & 1), nullptr, 0);
+		}
+	}
+	else if (warp == 1)
+	{
+		// ---- MMA issue: S_j = Q K_j^T into S[j % 2], then O += P_{j-1} V_{j-1} ----
+		if (lane == 0)
+		{
+			constexpr uint32_t ID_QK = idesc(false), ID_PV = idesc(true);
+			const uint32_t qa = smem_u32(smem + SM_Q), pa = smem_u32(smem + SM_P);
+			bool ok = mbar_wait_bounded(q_full, 0, P.err, DEVERR_WAIT_FULL);
+			auto issue_pv = [&](int jj) -> bool {
+				if (!mbar_wait_bounded(p_full, (uint32_t)(jj & 1), P.err, DEVERR_WAIT_FULL)) return false;
+				tc_fence_after();
+				const uint32_t va = smem_u32(smem + SM_KV + (jj & 1) * 2 * TILE + TILE);
+#pragma unroll
+				for (int k = 0; k < PF_BN / 16; ++k)
+					mma_f16(TO, sdesc(pa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024), sdesc(va + k * 2048, PANEL, 1024),
+					        ID_PV, (jj > 0 || k > 0) ? 1u : 0u);
+				mma_commit(pv_done);
+				mma_commit(&kv_empty[jj & 1]);
+				return true;
+			};
+			int jj = 0;
+			for (; ok && jj < n_tiles; ++jj)
+			{
+				const int s = jj & 1;
+				ok = !flags[0] && mbar_wait_bounded(&kv_full[s], (uint32_t)((jj >> 1) & 1), P.err, DEVERR_WAIT_FULL);
+				if (ok && jj >= 2)
+					ok = mbar_wait_bounded(&s_empty[s], (uint32_t)(((jj >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY);
+				if (!ok) break;
+				tc_fence_after();
+				const uint32_t ka = smem_u32(smem + SM_KV + s * 2 * TILE);
+#pragma unroll
+				for (int k = 0; k < PF_D / 16; ++k)
+					mma_f16(TS[s], sdesc(qa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
+					        sdesc(ka + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024), ID_QK, k > 0 ? 1u : 0u);
+				mma_commit(&s_full[s]);
+				if (jj >= 1) ok = issue_pv(jj - 1);
+			}
+			if (ok && n_tiles > 0) ok = issue_pv(n_tiles - 1);
+			if (!ok) flags[0] = 1;
+			// every MMA issued has completed before TMEM is freed
+			mma_commit(mma_done);
+			mbar_wait_bounded(mma_done, 0, nullptr, 0);
+		}
+	}
+	else if (warp >= 4)
+	{
+		// ---- softmax, O in scale, output: one query row per thread ----
+		const int wq = warp & 3; // TMEM lanes 32 wq .. 32 wq + 31
+		const int r = wq * 32 + lane;
+		const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+		const int qp = P.pos0 + q0 + r;
+		const int kf = (P.window > 0 && qp + 1 > P.window) ? qp + 1 - P.window : 0;
+		const int kl = min(qp, P.n_seq - 1);
+		float m_used = -CUDART_INF_F, l = 0.0f;
+		bool ok = true;
+		unsigned char* prow = smem + SM_P + r * 128;
+		for (int jj = 0; jj < n_tiles; ++jj)
+		{
+			const int s = jj & 1;
+			if (ok) ok = !flags[0] && mbar_wait_bounded(&s_full[s], (uint32_t)((jj >> 1) & 1), P.err, DEVERR_WAIT_FULL);
+			ok = __all_sync(0xffffffffu, ok);
+			if (!ok) break;
+			tc_fence_after();
+			float x[PF_BN];
+#pragma unroll
+			for (int c = 0; c < PF_BN / 32; ++c) tmem_ld32(TS[s] + lane_off + c * 32, x + 32 * c);
+			tmem_wait_ld();
+			tc_fence_before();
+			mbar_arrive(&s_empty[s]);
+			const int key0 = (j_lo + jj) * PF_BN;
+			float mx = -CUDART_INF_F;
+#pragma unroll
+			for (int c = 0; c < PF_BN; ++c)
+			{
+				float v = P.softcap > 0.0f ? P.softcap * tanhf(x[c] * P.scale / P.softcap) * P.log2e
+				                            : x[c] * P.scale * P.log2e;
+				const int kp = key0 + c;
+				if (kp < kf || kp > kl) v = -CUDART_INF_F;
+				x[c] = v;
+				mx = fmaxf(mx, v);
+			}
+			// the row's reference maximum moves only when a score exceeds it by
+			// more than 2^LAZY; then O (in TMEM) and l are rescaled
+			const bool move = mx > m_used + LAZY;
+			const float m_new = move ? mx : m_used;
+			const float alpha = (move && m_used != -CUDART_INF_F) ? ex2(m_used - m_new) : 1.0f;
+			const bool rescale = move && m_used != -CUDART_INF_F;
+			if (jj > 0)
+			{
+				// O is stable and the P buffer free once P_{j-1} V_{j-1} is done
+				ok = mbar_wait_bounded(pv_done, (uint32_t)((jj - 1) & 1), P.err, DEVERR_WAIT_FULL);
+				ok = __all_sync(0xffffffffu, ok);
+				if (!ok) break;
+				tc_fence_after();
+				if (__any_sync(0xffffffffu, rescale))
+				{
+#pragma unroll
+					for (int c = 0; c < PF_D / 32; ++c)
+					{
+						float o[32];
+						tmem_ld32(TO + lane_off + c * 32, o);
+						tmem_wait_ld();
+#pragma unroll
+						for (int i = 0; i < 32; ++i) o[i] *= alpha;
+						tmem_st32(TO + lane_off + c * 32, o);
+					}
+					tmem_wait_st();
+				}
+			}
+			l *= alpha;
+			m_used = m_new;
+			// P (bf16) into this thread's row, in the 128-byte swizzled layout
+#pragma unroll
+			for (int c16 = 0; c16 < PF_BN / 8; ++c16)
+			{
+				float p[8];
+#pragma unroll
+				for (int i = 0; i < 8; ++i)
+				{
+					const float v = x[c16 * 8 + i];
+					p[i] = v == -CUDART_INF_F ? 0.0f : ex2(v - m_used);
+					l += p[i];
+				}
+				uint32_t w[4];
+#pragma unroll
+				for (int i = 0; i < 4; ++i)
+				{
+					__nv_bfloat162 b2 = __floats2bfloat162_rn(p[2 * i], p[2 * i + 1]);
+					w[i] = *reinterpret_cast<uint32_t*>(&b2);
+				}
+				const int panel = c16 >> 3, chunk = (c16 & 7) ^ (r & 7);
+				*reinterpret_cast<uint4*>(prow + panel * PANEL + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+			}
+			asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+			tc_fence_before();
+			mbar_arrive(p_full);
+		}
+		// the output: O / l, once the last P V is done
+		if (ok && n_tiles > 0)
+			ok = mbar_wait_bounded(pv_done, (uint32_t)((n_tiles - 1) & 1), P.err, DEVERR_WAIT_FULL);
+		ok = __all_sync(0xffffffffu, ok);
+		if (ok)
+		{
+			tc_fence_after();
+			const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+			const bool row_ok = q0 + r < P.n_tok;
+			float* orow = P.out + ((size_t)(q0 + r) * P.n_head + h) * PF_D;
+#pragma unroll
+			for (int c = 0; c < PF_D / 32; ++c)
+			{
+				float o[32];
+				tmem_ld32(TO + lane_off + c * 32, o);
+				tmem_wait_ld();
+				if (row_ok)
+				{
+#pragma unroll
+					for (int i = 0; i < 32; i += 4)
+						*reinterpret_cast<float4*>(orow + c * 32 + i) =
+							make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+				}
+			}
+		}
+	}
+	tc_fence_before();
+	__syncthreads();
+	if (warp == 1)
+	{
+		tc_fence_after();
+		asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+	}
+}
+
+// The query rows of a prefill, in the tensor-core kernel's operand form:
+// RMSNorm with the gains and RoPE at each token's position (model.cpp:
+// 1616-1660, as the decode kernel does in its slots), rounded to bf16 and
+// laid out head-major, [n_head][n_tok][128]. A warp per (token, head).
+__global__ void __launch_bounds__(256) prefill_q_kernel(const __grid_constant__ DevJob j, __nv_bfloat16* qb)
+{
+	__shared__ float bufs[8][PF_D];
+	__shared__ float s_g[PF_D], s_inv[PF_D / 2], s_ff[PF_D / 2];
+	const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const int h = blockIdx.y * 8 + warp;
+	const int half = j.n_rot / 2;
+	HeadRegs x;
+	if (h < j.n_head) load_head(x, j.q + ((size_t)t * j.n_head + h) * PF_D, PF_D);
+	for (int i = threadIdx.x; i < PF_D; i += blockDim.x)
+	{
+		s_g[i] = j.q_gamma ? j.q_gamma[i] : 0.0f;
+		if (i < PF_D / 2)
+		{
+			s_inv[i] = i < half ? j.rope_inv[i] : 0.0f;
+			s_ff[i] = (j.freq_factors && i < half) ? j.freq_factors[i] : 0.0f;
+		}
+	}
+	__syncthreads();
+	if (h >= j.n_head) return;
+	float* buf = bufs[warp];
+	prep_head(buf, x, PF_D, j.q_gamma ? s_g : nullptr, false, j.eps, true, j.n_rot, j.rope_mode,
+	          (float)(j.pos0 + t) * j.rope_scale, s_inv, j.freq_factors ? s_ff : nullptr);
+	__nv_bfloat16* dst = qb + ((size_t)h * j.n_tok + t) * PF_D;
+	for (int i = lane; i < PF_D; i += 32) dst[i] = __float2bfloat16_rn(buf[i]);
+}
+
+// A 3-D tensor map over a head-major bf16 array [z][y][128] with a
+// 64 x 128 x 1 box, 128-byte swizzled (the kernels' operand layout).
+int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads)
+{
+	const cuuint64_t dims[3] = {(cuuint64_t)PF_D, (cuuint64_t)rows, (cuuint64_t)heads};
+	const cuuint64_t strides[2] = {(cuuint64_t)PF_D * 2, (cuuint64_t)rows * PF_D * 2};
+	const cuuint32_t box[3] = {64, 128, 1};
+	const cuuint32_t estr[3] = {1, 1, 1};
+	// the driver's encoder, looked up through the runtime (the library loads
+	// without the driver library present, e.g. for its CPU-side checks)
+	using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+	                            const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+	                            CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+	static Encode encode = nullptr;
+	if (!encode)
+	{
+		void* fn = nullptr;
+		cudaDriverEntryPointQueryResult q;
+		if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+		    q != cudaDriverEntryPointSuccess || !fn)
+			return (int)cudaErrorNotSupported;
+		encode = reinterpret_cast<Encode>(fn);
+	}
+	const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+	                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+	                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+	return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
+} // namespace
+
+bool prefill_supported(int D, int kv_type) { return D == PF_D && kv_type == KV_BF16; }
+
+size_t prefill_qbuf_bytes(int n_tok, int n_head) { return (size_t)n_head * n_tok * PF_D * 2; }
+
+int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream)
+{
+	if (j.D != PF_D || j.n_tok <= 0 || j.n_head % j.n_kv) return (int)cudaErrorInvalidValue;
+	auto st = static_cast<cudaStream_t>(stream);
+	CUtensorMap qmap, kmap, vmap;
+	int e = make_map(&qmap, qbuf, (uint64_t)j.n_tok, (uint64_t)j.n_head);
+	if (!e) e = make_map(&kmap, j.K, (uint64_t)j.rows, (uint64_t)j.n_kv);
+	if (!e) e = make_map(&vmap, j.V, (uint64_t)j.rows, (uint64_t)j.n_kv);
+	if (e) return e;
+	prefill_q_kernel<<<dim3((unsigned)j.n_tok, (unsigned)((j.n_head + 7) / 8)), 256, 0, st>>>(
+		j, static_cast<__nv_bfloat16*>(qbuf));
+	cudaError_t ce = cudaGetLastError();
+	if (ce != cudaSuccess) return (int)ce;
+	static bool configured[64] = {};
+	int dev = 0;
+	cudaGetDevice(&dev);
+	if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+	if (!configured[dev])
+	{
+		ce = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
+		if (ce != cudaSuccess) return (int)ce;
+		configured[dev] = true;
+	}
+	PrefillPlan P{};
+	P.n_tok = j.n_tok;
+	P.pos0 = j.pos0;
+	P.n_seq = j.n_seq;
+	P.n_head = j.n_head;
+	P.n_kv = j.n_kv;
+	P.window = j.window;
+	P.q_tiles = (j.n_tok + PF_BM - 1) / PF_BM;
+	P.scale = j.scale;
+	P.log2e = 1.4426950408889634f;
+	P.softcap = j.softcap;
+	P.out = j.out;
+	P.err = err;
+	prefill_kernel<<<(unsigned)(P.q_tiles * j.n_head), PF_THREADS, PF_SMEM, st>>>(qmap, kmap, vmap, P);
+	return (int)cudaGetLastError();
+}
+
+} // namespace nncu

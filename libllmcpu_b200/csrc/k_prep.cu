@@ -21,8 +21,9 @@ namespace
 constexpr int PREP_WARPS = 8;
 constexpr int PREP_MAX_D = 512;
 
+// Token t of job j (one CTA).
 template <typename KV>
-__global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __restrict__ jobs)
+__device__ __forceinline__ void prep_token(const DevJob& j, int t)
 {
 	using T = typename KV::T;
 	// The attention kernel that follows may start now: it streams the K/V
@@ -32,8 +33,6 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __r
 	__shared__ float bufs[PREP_WARPS][PREP_MAX_D];
 	__shared__ float s_kg[PREP_MAX_D], s_inv[PREP_MAX_D / 2], s_ff[PREP_MAX_D / 2];
 	// block (t, job): token t of job blockIdx.y
-	const DevJob& j = jobs[blockIdx.y];
-	const int t = blockIdx.x;
 	if (t >= j.n_tok || j.pos0 + t < j.key_lo || j.pos0 + t >= j.key_hi) return; // not this launch's row
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int D = j.D, half = j.n_rot / 2;
@@ -77,6 +76,19 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __r
 		for (int i = lane; i < D; i += 32) store_elem(dst + i, buf[i]);
 		__syncwarp();
 	}
+}
+
+template <typename KV>
+__global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __restrict__ jobs)
+{
+	prep_token<KV>(jobs[blockIdx.y], blockIdx.x); // block (t, job)
+}
+
+// One job passed by value (the tensor-core prefill's append: no job table).
+template <typename KV>
+__global__ void __launch_bounds__(PREP_WARPS * 32) prep_one_kernel(const __grid_constant__ DevJob j)
+{
+	prep_token<KV>(j, blockIdx.x);
 }
 
 // ---- unit seam ---------------------------------------------------------------
@@ -132,6 +144,20 @@ int launch_prep(const DecodePlan& P, void* stream)
 	case KV_F32: prep_kernel<kv_f32><<<grid, PREP_WARPS * 32, 0, st>>>(P.jobs); break;
 	case KV_BF16: prep_kernel<kv_bf16><<<grid, PREP_WARPS * 32, 0, st>>>(P.jobs); break;
 	default: prep_kernel<kv_f16><<<grid, PREP_WARPS * 32, 0, st>>>(P.jobs); break;
+	}
+	return (int)cudaGetLastError();
+}
+
+int launch_prep_one(const DevJob& j, int kv_type, void* stream)
+{
+	if (j.D > PREP_MAX_D) return (int)cudaErrorInvalidValue;
+	if (j.n_tok <= 0) return 0;
+	auto st = static_cast<cudaStream_t>(stream);
+	switch (kv_type)
+	{
+	case KV_F32: prep_one_kernel<kv_f32><<<(unsigned)j.n_tok, PREP_WARPS * 32, 0, st>>>(j); break;
+	case KV_BF16: prep_one_kernel<kv_bf16><<<(unsigned)j.n_tok, PREP_WARPS * 32, 0, st>>>(j); break;
+	default: prep_one_kernel<kv_f16><<<(unsigned)j.n_tok, PREP_WARPS * 32, 0, st>>>(j); break;
 	}
 	return (int)cudaGetLastError();
 }
