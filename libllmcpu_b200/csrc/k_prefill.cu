@@ -307,16 +307,35 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			tc_fence_before();
 			mbar_arrive(&s_empty[s]);
 			const int key0 = (j_lo + jj) * PF_BN;
-			float mx = -CUDART_INF_F;
-#pragma unroll
-			for (int c = 0; c < PF_BN; ++c)
+			// scores in log2 units (the soft-cap, when there is one, in its own
+			// loop: a select would evaluate tanh for every score)
+			if (P.softcap > 0.0f)
 			{
-				float v = P.softcap > 0.0f ? P.softcap * tanhf(x[c] * P.scale / P.softcap) * P.log2e
-				                            : x[c] * P.scale * P.log2e;
-				const int kp = key0 + c;
-				if (kp < kf || kp > kl) v = -CUDART_INF_F;
-				x[c] = v;
-				mx = fmaxf(mx, v);
+				const float cs = P.scale / P.softcap, cl = P.softcap * P.log2e;
+#pragma unroll
+				for (int c = 0; c < PF_BN; ++c) x[c] = tanhf(x[c] * cs) * cl;
+			}
+			else
+			{
+				const float sl = P.scale * P.log2e;
+#pragma unroll
+				for (int c = 0; c < PF_BN; ++c) x[c] *= sl;
+			}
+			float mx = -CUDART_INF_F;
+			if (key0 >= kf && key0 + PF_BN - 1 <= kl)
+			{
+#pragma unroll
+				for (int c = 0; c < PF_BN; ++c) mx = fmaxf(mx, x[c]);
+			}
+			else
+			{
+#pragma unroll
+				for (int c = 0; c < PF_BN; ++c)
+				{
+					const int kp = key0 + c;
+					if (kp < kf || kp > kl) x[c] = -CUDART_INF_F;
+					mx = fmaxf(mx, x[c]);
+				}
 			}
 			// the row's reference maximum moves only when a score exceeds it by
 			// more than 2^LAZY; then O (in TMEM) and l are rescaled
