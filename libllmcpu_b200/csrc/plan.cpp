@@ -95,29 +95,32 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 			fused = 0;
 	}
 
-	// chunks: each segment in ceil(n_tiles / C) equal runs, C the tiles per SM
+	// chunks: each segment in ceil(n_tiles / C) equal runs of whole tiles
 	const int ctas_max = std::max(1, std::min(num_sms, max_starts));
-	const long long C = total > 0 ? (total + ctas_max - 1) / ctas_max : 1;
 	long long parts = 0, max_chunk = 1;
-	for (int i = 0; i < n; ++i)
-	{
-		DevJob& j = jobs[i];
-		if (j.n_tiles == 0)
+	auto cut = [&](long long C) {
+		parts = 0;
+		max_chunk = 1;
+		for (int i = 0; i < n; ++i)
 		{
-			j.chunk = 1;
-			j.n_chunks = 0;
-			j.part0 = 0;
-			continue;
+			DevJob& j = jobs[i];
+			if (j.n_tiles == 0)
+			{
+				j.chunk = 1;
+				j.n_chunks = 0;
+				j.part0 = 0;
+				continue;
+			}
+			const int k = (int)((j.n_tiles + C - 1) / C);
+			j.chunk = (j.n_tiles + k - 1) / k;
+			j.n_chunks = (j.n_tiles + j.chunk - 1) / j.chunk;
+			j.part0 = (int)parts;
+			if (j.n_chunks > 1) parts += (long long)j.n_kv * j.n_rowgroups * j.n_chunks;
+			max_chunk = std::max<long long>(max_chunk, j.chunk);
 		}
-		int k = (int)((j.n_tiles + C - 1) / C);
-		j.chunk = (j.n_tiles + k - 1) / k;
-		j.n_chunks = (j.n_tiles + j.chunk - 1) / j.chunk;
-		j.part0 = (int)parts;
-		if (j.n_chunks > 1) parts += (long long)j.n_kv * j.n_rowgroups * j.n_chunks;
-		max_chunk = std::max<long long>(max_chunk, j.chunk);
-	}
+	};
 
-	// CTAs: runs of consecutive chunks of at most `cap` tiles, as few as fit
+	// CTAs: runs of consecutive chunks of at most `cap` tiles
 	auto pack = [&](long long cap, bool write) -> long long {
 		long long ctas = 0, cur = 0;
 		for (int i = 0; i < n; ++i)
@@ -144,9 +147,17 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 		}
 		return cur > 0 ? ctas + 1 : ctas;
 	};
-	long long cap = std::max(C, max_chunk);
-	while (pack(cap, false) > ctas_max) cap += std::max<long long>(1, cap / 32);
-	const long long n_ctas = pack(cap, true);
+	// the smallest chunk target C (from the tiles per SM up) whose chunks pack
+	// into the SMs with runs of at most max(C, largest chunk) tiles: growing
+	// C, not the runs, keeps a run from holding two big chunks
+	long long C = total > 0 ? (total + ctas_max - 1) / ctas_max : 1;
+	for (;;)
+	{
+		cut(C);
+		if (pack(std::max(C, max_chunk), false) <= ctas_max) break;
+		C += std::max<long long>(1, C / 64);
+	}
+	const long long n_ctas = pack(std::max(C, max_chunk), true);
 	if (n_ctas > max_starts) return set_error(NNCU_ERR_INVALID_ARGUMENT, "decode plan: too many CTAs");
 
 	// each CTA's first tiles, issued before it reads its job: a contiguous run
