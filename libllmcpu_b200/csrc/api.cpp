@@ -808,8 +808,8 @@ void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 // Launch K1 and K2 for jobs whose DevJob pointers are all device pointers,
 // on `st`.
 // A long causal batch on a bf16 cache of head_dim 128 (a prefill) runs on
-// the tensor cores: K1 appends its rows, then the q rows' norm and RoPE and
-// the attention of every row (k_prefill.cu).
+// the tensor cores: one kernel does every head's norm and RoPE and appends
+// the k, v rows, then the attention of every row (k_prefill.cu).
 bool prefill_eligible(const nncu_kv* kv, const DevJob& j, const nncu_attn_job& pub)
 {
 	const Buffer& b = kv->bufs[kv->kv_buf[pub.layer]];
@@ -826,9 +826,9 @@ int run_prefill(nncu_kv* kv, const DevJob& j, cudaStream_t st)
 	int e = 0;
 	{
 		PerfScope ps(NNCU_PERF_ATTN_ROPE, kvb * (8 + 2 * es) + (uint64_t)j.n_tok * j.n_head * j.D * 6, st);
-		e = j.reuse_kv ? 0 : launch_prep_one(j, kv->kv_type, st);
+		e = launch_prefill_prep(j, kv->qbuf.p, st);
 	}
-	if (e) return cuda_fail((cudaError_t)e, "K1 (norm, RoPE, append) launch");
+	if (e) return cuda_fail((cudaError_t)e, "prefill norm, RoPE, append launch");
 	{
 		PerfScope ps(NNCU_PERF_ATTN_CORE,
 		             keys * j.n_kv * j.D * es * 2 + (uint64_t)j.n_tok * j.n_head * j.D * (2 + 4), st);

@@ -389,6 +389,23 @@ __device__ __forceinline__ void rope_vec(float* buf, int n_rot, int mode, float 
 	}
 }
 
+// The same rotation with the angles' cosines and sines computed beforehand
+// (cs[i], sn[i] for pair i, as rope_vec forms them): the table depends only on
+// the token's position, so one table serves every head of the token.
+__device__ __forceinline__ void rope_apply(float* buf, int n_rot, int mode, const float* cs, const float* sn)
+{
+	const int half = n_rot / 2;
+	const int step = mode == 0 ? 1 : 2;
+	const int other = mode == 0 ? half : 1;
+	for (int i = threadIdx.x & 31; i < half; i += 32)
+	{
+		float* p = buf + i * step;
+		const float a = p[0], b = p[other];
+		p[0] = cs[i] * a - sn[i] * b;
+		p[other] = sn[i] * a + cs[i] * b;
+	}
+}
+
 // A head vector of up to 512 floats held by a warp, lane-strided: element
 // lane + 32 k in slot k. Loading all of it into registers before writing any
 // of it to shared memory lets the loads overlap (through generic pointers the

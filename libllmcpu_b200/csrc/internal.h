@@ -131,9 +131,10 @@ struct PrefillPlan
 };
 bool prefill_supported(int D, int kv_type);
 size_t prefill_qbuf_bytes(int n_tok, int n_head);
-// The q rows' norm + RoPE into `qbuf` (bf16, head-major), then the attention
-// of every row over its causal span into j.out; the cache already holds the
-// new rows (K1). j is the host copy of the job.
+// The prefill's per-head work: q rows normed and rotated into `qbuf` (bf16,
+// head-major), k and v rows appended to the cache. j is the host copy of the job.
+int launch_prefill_prep(const DevJob& j, void* qbuf, void* stream);
+// The attention of every row over its causal span into j.out (after the prep).
 int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream);
 
 // Record a failure for nncu_last_error() (api.cpp); return `status`.
@@ -142,7 +143,6 @@ int set_cuda_error(int cuda_status, const char* what);
 
 // Launchers (implemented in the .cu files). Each returns a cudaError_t value.
 int launch_prep(const DecodePlan& plan, void* stream);
-int launch_prep_one(const DevJob& job, int kv_type, void* stream); // K1 for one job passed by value
 int launch_decode(const DecodePlan& plan, void* stream);
 int launch_split_wait(const DecodePlan& plan, void* stream); // a split call's end: this GPU's rows merged
 

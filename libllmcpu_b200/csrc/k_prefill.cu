@@ -11,14 +11,16 @@
 //   P = softmax    4 warps, one query row per thread, read from TMEM
 //   O += P V       tcgen05.mma, P (bf16) from shared memory, O in TMEM
 //
-// Roles: warp 0 issues the TMA loads (Q once, then K and V tiles into a
-// 2-stage ring); warp 1 owns the TMEM allocation and, from one lane, issues
-// the MMAs (S into two TMEM buffers in turn, so the next tile's S is computed
-// while this tile's softmax runs); warps 4-7 do the softmax, keep O in scale
-// and write the output. Online softmax in base 2 with a lazily moved maximum:
-// a row's reference maximum moves (and O and l are rescaled) only when a new
-// score exceeds it by more than 2^8, so O is rarely touched; the result is
-// the same softmax, divided by the same l.
+// Roles: warps 0 and 2 issue the TMA loads (Q once and the K tiles; the V
+// tiles), each into its own 2-stage ring, K free again as soon as its S is
+// done; warp 1 owns the TMEM allocation and, from one lane, issues the MMAs
+// (S into two TMEM buffers in turn, so the next tile's S is computed while
+// this tile's softmax runs); warps 4-11 do the softmax, two threads per query
+// row (64 columns each, the row maximum exchanged through shared memory),
+// keep O in scale and write the output. Online softmax in base 2 with a
+// lazily moved maximum: a row's reference maximum moves (and O and l are
+// rescaled) only when a new score exceeds it by more than 2^8, so O is rarely
+// touched; the result is the same softmax, divided by the same l.
 //
 // Operands in shared memory use the 128-byte swizzled K-major layout TMA
 // writes (8-row atoms of 1 KB), described to tcgen05.mma by shared memory
@@ -41,14 +43,15 @@ namespace
 constexpr int PF_BM = 128;                      // query rows per CTA
 constexpr int PF_BN = 128;                      // keys per tile
 constexpr int PF_D = 128;                       // head_dim
-constexpr int PF_THREADS = 256;                 // 8 warps
+constexpr int PF_THREADS = 384;                 // 12 warps
 constexpr int PANEL = 128 * 128;                // 128 rows x 64 bf16: one 128-byte-swizzled panel
 constexpr int TILE = 2 * PANEL;                 // 128 rows x 128 bf16
-constexpr int KV_STAGES = 2;
 constexpr int SM_Q = 0;                         // Q tile
-constexpr int SM_KV = SM_Q + TILE;              // [stage][K tile, V tile]
-constexpr int SM_P = SM_KV + KV_STAGES * 2 * TILE; // P tile
-constexpr int SM_BAR = SM_P + TILE;             // barriers, TMEM address
+constexpr int SM_K = SM_Q + TILE;               // [2] K tiles
+constexpr int SM_V = SM_K + 2 * TILE;           // [2] V tiles
+constexpr int SM_P = SM_V + 2 * TILE;           // P tile
+constexpr int SM_RED = SM_P + TILE;             // [2 tiles][2 halves][128 rows] row maxima, then [2][128] row sums
+constexpr int SM_BAR = SM_RED + 4 * 128 * 4;    // barriers, TMEM address
 constexpr int PF_SMEM = SM_BAR + 256 + 1024;    // + alignment slack
 constexpr int TMEM_COLS = 512;                  // S0, S1, O (128 columns each)
 constexpr float LAZY = 8.0f;                    // log2 headroom before the row maximum moves
@@ -151,15 +154,17 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 		reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 	uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
 	uint64_t* q_full = bars + 0;
-	uint64_t* kv_full = bars + 1;  // [2]
-	uint64_t* kv_empty = bars + 3; // [2]
-	uint64_t* s_full = bars + 5;   // [2]
-	uint64_t* s_empty = bars + 7;  // [2]
-	uint64_t* p_full = bars + 9;
-	uint64_t* pv_done = bars + 10;
-	uint64_t* mma_done = bars + 11;
-	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-	volatile int* flags = reinterpret_cast<volatile int*>(bars + 13); // [0] abort
+	uint64_t* k_full = bars + 1;   // [2]
+	uint64_t* k_empty = bars + 3;  // [2]: K_j no longer needed once S_j is done
+	uint64_t* v_full = bars + 5;   // [2]
+	uint64_t* v_empty = bars + 7;  // [2]: V_j no longer needed once P_j V_j is done
+	uint64_t* s_full = bars + 9;   // [2]
+	uint64_t* s_empty = bars + 11; // [2]
+	uint64_t* p_full = bars + 13;
+	uint64_t* pv_done = bars + 14;
+	uint64_t* mma_done = bars + 16;
+	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+	volatile int* flags = reinterpret_cast<volatile int*>(bars + 18); // [0] abort
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	// the heaviest query tiles (the longest causal spans) go first
@@ -177,12 +182,14 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 		mbar_init(q_full, 1);
 		for (int s = 0; s < 2; ++s)
 		{
-			mbar_init(&kv_full[s], 1);
-			mbar_init(&kv_empty[s], 1);
+			mbar_init(&k_full[s], 1);
+			mbar_init(&k_empty[s], 1);
+			mbar_init(&v_full[s], 1);
+			mbar_init(&v_empty[s], 1);
 			mbar_init(&s_full[s], 1);
-			mbar_init(&s_empty[s], 128);
+			mbar_init(&s_empty[s], 256);
 		}
-		mbar_init(p_full, 128);
+		mbar_init(p_full, 256);
 		mbar_init(pv_done, 1);
 		mbar_init(mma_done, 1);
 		flags[0] = 0;
@@ -202,39 +209,45 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 	const uint32_t TS[2] = {tmem, tmem + 128};
 	const uint32_t TO = tmem + 256;
 
-	if (warp == 0)
+	if (warp == 0 || warp == 2)
 	{
-		// ---- TMA: Q once, then the K and V tiles through the 2-stage ring ----
+		// ---- TMA: warp 0 Q once, then the K tiles; warp 2 the V tiles; each
+		// through its own 2-stage ring (K is free again as soon as S is done) ----
 		if (lane == 0)
 		{
-			mbar_arrive_expect_tx(q_full, TILE);
-			tma3(smem + SM_Q, &qmap, 0, q0, h, q_full);
-			tma3(smem + SM_Q + PANEL, &qmap, 64, q0, h, q_full);
+			const bool is_k = warp == 0;
+			const CUtensorMap* map = is_k ? &kmap : &vmap;
+			uint64_t* full = is_k ? k_full : v_full;
+			uint64_t* empty = is_k ? k_empty : v_empty;
+			unsigned char* ring = smem + (is_k ? SM_K : SM_V);
+			if (is_k)
+			{
+				mbar_arrive_expect_tx(q_full, TILE);
+				tma3(smem + SM_Q, &qmap, 0, q0, h, q_full);
+				tma3(smem + SM_Q + PANEL, &qmap, 64, q0, h, q_full);
+			}
 			int issued = 0;
 			for (int jj = 0; jj < n_tiles; ++jj)
 			{
 				const int s = jj & 1;
-				if (jj >= 2 && !mbar_wait_bounded(&kv_empty[s], (uint32_t)(((jj >> 1) - 1) & 1), P.err,
-				                                  DEVERR_WAIT_EMPTY))
+				if (jj >= 2 &&
+				    !mbar_wait_bounded(&empty[s], (uint32_t)(((jj >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
 				{
 					flags[0] = 1;
 					break;
 				}
 				if (flags[0]) break;
-				unsigned char* kt = smem + SM_KV + s * 2 * TILE;
-				unsigned char* vt = kt + TILE;
+				unsigned char* t = ring + s * TILE;
 				const int key0 = (j_lo + jj) * PF_BN;
-				mbar_arrive_expect_tx(&kv_full[s], 2 * TILE);
-				tma3(kt, &kmap, 0, key0, hk, &kv_full[s]);
-				tma3(kt + PANEL, &kmap, 64, key0, hk, &kv_full[s]);
-				tma3(vt, &vmap, 0, key0, hk, &kv_full[s]);
-				tma3(vt + PANEL, &vmap, 64, key0, hk, &kv_full[s]);
+				mbar_arrive_expect_tx(&full[s], TILE);
+				tma3(t, map, 0, key0, hk, &full[s]);
+				tma3(t + PANEL, map, 64, key0, hk, &full[s]);
 				issued = jj + 1;
 			}
 			// on an abort, do not leave while a copy may still land here
-			mbar_wait_bounded(q_full, 0, nullptr, 0);
+			if (is_k) mbar_wait_bounded(q_full, 0, nullptr, 0);
 			for (int jj = max(0, issued - 2); jj < issued; ++jj)
-				mbar_wait_bounded(&kv_full[jj & 1], (uint32_t)((jj >> 1) & 1), nullptr, 0);
+				mbar_wait_bounded(&full[jj & 1], (uint32_t)((jj >> 1) & 1), nullptr, 0);
 		}
 	}
 	else if (warp == 1)
@@ -243,35 +256,39 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 		if (lane == 0)
 		{
 			constexpr uint32_t ID_QK = idesc(false), ID_PV = idesc(true);
-			const uint32_t qa = smem_u32(smem + SM_Q), pa = smem_u32(smem + SM_P);
+			const uint32_t qa = smem_u32(smem + SM_Q), pa0 = smem_u32(smem + SM_P);
 			bool ok = mbar_wait_bounded(q_full, 0, P.err, DEVERR_WAIT_FULL);
 			auto issue_pv = [&](int jj) -> bool {
-				if (!mbar_wait_bounded(p_full, (uint32_t)(jj & 1), P.err, DEVERR_WAIT_FULL)) return false;
+				if (!mbar_wait_bounded(p_full, (uint32_t)(jj & 1), P.err, DEVERR_WAIT_FULL) ||
+				    !mbar_wait_bounded(&v_full[jj & 1], (uint32_t)((jj >> 1) & 1), P.err, DEVERR_WAIT_FULL))
+					return false;
 				tc_fence_after();
-				const uint32_t va = smem_u32(smem + SM_KV + (jj & 1) * 2 * TILE + TILE);
+				const uint32_t va = smem_u32(smem + SM_V + (jj & 1) * TILE);
+				const uint32_t pa = pa0;
 #pragma unroll
 				for (int k = 0; k < PF_BN / 16; ++k)
 					mma_f16(TO, sdesc(pa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024), sdesc(va + k * 2048, PANEL, 1024),
 					        ID_PV, (jj > 0 || k > 0) ? 1u : 0u);
 				mma_commit(pv_done);
-				mma_commit(&kv_empty[jj & 1]);
+				mma_commit(&v_empty[jj & 1]);
 				return true;
 			};
 			int jj = 0;
 			for (; ok && jj < n_tiles; ++jj)
 			{
 				const int s = jj & 1;
-				ok = !flags[0] && mbar_wait_bounded(&kv_full[s], (uint32_t)((jj >> 1) & 1), P.err, DEVERR_WAIT_FULL);
+				ok = !flags[0] && mbar_wait_bounded(&k_full[s], (uint32_t)((jj >> 1) & 1), P.err, DEVERR_WAIT_FULL);
 				if (ok && jj >= 2)
 					ok = mbar_wait_bounded(&s_empty[s], (uint32_t)(((jj >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY);
 				if (!ok) break;
 				tc_fence_after();
-				const uint32_t ka = smem_u32(smem + SM_KV + s * 2 * TILE);
+				const uint32_t ka = smem_u32(smem + SM_K + s * TILE);
 #pragma unroll
 				for (int k = 0; k < PF_D / 16; ++k)
 					mma_f16(TS[s], sdesc(qa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
 					        sdesc(ka + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024), ID_QK, k > 0 ? 1u : 0u);
 				mma_commit(&s_full[s]);
+				mma_commit(&k_empty[s]);
 				if (jj >= 1) ok = issue_pv(jj - 1);
 			}
 			if (ok && n_tiles > 0) ok = issue_pv(n_tiles - 1);
@@ -283,16 +300,22 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 	}
 	else if (warp >= 4)
 	{
-		// ---- softmax, O in scale, output: one query row per thread ----
-		const int wq = warp & 3; // TMEM lanes 32 wq .. 32 wq + 31
+		// ---- softmax, O in scale, output: two threads per query row (warps
+		// 4-7 take its columns 0-63, warps 8-11 columns 64-127; a warp reaches
+		// TMEM lanes 32 (warp % 4) .. +31), the row maximum shared through
+		// shared memory by the pair of warps on the same lanes ----
+		const int wq = warp & 3;
+		const int hf = (warp >> 2) - 1; // column half
 		const int r = wq * 32 + lane;
 		const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+		const uint32_t col0 = (uint32_t)(hf * 64);
 		const int qp = P.pos0 + q0 + r;
 		const int kf = (P.window > 0 && qp + 1 > P.window) ? qp + 1 - P.window : 0;
 		const int kl = min(qp, P.n_seq - 1);
+		float* red = reinterpret_cast<float*>(smem + SM_RED); // maxima [2][2][128], then sums [2][128]
 		float m_used = -CUDART_INF_F, l = 0.0f;
 		bool ok = true;
-		unsigned char* prow = smem + SM_P + r * 128;
+		unsigned char* prow = smem + SM_P + hf * PANEL + r * 128;
 		for (int jj = 0; jj < n_tiles; ++jj)
 		{
 			const int s = jj & 1;
@@ -300,52 +323,63 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			ok = __all_sync(0xffffffffu, ok);
 			if (!ok) break;
 			tc_fence_after();
-			float x[PF_BN];
-#pragma unroll
-			for (int c = 0; c < PF_BN / 32; ++c) tmem_ld32(TS[s] + lane_off + c * 32, x + 32 * c);
+			float x[64];
+			tmem_ld32(TS[s] + lane_off + col0, x);
+			tmem_ld32(TS[s] + lane_off + col0 + 32, x + 32);
 			tmem_wait_ld();
 			tc_fence_before();
 			mbar_arrive(&s_empty[s]);
-			const int key0 = (j_lo + jj) * PF_BN;
+			const int key0 = (j_lo + jj) * PF_BN + hf * 64;
 			// scores in log2 units (the soft-cap, when there is one, in its own
-			// loop: a select would evaluate tanh for every score)
+			// loop: a select would evaluate tanh for every score), the span mask
+			// only on tiles that cross the span's ends
 			if (P.softcap > 0.0f)
 			{
 				const float cs = P.scale / P.softcap, cl = P.softcap * P.log2e;
 #pragma unroll
-				for (int c = 0; c < PF_BN; ++c) x[c] = tanhf(x[c] * cs) * cl;
+				for (int c = 0; c < 64; ++c) x[c] = tanhf(x[c] * cs) * cl;
 			}
 			else
 			{
 				const float sl = P.scale * P.log2e;
 #pragma unroll
-				for (int c = 0; c < PF_BN; ++c) x[c] *= sl;
+				for (int c = 0; c < 64; ++c) x[c] *= sl;
 			}
-			float mx = -CUDART_INF_F;
-			if (key0 >= kf && key0 + PF_BN - 1 <= kl)
+			if (key0 < kf || key0 + 63 > kl)
 			{
 #pragma unroll
-				for (int c = 0; c < PF_BN; ++c) mx = fmaxf(mx, x[c]);
+				for (int c = 0; c < 64; ++c)
+					if (key0 + c < kf || key0 + c > kl) x[c] = -CUDART_INF_F;
 			}
-			else
-			{
+			float mq[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F}; // four chains
 #pragma unroll
-				for (int c = 0; c < PF_BN; ++c)
-				{
-					const int kp = key0 + c;
-					if (kp < kf || kp > kl) x[c] = -CUDART_INF_F;
-					mx = fmaxf(mx, x[c]);
-				}
-			}
+			for (int c = 0; c < 64; ++c) mq[c & 3] = fmaxf(mq[c & 3], x[c]);
+			float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+			float* mxs = red + s * 256;
+			mxs[hf * 128 + r] = mx;
+			named_sync(2 + wq, 64); // the two warps on these TMEM lanes
+			mx = fmaxf(mx, mxs[(hf ^ 1) * 128 + r]);
 			// the row's reference maximum moves only when a score exceeds it by
 			// more than 2^LAZY; then O (in TMEM) and l are rescaled
 			const bool move = mx > m_used + LAZY;
 			const float m_new = move ? mx : m_used;
 			const float alpha = (move && m_used != -CUDART_INF_F) ? ex2(m_used - m_new) : 1.0f;
 			const bool rescale = move && m_used != -CUDART_INF_F;
+			const float m_ref = m_new == -CUDART_INF_F ? 0.0f : m_new; // a row with no key yet: all p are 0
+			// P (bf16) in registers first, then into the P tile once the previous
+			// P V has read it
+			uint32_t pk[32];
+			float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+			for (int c = 0; c < 64; c += 2)
+			{
+				const float p0 = ex2(x[c] - m_ref), p1 = ex2(x[c + 1] - m_ref); // a masked score (-inf) gives 0
+				ls[(c >> 1) & 3] += p0 + p1;
+				__nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
+				pk[c >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+			}
 			if (jj > 0)
 			{
-				// O is stable and the P buffer free once P_{j-1} V_{j-1} is done
 				ok = mbar_wait_bounded(pv_done, (uint32_t)((jj - 1) & 1), P.err, DEVERR_WAIT_FULL);
 				ok = __all_sync(0xffffffffu, ok);
 				if (!ok) break;
@@ -353,61 +387,49 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 				if (__any_sync(0xffffffffu, rescale))
 				{
 #pragma unroll
-					for (int c = 0; c < PF_D / 32; ++c)
+					for (int c = 0; c < 2; ++c)
 					{
 						float o[32];
-						tmem_ld32(TO + lane_off + c * 32, o);
+						tmem_ld32(TO + lane_off + col0 + c * 32, o);
 						tmem_wait_ld();
 #pragma unroll
 						for (int i = 0; i < 32; ++i) o[i] *= alpha;
-						tmem_st32(TO + lane_off + c * 32, o);
+						tmem_st32(TO + lane_off + col0 + c * 32, o);
 					}
 					tmem_wait_st();
 				}
 			}
-			l *= alpha;
-			m_used = m_new;
-			// P (bf16) into this thread's row, in the 128-byte swizzled layout
 #pragma unroll
-			for (int c16 = 0; c16 < PF_BN / 8; ++c16)
+			for (int c16 = 0; c16 < 8; ++c16)
 			{
-				float p[8];
-#pragma unroll
-				for (int i = 0; i < 8; ++i)
-				{
-					const float v = x[c16 * 8 + i];
-					p[i] = v == -CUDART_INF_F ? 0.0f : ex2(v - m_used);
-					l += p[i];
-				}
-				uint32_t w[4];
-#pragma unroll
-				for (int i = 0; i < 4; ++i)
-				{
-					__nv_bfloat162 b2 = __floats2bfloat162_rn(p[2 * i], p[2 * i + 1]);
-					w[i] = *reinterpret_cast<uint32_t*>(&b2);
-				}
-				const int panel = c16 >> 3, chunk = (c16 & 7) ^ (r & 7);
-				*reinterpret_cast<uint4*>(prow + panel * PANEL + chunk * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+				const int chunk = c16 ^ (r & 7);
+				*reinterpret_cast<uint4*>(prow + chunk * 16) =
+					make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
 			}
+			l = fmaf(l, alpha, (ls[0] + ls[1]) + (ls[2] + ls[3]));
+			m_used = m_new;
 			asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 			tc_fence_before();
 			mbar_arrive(p_full);
 		}
-		// the output: O / l, once the last P V is done
-		if (ok && n_tiles > 0)
-			ok = mbar_wait_bounded(pv_done, (uint32_t)((n_tiles - 1) & 1), P.err, DEVERR_WAIT_FULL);
+		// the output: O / l, once the last P V is done (l: the two halves' sums)
+		if (ok && n_tiles > 0) ok = mbar_wait_bounded(pv_done, (uint32_t)((n_tiles - 1) & 1), P.err, DEVERR_WAIT_FULL);
 		ok = __all_sync(0xffffffffu, ok);
+		float* sums = red + 512;
+		sums[hf * 128 + r] = l;
+		named_sync(2 + wq, 64);
+		l += sums[(hf ^ 1) * 128 + r];
 		if (ok)
 		{
 			tc_fence_after();
 			const float inv = l > 0.0f ? 1.0f / l : 0.0f;
 			const bool row_ok = q0 + r < P.n_tok;
-			float* orow = P.out + ((size_t)(q0 + r) * P.n_head + h) * PF_D;
+			float* orow = P.out + ((size_t)(q0 + r) * P.n_head + h) * PF_D + col0;
 #pragma unroll
-			for (int c = 0; c < PF_D / 32; ++c)
+			for (int c = 0; c < 2; ++c)
 			{
 				float o[32];
-				tmem_ld32(TO + lane_off + c * 32, o);
+				tmem_ld32(TO + lane_off + col0 + c * 32, o);
 				tmem_wait_ld();
 				if (row_ok)
 				{
@@ -428,35 +450,71 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 	}
 }
 
-// The query rows of a prefill, in the tensor-core kernel's operand form:
-// RMSNorm with the gains and RoPE at each token's position (model.cpp:
-// 1616-1660, as the decode kernel does in its slots), rounded to bf16 and
-// laid out head-major, [n_head][n_tok][128]. A warp per (token, head).
-__global__ void __launch_bounds__(256) prefill_q_kernel(const __grid_constant__ DevJob j, __nv_bfloat16* qb)
+// The per-head work of a prefill's tokens before the attention (model.cpp:
+// 1616-1694), one CTA per token, a warp per head vector: the q rows get
+// RMSNorm with the gains and RoPE and go out in the tensor-core kernel's
+// operand form (bf16, head-major [n_head][n_tok][128]); the k rows get
+// RMSNorm and RoPE, the v rows the plain norm where asked, and both are
+// appended to the cache at row pos % rows in its type. The rotation's
+// cosines and sines depend only on the token, so each CTA forms them once
+// (64 angles) for all its heads.
+template <typename KV>
+__global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant__ DevJob j, __nv_bfloat16* qb)
 {
+	using T = typename KV::T;
 	__shared__ float bufs[8][PF_D];
-	__shared__ float s_g[PF_D], s_inv[PF_D / 2], s_ff[PF_D / 2];
+	__shared__ float s_qg[PF_D], s_kg[PF_D], s_cs[PF_D / 2], s_sn[PF_D / 2];
 	const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	const int h = blockIdx.y * 8 + warp;
 	const int half = j.n_rot / 2;
+	const int pos = j.pos0 + t;
+	const bool append = !j.reuse_kv && pos >= j.key_lo && pos < j.key_hi;
+	const int n_tasks = j.n_head + (append ? 2 * j.n_kv : 0); // q heads, then k heads, then v heads
+	auto src_of = [&](int task) -> const float* {
+		if (task < j.n_head) return j.q + ((size_t)t * j.n_head + task) * PF_D;
+		const int u = task - j.n_head;
+		return (u < j.n_kv ? j.k : j.v) + ((size_t)t * j.n_kv + u % j.n_kv) * PF_D;
+	};
 	HeadRegs x;
-	if (h < j.n_head) load_head(x, j.q + ((size_t)t * j.n_head + h) * PF_D, PF_D);
+	if (warp < n_tasks) load_head(x, src_of(warp), PF_D);
+	const float rpos = (float)pos * j.rope_scale;
 	for (int i = threadIdx.x; i < PF_D; i += blockDim.x)
 	{
-		s_g[i] = j.q_gamma ? j.q_gamma[i] : 0.0f;
-		if (i < PF_D / 2)
+		s_qg[i] = j.q_gamma ? j.q_gamma[i] : 0.0f;
+		s_kg[i] = j.k_gamma ? j.k_gamma[i] : 0.0f;
+		if (i < half)
 		{
-			s_inv[i] = i < half ? j.rope_inv[i] : 0.0f;
-			s_ff[i] = (j.freq_factors && i < half) ? j.freq_factors[i] : 0.0f;
+			float theta = rpos * j.rope_inv[i];
+			if (j.freq_factors) theta = __fdiv_rn(theta, j.freq_factors[i]);
+			sincosf(theta, &s_sn[i], &s_cs[i]);
 		}
 	}
 	__syncthreads();
-	if (h >= j.n_head) return;
+	const int row = pos % j.rows;
 	float* buf = bufs[warp];
-	prep_head(buf, x, PF_D, j.q_gamma ? s_g : nullptr, false, j.eps, true, j.n_rot, j.rope_mode,
-	          (float)(j.pos0 + t) * j.rope_scale, s_inv, j.freq_factors ? s_ff : nullptr);
-	__nv_bfloat16* dst = qb + ((size_t)h * j.n_tok + t) * PF_D;
-	for (int i = lane; i < PF_D; i += 32) dst[i] = __float2bfloat16_rn(buf[i]);
+	for (int task = warp; task < n_tasks; task += 8)
+	{
+		if (task != warp) load_head(x, src_of(task), PF_D);
+		const bool is_q = task < j.n_head, is_k = !is_q && task - j.n_head < j.n_kv;
+#pragma unroll
+		for (int k = 0; k < 4; ++k) buf[lane + 32 * k] = x.x[k];
+		__syncwarp();
+		const float* gamma = is_q ? (j.q_gamma ? s_qg : nullptr) : (is_k && j.k_gamma ? s_kg : nullptr);
+		prep_buf(buf, PF_D, gamma, !is_q && !is_k && j.v_rmsnorm, j.eps, false, 0, 0, 0.0f, nullptr, nullptr);
+		if ((is_q || is_k) && half > 0) rope_apply(buf, j.n_rot, j.rope_mode, s_cs, s_sn);
+		__syncwarp();
+		if (is_q)
+		{
+			__nv_bfloat16* dst = qb + ((size_t)task * j.n_tok + t) * PF_D;
+			for (int i = lane; i < PF_D; i += 32) dst[i] = __float2bfloat16_rn(buf[i]);
+		}
+		else
+		{
+			const int h = (task - j.n_head) % j.n_kv;
+			T* dst = reinterpret_cast<T*>((is_k ? j.K : j.V) + (size_t)h * j.head_bytes) + (size_t)row * PF_D;
+			for (int i = lane; i < PF_D; i += 32) store_elem(dst + i, buf[i]);
+		}
+		__syncwarp();
+	}
 }
 
 // A 3-D tensor map over a head-major bf16 array [z][y][128] with a
@@ -494,6 +552,14 @@ bool prefill_supported(int D, int kv_type) { return D == PF_D && kv_type == KV_B
 
 size_t prefill_qbuf_bytes(int n_tok, int n_head) { return (size_t)n_head * n_tok * PF_D * 2; }
 
+int launch_prefill_prep(const DevJob& j, void* qbuf, void* stream)
+{
+	if (j.D != PF_D || j.n_tok <= 0) return (int)cudaErrorInvalidValue;
+	prefill_prep_kernel<kv_bf16><<<(unsigned)j.n_tok, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+		j, static_cast<__nv_bfloat16*>(qbuf));
+	return (int)cudaGetLastError();
+}
+
 int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream)
 {
 	if (j.D != PF_D || j.n_tok <= 0 || j.n_head % j.n_kv) return (int)cudaErrorInvalidValue;
@@ -503,10 +569,7 @@ int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream)
 	if (!e) e = make_map(&kmap, j.K, (uint64_t)j.rows, (uint64_t)j.n_kv);
 	if (!e) e = make_map(&vmap, j.V, (uint64_t)j.rows, (uint64_t)j.n_kv);
 	if (e) return e;
-	prefill_q_kernel<<<dim3((unsigned)j.n_tok, (unsigned)((j.n_head + 7) / 8)), 256, 0, st>>>(
-		j, static_cast<__nv_bfloat16*>(qbuf));
-	cudaError_t ce = cudaGetLastError();
-	if (ce != cudaSuccess) return (int)ce;
+	cudaError_t ce;
 	static bool configured[64] = {};
 	int dev = 0;
 	cudaGetDevice(&dev);

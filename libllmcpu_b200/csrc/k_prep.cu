@@ -84,13 +84,6 @@ __global__ void __launch_bounds__(PREP_WARPS * 32) prep_kernel(const DevJob* __r
 	prep_token<KV>(jobs[blockIdx.y], blockIdx.x); // block (t, job)
 }
 
-// One job passed by value (the tensor-core prefill's append: no job table).
-template <typename KV>
-__global__ void __launch_bounds__(PREP_WARPS * 32) prep_one_kernel(const __grid_constant__ DevJob j)
-{
-	prep_token<KV>(j, blockIdx.x);
-}
-
 // ---- unit seam ---------------------------------------------------------------
 
 __global__ void rmsnorm_kernel(float* y, const float* x, size_t n_groups, size_t dim, const float* gamma, float eps)
@@ -144,20 +137,6 @@ int launch_prep(const DecodePlan& P, void* stream)
 	case KV_F32: prep_kernel<kv_f32><<<grid, PREP_WARPS * 32, 0, st>>>(P.jobs); break;
 	case KV_BF16: prep_kernel<kv_bf16><<<grid, PREP_WARPS * 32, 0, st>>>(P.jobs); break;
 	default: prep_kernel<kv_f16><<<grid, PREP_WARPS * 32, 0, st>>>(P.jobs); break;
-	}
-	return (int)cudaGetLastError();
-}
-
-int launch_prep_one(const DevJob& j, int kv_type, void* stream)
-{
-	if (j.D > PREP_MAX_D) return (int)cudaErrorInvalidValue;
-	if (j.n_tok <= 0) return 0;
-	auto st = static_cast<cudaStream_t>(stream);
-	switch (kv_type)
-	{
-	case KV_F32: prep_one_kernel<kv_f32><<<(unsigned)j.n_tok, PREP_WARPS * 32, 0, st>>>(j); break;
-	case KV_BF16: prep_one_kernel<kv_bf16><<<(unsigned)j.n_tok, PREP_WARPS * 32, 0, st>>>(j); break;
-	default: prep_one_kernel<kv_f16><<<(unsigned)j.n_tok, PREP_WARPS * 32, 0, st>>>(j); break;
 	}
 	return (int)cudaGetLastError();
 }
