@@ -354,6 +354,20 @@ __device__ __forceinline__ void span_of(int causal, int window, int pos, int n_s
 	}
 }
 
+// Two floats to bf16 with round-to-nearest-even, packed (lo in the low half),
+// on the integer pipe: the conversion instruction runs on the transcendental
+// unit, which the softmax's exponentials already saturate. Exact RNE for
+// every finite value and for infinities (the values rounded here are finite).
+__device__ __forceinline__ uint32_t bf16_rne_bits(float f)
+{
+	const uint32_t u = __float_as_uint(f);
+	return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi)
+{
+	return bf16_rne_bits(lo) | (bf16_rne_bits(hi) << 16);
+}
+
 // ---- per-head preparation (norms and RoPE) on a warp ------------------------
 
 // RMS scale of a D-vector held in shared `buf`, the reference's form:

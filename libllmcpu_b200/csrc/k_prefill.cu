@@ -15,8 +15,8 @@
 // tiles), each into its own 2-stage ring, K free again as soon as its S is
 // done; warp 1 owns the TMEM allocation and, from one lane, issues the MMAs
 // (S into two TMEM buffers in turn, so the next tile's S is computed while
-// this tile's softmax runs); warps 4-11 do the softmax, two threads per query
-// row (64 columns each, the row maximum exchanged through shared memory),
+// this tile's softmax runs); warps 4 on do the softmax, PF_NH threads per
+// query row (the row maximum exchanged through shared memory),
 // keep O in scale and write the output. Online softmax in base 2 with a
 // lazily moved maximum: a row's reference maximum moves (and O and l are
 // rescaled) only when a new score exceeds it by more than 2^8, so O is rarely
@@ -43,15 +43,17 @@ namespace
 constexpr int PF_BM = 128;                      // query rows per CTA
 constexpr int PF_BN = 128;                      // keys per tile
 constexpr int PF_D = 128;                       // head_dim
-constexpr int PF_THREADS = 384;                 // 12 warps
+constexpr int PF_NH = 4;                        // softmax threads per query row (32 columns each)
+constexpr int PF_CW = PF_BN / PF_NH;            // columns per softmax thread
+constexpr int PF_THREADS = 128 + 128 * PF_NH;   // warps 0-3: TMA, MMA; then the softmax warps
 constexpr int PANEL = 128 * 128;                // 128 rows x 64 bf16: one 128-byte-swizzled panel
 constexpr int TILE = 2 * PANEL;                 // 128 rows x 128 bf16
 constexpr int SM_Q = 0;                         // Q tile
 constexpr int SM_K = SM_Q + TILE;               // [2] K tiles
 constexpr int SM_V = SM_K + 2 * TILE;           // [2] V tiles
 constexpr int SM_P = SM_V + 2 * TILE;           // P tile
-constexpr int SM_RED = SM_P + TILE;             // [2 tiles][2 halves][128 rows] row maxima, then [2][128] row sums
-constexpr int SM_BAR = SM_RED + 4 * 128 * 4;    // barriers, TMEM address
+constexpr int SM_RED = SM_P + TILE;             // [2 tiles][PF_NH parts][128 rows] row maxima, then [PF_NH][128] row sums
+constexpr int SM_BAR = SM_RED + 3 * PF_NH * 128 * 4; // barriers, TMEM address
 constexpr int PF_SMEM = SM_BAR + 256 + 1024;    // + alignment slack
 constexpr int TMEM_COLS = 512;                  // S0, S1, O (128 columns each)
 constexpr float LAZY = 8.0f;                    // log2 headroom before the row maximum moves
@@ -187,9 +189,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			mbar_init(&v_full[s], 1);
 			mbar_init(&v_empty[s], 1);
 			mbar_init(&s_full[s], 1);
-			mbar_init(&s_empty[s], 256);
+			mbar_init(&s_empty[s], 128 * PF_NH);
 		}
-		mbar_init(p_full, 256);
+		mbar_init(p_full, 128 * PF_NH);
 		mbar_init(pv_done, 1);
 		mbar_init(mma_done, 1);
 		flags[0] = 0;
@@ -300,22 +302,23 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 	}
 	else if (warp >= 4)
 	{
-		// ---- softmax, O in scale, output: two threads per query row (warps
-		// 4-7 take its columns 0-63, warps 8-11 columns 64-127; a warp reaches
-		// TMEM lanes 32 (warp % 4) .. +31), the row maximum shared through
-		// shared memory by the pair of warps on the same lanes ----
+		// ---- softmax, O in scale, output: PF_NH threads per query row (warp
+		// 4 + 4 part + lane group takes columns [32 part, 32 part + 32); a warp
+		// reaches TMEM lanes 32 (warp % 4) .. +31), the row maximum shared
+		// through shared memory by the warps on the same lanes ----
 		const int wq = warp & 3;
-		const int hf = (warp >> 2) - 1; // column half
+		const int hf = (warp >> 2) - 1; // column part
 		const int r = wq * 32 + lane;
 		const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-		const uint32_t col0 = (uint32_t)(hf * 64);
+		const uint32_t col0 = (uint32_t)(hf * PF_CW);
 		const int qp = P.pos0 + q0 + r;
 		const int kf = (P.window > 0 && qp + 1 > P.window) ? qp + 1 - P.window : 0;
 		const int kl = min(qp, P.n_seq - 1);
-		float* red = reinterpret_cast<float*>(smem + SM_RED); // maxima [2][2][128], then sums [2][128]
+		float* red = reinterpret_cast<float*>(smem + SM_RED); // maxima [2][PF_NH][128], then sums [PF_NH][128]
 		float m_used = -CUDART_INF_F, l = 0.0f;
 		bool ok = true;
-		unsigned char* prow = smem + SM_P + hf * PANEL + r * 128;
+		// this thread's 32 columns: 4 chunks of 8 in its row of panel hf / 2
+		unsigned char* prow = smem + SM_P + (hf >> 1) * PANEL + r * 128;
 		for (int jj = 0; jj < n_tiles; ++jj)
 		{
 			const int s = jj & 1;
@@ -323,42 +326,38 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			ok = __all_sync(0xffffffffu, ok);
 			if (!ok) break;
 			tc_fence_after();
-			float x[64];
+			float x[PF_CW];
 			tmem_ld32(TS[s] + lane_off + col0, x);
-			tmem_ld32(TS[s] + lane_off + col0 + 32, x + 32);
 			tmem_wait_ld();
 			tc_fence_before();
 			mbar_arrive(&s_empty[s]);
-			const int key0 = (j_lo + jj) * PF_BN + hf * 64;
-			// scores in log2 units (the soft-cap, when there is one, in its own
-			// loop: a select would evaluate tanh for every score), the span mask
-			// only on tiles that cross the span's ends
+			const int key0 = (j_lo + jj) * PF_BN + hf * PF_CW;
+			// scores in log2 units: sl * s, folded into the exponentials' FMA
+			// (sl > 0 keeps the maximum's place); with a soft-cap, capped first
+			// in their own loop (a select would evaluate tanh for every score)
+			float sl = P.scale * P.log2e;
 			if (P.softcap > 0.0f)
 			{
 				const float cs = P.scale / P.softcap, cl = P.softcap * P.log2e;
 #pragma unroll
-				for (int c = 0; c < 64; ++c) x[c] = tanhf(x[c] * cs) * cl;
+				for (int c = 0; c < PF_CW; ++c) x[c] = tanhf(x[c] * cs) * cl;
+				sl = 1.0f;
 			}
-			else
-			{
-				const float sl = P.scale * P.log2e;
-#pragma unroll
-				for (int c = 0; c < 64; ++c) x[c] *= sl;
-			}
-			if (key0 < kf || key0 + 63 > kl)
+			if (key0 < kf || key0 + PF_CW - 1 > kl)
 			{
 #pragma unroll
-				for (int c = 0; c < 64; ++c)
+				for (int c = 0; c < PF_CW; ++c)
 					if (key0 + c < kf || key0 + c > kl) x[c] = -CUDART_INF_F;
 			}
 			float mq[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F}; // four chains
 #pragma unroll
-			for (int c = 0; c < 64; ++c) mq[c & 3] = fmaxf(mq[c & 3], x[c]);
-			float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-			float* mxs = red + s * 256;
+			for (int c = 0; c < PF_CW; ++c) mq[c & 3] = fmaxf(mq[c & 3], x[c]);
+			float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl;
+			float* mxs = red + s * PF_NH * 128;
 			mxs[hf * 128 + r] = mx;
-			named_sync(2 + wq, 64); // the two warps on these TMEM lanes
-			mx = fmaxf(mx, mxs[(hf ^ 1) * 128 + r]);
+			named_sync(2 + wq, 32 * PF_NH); // the warps on these TMEM lanes
+#pragma unroll
+			for (int o = 1; o < PF_NH; ++o) mx = fmaxf(mx, mxs[((hf + o) % PF_NH) * 128 + r]);
 			// the row's reference maximum moves only when a score exceeds it by
 			// more than 2^LAZY; then O (in TMEM) and l are rescaled
 			const bool move = mx > m_used + LAZY;
@@ -366,14 +365,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			const float alpha = (move && m_used != -CUDART_INF_F) ? ex2(m_used - m_new) : 1.0f;
 			const bool rescale = move && m_used != -CUDART_INF_F;
 			const float m_ref = m_new == -CUDART_INF_F ? 0.0f : m_new; // a row with no key yet: all p are 0
-			// P (bf16) in registers first, then into the P tile once the previous
-			// P V has read it
-			uint32_t pk[32];
+			// the weights and their bf16 pairs, in registers first, then into the
+			// P tile once the previous P V has read it
+			uint32_t pk[PF_CW / 2];
 			float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+			const float nm = -m_ref;
 #pragma unroll
-			for (int c = 0; c < 64; c += 2)
+			for (int c = 0; c < PF_CW; c += 2)
 			{
-				const float p0 = ex2(x[c] - m_ref), p1 = ex2(x[c + 1] - m_ref); // a masked score (-inf) gives 0
+				const float p0 = ex2(fmaf(x[c], sl, nm)), p1 = ex2(fmaf(x[c + 1], sl, nm)); // masked (-inf): 0
 				ls[(c >> 1) & 3] += p0 + p1;
 				__nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
 				pk[c >> 1] = *reinterpret_cast<uint32_t*>(&b2);
@@ -386,25 +386,21 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 				tc_fence_after();
 				if (__any_sync(0xffffffffu, rescale))
 				{
+					float o[32];
+					tmem_ld32(TO + lane_off + col0, o);
+					tmem_wait_ld();
 #pragma unroll
-					for (int c = 0; c < 2; ++c)
-					{
-						float o[32];
-						tmem_ld32(TO + lane_off + col0 + c * 32, o);
-						tmem_wait_ld();
-#pragma unroll
-						for (int i = 0; i < 32; ++i) o[i] *= alpha;
-						tmem_st32(TO + lane_off + col0 + c * 32, o);
-					}
+					for (int i = 0; i < 32; ++i) o[i] *= alpha;
+					tmem_st32(TO + lane_off + col0, o);
 					tmem_wait_st();
 				}
 			}
 #pragma unroll
-			for (int c16 = 0; c16 < 8; ++c16)
+			for (int c4 = 0; c4 < PF_CW / 8; ++c4)
 			{
-				const int chunk = c16 ^ (r & 7);
+				const int chunk = ((hf & 1) * (PF_CW / 8) + c4) ^ (r & 7);
 				*reinterpret_cast<uint4*>(prow + chunk * 16) =
-					make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
+					make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]);
 			}
 			l = fmaf(l, alpha, (ls[0] + ls[1]) + (ls[2] + ls[3]));
 			m_used = m_new;
@@ -412,32 +408,28 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			tc_fence_before();
 			mbar_arrive(p_full);
 		}
-		// the output: O / l, once the last P V is done (l: the two halves' sums)
+		// the output: O / l, once the last P V is done (l: the parts' sums)
 		if (ok && n_tiles > 0) ok = mbar_wait_bounded(pv_done, (uint32_t)((n_tiles - 1) & 1), P.err, DEVERR_WAIT_FULL);
 		ok = __all_sync(0xffffffffu, ok);
-		float* sums = red + 512;
+		float* sums = red + 2 * PF_NH * 128;
 		sums[hf * 128 + r] = l;
-		named_sync(2 + wq, 64);
-		l += sums[(hf ^ 1) * 128 + r];
+		named_sync(2 + wq, 32 * PF_NH);
+#pragma unroll
+		for (int o = 1; o < PF_NH; ++o) l += sums[((hf + o) % PF_NH) * 128 + r];
 		if (ok)
 		{
 			tc_fence_after();
 			const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-			const bool row_ok = q0 + r < P.n_tok;
-			float* orow = P.out + ((size_t)(q0 + r) * P.n_head + h) * PF_D + col0;
-#pragma unroll
-			for (int c = 0; c < 2; ++c)
+			float o[32];
+			tmem_ld32(TO + lane_off + col0, o);
+			tmem_wait_ld();
+			if (q0 + r < P.n_tok)
 			{
-				float o[32];
-				tmem_ld32(TO + lane_off + col0 + c * 32, o);
-				tmem_wait_ld();
-				if (row_ok)
-				{
+				float* orow = P.out + ((size_t)(q0 + r) * P.n_head + h) * PF_D + col0;
 #pragma unroll
-					for (int i = 0; i < 32; i += 4)
-						*reinterpret_cast<float4*>(orow + c * 32 + i) =
-							make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
-				}
+				for (int i = 0; i < 32; i += 4)
+					*reinterpret_cast<float4*>(orow + i) =
+						make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
 			}
 		}
 	}
@@ -462,7 +454,7 @@ template <typename KV>
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant__ DevJob j, __nv_bfloat16* qb)
 {
 	using T = typename KV::T;
-	__shared__ float bufs[8][PF_D];
+	__shared__ __align__(16) float bufs[8][PF_D];
 	__shared__ float s_qg[PF_D], s_kg[PF_D], s_cs[PF_D / 2], s_sn[PF_D / 2];
 	const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int half = j.n_rot / 2;
@@ -502,16 +494,17 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 		prep_buf(buf, PF_D, gamma, !is_q && !is_k && j.v_rmsnorm, j.eps, false, 0, 0, 0.0f, nullptr, nullptr);
 		if ((is_q || is_k) && half > 0) rope_apply(buf, j.n_rot, j.rope_mode, s_cs, s_sn);
 		__syncwarp();
+		// four consecutive elements per lane, rounded to bf16 and stored as 8 bytes
+		static_assert(sizeof(T) == 2, "the prefill's cache and q rows are bf16");
+		const float4 f4 = *reinterpret_cast<const float4*>(buf + 4 * lane);
+		const uint2 w = make_uint2(pack_bf16x2(f4.x, f4.y), pack_bf16x2(f4.z, f4.w));
 		if (is_q)
-		{
-			__nv_bfloat16* dst = qb + ((size_t)task * j.n_tok + t) * PF_D;
-			for (int i = lane; i < PF_D; i += 32) dst[i] = __float2bfloat16_rn(buf[i]);
-		}
+			*reinterpret_cast<uint2*>(qb + ((size_t)task * j.n_tok + t) * PF_D + 4 * lane) = w;
 		else
 		{
 			const int h = (task - j.n_head) % j.n_kv;
 			T* dst = reinterpret_cast<T*>((is_k ? j.K : j.V) + (size_t)h * j.head_bytes) + (size_t)row * PF_D;
-			for (int i = lane; i < PF_D; i += 32) store_elem(dst + i, buf[i]);
+			*reinterpret_cast<uint2*>(dst + 4 * lane) = w;
 		}
 		__syncwarp();
 	}
