@@ -813,8 +813,10 @@ void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 bool prefill_eligible(const nncu_kv* kv, const DevJob& j, const nncu_attn_job& pub)
 {
 	const Buffer& b = kv->bufs[kv->kv_buf[pub.layer]];
+	// the prep kernel rotates NEOX pairs within a lane: n_rot / 2 of 32 or 64
+	const bool rope_ok = j.rope_mode != NNCU_ROPE_NEOX || j.n_rot == 0 || j.n_rot == 64 || j.n_rot == 128;
 	return prefill_supported(j.D, kv->kv_type) && j.causal && j.n_tok >= 128 && b.window == 0 && j.key_lo == 0 &&
-	       j.key_hi == INT_MAX;
+	       j.key_hi == INT_MAX && rope_ok;
 }
 
 int run_prefill(nncu_kv* kv, const DevJob& j, cudaStream_t st)

@@ -454,20 +454,28 @@ template <typename KV>
 __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant__ DevJob j, __nv_bfloat16* qb)
 {
 	using T = typename KV::T;
-	__shared__ __align__(16) float bufs[8][PF_D];
+	static_assert(sizeof(T) == 2, "the prefill's cache and q rows are bf16");
 	__shared__ float s_qg[PF_D], s_kg[PF_D], s_cs[PF_D / 2], s_sn[PF_D / 2];
 	const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int half = j.n_rot / 2;
 	const int pos = j.pos0 + t;
 	const bool append = !j.reuse_kv && pos >= j.key_lo && pos < j.key_hi;
-	const int n_tasks = j.n_head + (append ? 2 * j.n_kv : 0); // q heads, then k heads, then v heads
+	const int n_head = j.n_head, n_kv = j.n_kv;
+	const int n_tasks = n_head + (append ? 2 * n_kv : 0); // q heads, then k heads, then v heads
 	auto src_of = [&](int task) -> const float* {
-		if (task < j.n_head) return j.q + ((size_t)t * j.n_head + task) * PF_D;
-		const int u = task - j.n_head;
-		return (u < j.n_kv ? j.k : j.v) + ((size_t)t * j.n_kv + u % j.n_kv) * PF_D;
+		if (task < n_head) return j.q + ((size_t)t * n_head + task) * PF_D;
+		const int u = task - n_head;
+		return u < n_kv ? j.k + ((size_t)t * n_kv + u) * PF_D : j.v + ((size_t)t * n_kv + (u - n_kv)) * PF_D;
 	};
-	HeadRegs x;
-	if (warp < n_tasks) load_head(x, src_of(warp), PF_D);
+	// a head vector in registers, element lane + 32 i in v[i]; the warp's
+	// next vector is loaded while this one is worked on
+	float v[PF_D / 32], vn[PF_D / 32];
+	auto load = [&](float* dst, int task) {
+		const float* src = src_of(task);
+#pragma unroll
+		for (int i = 0; i < PF_D / 32; ++i) dst[i] = src[lane + 32 * i];
+	};
+	if (warp < n_tasks) load(v, warp);
 	const float rpos = (float)pos * j.rope_scale;
 	for (int i = threadIdx.x; i < PF_D; i += blockDim.x)
 	{
@@ -481,32 +489,75 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 		}
 	}
 	__syncthreads();
+	// NEOX pairs elements e and e + n_rot/2: the same lane when n_rot/2 is a
+	// multiple of 32; NORM pairs e and e ^ 1: neighbouring lanes
+	const bool neox = j.rope_mode == 0;
 	const int row = pos % j.rows;
-	float* buf = bufs[warp];
 	for (int task = warp; task < n_tasks; task += 8)
 	{
-		if (task != warp) load_head(x, src_of(task), PF_D);
-		const bool is_q = task < j.n_head, is_k = !is_q && task - j.n_head < j.n_kv;
-#pragma unroll
-		for (int k = 0; k < 4; ++k) buf[lane + 32 * k] = x.x[k];
-		__syncwarp();
+		if (task + 8 < n_tasks) load(vn, task + 8);
+		const bool is_q = task < n_head, is_k = !is_q && task - n_head < n_kv;
 		const float* gamma = is_q ? (j.q_gamma ? s_qg : nullptr) : (is_k && j.k_gamma ? s_kg : nullptr);
-		prep_buf(buf, PF_D, gamma, !is_q && !is_k && j.v_rmsnorm, j.eps, false, 0, 0, 0.0f, nullptr, nullptr);
-		if ((is_q || is_k) && half > 0) rope_apply(buf, j.n_rot, j.rope_mode, s_cs, s_sn);
-		__syncwarp();
-		// four consecutive elements per lane, rounded to bf16 and stored as 8 bytes
-		static_assert(sizeof(T) == 2, "the prefill's cache and q rows are bf16");
-		const float4 f4 = *reinterpret_cast<const float4*>(buf + 4 * lane);
-		const uint2 w = make_uint2(pack_bf16x2(f4.x, f4.y), pack_bf16x2(f4.z, f4.w));
+		const bool plain = !is_q && !is_k && j.v_rmsnorm;
+		if (gamma || plain)
+		{
+			// RMSNorm as rms_scale does: squares in fp32, the scale in double
+			float ss = 0.0f;
+#pragma unroll
+			for (int i = 0; i < PF_D / 32; ++i) ss = fmaf(v[i], v[i], ss);
+			ss = warp_sum(ss);
+			const double mean = gamma ? (double)ss * (double)(1.0f / (float)PF_D) : (double)ss / (double)PF_D;
+			const float sc = (float)(1.0 / sqrt(mean + (double)j.eps));
+#pragma unroll
+			for (int i = 0; i < PF_D / 32; ++i) v[i] = gamma ? v[i] * sc * gamma[lane + 32 * i] : v[i] * sc;
+		}
+		if ((is_q || is_k) && half > 0)
+		{
+			if (neox)
+			{
+				// half is 32 or 64 here (a multiple of 32, checked on the host)
+				auto rot = [&](float& a_, float& b_, int e) {
+					const float a = a_, b = b_;
+					a_ = s_cs[e] * a - s_sn[e] * b;
+					b_ = s_sn[e] * a + s_cs[e] * b;
+				};
+				if (half == 64)
+				{
+					rot(v[0], v[2], lane);
+					rot(v[1], v[3], lane + 32);
+				}
+				else
+					rot(v[0], v[1], lane);
+			}
+			else
+			{
+#pragma unroll
+				for (int i = 0; i < PF_D / 32; ++i)
+				{
+					const int e = lane + 32 * i;
+					const float other = __shfl_xor_sync(0xffffffffu, v[i], 1);
+					if (e < j.n_rot)
+					{
+						const float cs = s_cs[e >> 1], sn = s_sn[e >> 1];
+						v[i] = (lane & 1) ? sn * other + cs * v[i] : cs * v[i] - sn * other;
+					}
+				}
+			}
+		}
+		T* dst;
 		if (is_q)
-			*reinterpret_cast<uint2*>(qb + ((size_t)task * j.n_tok + t) * PF_D + 4 * lane) = w;
+			dst = reinterpret_cast<T*>(qb) + ((size_t)task * j.n_tok + t) * PF_D;
 		else
 		{
-			const int h = (task - j.n_head) % j.n_kv;
-			T* dst = reinterpret_cast<T*>((is_k ? j.K : j.V) + (size_t)h * j.head_bytes) + (size_t)row * PF_D;
-			*reinterpret_cast<uint2*>(dst + 4 * lane) = w;
+			const int h = is_k ? task - n_head : task - n_head - n_kv;
+			dst = reinterpret_cast<T*>((is_k ? j.K : j.V) + (size_t)h * j.head_bytes) + (size_t)row * PF_D;
 		}
-		__syncwarp();
+#pragma unroll
+		for (int i = 0; i < PF_D / 32; ++i)
+		{
+			store_elem(dst + lane + 32 * i, v[i]);
+			v[i] = vn[i];
+		}
 	}
 }
 
