@@ -87,14 +87,14 @@ struct Cfg
 	static constexpr int QFF = QINV + D / 2;               // D / 2
 	static constexpr int QKG = QFF + D / 2;                // D (only with NT > 0)
 	static constexpr int QNEW = QKG + D;                   // NT * D k rows, then NT * D v rows
-	static constexpr int FIXED0 = (AREA_FLOATS + 2 * NW * RMW + 2 * QKG) * 4 + 256;
+	static constexpr int FIXED0 = (AREA_FLOATS + 2 * NW * RMW + NW * 32 + 2 * QKG) * 4 + 256;
 	static constexpr int FIT = (SMEM_LIMIT - FIXED0) / STAGE_BYTES;
 	static constexpr int STAGES = FIT < MAX_STAGES ? FIT : MAX_STAGES;
 	// new tokens per launch this kernel can append itself, in what the stages leave
 	static constexpr int NT_FIT = (SMEM_LIMIT - FIXED0 - STAGES * STAGE_BYTES - 2 * D * 4) / (2 * 2 * D * 4);
 	static constexpr int NT = NT_FIT < 0 ? 0 : NT_FIT < 16 ? NT_FIT : 16;
 	static constexpr int QSLOT_FLOATS = NT > 0 ? QNEW + 2 * NT * D : QKG;
-	static constexpr int FIXED_BYTES = (AREA_FLOATS + 2 * NW * RMW + 2 * QSLOT_FLOATS) * 4 + 256;
+	static constexpr int FIXED_BYTES = (AREA_FLOATS + 2 * NW * RMW + NW * 32 + 2 * QSLOT_FLOATS) * 4 + 256;
 	static constexpr int SMEM = STAGES * STAGE_BYTES + FIXED_BYTES;
 	static_assert(SMEM <= SMEM_LIMIT, "shared memory");
 	static_assert(STAGES >= 3, "shared memory for at least three stages");
@@ -253,7 +253,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	float* area = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES); // [NW/2][RMW][D]
 	float* m_s = area + C::AREA_FLOATS;                                      // [NW][RMW]
 	float* l_s = m_s + NW * RMW;                                             // [NW][RMW]
-	float* qslot = l_s + NW * RMW;                                           // [2][RM][D]
+	float* pbuf = l_s + NW * RMW;                                            // [NW][32] a batch's weights
+	float* qslot = pbuf + NW * 32;                                           // [2][RM][D]
 	uint64_t* full = reinterpret_cast<uint64_t*>(qslot + 2 * C::QSLOT_FLOATS);
 	uint64_t* empty = full + STAGES;
 	uint64_t* qfull = empty + STAGES;  // [2]
@@ -818,7 +819,15 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 #pragma unroll
 							for (int e = 0; e < E; ++e) o[r][e] *= alpha[r];
 					}
-					// o += p v over the batch's keys
+					// o += p v over the batch's keys. With four or more rows per warp
+					// the batch's weights go through this warp's scratch and come back
+					// four at a time as broadcast loads, instead of a shuffle each
+					float* pb = pbuf + warp * 32;
+					if constexpr (RMW >= 4)
+					{
+						if ((lane & ((1 << SHIFT) - 1)) == 0) pb[lane >> SHIFT] = pv;
+						__syncwarp();
+					}
 #pragma unroll
 					for (int kk = 0; kk < KS; ++kk)
 					{
@@ -829,11 +838,19 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 #pragma unroll
 						for (int r = 0; r < RMW; ++r)
 						{
-							const float p = __shfl_sync(0xffffffffu, pv, (kk * RMW + r) << SHIFT);
+							float p;
+							if constexpr (RMW >= 4)
+							{
+								const float4 p4 = *reinterpret_cast<const float4*>(pb + kk * RMW + (r & ~3));
+								p = (r & 3) == 0 ? p4.x : (r & 3) == 1 ? p4.y : (r & 3) == 2 ? p4.z : p4.w;
+							}
+							else
+								p = __shfl_sync(0xffffffffu, pv, (kk * RMW + r) << SHIFT);
 #pragma unroll
 							for (int e = 0; e < E; ++e) o[r][e] = fmaf(p, vv[e], o[r][e]);
 						}
 					}
+					if constexpr (RMW >= 4) __syncwarp(); // the scratch is read before the next batch writes it
 				}
 			}
 			__syncwarp();
