@@ -165,6 +165,15 @@ __device__ __forceinline__ int atomic_add_acq_rel_sys(int* p, int v)
 	return old;
 }
 
+__device__ __forceinline__ int atomic_add_relaxed_sys(int* p, int v)
+{
+	int old;
+	asm volatile("atom.relaxed.sys.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+	return old;
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 __device__ __forceinline__ int ld_acquire_sys(const int* p)
 {
 	int v;
@@ -697,38 +706,67 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		}
 		if (split && have)
 		{
-			// Arrive on every GPU's counter for this segment; where this partial
-			// is the last of the split to arrive, merge the ranks' partials in
-			// rank order into that GPU's output rows, then count the segment done
-			// there. Nothing waits: whoever arrives last does the merge.
+			// Arrive on every GPU's counter for this segment: one system-scope
+			// fence orders the partial's stores (every thread's, through the CTA
+			// barrier) before the arrivals, which then go out together. Where
+			// this partial is the last of the split to arrive, merge the ranks'
+			// partials in rank order into that GPU's output rows (a group of
+			// threads per such GPU), then count the segment done there. Nothing
+			// waits: whoever arrives last does the merge.
 			named_sync(1, NW * 32);
 			if (ctid == 0)
 			{
+				fence_acq_rel_sys();
+				int old[MAX_WORLD];
+#pragma unroll
+				for (int g = 0; g < MAX_WORLD; ++g)
+					old[g] = g < P.world ? atomic_add_relaxed_sys(P.arrive[g] + seg, 1) : 0;
 				int mask = 0;
-				for (int g = 0; g < P.world; ++g)
-					if (atomic_add_acq_rel_sys(P.arrive[g] + seg, 1) == P.world - 1) mask |= 1 << g;
+#pragma unroll
+				for (int g = 0; g < MAX_WORLD; ++g)
+					if (g < P.world && old[g] == P.world - 1) mask |= 1 << g;
+				if (mask) fence_acq_rel_sys(); // the other partials' stores before this CTA reads them
 				s_flags[2] = mask;
 			}
 			named_sync(1, NW * 32);
 			const int mask = s_flags[2];
-			for (int g = 0; g < P.world; ++g)
+			const int n_m = __popc(mask);
+			if (n_m)
 			{
-				if (!(mask >> g & 1)) continue;
-				float* out_g = P.out[g] + (size_t)pe.out_row0 * D;
-				merge_pieces<D, RM>(recv_row(g, 0, 0), (size_t)P.recv_stride, P.world, rows_valid, ctid, NW * 32,
-				                    [&](int R, int d, float4 acc, float M, float L) {
-					                    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-					                    acc.x *= inv;
-					                    acc.y *= inv;
-					                    acc.z *= inv;
-					                    acc.w *= inv;
-					                    *reinterpret_cast<float4*>(out_row(out_g, R) + d) = acc;
-				                    });
+				const int per = (NW * 32 / n_m) & ~31; // threads per merging GPU, whole warps
+				const int gi = ctid / per;
+				if (gi < n_m)
+				{
+					int g = 0;
+					for (int k = 0, seen = 0; k < MAX_WORLD; ++k)
+						if (mask >> k & 1)
+						{
+							if (seen == gi) g = k;
+							++seen;
+						}
+					float* out_g = P.out[g] + (size_t)pe.out_row0 * D;
+					merge_pieces<D, RM>(recv_row(g, 0, 0), (size_t)P.recv_stride, P.world, rows_valid, ctid - gi * per, per,
+					                    [&](int R, int d, float4 acc, float M, float L) {
+						                    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+						                    acc.x *= inv;
+						                    acc.y *= inv;
+						                    acc.z *= inv;
+						                    acc.w *= inv;
+						                    *reinterpret_cast<float4*>(out_row(out_g, R) + d) = acc;
+					                    });
+				}
 				named_sync(1, NW * 32);
 				if (ctid == 0)
 				{
-					atomicExch(P.arrive[g] + seg, 0); // ready for this parity's next call
-					atomic_add_acq_rel_sys(P.done[g], 1);
+					// the counters cleared for this parity's next call, then (after the
+					// merged rows and the clears) the segment counted done on each GPU
+#pragma unroll
+					for (int g = 0; g < MAX_WORLD; ++g)
+						if (mask >> g & 1) atomicExch(P.arrive[g] + seg, 0);
+					fence_acq_rel_sys();
+#pragma unroll
+					for (int g = 0; g < MAX_WORLD; ++g)
+						if (mask >> g & 1) atomic_add_relaxed_sys(P.done[g], 1);
 				}
 			}
 		}
