@@ -552,10 +552,12 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 			const int h = is_k ? task - n_head : task - n_head - n_kv;
 			dst = reinterpret_cast<T*>((is_k ? j.K : j.V) + (size_t)h * j.head_bytes) + (size_t)row * PF_D;
 		}
+		// rounded to bf16 on the integer pipe (the conversion instruction would
+		// queue on the transcendental unit)
 #pragma unroll
 		for (int i = 0; i < PF_D / 32; ++i)
 		{
-			store_elem(dst + lane + 32 * i, v[i]);
+			reinterpret_cast<uint16_t*>(dst)[lane + 32 * i] = (uint16_t)bf16_rne_bits(v[i]);
 			v[i] = vn[i];
 		}
 	}
