@@ -118,8 +118,11 @@ struct DecodePlan
 // Plan one launch over jobs[0, n) (their D, kv geometry, positions and
 // pointers filled): the row group size, every job's tiles, chunks and
 // partial slots, whether K2 appends itself, and the per-CTA starts (at most
-// max_starts, at most num_sms). Host code; allocates nothing.
-int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, CtaStart* starts, int max_starts);
+// max_starts, at most num_sms). With small_chunks, launches of many tiles
+// per SM are cut finer for balance (more partial slots). Host code;
+// allocates nothing.
+int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, CtaStart* starts, int max_starts,
+                bool small_chunks = true);
 
 // One causal prefill on the tensor cores (k_prefill.cu): bf16 cache, head_dim 128.
 struct PrefillPlan

@@ -192,7 +192,7 @@ __device__ __forceinline__ void merge_pieces(const float* base, size_t stride, i
                                              int nthreads, Emit emit)
 {
 	constexpr int PW = D + 4;
-	constexpr int FB = 16;
+	constexpr int FB = RM <= 4 && D <= 256 ? 20 : 16; // as many as the registers allow without spills
 	for (int idx = tid; idx < RM * (D / 4); idx += nthreads)
 	{
 		const int R = idx / (D / 4), d = 4 * (idx % (D / 4));
@@ -541,12 +541,13 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		if (lane == 0 && !append) mbar_arrive(&qempty[sl]);
 	};
 
-	// Merge the warps' states of the finished piece (two rounds: the upper half
-	// of the warps hands its state to the lower half, which folds it in
-	// registers and leaves the result for the CTA); write the output (whole
+	// Merge the warps' states of the finished piece; write the output (whole
 	// segment in this CTA) or a partial, and fold the partials if this CTA
-	// completes the segment.
-	auto finish_piece = [&]() {
+	// completes the segment. After the CTA's last tile (`flat`) the stage
+	// buffers are free: every warp leaves its state there and the CTA merges
+	// all of them in one round. Otherwise the states go through two warps'
+	// worth of area in a pairwise tree.
+	auto finish_piece = [&](bool flat) {
 		// l of each row: sum over the batch's key slots (lanes differing in the
 		// key bits), then every row's l in every lane
 		float lsum = l_lane;
@@ -556,52 +557,106 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		float lrow[RMW];
 #pragma unroll
 		for (int r = 0; r < RMW; ++r) lrow[r] = __shfl_sync(0xffffffffu, lsum, r << SHIFT);
-		// Pairwise tree over the warps through two warps' worth of area: 6,7 into
-		// 2,3; 4,5 into 0,1; 2,3 into 0,1. Partners have the same row slice.
-		auto put = [&](int slot_i) {
+		// one round: fo[w][r][:] = warp w's o of its row r, fm / fl its m and l;
+		// fc[w][r] the weight of warp w's state in its row's merge, and fM / fL
+		// each segment row's merged m and l
+		float* fo = reinterpret_cast<float*>(stages); // [NW][RMW][D]
+		float* fm = fo + NW * RMW * D;                // [NW][RMW]
+		float* fl = fm + NW * RMW;                    // [NW][RMW]
+		float* fc = fl + NW * RMW;                    // [NW][RMW]
+		float* fM = fc + NW * RMW;                    // [RM]
+		float* fL = fM + RM;                          // [RM]
+		if (flat)
+		{
 #pragma unroll
 			for (int r = 0; r < RMW; ++r)
 			{
 #pragma unroll
-				for (int e = 0; e < E; ++e) area[(slot_i * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
-				if (lane == 0)
+				for (int e = 0; e < E; ++e) fo[(warp * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
+			}
+			if (lane < RMW)
+			{
+#pragma unroll
+				for (int r = 0; r < RMW; ++r)
+					if (r == lane)
+					{
+						fm[warp * RMW + r] = m[r];
+						fl[warp * RMW + r] = lrow[r];
+					}
+			}
+			named_sync(1, NW * 32);
+			if (ctid < NW * RMW)
+			{
+				const int w = ctid / RMW, r = ctid % RMW, sl = w % RS;
+				float M = -CUDART_INF_F;
+#pragma unroll
+				for (int k = 0; k < NW / RS; ++k) M = fmaxf(M, fm[(k * RS + sl) * RMW + r]);
+				const float mw = fm[ctid];
+				fc[ctid] = mw == -CUDART_INF_F ? 0.0f : ex2(mw - M);
+				if (w == sl) // the slice's first warp: the row's m and l
 				{
-					m_s[slot_i * RMW + r] = m[r];
-					l_s[slot_i * RMW + r] = lrow[r];
+					float L = 0.0f;
+#pragma unroll
+					for (int k = 0; k < NW / RS; ++k)
+					{
+						const float mk = fm[(k * RS + sl) * RMW + r];
+						L = fmaf(fl[(k * RS + sl) * RMW + r], mk == -CUDART_INF_F ? 0.0f : ex2(mk - M), L);
+					}
+					fM[sl * RMW + r] = M;
+					fL[sl * RMW + r] = L;
 				}
 			}
-		};
-		auto take = [&](int slot_i) {
+			named_sync(1, NW * 32);
+		}
+		else
+		{
+			// Pairwise tree over the warps through two warps' worth of area: 6,7 into
+			// 2,3; 4,5 into 0,1; 2,3 into 0,1. Partners have the same row slice.
+			auto put = [&](int slot_i) {
 #pragma unroll
-			for (int r = 0; r < RMW; ++r)
-			{
-				const float mo = m_s[slot_i * RMW + r], lo = l_s[slot_i * RMW + r];
-				const float M = fmaxf(m[r], mo);
-				const float ca = m[r] == -CUDART_INF_F ? 0.0f : ex2(m[r] - M);
-				const float cb = mo == -CUDART_INF_F ? 0.0f : ex2(mo - M);
+				for (int r = 0; r < RMW; ++r)
+				{
 #pragma unroll
-				for (int e = 0; e < E; ++e)
-					o[r][e] = fmaf(o[r][e], ca, area[(slot_i * RMW + r) * D + lane_elem<E, VEC>(lane, e)] * cb);
-				m[r] = M;
-				lrow[r] = fmaf(lrow[r], ca, lo * cb);
-			}
-		};
-		if (warp >= 6) put(warp - 6);
-		named_sync(1, NW * 32);
-		if (warp == 2 || warp == 3) take(warp - 2);
-		named_sync(1, NW * 32);
-		if (warp == 4 || warp == 5) put(warp - 4);
-		named_sync(1, NW * 32);
-		if (warp < 2) take(warp);
-		named_sync(1, NW * 32);
-		if (warp == 2 || warp == 3) put(warp - 2);
-		named_sync(1, NW * 32);
-		if (warp < 2) take(warp);
-		named_sync(1, NW * 32);
-		if (warp < 2) put(warp);
-		named_sync(1, NW * 32);
-		// area slot 0 holds warp 0's merged state, slot 1 warp 1's: the same rows
-		// (one row slice) or the two slices
+					for (int e = 0; e < E; ++e) area[(slot_i * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
+					if (lane == 0)
+					{
+						m_s[slot_i * RMW + r] = m[r];
+						l_s[slot_i * RMW + r] = lrow[r];
+					}
+				}
+			};
+			auto take = [&](int slot_i) {
+#pragma unroll
+				for (int r = 0; r < RMW; ++r)
+				{
+					const float mo = m_s[slot_i * RMW + r], lo = l_s[slot_i * RMW + r];
+					const float M = fmaxf(m[r], mo);
+					const float ca = m[r] == -CUDART_INF_F ? 0.0f : ex2(m[r] - M);
+					const float cb = mo == -CUDART_INF_F ? 0.0f : ex2(mo - M);
+#pragma unroll
+					for (int e = 0; e < E; ++e)
+						o[r][e] = fmaf(o[r][e], ca, area[(slot_i * RMW + r) * D + lane_elem<E, VEC>(lane, e)] * cb);
+					m[r] = M;
+					lrow[r] = fmaf(lrow[r], ca, lo * cb);
+				}
+			};
+			if (warp >= 6) put(warp - 6);
+			named_sync(1, NW * 32);
+			if (warp == 2 || warp == 3) take(warp - 2);
+			named_sync(1, NW * 32);
+			if (warp == 4 || warp == 5) put(warp - 4);
+			named_sync(1, NW * 32);
+			if (warp < 2) take(warp);
+			named_sync(1, NW * 32);
+			if (warp == 2 || warp == 3) put(warp - 2);
+			named_sync(1, NW * 32);
+			if (warp < 2) take(warp);
+			named_sync(1, NW * 32);
+			if (warp < 2) put(warp);
+			named_sync(1, NW * 32);
+			// area slot 0 holds warp 0's merged state, slot 1 warp 1's: the same rows
+			// (one row slice) or the two slices
+		}
 
 		const int G = pe.G, h = pe.h, rg = pe.rg, n_tok = pe.n_tok, n_head = pe.n_head;
 		const int seg = pe.seg, n_pieces = pe.n_pieces;
@@ -623,18 +678,31 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		{
 			const int R = idx / D, d = idx % D;
 			const int sl = R / RMW, r = R % RMW; // the row's slice and its row within the slice
-			float M = -CUDART_INF_F;
-#pragma unroll
-			for (int k = 0; k < 2 / RS; ++k) M = fmaxf(M, m_s[(k * RS + sl) * RMW + r]);
-			float acc = 0.0f, L = 0.0f;
-#pragma unroll
-			for (int k = 0; k < 2 / RS; ++k)
+			float M = -CUDART_INF_F, acc = 0.0f, L = 0.0f;
+			if (flat)
 			{
-				const int w = k * RS + sl;
-				const float mw = m_s[w * RMW + r];
-				const float c = mw == -CUDART_INF_F ? 0.0f : ex2(mw - M);
-				acc = fmaf(area[(w * RMW + r) * D + d], c, acc);
-				L = fmaf(l_s[w * RMW + r], c, L);
+				M = fM[R];
+				L = fL[R];
+#pragma unroll
+				for (int k = 0; k < NW / RS; ++k)
+				{
+					const int w = k * RS + sl;
+					acc = fmaf(fo[(w * RMW + r) * D + d], fc[w * RMW + r], acc);
+				}
+			}
+			else
+			{
+#pragma unroll
+				for (int k = 0; k < 2 / RS; ++k) M = fmaxf(M, m_s[(k * RS + sl) * RMW + r]);
+#pragma unroll
+				for (int k = 0; k < 2 / RS; ++k)
+				{
+					const int w = k * RS + sl;
+					const float mw = m_s[w * RMW + r];
+					const float c = mw == -CUDART_INF_F ? 0.0f : ex2(mw - M);
+					acc = fmaf(area[(w * RMW + r) * D + d], c, acc);
+					L = fmaf(l_s[w * RMW + r], c, L);
+				}
 			}
 			if (single && !split)
 			{
@@ -897,7 +965,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		}
 		if (append && lane == 0) mbar_arrive(&qempty[sl]); // the new keys are no longer needed
 		n_new = 0;
-		finish_piece();
+		finish_piece(i == n_mine && !s_flags[0]);
 	}
 	const int n_done = i;
 	if (s_flags[0] && ctid == 0)

@@ -173,7 +173,8 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	j.key_lo = 0;
 	j.key_hi = INT_MAX;
 	DecodePlan P{};
-	rc = plan_launch(&j, 1, kv_type, std::min(n_sms, MAX_CTAS), P, hh.starts, MAX_CTAS);
+	// whole chunks: the partial slots stay within the fixed scratch
+	rc = plan_launch(&j, 1, kv_type, std::min(n_sms, MAX_CTAS), P, hh.starts, MAX_CTAS, false);
 	if (rc != NNCU_OK) return rc;
 
 	const size_t off_job = up256(256 * sizeof(float));

@@ -28,6 +28,9 @@ namespace
 // ring of them, and the consumers can start on the first tile sooner.
 constexpr int PREFETCH_TILES = 1;
 
+// Tiles per SM from which a launch's runs are cut from small chunks.
+constexpr long long LONG_RUN = 256;
+
 // The positions a job appends in this launch: its new tokens within its key range.
 int append_lo(const DevJob& j) { return j.reuse_kv ? 0 : std::max(j.pos0, j.key_lo); }
 int append_hi(const DevJob& j) { return j.reuse_kv ? 0 : std::min(j.pos0 + j.n_tok, j.key_hi); }
@@ -40,7 +43,8 @@ bool holds_new_rows(const DevJob& j, int tis, int len, int T)
 
 } // namespace
 
-int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, CtaStart* starts, int max_starts)
+int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, CtaStart* starts, int max_starts,
+                bool small_chunks)
 {
 	const int D = jobs[0].D;
 	const int T = decode_tile_keys(D, kv_type);
@@ -147,17 +151,25 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 		}
 		return cur > 0 ? ctas + 1 : ctas;
 	};
-	// the smallest chunk target C (from the tiles per SM up) whose chunks pack
-	// into the SMs with runs of at most max(C, largest chunk) tiles: growing
-	// C, not the runs, keeps a run from holding two big chunks
+	// the smallest run length C (from the tiles per SM up) whose chunks pack
+	// into the SMs with runs of at most max(C, largest chunk) tiles. Short
+	// runs take whole chunks of about C tiles (growing C, not the runs, keeps
+	// a run from holding two big chunks). Long runs (a launch of many tiles
+	// per SM) take chunks of about C / 16 tiles, so that a run ends within
+	// 1/16 of C wherever the segments' own lengths fall; each chunk is a
+	// piece with its own partial, a cost of a few microseconds against
+	// the chunk's 64 or more tiles.
+	auto chunk_target = [&](long long C) {
+		return small_chunks && C >= LONG_RUN ? std::max<long long>(64, C / 16) : C;
+	};
 	long long C = total > 0 ? (total + ctas_max - 1) / ctas_max : 1;
 	for (;;)
 	{
-		cut(C);
+		cut(chunk_target(C));
 		if (pack(std::max(C, max_chunk), false) <= ctas_max) break;
 		C += std::max<long long>(1, C / 64);
 	}
-	const long long n_ctas = pack(std::max(C, max_chunk), true);
+	const long long n_ctas = pack(std::max(C, max_chunk), true); // with the chunks of the last cut(C)
 	if (n_ctas > max_starts) return set_error(NNCU_ERR_INVALID_ARGUMENT, "decode plan: too many CTAs");
 
 	// each CTA's first tiles, issued before it reads its job: a contiguous run
