@@ -45,11 +45,12 @@ __device__ __forceinline__ float load_elem(const float* p) { return *p; }
 __device__ __forceinline__ float load_elem(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 __device__ __forceinline__ float load_elem(const __half* p) { return __half2float(*p); }
 
-// A lane's share of a D-element row: E = D/32 elements, taken as chunks of
-// VEC consecutive elements (16 bytes, or all E if fewer) with the lanes'
-// chunks side by side, so each load instruction of a warp reads one
-// contiguous run of shared memory (no bank conflicts). Element e of lane
-// `lane` is row[lane_elem<E, VEC>(lane, e)].
+// A lane's share of a D-element row spread over LK lanes (32: the whole
+// warp; fewer: the warp holds 32/LK rows side by side): E = D/LK elements,
+// taken as chunks of VEC consecutive elements (16 bytes, or all E if fewer)
+// with the lanes' chunks side by side, so each load instruction of a warp
+// reads contiguous runs of shared memory (no bank conflicts). Element e of
+// lane j (0 <= j < LK) is row[lane_elem<E, VEC, LK>(j, e)].
 template <int E, int ESIZE>
 struct LaneVec
 {
@@ -57,10 +58,10 @@ struct LaneVec
 	static_assert(E % VEC == 0, "chunking");
 };
 
-template <int E, int VEC>
+template <int E, int VEC, int LK = 32>
 __device__ __forceinline__ int lane_elem(int lane, int e)
 {
-	return (e / VEC) * 32 * VEC + lane * VEC + (e % VEC);
+	return (e / VEC) * LK * VEC + lane * VEC + (e % VEC);
 }
 
 __device__ __forceinline__ float2 widen2(uint32_t w, const __half*)
@@ -73,14 +74,14 @@ __device__ __forceinline__ float2 widen2(uint32_t w, const __nv_bfloat16*)
 }
 
 // Load lane `lane`'s E elements of `row` (shared or global) as floats.
-template <int E>
+template <int E, int LK = 32>
 __device__ __forceinline__ void load_lane(const float* row, int lane, float (&v)[E])
 {
 	constexpr int VEC = LaneVec<E, 4>::VEC;
 #pragma unroll
 	for (int c = 0; c < E / VEC; ++c)
 	{
-		const float* p = row + c * 32 * VEC + lane * VEC;
+		const float* p = row + c * LK * VEC + lane * VEC;
 		if constexpr (VEC == 4)
 		{
 			const float4 x = *reinterpret_cast<const float4*>(p);
@@ -100,13 +101,13 @@ __device__ __forceinline__ void load_lane(const float* row, int lane, float (&v)
 }
 
 // fp32 rows read with another element type's lane mapping (VEC per chunk).
-template <int E, int VEC>
+template <int E, int VEC, int LK = 32>
 __device__ __forceinline__ void load_lane_f(const float* row, int lane, float (&v)[E])
 {
 #pragma unroll
 	for (int c = 0; c < E / VEC; ++c)
 	{
-		const float* p = row + c * 32 * VEC + lane * VEC;
+		const float* p = row + c * LK * VEC + lane * VEC;
 		if constexpr (VEC % 4 == 0)
 		{
 #pragma unroll
@@ -133,14 +134,14 @@ __device__ __forceinline__ void load_lane_f(const float* row, int lane, float (&
 	}
 }
 
-template <int E, typename H>
+template <int E, int LK, typename H>
 __device__ __forceinline__ void load_lane_h(const H* row, int lane, float (&v)[E])
 {
 	constexpr int VEC = LaneVec<E, 2>::VEC;
 #pragma unroll
 	for (int c = 0; c < E / VEC; ++c)
 	{
-		const H* p = row + c * 32 * VEC + lane * VEC;
+		const H* p = row + c * LK * VEC + lane * VEC;
 		if constexpr (VEC == 8)
 		{
 			const uint4 x = *reinterpret_cast<const uint4*>(p);
@@ -171,12 +172,15 @@ __device__ __forceinline__ void load_lane_h(const H* row, int lane, float (&v)[E
 	}
 }
 
-template <int E>
-__device__ __forceinline__ void load_lane(const __half* row, int lane, float (&v)[E]) { load_lane_h<E>(row, lane, v); }
-template <int E>
+template <int E, int LK = 32>
+__device__ __forceinline__ void load_lane(const __half* row, int lane, float (&v)[E])
+{
+	load_lane_h<E, LK>(row, lane, v);
+}
+template <int E, int LK = 32>
 __device__ __forceinline__ void load_lane(const __nv_bfloat16* row, int lane, float (&v)[E])
 {
-	load_lane_h<E>(row, lane, v);
+	load_lane_h<E, LK>(row, lane, v);
 }
 
 // ---- warp helpers ---------------------------------------------------------
@@ -224,15 +228,18 @@ __device__ __forceinline__ float transpose_reduce_step(const float (&v)[N], int 
 	}
 }
 
-// Sum N per-lane values over the warp, leaving each lane with ONE full sum:
-// lane l holds the sum of value index (l >> (5 - log2 N)). Each exchange
-// round hands half of the remaining values to the partner lane and keeps the
-// other half, so N values cost about N shuffles instead of 5 per value.
-template <int N>
+// Sum N per-lane values over each aligned group of LK lanes (the whole warp
+// for LK = 32), leaving each lane with ONE full sum: lane l holds the sum
+// of value index ((l % LK) >> (log2 LK - log2 N)) of its group. Each
+// exchange round hands half of the remaining values to the partner lane and
+// keeps the other half, so N values cost about N shuffles instead of log2 LK
+// per value.
+template <int N, int LK = 32>
 __device__ __forceinline__ float transpose_reduce(const float (&v)[N], int lane)
 {
-	static_assert(N >= 1 && N <= 32 && (N & (N - 1)) == 0, "N: power of two up to 32");
-	return transpose_reduce_step<N, 16>(v, lane);
+	static_assert(N >= 1 && N <= LK && (N & (N - 1)) == 0, "N: power of two up to LK");
+	static_assert(LK >= 2 && LK <= 32 && (LK & (LK - 1)) == 0, "LK: power of two up to 32");
+	return transpose_reduce_step<N, LK / 2>(v, lane);
 }
 
 // ---- asynchronous copies and barriers (PTX ISA 8.x, sm_90+) ----------------

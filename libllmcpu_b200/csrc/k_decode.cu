@@ -34,11 +34,14 @@
 //    Longer batches have K1 (k_prep.cu) append first; the kernel is then its
 //    programmatic dependent, starts while K1 runs, and waits for K1 only
 //    before the tiles that hold the new rows, which it streams last.
-//  * Math. fp32 throughout. A warp owns T/8 keys of each tile; its lanes
-//    split head_dim (D/32 elements each). The q.k partial sums of a batch of
-//    keys x rows are summed across lanes with a transposing reduction, the
-//    online softmax runs in registers in base 2, and o accumulates in
-//    registers. Warps merge their (o, m, l) in shared memory at piece end.
+//  * Math. fp32 throughout. A warp owns T/8 keys of each tile. For head_dim
+//    256 and up its lanes split head_dim (D/32 elements each); below that a
+//    key takes LK = D/8 lanes (8 elements each) and the warp works on 32/LK
+//    keys side by side, each lane group with its own softmax state. The
+//    q.k partial sums of a batch of keys x rows are summed across a key's
+//    lanes with a transposing reduction, the online softmax runs in
+//    registers in base 2, and o accumulates in registers. The lane groups,
+//    then the warps, merge their (o, m, l) at piece end.
 #include <cuda_runtime.h>
 
 #include <math_constants.h>
@@ -61,16 +64,23 @@ constexpr float LOG2E = 1.4426950408889634f;
 template <int D, typename KV, int RM>
 struct Cfg
 {
-	static constexpr int E = D / 32;                       // elements per lane
+	// lanes per key: a key row spans the warp for head_dim 256 and up (and
+	// for many rows); below that each lane takes 8 elements and the warp
+	// works on 32 / LK keys side by side, so a score is summed over LK lanes
+	// instead of 32
+	static constexpr int LK = (D < 256 && RM <= 8) ? D / 8 : 32;
+	static constexpr int LG = 32 / LK;                     // lane groups (keys side by side) per warp
+	static constexpr int LOG2LK = LK >= 32 ? 5 : LK >= 16 ? 4 : LK >= 8 ? 3 : LK >= 4 ? 2 : 1;
+	static constexpr int E = D / LK;                       // elements per lane
 	static constexpr int RS = RM * E > 32 ? RM * E / 32 : 1; // row slices: warps sharing keys, splitting rows
 	static constexpr int RMW = RM / RS;                    // rows per warp
 	static constexpr int NKG = NW / RS;                    // key groups
 	static constexpr int T = TILE_BYTES / (D * KV::esize); // keys per tile
 	static constexpr int KB = T / NKG;                     // keys per warp per tile
-	static constexpr int KS = KB < 32 / RMW ? KB : 32 / RMW; // keys per reduction batch
+	static constexpr int KS = KB / LG < LK / RMW ? KB / LG : LK / RMW; // keys per lane group per reduction batch
 	static constexpr int N = KS * RMW;                     // values per reduction
 	static constexpr int LOG2N = N >= 32 ? 5 : N >= 16 ? 4 : N >= 8 ? 3 : N >= 4 ? 2 : N >= 2 ? 1 : 0;
-	static constexpr int SHIFT = 5 - LOG2N;                // lane >> SHIFT = value index after the reduction
+	static constexpr int SHIFT = LOG2LK - LOG2N;           // (lane % LK) >> SHIFT = value index after the reduction
 	static constexpr int LOG2RMW = RMW >= 32 ? 5 : RMW >= 16 ? 4 : RMW >= 8 ? 3 : RMW >= 4 ? 2 : RMW >= 2 ? 1 : 0;
 	static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
 	// the warps' (o, m, l) at a piece's end pass through two warps' worth of
@@ -101,7 +111,8 @@ struct Cfg
 	static_assert(D % 32 == 0, "D: a multiple of 32");
 	static_assert(RM % RS == 0 && NW == 8 && RS <= 2, "row slices");
 	static_assert(T >= NKG && T <= ATTN_BLOCK && ATTN_BLOCK % T == 0 && T % NKG == 0, "tile keys");
-	static_assert(KB % KS == 0, "batches per warp");
+	static_assert(KS >= 1 && KB % (KS * LG) == 0, "batches per warp");
+	static_assert(N <= LK && LK * LG == 32, "lane groups");
 	static_assert(RMW * E <= 32, "accumulator registers");
 };
 
@@ -192,7 +203,7 @@ __device__ __forceinline__ void merge_pieces(const float* base, size_t stride, i
                                              int nthreads, Emit emit)
 {
 	constexpr int PW = D + 4;
-	constexpr int FB = RM <= 4 && D <= 256 ? 20 : 16; // as many as the registers allow without spills
+	constexpr int FB = RM <= 4 && D == 256 ? 20 : 16; // as many as the registers allow without spills
 	for (int idx = tid; idx < RM * (D / 4); idx += nthreads)
 	{
 		const int R = idx / (D / 4), d = 4 * (idx % (D / 4));
@@ -419,11 +430,17 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 
 	// ---- consumers ----
 	// Warp w takes rows [rs*RMW, rs*RMW + RMW) of the segment (rs = w % RS)
-	// for the keys [kg*KB, kg*KB + KB) of every tile (kg = w / RS).
+	// for the keys [kg*KB, kg*KB + KB) of every tile (kg = w / RS). Within
+	// the warp, lane group lg (LK lanes) takes KS keys of each batch and
+	// keeps its own softmax state; the groups merge at the piece's end.
+	constexpr int LK = C::LK, LG = C::LG;
 	const int ctid = threadIdx.x; // 0 .. NW*32-1
 	const int rs = warp % RS, kg = warp / RS;
-	const int r_v = (lane >> SHIFT) % RMW;  // the row (within the warp's rows) of this lane's reduced value
-	const int kk_v = (lane >> SHIFT) / RMW; // its key within the batch
+	const int lj = lane & (LK - 1);        // this lane within its group
+	const int lg = lane / LK;              // its group
+	const int gbase = lane & ~(LK - 1);    // the group's first lane
+	const int r_v = (lj >> SHIFT) % RMW;   // the row (within the warp's rows) of this lane's reduced value
+	const int kk_v = (lj >> SHIFT) / RMW;  // its key within the group's batch
 
 	float q[RMW][E];
 	float o[RMW][E];
@@ -504,7 +521,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			const int R = rs * RMW + r;
 			const bool ok = R < rows; // warp-uniform
 			float tmp[E];
-			if (ok) load_lane_f<E, VEC>(qs + R * D, lane, tmp);
+			if (ok) load_lane_f<E, VEC, LK>(qs + R * D, lj, tmp);
 #pragma unroll
 			for (int e = 0; e < E; ++e)
 			{
@@ -552,11 +569,37 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		// key bits), then every row's l in every lane
 		float lsum = l_lane;
 #pragma unroll
-		for (int off = 1 << (SHIFT + C::LOG2RMW); off < 32; off <<= 1)
+		for (int off = 1 << (SHIFT + C::LOG2RMW); off < LK; off <<= 1)
 			lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
 		float lrow[RMW];
 #pragma unroll
-		for (int r = 0; r < RMW; ++r) lrow[r] = __shfl_sync(0xffffffffu, lsum, r << SHIFT);
+		for (int r = 0; r < RMW; ++r) lrow[r] = __shfl_sync(0xffffffffu, lsum, gbase + (r << SHIFT));
+		// the lane groups' states merged across the warp: every group then
+		// holds the warp's (o, m, l)
+		if constexpr (LG > 1)
+		{
+#pragma unroll
+			for (int r = 0; r < RMW; ++r)
+			{
+				float M = m[r];
+#pragma unroll
+				for (int off = LK; off < 32; off <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+				const float c = m[r] == -CUDART_INF_F ? 0.0f : ex2(m[r] - M);
+				float lr = lrow[r] * c;
+#pragma unroll
+				for (int off = LK; off < 32; off <<= 1) lr += __shfl_xor_sync(0xffffffffu, lr, off);
+				lrow[r] = lr;
+#pragma unroll
+				for (int e = 0; e < E; ++e)
+				{
+					float x = o[r][e] * c;
+#pragma unroll
+					for (int off = LK; off < 32; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+					o[r][e] = x;
+				}
+				m[r] = M;
+			}
+		}
 		// one round: fo[w][r][:] = warp w's o of its row r, fm / fl its m and l;
 		// fc[w][r] the weight of warp w's state in its row's merge, and fM / fL
 		// each segment row's merged m and l
@@ -572,7 +615,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			for (int r = 0; r < RMW; ++r)
 			{
 #pragma unroll
-				for (int e = 0; e < E; ++e) fo[(warp * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
+				for (int e = 0; e < E; ++e) fo[(warp * RMW + r) * D + lane_elem<E, VEC, LK>(lj, e)] = o[r][e];
 			}
 			if (lane < RMW)
 			{
@@ -617,7 +660,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 				for (int r = 0; r < RMW; ++r)
 				{
 #pragma unroll
-					for (int e = 0; e < E; ++e) area[(slot_i * RMW + r) * D + lane_elem<E, VEC>(lane, e)] = o[r][e];
+					for (int e = 0; e < E; ++e) area[(slot_i * RMW + r) * D + lane_elem<E, VEC, LK>(lj, e)] = o[r][e];
 					if (lane == 0)
 					{
 						m_s[slot_i * RMW + r] = m[r];
@@ -635,7 +678,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					const float cb = mo == -CUDART_INF_F ? 0.0f : ex2(mo - M);
 #pragma unroll
 					for (int e = 0; e < E; ++e)
-						o[r][e] = fmaf(o[r][e], ca, area[(slot_i * RMW + r) * D + lane_elem<E, VEC>(lane, e)] * cb);
+						o[r][e] = fmaf(o[r][e], ca, area[(slot_i * RMW + r) * D + lane_elem<E, VEC, LK>(lj, e)] * cb);
 					m[r] = M;
 					lrow[r] = fmaf(lrow[r], ca, lo * cb);
 				}
@@ -870,9 +913,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			if (!s_flags[0])
 			{
 #pragma unroll
-				for (int b = 0; b < KB / KS; ++b)
+				for (int b = 0; b < KB / (KS * LG); ++b)
 				{
-					const int k0 = kg * KB + b * KS; // key index within the tile
+					const int k0 = kg * KB + (b * LG + lg) * KS; // the lane group's first key of the batch, in the tile
 					// scores of KS keys x RMW rows: lane-partial dot products, then reduced
 					float part[N];
 #pragma unroll
@@ -880,8 +923,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					{
 						float kv[E];
 						const int np = key_base + k0 + kk - new_lo; // a new key: its row from the slot
-						load_lane<E>((unsigned)np < (unsigned)n_new ? new_k + np * NSTRIDE : Kt + (size_t)(k0 + kk) * D,
-						             lane, kv);
+						load_lane<E, LK>((unsigned)np < (unsigned)n_new ? new_k + np * NSTRIDE : Kt + (size_t)(k0 + kk) * D,
+						                 lj, kv);
 #pragma unroll
 						for (int r = 0; r < RMW; ++r)
 						{
@@ -891,14 +934,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 							part[kk * RMW + r] = acc;
 						}
 					}
-					float sv = transpose_reduce<N>(part, lane);
+					float sv = transpose_reduce<N, LK>(part, lane);
 					const int pos = key_base + k0 + kk_v;
 					if (softcap) sv = cap * tanhf(sv / cap) * LOG2E;
 					if (pos < first_v || pos > last_v) sv = -CUDART_INF_F;
 					// the batch's max of each row, then the new running max of every row
 					float mx = sv;
 #pragma unroll
-					for (int off = 1 << (SHIFT + C::LOG2RMW); off < 32; off <<= 1)
+					for (int off = 1 << (SHIFT + C::LOG2RMW); off < LK; off <<= 1)
 						mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
 					float alpha[RMW];
 					bool moved = false;
@@ -906,7 +949,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 #pragma unroll
 					for (int r = 0; r < RMW; ++r)
 					{
-						const float mn = fmaxf(m[r], __shfl_sync(0xffffffffu, mx, r << SHIFT));
+						const float mn = fmaxf(m[r], __shfl_sync(0xffffffffu, mx, gbase + (r << SHIFT)));
 						moved |= mn != m[r];
 						alpha[r] = mn == -CUDART_INF_F ? 1.0f : ex2(m[r] - mn);
 						m[r] = mn;
@@ -918,7 +961,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					}
 					const float pv = sv == -CUDART_INF_F ? 0.0f : ex2(sv - m_v);
 					l_lane = fmaf(l_lane, alpha_v, pv);
-					if (moved) // warp-uniform: m is the same in every lane
+					if (moved) // uniform in the lane group: its lanes share m
 					{
 #pragma unroll
 						for (int r = 0; r < RMW; ++r)
@@ -931,7 +974,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					float* pb = pbuf + warp * 32;
 					if constexpr (RMW >= 4)
 					{
-						if ((lane & ((1 << SHIFT) - 1)) == 0) pb[lane >> SHIFT] = pv;
+						if ((lj & ((1 << SHIFT) - 1)) == 0) pb[lg * N + (lj >> SHIFT)] = pv;
 						__syncwarp();
 					}
 #pragma unroll
@@ -939,19 +982,19 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					{
 						float vv[E];
 						const int np = key_base + k0 + kk - new_lo;
-						load_lane<E>((unsigned)np < (unsigned)n_new ? new_v + np * NSTRIDE : Vt + (size_t)(k0 + kk) * D,
-						             lane, vv);
+						load_lane<E, LK>((unsigned)np < (unsigned)n_new ? new_v + np * NSTRIDE : Vt + (size_t)(k0 + kk) * D,
+						                 lj, vv);
 #pragma unroll
 						for (int r = 0; r < RMW; ++r)
 						{
 							float p;
 							if constexpr (RMW >= 4)
 							{
-								const float4 p4 = *reinterpret_cast<const float4*>(pb + kk * RMW + (r & ~3));
+								const float4 p4 = *reinterpret_cast<const float4*>(pb + lg * N + kk * RMW + (r & ~3));
 								p = (r & 3) == 0 ? p4.x : (r & 3) == 1 ? p4.y : (r & 3) == 2 ? p4.z : p4.w;
 							}
 							else
-								p = __shfl_sync(0xffffffffu, pv, (kk * RMW + r) << SHIFT);
+								p = __shfl_sync(0xffffffffu, pv, gbase + ((kk * RMW + r) << SHIFT));
 #pragma unroll
 							for (int e = 0; e < E; ++e) o[r][e] = fmaf(p, vv[e], o[r][e]);
 						}
@@ -1186,10 +1229,6 @@ int decode_tile_keys(int D, int kv_type) { return TILE_BYTES / (D * kv_esize(kv_
 
 int decode_rows_max(int D) { return 64 / (D / 32) < 32 ? 64 / (D / 32) : 32; }
 
-namespace
-{
-constexpr int slices(int D, int RM) { return RM * (D / 32) > 32 ? RM * (D / 32) / 32 : 1; }
-} // namespace
 
 namespace
 {
@@ -1240,7 +1279,6 @@ int decode_fuse_tokens(int D, int kv_type, int RM)
 	}
 }
 
-int decode_fold_pieces(int D, int RM) { return 2 * (RM / slices(D, RM)) * D / RM; }
 
 int launch_decode(const DecodePlan& P, void* stream)
 {
