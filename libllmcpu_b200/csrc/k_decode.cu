@@ -82,6 +82,12 @@ struct Cfg
 	static constexpr int LOG2N = N >= 32 ? 5 : N >= 16 ? 4 : N >= 8 ? 3 : N >= 4 ? 2 : N >= 2 ? 1 : 0;
 	static constexpr int SHIFT = LOG2LK - LOG2N;           // (lane % LK) >> SHIFT = value index after the reduction
 	static constexpr int LOG2RMW = RMW >= 32 ? 5 : RMW >= 16 ? 4 : RMW >= 8 ? 3 : RMW >= 4 ? 2 : RMW >= 2 ? 1 : 0;
+	static constexpr int NB = KB / (KS * LG);              // reduction batches per warp per tile
+	// batches sharing one softmax update: with lane groups, all of a tile's
+	// (their weights fit 128 floats of warp scratch); otherwise one, as a
+	// batch then already spans 32 / RMW keys
+	static constexpr int NBS = LG == 1 ? 1 : NB * LG * N <= 128 ? NB : (128 / (LG * N) >= 1 ? 128 / (LG * N) : 1);
+	static constexpr int PBW = NBS * LG * N > 32 ? NBS * LG * N : 32; // warp scratch floats
 	static constexpr int STAGE_BYTES = 2 * TILE_BYTES;
 	// the warps' (o, m, l) at a piece's end pass through two warps' worth of
 	// area in a pairwise tree; the fold's weights reuse the same area
@@ -97,21 +103,21 @@ struct Cfg
 	static constexpr int QFF = QINV + D / 2;               // D / 2
 	static constexpr int QKG = QFF + D / 2;                // D (only with NT > 0)
 	static constexpr int QNEW = QKG + D;                   // NT * D k rows, then NT * D v rows
-	static constexpr int FIXED0 = (AREA_FLOATS + 2 * NW * RMW + NW * 32 + 2 * QKG) * 4 + 256;
+	static constexpr int FIXED0 = (AREA_FLOATS + 2 * NW * RMW + NW * PBW + 2 * QKG) * 4 + 256;
 	static constexpr int FIT = (SMEM_LIMIT - FIXED0) / STAGE_BYTES;
 	static constexpr int STAGES = FIT < MAX_STAGES ? FIT : MAX_STAGES;
 	// new tokens per launch this kernel can append itself, in what the stages leave
 	static constexpr int NT_FIT = (SMEM_LIMIT - FIXED0 - STAGES * STAGE_BYTES - 2 * D * 4) / (2 * 2 * D * 4);
 	static constexpr int NT = NT_FIT < 0 ? 0 : NT_FIT < 16 ? NT_FIT : 16;
 	static constexpr int QSLOT_FLOATS = NT > 0 ? QNEW + 2 * NT * D : QKG;
-	static constexpr int FIXED_BYTES = (AREA_FLOATS + 2 * NW * RMW + NW * 32 + 2 * QSLOT_FLOATS) * 4 + 256;
+	static constexpr int FIXED_BYTES = (AREA_FLOATS + 2 * NW * RMW + NW * PBW + 2 * QSLOT_FLOATS) * 4 + 256;
 	static constexpr int SMEM = STAGES * STAGE_BYTES + FIXED_BYTES;
 	static_assert(SMEM <= SMEM_LIMIT, "shared memory");
 	static_assert(STAGES >= 3, "shared memory for at least three stages");
 	static_assert(D % 32 == 0, "D: a multiple of 32");
 	static_assert(RM % RS == 0 && NW == 8 && RS <= 2, "row slices");
 	static_assert(T >= NKG && T <= ATTN_BLOCK && ATTN_BLOCK % T == 0 && T % NKG == 0, "tile keys");
-	static_assert(KS >= 1 && KB % (KS * LG) == 0, "batches per warp");
+	static_assert(KS >= 1 && KB % (KS * LG) == 0 && NB % NBS == 0, "batches per warp");
 	static_assert(N <= LK && LK * LG == 32, "lane groups");
 	static_assert(RMW * E <= 32, "accumulator registers");
 };
@@ -262,7 +268,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 {
 	using C = Cfg<D, KV, RM>;
 	using T_ = typename KV::T;
-	constexpr int E = C::E, T = C::T, KB = C::KB, KS = C::KS, N = C::N, SHIFT = C::SHIFT;
+	constexpr int E = C::E, T = C::T, KB = C::KB, KS = C::KS, N = C::N, SHIFT = C::SHIFT, NBS = C::NBS;
 	constexpr int VEC = LaneVec<E, KV::esize>::VEC; // lane <-> element mapping of K, V, q and o
 	constexpr int RS = C::RS, RMW = C::RMW;
 	constexpr int PW = D + 4; // a partial row: o[D], m, l, two pad floats (16-byte rows)
@@ -273,8 +279,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	float* area = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES); // [NW/2][RMW][D]
 	float* m_s = area + C::AREA_FLOATS;                                      // [NW][RMW]
 	float* l_s = m_s + NW * RMW;                                             // [NW][RMW]
-	float* pbuf = l_s + NW * RMW;                                            // [NW][32] a batch's weights
-	float* qslot = pbuf + NW * 32;                                           // [2][RM][D]
+	float* pbuf = l_s + NW * RMW;                                            // [NW][PBW] batches' weights
+	float* qslot = pbuf + NW * C::PBW;                                       // [2][RM][D]
 	uint64_t* full = reinterpret_cast<uint64_t*>(qslot + 2 * C::QSLOT_FLOATS);
 	uint64_t* empty = full + STAGES;
 	uint64_t* qfull = empty + STAGES;  // [2]
@@ -611,6 +617,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 		float* fL = fM + RM;                          // [RM]
 		if (flat)
 		{
+			named_sync(1, NW * 32); // every warp is done reading the last tile's stage
 #pragma unroll
 			for (int r = 0; r < RMW; ++r)
 			{
@@ -913,33 +920,44 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			if (!s_flags[0])
 			{
 #pragma unroll
-				for (int b = 0; b < KB / (KS * LG); ++b)
+				for (int sb = 0; sb < C::NB / NBS; ++sb)
 				{
-					const int k0 = kg * KB + (b * LG + lg) * KS; // the lane group's first key of the batch, in the tile
-					// scores of KS keys x RMW rows: lane-partial dot products, then reduced
-					float part[N];
+					// The scores of NBS batches (each KS keys x RMW rows per lane
+					// group): lane-partial dot products, reduced across the key's
+					// lanes; then one softmax update for all of them
+					float sv[NBS];
 #pragma unroll
-					for (int kk = 0; kk < KS; ++kk)
+					for (int bb = 0; bb < NBS; ++bb)
 					{
-						float kv[E];
-						const int np = key_base + k0 + kk - new_lo; // a new key: its row from the slot
-						load_lane<E, LK>((unsigned)np < (unsigned)n_new ? new_k + np * NSTRIDE : Kt + (size_t)(k0 + kk) * D,
-						                 lj, kv);
+						const int k0 = kg * KB + ((sb * NBS + bb) * LG + lg) * KS; // the lane group's first key, in the tile
+						float part[N];
 #pragma unroll
-						for (int r = 0; r < RMW; ++r)
+						for (int kk = 0; kk < KS; ++kk)
 						{
-							float acc = 0.0f;
+							float kv[E];
+							const int np = key_base + k0 + kk - new_lo; // a new key: its row from the slot
+							load_lane<E, LK>((unsigned)np < (unsigned)n_new ? new_k + np * NSTRIDE
+							                                                : Kt + (size_t)(k0 + kk) * D,
+							                 lj, kv);
 #pragma unroll
-							for (int e = 0; e < E; ++e) acc = fmaf(q[r][e], kv[e], acc);
-							part[kk * RMW + r] = acc;
+							for (int r = 0; r < RMW; ++r)
+							{
+								float acc = 0.0f;
+#pragma unroll
+								for (int e = 0; e < E; ++e) acc = fmaf(q[r][e], kv[e], acc);
+								part[kk * RMW + r] = acc;
+							}
 						}
+						float x = transpose_reduce<N, LK>(part, lane);
+						const int pos = key_base + k0 + kk_v;
+						if (softcap) x = cap * tanhf(x / cap) * LOG2E;
+						if (pos < first_v || pos > last_v) x = -CUDART_INF_F;
+						sv[bb] = x;
 					}
-					float sv = transpose_reduce<N, LK>(part, lane);
-					const int pos = key_base + k0 + kk_v;
-					if (softcap) sv = cap * tanhf(sv / cap) * LOG2E;
-					if (pos < first_v || pos > last_v) sv = -CUDART_INF_F;
-					// the batch's max of each row, then the new running max of every row
-					float mx = sv;
+					// the batches' max of each row, then the new running max of every row
+					float mx = sv[0];
+#pragma unroll
+					for (int bb = 1; bb < NBS; ++bb) mx = fmaxf(mx, sv[bb]);
 #pragma unroll
 					for (int off = 1 << (SHIFT + C::LOG2RMW); off < LK; off <<= 1)
 						mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -959,8 +977,21 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 							alpha_v = alpha[r];
 						}
 					}
-					const float pv = sv == -CUDART_INF_F ? 0.0f : ex2(sv - m_v);
-					l_lane = fmaf(l_lane, alpha_v, pv);
+					// the weights; with four or more rows per warp they go through this
+					// warp's scratch and come back four at a time as broadcast loads,
+					// instead of a shuffle each
+					float* pb = pbuf + warp * C::PBW;
+					float pv[NBS];
+					float psum = 0.0f;
+#pragma unroll
+					for (int bb = 0; bb < NBS; ++bb)
+					{
+						pv[bb] = sv[bb] == -CUDART_INF_F ? 0.0f : ex2(sv[bb] - m_v);
+						psum += pv[bb];
+						if constexpr (RMW >= 4)
+							if ((lj & ((1 << SHIFT) - 1)) == 0) pb[(bb * LG + lg) * N + (lj >> SHIFT)] = pv[bb];
+					}
+					l_lane = fmaf(l_lane, alpha_v, psum);
 					if (moved) // uniform in the lane group: its lanes share m
 					{
 #pragma unroll
@@ -968,38 +999,38 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 #pragma unroll
 							for (int e = 0; e < E; ++e) o[r][e] *= alpha[r];
 					}
-					// o += p v over the batch's keys. With four or more rows per warp
-					// the batch's weights go through this warp's scratch and come back
-					// four at a time as broadcast loads, instead of a shuffle each
-					float* pb = pbuf + warp * 32;
-					if constexpr (RMW >= 4)
-					{
-						if ((lj & ((1 << SHIFT) - 1)) == 0) pb[lg * N + (lj >> SHIFT)] = pv;
-						__syncwarp();
-					}
+					if constexpr (RMW >= 4) __syncwarp();
+					// o += p v over the batches' keys
 #pragma unroll
-					for (int kk = 0; kk < KS; ++kk)
+					for (int bb = 0; bb < NBS; ++bb)
 					{
-						float vv[E];
-						const int np = key_base + k0 + kk - new_lo;
-						load_lane<E, LK>((unsigned)np < (unsigned)n_new ? new_v + np * NSTRIDE : Vt + (size_t)(k0 + kk) * D,
-						                 lj, vv);
+						const int k0 = kg * KB + ((sb * NBS + bb) * LG + lg) * KS;
 #pragma unroll
-						for (int r = 0; r < RMW; ++r)
+						for (int kk = 0; kk < KS; ++kk)
 						{
-							float p;
-							if constexpr (RMW >= 4)
-							{
-								const float4 p4 = *reinterpret_cast<const float4*>(pb + lg * N + kk * RMW + (r & ~3));
-								p = (r & 3) == 0 ? p4.x : (r & 3) == 1 ? p4.y : (r & 3) == 2 ? p4.z : p4.w;
-							}
-							else
-								p = __shfl_sync(0xffffffffu, pv, gbase + ((kk * RMW + r) << SHIFT));
+							float vv[E];
+							const int np = key_base + k0 + kk - new_lo;
+							load_lane<E, LK>((unsigned)np < (unsigned)n_new ? new_v + np * NSTRIDE
+							                                                : Vt + (size_t)(k0 + kk) * D,
+							                 lj, vv);
 #pragma unroll
-							for (int e = 0; e < E; ++e) o[r][e] = fmaf(p, vv[e], o[r][e]);
+							for (int r = 0; r < RMW; ++r)
+							{
+								float p;
+								if constexpr (RMW >= 4)
+								{
+									const float4 p4 = *reinterpret_cast<const float4*>(pb + (bb * LG + lg) * N + kk * RMW +
+									                                                    (r & ~3));
+									p = (r & 3) == 0 ? p4.x : (r & 3) == 1 ? p4.y : (r & 3) == 2 ? p4.z : p4.w;
+								}
+								else
+									p = __shfl_sync(0xffffffffu, pv[bb], gbase + ((kk * RMW + r) << SHIFT));
+#pragma unroll
+								for (int e = 0; e < E; ++e) o[r][e] = fmaf(p, vv[e], o[r][e]);
+							}
 						}
 					}
-					if constexpr (RMW >= 4) __syncwarp(); // the scratch is read before the next batch writes it
+					if constexpr (RMW >= 4) __syncwarp(); // the scratch is read before the next batches write it
 				}
 			}
 			__syncwarp();
