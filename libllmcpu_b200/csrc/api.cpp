@@ -917,7 +917,10 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	const size_t sb = (size_t)P.n_ctas * sizeof(CtaStart);
 	auto& slot = kv->slots[kv->slot_next];
 	kv->slot_next = (kv->slot_next + 1) % nncu_kv::JOB_SLOTS;
-	CU(cudaEventSynchronize(slot.up), "job table reuse"); // its pinned copy was read
+	// its pinned copy was read (usually long since: a query is cheaper than a wait)
+	cudaError_t q = cudaEventQuery(slot.up);
+	if (q == cudaErrorNotReady) q = cudaEventSynchronize(slot.up);
+	CU(q, "job table reuse");
 	CU(slot.host.reserve(jb + sb), "job table (host)");
 	if (slot.dev.cap < jb + sb)
 	{
