@@ -497,10 +497,18 @@ def run_e2e(args, w: Workload, N, kv, layers, share: Share, host, grp, stream, d
             grp.attention(kv, arr, share.key_lo, share.key_hi, stream)
             grp.read_output(rows_out * layers[0].D, stream)
         api = "host inputs up + nncu_attention_split_dev + nncu_group_copy_output down"
-    for _ in range(args.warmup):
-        one()
+    # warm up to a steady state (the host path's first few hundred calls run
+    # slower than the rest): at least W steps and a third of a second on one
+    # GPU; a fixed count on several, where every rank must take the same steps
     if dist:
+        for _ in range(max(args.warmup, 100)):
+            one()
         dist.barrier()
+    else:
+        n_warm, t_warm = 0, time.perf_counter() + 0.33
+        while n_warm < args.warmup or time.perf_counter() < t_warm:
+            one()
+            n_warm += 1
     t0 = time.perf_counter()
     for _ in range(args.steps):
         one()

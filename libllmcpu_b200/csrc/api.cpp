@@ -929,7 +929,16 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	const size_t jb = align_up((size_t)n * sizeof(DevJob), 16);
 	const size_t sb = (size_t)P.n_ctas * sizeof(CtaStart);
 	nncu_kv::JobSlot* used = nullptr;
-	if (staged && jb + sb <= staged->cap)
+	InlineTable tab_inline;
+	const InlineTable* tab = nullptr;
+	if (!group && !staged && P.fused && jb + sb <= (size_t)INLINE_TABLE_BYTES)
+	{
+		// small enough to travel with the launch: no upload, no events
+		std::memcpy(tab_inline.b, jobs.data(), (size_t)n * sizeof(DevJob));
+		std::memcpy(tab_inline.b + jb, kv->starts_tmp.data(), sb);
+		tab = &tab_inline;
+	}
+	else if (staged && jb + sb <= staged->cap)
 	{
 		std::memcpy(staged->host + staged->lead, jobs.data(), (size_t)n * sizeof(DevJob));
 		std::memcpy(staged->host + staged->lead + jb, kv->starts_tmp.data(), sb);
@@ -1007,7 +1016,7 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	if (e) return cuda_fail((cudaError_t)e, "K1 (norm, RoPE, append) launch");
 	{
 		PerfScope ps(NNCU_PERF_ATTN_CORE, core_bytes, st);
-		e = launch_decode(P, st);
+		e = launch_decode(P, st, tab);
 	}
 	if (e) return cuda_fail((cudaError_t)e, "K2 (attention) launch");
 	if (group)

@@ -84,6 +84,16 @@ struct alignas(16) CtaStart
 };
 static_assert(sizeof(CtaStart) == 48, "CtaStart layout");
 
+// A small launch's job table (n DevJobs, then the CTA starts at the next
+// 16-byte boundary) passed by value as a kernel parameter, so the launch
+// needs no upload. Sized so that it and the DecodePlan stay within the
+// 4 KB of ordinary kernel parameters.
+constexpr int INLINE_TABLE_BYTES = 3712;
+struct alignas(16) InlineTable
+{
+	unsigned char b[INLINE_TABLE_BYTES];
+};
+
 constexpr int MAX_WORLD = 8; // GPUs a sequence may be split over (one NVSwitch node)
 
 // One launch of K1 and K2: each CTA streams a run of whole chunks (of one or
@@ -146,7 +156,10 @@ int set_cuda_error(int cuda_status, const char* what);
 
 // Launchers (implemented in the .cu files). Each returns a cudaError_t value.
 int launch_prep(const DecodePlan& plan, void* stream);
-int launch_decode(const DecodePlan& plan, void* stream);
+// The decode kernel; with `tab`, its job table and CTA starts travel in the
+// launch's parameters (a fused launch whose table fits) and plan.jobs /
+// plan.cta_start are not read.
+int launch_decode(const DecodePlan& plan, void* stream, const InlineTable* tab = nullptr);
 int launch_split_wait(const DecodePlan& plan, void* stream); // a split call's end: this GPU's rows merged
 
 // Fill the split fields of a plan from a group (split.cpp): its peers'

@@ -130,29 +130,33 @@ struct Cursor
 	int n_tiles = 1, n_segs = 1;
 };
 
-__device__ __forceinline__ void cursor_load(const DecodePlan& P, Cursor& c)
+// `jobs`: the job table in global memory, or (INL) in the kernel's
+// parameters.
+template <bool INL>
+__device__ __forceinline__ void cursor_load(const DevJob* jobs, int n_jobs, Cursor& c)
 {
-	const DevJob& J = P.jobs[c.job];
+	const DevJob& J = jobs[c.job];
 	c.n_tiles = J.n_tiles;
 	c.n_segs = J.n_kv * J.n_rowgroups;
-	if (c.job + 1 < P.n_jobs)
+	if (!INL && c.job + 1 < n_jobs)
 	{
 		// the next job's descriptor into L1 ahead of the job change
-		const char* nx = reinterpret_cast<const char*>(P.jobs + c.job + 1);
+		const char* nx = reinterpret_cast<const char*>(jobs + c.job + 1);
 		for (int b = 0; b < (int)sizeof(DevJob); b += 128) asm volatile("prefetch.global.L1 [%0];" ::"l"(nx + b));
 	}
 }
 
 // On to the first tile of the next segment.
-__device__ __forceinline__ void cursor_next_segment(const DecodePlan& P, Cursor& c)
+template <bool INL>
+__device__ __forceinline__ void cursor_next_segment(const DevJob* jobs, int n_jobs, Cursor& c)
 {
 	c.tis = 0;
 	if (++c.seg < c.n_segs) return;
 	c.seg = 0;
 	do
 		++c.job;
-	while (c.job < P.n_jobs && P.jobs[c.job].n_tiles == 0);
-	if (c.job < P.n_jobs) cursor_load(P, c);
+	while (c.job < n_jobs && jobs[c.job].n_tiles == 0);
+	if (c.job < n_jobs) cursor_load<INL>(jobs, n_jobs, c);
 }
 
 // Whether tiles [tis, tis + n) of a job's segment hold keys appended in this
@@ -171,14 +175,6 @@ __device__ __forceinline__ int atomic_add_acq_rel(int* p, int v)
 {
 	int old;
 	asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-	return old;
-}
-
-// The same at system scope: partials crossing to other GPUs of a split.
-__device__ __forceinline__ int atomic_add_acq_rel_sys(int* p, int v)
-{
-	int old;
-	asm volatile("atom.acq_rel.sys.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
 	return old;
 }
 
@@ -263,8 +259,11 @@ __device__ __forceinline__ int seg_rows(const DevJob& J, int rg, int RM)
 	return min(RM, (J.n_head / J.n_kv) * J.n_tok - rg * RM);
 }
 
-template <int D, typename KV, int RM>
-__global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePlan P)
+// The kernel's body. INL: the job table and the CTA starts are the bytes
+// `tab` of the kernel's parameters (a small launch, no upload) instead of
+// P.jobs and P.cta_start in global memory.
+template <int D, typename KV, int RM, bool INL>
+__device__ __forceinline__ void decode_body(const DecodePlan& P, const unsigned char* tab)
 {
 	using C = Cfg<D, KV, RM>;
 	using T_ = typename KV::T;
@@ -290,10 +289,13 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	CtaStart* s_start = reinterpret_cast<CtaStart*>(qempty + 4);          // this CTA's start (16-byte aligned)
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+	const DevJob* jobs = INL ? reinterpret_cast<const DevJob*>(tab) : P.jobs;
+	const CtaStart* starts =
+		INL ? reinterpret_cast<const CtaStart*>(tab + ((P.n_jobs * sizeof(DevJob) + 15) & ~size_t(15))) : P.cta_start;
 
 	if (threadIdx.x == 0)
 	{
-		*s_start = P.cta_start[blockIdx.x];
+		*s_start = starts[blockIdx.x];
 		for (int s = 0; s < STAGES; ++s)
 		{
 			mbar_init(&full[s], 1);
@@ -334,7 +336,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 			c0.job = S.job;
 			c0.seg = S.seg;
 			c0.tis = S.tis;
-			cursor_load(P, c0);
+			cursor_load<INL>(jobs, P.n_jobs, c0);
 			int piece = 0, i = 0;
 			bool waited = false;
 			for (int pass = 0; pass < (P.fused ? 1 : 2) && !s_flags[0]; ++pass)
@@ -342,7 +344,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 				Cursor cur = c0;
 				for (int left = n_mine; left > 0 && !s_flags[0];)
 				{
-					const DevJob& J = P.jobs[cur.job];
+					const DevJob& J = jobs[cur.job];
 					const int n = min(min(cur.n_tiles - cur.tis, J.chunk - cur.tis % J.chunk), left);
 					const bool fresh = holds_new_rows(J, cur.tis, n, T);
 					if (P.fused || (int)fresh == pass)
@@ -373,8 +375,15 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 							(uint32_t)(sizeof(DevJob) + rows * D * 4 + (J.q_gamma ? D * 4 : 0) + inv_bytes +
 						               (J.freq_factors ? half * 4 : 0) +
 						               (append ? (J.k_gamma ? D * 4 : 0) + 2 * J.n_tok * D * 4 : 0));
-						mbar_arrive_expect_tx(&qfull[sl], bytes); // also releases the stores above
-						bulk_g2s(slot, &J, (uint32_t)sizeof(DevJob), &qfull[sl]);
+						if constexpr (INL)
+						{
+							// from the parameters: plain copies (the bulk copy reads global memory only)
+#pragma unroll
+							for (int w = 0; w < (int)(sizeof(DevJob) / 16); ++w)
+								reinterpret_cast<uint4*>(slot)[w] = reinterpret_cast<const uint4*>(&J)[w];
+						}
+						mbar_arrive_expect_tx(&qfull[sl], bytes - (INL ? (uint32_t)sizeof(DevJob) : 0u)); // also releases the stores above
+						if constexpr (!INL) bulk_g2s(slot, &J, (uint32_t)sizeof(DevJob), &qfull[sl]);
 						if (J.q_gamma) bulk_g2s(slot + C::QGAIN, J.q_gamma, (uint32_t)(D * 4), &qfull[sl]);
 						if (inv_bytes) bulk_g2s(slot + C::QINV, J.rope_inv, inv_bytes, &qfull[sl]);
 						if (J.freq_factors) bulk_g2s(slot + C::QFF, J.freq_factors, (uint32_t)(half * 4), &qfull[sl]);
@@ -427,7 +436,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 					}
 					left -= n;
 					cur.tis += n;
-					if (cur.tis >= cur.n_tiles) cursor_next_segment(P, cur);
+					if (cur.tis >= cur.n_tiles) cursor_next_segment<INL>(jobs, P.n_jobs, cur);
 				}
 			}
 		}
@@ -1052,6 +1061,20 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePl
 	}
 }
 
+template <int D, typename KV, int RM>
+__global__ void __launch_bounds__((NW + 1) * 32, 1) decode_kernel(const DecodePlan P)
+{
+	decode_body<D, KV, RM, false>(P, nullptr);
+}
+
+// A small launch: its job table and CTA starts come with the parameters.
+template <int D, typename KV, int RM>
+__global__ void __launch_bounds__((NW + 1) * 32, 1)
+	decode_kernel_inline(const DecodePlan P, const __grid_constant__ InlineTable tab)
+{
+	decode_body<D, KV, RM, true>(P, tab.b);
+}
+
 // The end of a split call on this GPU: wait (bounded) until every segment's
 // merge has landed here, then clear the count for this parity's next call. A
 // rank that never arrives makes this time out with DEVERR_SPLIT instead of
@@ -1183,19 +1206,21 @@ __global__ void attn_finish_kernel(float* out, size_t out_stride, const float* a
 // ---- dispatch over (D, element type, rows) -----------------------------------------
 
 template <int D, typename KV, int RM>
-int launch_one(const DecodePlan& P, cudaStream_t st)
+int launch_one(const DecodePlan& P, const InlineTable* tab, cudaStream_t st)
 {
 	using C = Cfg<D, KV, RM>;
-	static bool configured[64] = {};
+	static bool configured[2][64] = {};
 	int dev = 0;
 	cudaGetDevice(&dev);
 	if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-	if (!configured[dev])
+	if (!configured[tab != nullptr][dev])
 	{
-		cudaError_t e = cudaFuncSetAttribute(decode_kernel<D, KV, RM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-		                                     C::SMEM);
+		cudaError_t e = tab ? cudaFuncSetAttribute(decode_kernel_inline<D, KV, RM>,
+		                                           cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM)
+		                    : cudaFuncSetAttribute(decode_kernel<D, KV, RM>,
+		                                           cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
 		if (e != cudaSuccess) return (int)e;
-		configured[dev] = true;
+		configured[tab != nullptr][dev] = true;
 	}
 	// launched as a programmatic dependent of the K1 grid before it (when there
 	// is one): it starts while K1 runs and waits for it where it must
@@ -1209,26 +1234,27 @@ int launch_one(const DecodePlan& P, cudaStream_t st)
 	attr[0].val.programmaticStreamSerializationAllowed = 1;
 	cfg.attrs = attr;
 	cfg.numAttrs = P.fused ? 0 : 1; // appending itself, it follows the stream's previous work in full
+	if (tab) return (int)cudaLaunchKernelEx(&cfg, decode_kernel_inline<D, KV, RM>, P, *tab);
 	return (int)cudaLaunchKernelEx(&cfg, decode_kernel<D, KV, RM>, P);
 }
 
 template <int D, typename KV>
-int launch_rows(const DecodePlan& P, cudaStream_t st)
+int launch_rows(const DecodePlan& P, const InlineTable* tab, cudaStream_t st)
 {
 	constexpr int E = D / 32;
 	switch (P.RM)
 	{
-	case 1: return launch_one<D, KV, 1>(P, st);
-	case 2: return launch_one<D, KV, 2>(P, st);
-	case 4: return launch_one<D, KV, 4>(P, st);
+	case 1: return launch_one<D, KV, 1>(P, tab, st);
+	case 2: return launch_one<D, KV, 2>(P, tab, st);
+	case 4: return launch_one<D, KV, 4>(P, tab, st);
 	case 8:
-		if constexpr (8 * E <= 64) return launch_one<D, KV, 8>(P, st);
+		if constexpr (8 * E <= 64) return launch_one<D, KV, 8>(P, tab, st);
 		break;
 	case 16:
-		if constexpr (16 * E <= 64) return launch_one<D, KV, 16>(P, st);
+		if constexpr (16 * E <= 64) return launch_one<D, KV, 16>(P, tab, st);
 		break;
 	case 32:
-		if constexpr (32 * E <= 64) return launch_one<D, KV, 32>(P, st);
+		if constexpr (32 * E <= 64) return launch_one<D, KV, 32>(P, tab, st);
 		break;
 	default: break;
 	}
@@ -1236,14 +1262,14 @@ int launch_rows(const DecodePlan& P, cudaStream_t st)
 }
 
 template <typename KV>
-int launch_dims(const DecodePlan& P, cudaStream_t st)
+int launch_dims(const DecodePlan& P, const InlineTable* tab, cudaStream_t st)
 {
 	switch (P.D)
 	{
-	case 64: return launch_rows<64, KV>(P, st);
-	case 128: return launch_rows<128, KV>(P, st);
-	case 256: return launch_rows<256, KV>(P, st);
-	case 512: return launch_rows<512, KV>(P, st);
+	case 64: return launch_rows<64, KV>(P, tab, st);
+	case 128: return launch_rows<128, KV>(P, tab, st);
+	case 256: return launch_rows<256, KV>(P, tab, st);
+	case 512: return launch_rows<512, KV>(P, tab, st);
 	default: return (int)cudaErrorInvalidValue;
 	}
 }
@@ -1311,15 +1337,15 @@ int decode_fuse_tokens(int D, int kv_type, int RM)
 }
 
 
-int launch_decode(const DecodePlan& P, void* stream)
+int launch_decode(const DecodePlan& P, void* stream, const InlineTable* tab)
 {
 	if (P.n_ctas == 0) return 0;
 	auto st = static_cast<cudaStream_t>(stream);
 	switch (P.kv_type)
 	{
-	case KV_F32: return launch_dims<kv_f32>(P, st);
-	case KV_BF16: return launch_dims<kv_bf16>(P, st);
-	default: return launch_dims<kv_f16>(P, st);
+	case KV_F32: return launch_dims<kv_f32>(P, tab, st);
+	case KV_BF16: return launch_dims<kv_bf16>(P, tab, st);
+	default: return launch_dims<kv_f16>(P, tab, st);
 	}
 }
 
