@@ -833,68 +833,18 @@ __device__ __forceinline__ void decode_body(const DecodePlan& P, const unsigned 
 		}
 		if (split && have)
 		{
-			// Arrive on every GPU's counter for this segment: one system-scope
-			// fence orders the partial's stores (every thread's, through the CTA
-			// barrier) before the arrivals, which then go out together. Where
-			// this partial is the last of the split to arrive, merge the ranks'
-			// partials in rank order into that GPU's output rows (a group of
-			// threads per such GPU), then count the segment done there. Nothing
-			// waits: whoever arrives last does the merge.
+			// This GPU's result for the segment is in every GPU's receive buffer:
+			// one system-scope fence orders those stores (every thread's, through
+			// the CTA barrier) before the arrivals, which then go out together.
+			// Each GPU merges the world's partials at the end of its own call
+			// (split_merge_kernel), with loads and stores of its own memory.
 			named_sync(1, NW * 32);
 			if (ctid == 0)
 			{
 				fence_acq_rel_sys();
-				int old[MAX_WORLD];
 #pragma unroll
 				for (int g = 0; g < MAX_WORLD; ++g)
-					old[g] = g < P.world ? atomic_add_relaxed_sys(P.arrive[g] + seg, 1) : 0;
-				int mask = 0;
-#pragma unroll
-				for (int g = 0; g < MAX_WORLD; ++g)
-					if (g < P.world && old[g] == P.world - 1) mask |= 1 << g;
-				if (mask) fence_acq_rel_sys(); // the other partials' stores before this CTA reads them
-				s_flags[2] = mask;
-			}
-			named_sync(1, NW * 32);
-			const int mask = s_flags[2];
-			const int n_m = __popc(mask);
-			if (n_m)
-			{
-				const int per = (NW * 32 / n_m) & ~31; // threads per merging GPU, whole warps
-				const int gi = ctid / per;
-				if (gi < n_m)
-				{
-					int g = 0;
-					for (int k = 0, seen = 0; k < MAX_WORLD; ++k)
-						if (mask >> k & 1)
-						{
-							if (seen == gi) g = k;
-							++seen;
-						}
-					float* out_g = P.out[g] + (size_t)pe.out_row0 * D;
-					merge_pieces<D, RM>(recv_row(g, 0, 0), (size_t)P.recv_stride, P.world, rows_valid, ctid - gi * per, per,
-					                    [&](int R, int d, float4 acc, float M, float L) {
-						                    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-						                    acc.x *= inv;
-						                    acc.y *= inv;
-						                    acc.z *= inv;
-						                    acc.w *= inv;
-						                    *reinterpret_cast<float4*>(out_row(out_g, R) + d) = acc;
-					                    });
-				}
-				named_sync(1, NW * 32);
-				if (ctid == 0)
-				{
-					// the counters cleared for this parity's next call, then (after the
-					// merged rows and the clears) the segment counted done on each GPU
-#pragma unroll
-					for (int g = 0; g < MAX_WORLD; ++g)
-						if (mask >> g & 1) atomicExch(P.arrive[g] + seg, 0);
-					fence_acq_rel_sys();
-#pragma unroll
-					for (int g = 0; g < MAX_WORLD; ++g)
-						if (mask >> g & 1) atomic_add_relaxed_sys(P.done[g], 1);
-				}
+					if (g < P.world) atomic_add_relaxed_sys(P.arrive[g] + seg, 1);
 			}
 		}
 		named_sync(1, NW * 32); // the merge area is free again
@@ -1075,24 +1025,64 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
 	decode_body<D, KV, RM, true>(P, tab.b);
 }
 
-// The end of a split call on this GPU: wait (bounded) until every segment's
-// merge has landed here, then clear the count for this parity's next call. A
-// rank that never arrives makes this time out with DEVERR_SPLIT instead of
-// hanging; the host reports it as NNCU_ERR_TIMEOUT.
-__global__ void split_wait_kernel(int* done, int target, int* err)
+// The end of a split call on this GPU: a CTA per segment waits (bounded)
+// until every GPU's partial of the segment has landed in this GPU's receive
+// buffer, merges them in rank order (nnc_attn_merge, then nnc_attn_finish)
+// into this GPU's output rows, and clears the segment's count for this
+// parity's next call. A rank that never arrives makes the wait time out with
+// DEVERR_SPLIT instead of hanging; the host reports it as NNCU_ERR_TIMEOUT.
+__global__ void split_merge_kernel(const DecodePlan P)
 {
-	if (threadIdx.x != 0) return;
-	const uint64_t t0 = globaltimer_ns();
-	while (ld_acquire_sys(done) < target)
+	const int seg = blockIdx.x;
+	__shared__ int s_ok, s_job;
+	if (threadIdx.x == 0)
 	{
-		if (globaltimer_ns() - t0 > WAIT_LIMIT_NS)
+		const int* cnt = P.arrive[P.rank] + seg;
+		const uint64_t t0 = globaltimer_ns();
+		int ok = 1;
+		while (ld_acquire_sys(cnt) < P.world)
 		{
-			atomicExch(err, DEVERR_SPLIT);
-			return;
+			if (globaltimer_ns() - t0 > WAIT_LIMIT_NS)
+			{
+				atomicExch(P.err, DEVERR_SPLIT);
+				ok = 0;
+				break;
+			}
+			__nanosleep(100);
 		}
-		__nanosleep(200);
+		int j = 0; // the segment's job (jobs hold consecutive segment ranges)
+		while (j + 1 < P.n_jobs && P.jobs[j + 1].seg0 <= seg) ++j;
+		s_ok = ok;
+		s_job = j;
 	}
-	atomicExch(done, 0);
+	__syncthreads();
+	if (!s_ok) return;
+	const DevJob& J = P.jobs[s_job];
+	const int seg_local = seg - J.seg0;
+	const int h = seg_local / J.n_rowgroups, rg = seg_local % J.n_rowgroups;
+	const int G = J.n_head / J.n_kv, RM = P.RM, D = P.D, PW = D + 4;
+	const int rows_valid = min(RM, G * J.n_tok - rg * RM);
+	float* out = P.out[P.rank] + (size_t)J.out_row0 * D;
+	const float* base = P.recv[P.rank] + (size_t)seg * RM * PW; // rank r's partial at + r * recv_stride
+	for (int idx = threadIdx.x; idx < rows_valid * D; idx += blockDim.x)
+	{
+		const int R = idx / D, d = idx % D;
+		float M = -CUDART_INF_F;
+		for (int r = 0; r < P.world; ++r) M = fmaxf(M, __ldcg(base + (size_t)r * P.recv_stride + R * PW + D));
+		float acc = 0.0f, L = 0.0f;
+		for (int r = 0; r < P.world; ++r)
+		{
+			const float* pr = base + (size_t)r * P.recv_stride + R * PW;
+			const float m = __ldcg(pr + D);
+			const float c = m == -CUDART_INF_F ? 0.0f : ex2(m - M);
+			acc = fmaf(__ldcg(pr + d), c, acc);
+			L = fmaf(__ldcg(pr + D + 1), c, L);
+		}
+		const int gr = rg * RM + R;
+		out[((size_t)(gr / G) * J.n_head + (size_t)h * G + gr % G) * D + d] = acc * (L > 0.0f ? 1.0f / L : 0.0f);
+	}
+	__syncthreads();
+	if (threadIdx.x == 0) atomicExch(P.arrive[P.rank] + seg, 0); // ready for this parity's next call
 }
 
 // ---- unit seam: nnc_attn_block / merge / finish on device pointers ---------------
@@ -1351,7 +1341,7 @@ int launch_decode(const DecodePlan& P, void* stream, const InlineTable* tab)
 
 int launch_split_wait(const DecodePlan& P, void* stream)
 {
-	split_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(P.done[P.rank], P.n_segments, P.err);
+	split_merge_kernel<<<(unsigned)P.n_segments, 256, 0, static_cast<cudaStream_t>(stream)>>>(P);
 	return (int)cudaGetLastError();
 }
 
