@@ -254,10 +254,11 @@ int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_j
  * attend_blocks (model.cpp:1296-1319) merging 256-key blocks in order with
  * nnc_attn_merge (nn_ops.cpp:461-482): here GPU r holds and reads keys
  * [key_lo, key_hi) of the sequence, and the partials of all GPUs are merged
- * in rank order, on every GPU, inside the attention kernel: each GPU stores
- * its partial straight into every other GPU's receive buffer over NVLink and
- * the last to arrive merges. One process per GPU; every rank makes the same
- * calls in the same order.
+ * in rank order on every GPU: the attention kernel stores each GPU's partial
+ * straight into every GPU's receive buffer over NVLink, and a kernel at the
+ * end of the call merges, on each GPU, the partials that landed in its own
+ * memory. One process per GPU; every rank makes the same calls in the same
+ * order.
  *
  * nncu_group_create allocates this GPU's shared block (receive buffers,
  * counters, and the output: max_rows rows of head_dim floats, the jobs'

@@ -160,7 +160,7 @@ int launch_prep(const DecodePlan& plan, void* stream);
 // launch's parameters (a fused launch whose table fits) and plan.jobs /
 // plan.cta_start are not read.
 int launch_decode(const DecodePlan& plan, void* stream, const InlineTable* tab = nullptr);
-int launch_split_wait(const DecodePlan& plan, void* stream); // a split call's end: this GPU's rows merged
+int launch_split_wait(const DecodePlan& plan, void* stream); // a split call's end: the world's partials merged here
 
 // Fill the split fields of a plan from a group (split.cpp): its peers'
 // buffers for this call's parity; checks that the call fits the group.

@@ -4,13 +4,13 @@
 // holds and reads one 256-aligned range of the keys, and the per-range
 // partials (o, m, l) are merged by log-sum-exp in rank order, the reference's
 // nnc_attn_merge over blocks (nn_ops.cpp:461-482) with the blocks grouped by
-// GPU. The merge crosses NVLink inside the attention kernel itself: a
+// GPU. The partials cross NVLink inside the attention kernel itself: a
 // segment's partial is stored straight into every GPU's receive buffer (peer
-// stores through CUDA IPC mappings), and on each GPU the last partial to
-// arrive (a system-scope counter per segment) merges them into that GPU's
-// output. No kernel waits for another GPU's kernel in the data path; a small
-// kernel at the end of each call waits, bounded, for this GPU's merges to
-// land.
+// stores through CUDA IPC mappings) and counted on a system-scope counter per
+// segment there. A kernel at the end of each call waits, bounded, on each
+// GPU until the world's partials of every segment have landed in its own
+// memory, and merges them into that GPU's output with local loads and
+// stores.
 //
 // One process per GPU. The caller exchanges the groups' memory handles out of
 // band (torch.distributed in the Python binding) and opens each peer's.
