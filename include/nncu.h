@@ -213,7 +213,10 @@ int nncu_attention(nncu_kv* kv, int32_t layer, int32_t seq, const nncu_attn_para
  * nncu_attention's worth of work. In nncu_attention_batch every pointer is a
  * host pointer and the call is synchronous (one host->device copy of all
  * inputs, one device->host copy of all outputs). In nncu_attention_batch_dev
- * every pointer is a device pointer and the call is asynchronous on `stream`.
+ * every pointer is a device pointer and the call is asynchronous on `stream`;
+ * the kernels bulk-copy q, k, v and the gains and write out with 16-byte
+ * stores, so each of those must be 16-byte aligned (a misaligned one is
+ * refused with NNCU_ERR_INVALID_ARGUMENT before anything runs).
  * Jobs of one submission must not append to a cache another of its jobs
  * reads. */
 typedef struct nncu_attn_job
@@ -247,7 +250,12 @@ int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_j
  * overlap on the GPU race on it (order them on one stream); a call that would
  * need more fails with NNCU_ERR_INVALID_ARGUMENT and a message. The first call
  * on each device looks the array's device address up (cudaGetSymbolAddress)
- * with that device current; make that first call during set-up. */
+ * with that device current; make that first call during set-up. Every pointer
+ * (q, k, v, out, the gains, freq_factors, k_cache, v_cache) must be 16-byte
+ * aligned; a misaligned one is refused before anything runs.
+ *
+ * A kernel whose bounded wait runs out leaves an error word in the shared
+ * array, which later calls keep; nncu_noalloc_check (below) reads it. */
 /* ---- One sequence split over the GPUs of a node ----
  *
  * No counterpart in the reference (one CPU, one process). Its equivalent is
@@ -269,7 +277,16 @@ int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_j
  * only by the GPU whose range holds them) and leaves the merged attention in
  * nncu_group_output() of every GPU when `stream` reaches the end of the call.
  * A rank that does not take part makes the others' calls end with
- * NNCU_ERR_TIMEOUT (reported by nncu_sync) after 2 s instead of hanging. */
+ * NNCU_ERR_TIMEOUT (reported by nncu_sync) after 2 s (nncu_group_set_timeout)
+ * instead of hanging.
+ *
+ * After a timeout the group is poisoned on the GPU that saw it: a late
+ * partial may still be counted there, so every later split call on that GPU
+ * fails with NNCU_ERR_TIMEOUT rather than merge stale partials. To recover,
+ * every rank waits for its own calls (nncu_sync), the ranks meet on the host
+ * (a barrier), each calls nncu_group_reset, and they meet again before the
+ * next call: the counters of both parities are cleared and the call count
+ * restarts in step on every rank. */
 typedef struct nncu_group nncu_group;
 #define NNCU_GROUP_HANDLE_BYTES 64
 int nncu_group_create(int32_t device, int32_t rank, int32_t world, int32_t max_rows, int32_t head_dim,
@@ -281,12 +298,29 @@ float* nncu_group_output(const nncu_group* g);
  * memory), ordered on `stream` after the split calls before it. */
 int nncu_group_copy_output(const nncu_group* g, float* dst, size_t n_floats, void* stream);
 void nncu_group_free(nncu_group* g);
+/* The bounded wait of each GPU's end-of-call merge, in milliseconds (1 to
+ * 60000; 2000 by default). */
+int nncu_group_set_timeout(nncu_group* g, uint32_t ms);
+/* Clear this GPU's counters and poison word and restart its call count; only
+ * at a step boundary that every rank has reached with no call in flight
+ * (see above). Waits for this GPU to be idle. */
+int nncu_group_reset(nncu_group* g);
+/* Failure injection for tests: this rank's next n_calls split calls store
+ * their partials but never count them, so every GPU's merge of those calls
+ * runs out of time (NNCU_ERR_TIMEOUT) -- a message dropped on the host's
+ * side, with no fault on the device. */
+int nncu_group_inject_drop(nncu_group* g, int32_t n_calls);
 int nncu_attention_split_dev(nncu_kv* kv, nncu_group* group, const nncu_attn_job* jobs, int32_t n_jobs,
                              int32_t key_lo, int32_t key_hi, void* stream);
 
 #define NNCU_NOALLOC_MAX_TOKENS 64
 int nncu_attention_noalloc(const nncu_attn_params* p, const float* q, const float* k, const float* v, float* out,
                            void* k_cache, void* v_cache, int32_t kv_type, int32_t rows, void* stream);
+/* Wait for `stream` and report whether a no-allocation call on the current
+ * device since the last check had a kernel whose bounded wait ran out
+ * (NNCU_ERR_TIMEOUT: the outputs of those calls are void); the word is then
+ * cleared. Allocates nothing. No reference counterpart. */
+int nncu_noalloc_check(void* stream);
 
 /* Wait for `stream` (the asynchronous calls' completion) and report a kernel
  * whose bounded wait ran out (NNCU_ERR_TIMEOUT: the outputs are void). The

@@ -54,7 +54,8 @@ EXPORTS = [
     "nncu_attention_batch", "nncu_attention_batch_dev", "nncu_sync", "nncu_perf_enable", "nncu_perf_reset",
     "nncu_perf_read", "nncu_perf_report", "nncu_launch_count", "nncu_attention_noalloc", "nncu_group_create",
     "nncu_group_handle", "nncu_group_open", "nncu_group_output", "nncu_group_copy_output", "nncu_group_free",
-    "nncu_attention_split_dev",
+    "nncu_attention_split_dev", "nncu_group_set_timeout", "nncu_group_reset", "nncu_group_inject_drop",
+    "nncu_noalloc_check",
 ]
 GROUP_HANDLE_BYTES = 64
 
@@ -200,6 +201,10 @@ def lib() -> C.CDLL:
     L.nncu_group_free.argtypes = [vp]
     L.nncu_group_free.restype = None
     L.nncu_attention_split_dev.argtypes = [vp, vp, C.POINTER(AttnJob), i32, i32, i32, vp]
+    L.nncu_group_set_timeout.argtypes = [vp, C.c_uint32]
+    L.nncu_group_reset.argtypes = [vp]
+    L.nncu_group_inject_drop.argtypes = [vp, i32]
+    L.nncu_noalloc_check.argtypes = [vp]
     _lib = L
     return L
 
@@ -365,6 +370,12 @@ def attention_noalloc(p: AttnParams, q, k, v, out, k_cache, v_cache, kv_type: in
                                         _ptr(v_cache), int(kv_type), int(rows), _stream(stream)))
 
 
+def noalloc_check(stream=None) -> None:
+    """nncu_noalloc_check: wait for `stream`; raise (ERR_TIMEOUT) if a no-allocation
+    call on the current device timed out since the last check."""
+    _check(lib().nncu_noalloc_check(_stream(stream)))
+
+
 def job(layer: int, p: AttnParams, q, k, v, out, seq: int = 0) -> AttnJob:
     j = AttnJob(layer, seq, p, _ptr(q), _ptr(k), _ptr(v), _ptr(out))
     j._keep = (p, q, k, v, out)
@@ -468,6 +479,18 @@ class SplitGroup:
         arr = jobs if isinstance(jobs, C.Array) else (AttnJob * len(jobs))(*jobs)
         _check(lib().nncu_attention_split_dev(kv._h, self._h, arr, len(arr), int(key_lo), int(key_hi),
                                                _stream(stream)))
+
+    def set_timeout(self, ms: int) -> None:
+        """The bounded wait of this GPU's end-of-call merge."""
+        _check(lib().nncu_group_set_timeout(self._h, int(ms)))
+
+    def reset(self) -> None:
+        """nncu_group_reset: only at a step boundary every rank has reached."""
+        _check(lib().nncu_group_reset(self._h))
+
+    def inject_drop(self, n_calls: int) -> None:
+        """Test injection: this rank's next n_calls calls never count their partials."""
+        _check(lib().nncu_group_inject_drop(self._h, int(n_calls)))
 
     def close(self) -> None:
         if getattr(self, "_h", None):

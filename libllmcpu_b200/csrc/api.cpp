@@ -57,6 +57,32 @@ int nncu::set_error(int status, const char* msg)
 	return fail(status, "%s", msg);
 }
 
+// Every pointer a kernel bulk-copies from (q rows, the gains, the frequency
+// factors, the new k and v rows, the cache) or writes with 16-byte stores
+// (the output) must be 16-byte aligned; a misaligned one would fault the GPU
+// instead of failing the call, so it is refused here, before any launch.
+int nncu::check_alignment(const JobPointers& p, int job, const char* what)
+{
+	const struct
+	{
+		const void* ptr;
+		const char* name;
+	} ptrs[] = {{p.q, "q"},
+	            {p.k, "k"},
+	            {p.v, "v"},
+	            {p.out, "out"},
+	            {p.q_gamma, "q_gamma"},
+	            {p.k_gamma, "k_gamma"},
+	            {p.freq_factors, "freq_factors"},
+	            {p.k_cache, "k_cache"},
+	            {p.v_cache, "v_cache"}};
+	for (const auto& e : ptrs)
+		if (reinterpret_cast<uintptr_t>(e.ptr) & 15u)
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "%s: job %d: %s (%p) is not 16-byte aligned", what, job, e.name,
+			            e.ptr);
+	return NNCU_OK;
+}
+
 int nncu::set_cuda_error(int cuda_status, const char* what)
 {
 	return cuda_fail(static_cast<cudaError_t>(cuda_status), what);
@@ -1056,23 +1082,35 @@ int check_device_error(nncu_kv* kv)
 
 size_t fbytes(size_t n) { return align_up(n * sizeof(float), 256); }
 
+JobPointers job_pointers(const nncu_attn_job& j)
+{
+	JobPointers p{};
+	p.q = j.q;
+	p.k = j.p.reuse_kv ? nullptr : j.k;
+	p.v = j.p.reuse_kv ? nullptr : j.v;
+	p.out = j.out;
+	p.q_gamma = j.p.q_gamma;
+	p.k_gamma = j.p.k_gamma;
+	p.freq_factors = j.p.freq_factors;
+	return p;
+}
+
 } // namespace
 
 extern "C" int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs, void* stream)
 {
 	if (!kv || !jobs || n_jobs <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "no jobs");
+	int rc = NNCU_OK;
 	for (int i = 0; i < n_jobs; ++i)
 	{
-		int rc = validate_job(kv, jobs[i]);
+		rc = validate_job(kv, jobs[i]);
 		if (rc != NNCU_OK) return rc;
 		if (!jobs[i].q || !jobs[i].out || (!jobs[i].p.reuse_kv && (!jobs[i].k || !jobs[i].v)))
 			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: NULL input or output", i);
-		// q rows, the q gains and the frequency factors are bulk-copied into shared memory
-		auto misaligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; };
-		if (misaligned(jobs[i].q) || misaligned(jobs[i].p.q_gamma) || misaligned(jobs[i].p.freq_factors))
-			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: q, q_gamma and freq_factors must be 16-byte aligned", i);
+		rc = check_alignment(job_pointers(jobs[i]), i, "nncu_attention_batch_dev");
+		if (rc != NNCU_OK) return rc;
 	}
-	int rc = check_conflicts(kv, jobs, n_jobs);
+	rc = check_conflicts(kv, jobs, n_jobs);
 	if (rc != NNCU_OK) return rc;
 	DeviceGuard g(kv->device);
 	kv->jobs_tmp.resize(n_jobs);
@@ -1094,9 +1132,10 @@ extern "C" int nncu_attention_split_dev(nncu_kv* kv, nncu_group* group, const nn
 		if (rc != NNCU_OK) return rc;
 		if (!jobs[i].q || (!jobs[i].p.reuse_kv && (!jobs[i].k || !jobs[i].v)))
 			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: NULL input", i);
-		auto misaligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; };
-		if (misaligned(jobs[i].q) || misaligned(jobs[i].p.q_gamma) || misaligned(jobs[i].p.freq_factors))
-			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: q, q_gamma and freq_factors must be 16-byte aligned", i);
+		JobPointers jp = job_pointers(jobs[i]);
+		jp.out = nullptr; // the merged rows land in the group's output
+		rc = check_alignment(jp, i, "nncu_attention_split_dev");
+		if (rc != NNCU_OK) return rc;
 	}
 	int rc = check_conflicts(kv, jobs, n_jobs);
 	if (rc != NNCU_OK) return rc;

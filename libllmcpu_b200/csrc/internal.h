@@ -114,15 +114,18 @@ struct DecodePlan
 	int* err;       // device error word
 	// A sequence split over the GPUs of a group (world > 1; nncu_group, split.cpp):
 	// each segment's result over this GPU's keys goes, as a partial, to every
-	// GPU's receive buffer; on each GPU the last partial to arrive merges them
-	// in rank order into that GPU's output. All pointers are for this call's
-	// parity (calls alternate between two sets), GPU g's at index g.
+	// GPU's receive buffer and is counted there; at the end of the call each
+	// GPU merges, in rank order, the partials that landed in its own memory
+	// (split_merge_kernel). All pointers are for this call's parity (calls
+	// alternate between two sets), GPU g's at index g.
 	int world, rank;
 	long long recv_stride;       // floats between two ranks' blocks of a receive buffer
 	float* recv[MAX_WORLD];      // [world][segments][RM][D + 4]
 	int* arrive[MAX_WORLD];      // [segments] partials arrived, zero between calls
-	int* done[MAX_WORLD];        // segments merged on GPU g in this call
 	float* out[MAX_WORLD];       // GPU g's output rows (job i from its out_row0)
+	int* poison;                 // this GPU's: set by a merge wait that ran out; every later merge fails
+	unsigned long long wait_ns;  // the merge's bounded wait
+	int drop_arrivals;           // test injection: this rank's partials are stored but never counted
 };
 
 // Plan one launch over jobs[0, n) (their D, kv geometry, positions and
@@ -153,6 +156,25 @@ int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream);
 // Record a failure for nncu_last_error() (api.cpp); return `status`.
 int set_error(int status, const char* msg);
 int set_cuda_error(int cuda_status, const char* what);
+
+// The pointers of one job that the kernels read with bulk copies or write
+// with 16-byte vector stores, checked before anything is launched: a
+// misaligned one is refused with NNCU_ERR_INVALID_ARGUMENT (a bulk copy from
+// it would fault the GPU). NULL pointers pass (the caller checks which may be
+// NULL). `job` numbers the message; `what` names the call.
+struct JobPointers
+{
+	const void* q;
+	const void* k;
+	const void* v;
+	const void* out;
+	const void* q_gamma;
+	const void* k_gamma;
+	const void* freq_factors;
+	const void* k_cache;
+	const void* v_cache;
+};
+int check_alignment(const JobPointers& p, int job, const char* what);
 
 // Launchers (implemented in the .cu files). Each returns a cudaError_t value.
 int launch_prep(const DecodePlan& plan, void* stream);

@@ -839,7 +839,7 @@ __device__ __forceinline__ void decode_body(const DecodePlan& P, const unsigned 
 			// Each GPU merges the world's partials at the end of its own call
 			// (split_merge_kernel), with loads and stores of its own memory.
 			named_sync(1, NW * 32);
-			if (ctid == 0)
+			if (ctid == 0 && !P.drop_arrivals) // (a test drops them to make the merges' waits run out)
 			{
 				fence_acq_rel_sys();
 #pragma unroll
@@ -1031,6 +1031,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
 // into this GPU's output rows, and clears the segment's count for this
 // parity's next call. A rank that never arrives makes the wait time out with
 // DEVERR_SPLIT instead of hanging; the host reports it as NNCU_ERR_TIMEOUT.
+// The timeout also poisons this GPU's group: a late arrival may still count
+// into this call's counters, so no later merge trusts them (each fails at
+// once with DEVERR_SPLIT) until the host resets the group.
 __global__ void split_merge_kernel(const DecodePlan P)
 {
 	const int seg = blockIdx.x;
@@ -1038,13 +1041,19 @@ __global__ void split_merge_kernel(const DecodePlan P)
 	if (threadIdx.x == 0)
 	{
 		const int* cnt = P.arrive[P.rank] + seg;
-		const uint64_t t0 = globaltimer_ns();
 		int ok = 1;
-		while (ld_acquire_sys(cnt) < P.world)
+		if (ld_acquire_sys(P.poison) != 0)
 		{
-			if (globaltimer_ns() - t0 > WAIT_LIMIT_NS)
+			atomicExch(P.err, DEVERR_SPLIT);
+			ok = 0;
+		}
+		const uint64_t t0 = globaltimer_ns();
+		while (ok && ld_acquire_sys(cnt) < P.world)
+		{
+			if (globaltimer_ns() - t0 > P.wait_ns)
 			{
 				atomicExch(P.err, DEVERR_SPLIT);
+				atomicExch(P.poison, 1);
 				ok = 0;
 				break;
 			}

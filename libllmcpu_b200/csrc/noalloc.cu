@@ -20,7 +20,10 @@
 //    (different streams, or different host threads, without ordering between
 //    them) race on it and give wrong results; order them on one stream;
 //  * a call leaves its scratch behind for the next one, which clears the
-//    parts that must start at zero (the piece counters, the error word);
+//    parts that must start at zero (the piece counters);
+//  * the device error word (a kernel's bounded wait that ran out) stays set
+//    across calls until nncu_noalloc_check reads and clears it, so a timeout
+//    is never erased by the next call;
 //  * the first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current; make that first call
 //    before any use where even such a lookup is unwelcome.
@@ -74,6 +77,10 @@ int scratch_on_device(int dev, unsigned char** out)
 
 size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// Where the scratch keeps the device error word (first) and the rest.
+constexpr size_t OFF_ERR = 0;
+constexpr size_t OFF_ROPE = 256;
+
 // Host staging for the job descriptor, the CTA starts and the RoPE table:
 // static storage, so building them allocates nothing either.
 constexpr int MAX_CTAS = 256;
@@ -119,9 +126,18 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	if (p->window < 0 || p->softcap < 0.0f) return set_error(NNCU_ERR_INVALID_ARGUMENT, "negative window or softcap");
 	if (p->freq_factors && p->n_rot % 8)
 		return set_error(NNCU_ERR_INVALID_ARGUMENT, "freq_factors need n_rot to be a multiple of 8");
-	const auto misaligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; };
-	if (misaligned(q) || misaligned(p->q_gamma) || misaligned(p->freq_factors))
-		return set_error(NNCU_ERR_INVALID_ARGUMENT, "q, q_gamma and freq_factors must be 16-byte aligned");
+	JobPointers jp{};
+	jp.q = q;
+	jp.k = p->reuse_kv ? nullptr : k;
+	jp.v = p->reuse_kv ? nullptr : v;
+	jp.out = out;
+	jp.q_gamma = p->q_gamma;
+	jp.k_gamma = p->k_gamma;
+	jp.freq_factors = p->freq_factors;
+	jp.k_cache = k_cache;
+	jp.v_cache = v_cache;
+	int rc = check_alignment(jp, 0, "nncu_attention_noalloc");
+	if (rc != NNCU_OK) return rc;
 	// every key a query sees must still be in the caller's `rows` rows
 	const bool windowed = p->causal && p->window > 0;
 	if (windowed ? p->window + p->n_tok > rows : (p->pos0 + p->n_tok > rows || p->n_seq > rows))
@@ -131,7 +147,7 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	cudaError_t ce = cudaGetDevice(&dev);
 	if (ce != cudaSuccess) return set_cuda_error((int)ce, "cudaGetDevice");
 	unsigned char* scratch = nullptr;
-	int rc = scratch_on_device(dev, &scratch);
+	rc = scratch_on_device(dev, &scratch);
 	if (rc != NNCU_OK) return rc;
 	int n_sms = 148;
 	cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev);
@@ -141,7 +157,7 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	HostHead& hh = t_head;
 	std::memset(&hh.job, 0, sizeof hh.job);
 	DevJob& j = hh.job;
-	const size_t off_rope = 0; // scratch: [rope | job | starts | partials | counters | error]
+	const size_t off_rope = OFF_ROPE; // scratch: [error | rope | job | starts | partials | counters]
 	j.q = q;
 	j.k = k;
 	j.v = v;
@@ -177,13 +193,12 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	rc = plan_launch(&j, 1, kv_type, std::min(n_sms, MAX_CTAS), P, hh.starts, MAX_CTAS, false);
 	if (rc != NNCU_OK) return rc;
 
-	const size_t off_job = up256(256 * sizeof(float));
+	const size_t off_job = OFF_ROPE + up256(256 * sizeof(float));
 	const size_t off_starts = off_job + up256(sizeof(DevJob));
 	const size_t off_parts = off_starts + up256((size_t)MAX_CTAS * sizeof(CtaStart));
 	const size_t off_count =
 		off_parts + up256((size_t)std::max<long long>(P.n_parts, 1) * P.RM * (D + 4) * sizeof(float));
-	const size_t off_err = off_count + up256((size_t)P.n_segments * sizeof(int));
-	const size_t need = off_err + 256;
+	const size_t need = off_count + up256((size_t)P.n_segments * sizeof(int));
 	if (need > NOALLOC_SCRATCH_BYTES)
 	{
 		char msg[200];
@@ -219,7 +234,8 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 		ce = cudaMemcpyAsync(scratch + off_rope, hh.rope, (size_t)((half + 3) & ~3) * sizeof(float),
 		                     cudaMemcpyHostToDevice, st);
 	}
-	if (ce == cudaSuccess) ce = cudaMemsetAsync(scratch + off_count, 0, off_err + 256 - off_count, st);
+	// the piece counters start at zero; the error word is cleared by nncu_noalloc_check
+	if (ce == cudaSuccess) ce = cudaMemsetAsync(scratch + off_count, 0, need - off_count, st);
 	if (ce == cudaSuccess && j.n_tiles == 0)
 		ce = cudaMemsetAsync(out, 0, (size_t)p->n_tok * p->n_head * D * sizeof(float), st);
 	if (ce != cudaSuccess) return set_cuda_error((int)ce, "no-allocation call: staging");
@@ -228,13 +244,39 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	P.cta_start = reinterpret_cast<const CtaStart*>(scratch + off_starts);
 	P.parts = reinterpret_cast<float*>(scratch + off_parts);
 	P.counters = reinterpret_cast<int*>(scratch + off_count);
-	P.err = reinterpret_cast<int*>(scratch + off_err);
+	P.err = reinterpret_cast<int*>(scratch + OFF_ERR);
 	int e = P.fused ? 0 : launch_prep(P, st); // K2 appends itself when it can
 	if (e) return set_cuda_error(e, "K1 (norm, RoPE, append) launch");
 	if (P.n_ctas > 0)
 	{
 		e = launch_decode(P, st);
 		if (e) return set_cuda_error(e, "K2 (attention) launch");
+	}
+	return NNCU_OK;
+}
+
+extern "C" int nncu_noalloc_check(void* stream)
+{
+	int dev = 0;
+	cudaError_t ce = cudaGetDevice(&dev);
+	if (ce != cudaSuccess) return set_cuda_error((int)ce, "cudaGetDevice");
+	unsigned char* scratch = nullptr;
+	int rc = scratch_on_device(dev, &scratch);
+	if (rc != NNCU_OK) return rc;
+	ce = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+	if (ce != cudaSuccess) return set_cuda_error((int)ce, "no-allocation check: stream");
+	int word = 0;
+	// into this stack variable: a plain copy, nothing allocated
+	ce = cudaMemcpy(&word, scratch + OFF_ERR, sizeof word, cudaMemcpyDeviceToHost);
+	if (ce == cudaSuccess && word != 0) ce = cudaMemset(scratch + OFF_ERR, 0, sizeof word);
+	if (ce != cudaSuccess) return set_cuda_error((int)ce, "no-allocation check: error word");
+	if (word != 0)
+	{
+		char msg[160];
+		std::snprintf(msg, sizeof msg,
+		              "a no-allocation call's bounded wait timed out (code %d); the outputs since the last check are void",
+		              word);
+		return set_error(NNCU_ERR_TIMEOUT, msg);
 	}
 	return NNCU_OK;
 }

@@ -12,6 +12,12 @@
 // memory, and merges them into that GPU's output with local loads and
 // stores.
 //
+// A merge whose wait runs out marks this GPU's group as poisoned: its
+// counters may then be met late by the slow rank's arrival, so every later
+// merge on this GPU fails (NNCU_ERR_TIMEOUT through nncu_sync) instead of
+// merging stale partials, until every rank has called nncu_group_reset at a
+// common step boundary (no call of the group in flight on any GPU).
+//
 // One process per GPU. The caller exchanges the groups' memory handles out of
 // band (torch.distributed in the Python binding) and opens each peer's.
 #include <cuda_runtime.h>
@@ -30,8 +36,10 @@ struct nncu_group
 	char* base = nullptr;   // this GPU's shared block
 	char* peer[nncu::MAX_WORLD] = {};
 	bool opened[nncu::MAX_WORLD] = {};
-	size_t off_recv = 0, off_arrive = 0, off_done = 0, off_out = 0, bytes = 0;
+	size_t off_recv = 0, off_arrive = 0, off_state = 0, off_out = 0, bytes = 0;
 	int calls = 0;
+	unsigned long long wait_ns = nncu::WAIT_LIMIT_NS;
+	int drop_next = 0; // test injection: calls whose arrivals this rank drops
 };
 
 namespace
@@ -80,8 +88,8 @@ extern "C" int nncu_group_create(int32_t device, int32_t rank, int32_t world, in
 	const size_t arrive = 2 * (size_t)g->cap_rows * sizeof(int);
 	g->off_recv = 0;
 	g->off_arrive = up256(recv);
-	g->off_done = g->off_arrive + up256(arrive);
-	g->off_out = g->off_done + 256;
+	g->off_state = g->off_arrive + up256(arrive); // [0]: the poison word
+	g->off_out = g->off_state + 256;
 	g->bytes = g->off_out + up256((size_t)max_rows * head_dim * sizeof(float));
 	cudaError_t e = cudaMalloc(&g->base, g->bytes);
 	if (e == cudaSuccess) e = cudaMemset(g->base, 0, g->bytes);
@@ -148,6 +156,38 @@ extern "C" int nncu_group_copy_output(const nncu_group* g, float* dst, size_t n_
 	return NNCU_OK;
 }
 
+extern "C" int nncu_group_set_timeout(nncu_group* g, uint32_t ms)
+{
+	using namespace nncu;
+	if (!g) return set_error(NNCU_ERR_INVALID_ARGUMENT, "NULL group");
+	if (ms == 0 || ms > 60000) return set_error(NNCU_ERR_INVALID_ARGUMENT, "the timeout must be 1 to 60000 ms");
+	g->wait_ns = (unsigned long long)ms * 1000000ull;
+	return NNCU_OK;
+}
+
+extern "C" int nncu_group_reset(nncu_group* g)
+{
+	using namespace nncu;
+	if (!g) return set_error(NNCU_ERR_INVALID_ARGUMENT, "NULL group");
+	Guard dg(g->device);
+	// every kernel of this GPU that could still count into the block is done
+	cudaError_t e = cudaDeviceSynchronize();
+	if (e == cudaSuccess) e = cudaMemset(g->base + g->off_arrive, 0, g->off_out - g->off_arrive);
+	if (e == cudaSuccess) e = cudaDeviceSynchronize();
+	if (e != cudaSuccess) return set_cuda_error((int)e, "group reset");
+	g->calls = 0;
+	g->drop_next = 0;
+	return NNCU_OK;
+}
+
+extern "C" int nncu_group_inject_drop(nncu_group* g, int32_t n_calls)
+{
+	using namespace nncu;
+	if (!g || n_calls < 0) return set_error(NNCU_ERR_INVALID_ARGUMENT, "NULL group or negative count");
+	g->drop_next = n_calls;
+	return NNCU_OK;
+}
+
 extern "C" void nncu_group_free(nncu_group* g)
 {
 	if (!g) return;
@@ -180,8 +220,15 @@ int group_prepare(nncu_group* g, DecodePlan& P, int n_rows)
 		char* b = g->peer[r];
 		P.recv[r] = reinterpret_cast<float*>(b + g->off_recv) + (size_t)parity * g->world * P.recv_stride;
 		P.arrive[r] = reinterpret_cast<int*>(b + g->off_arrive) + (size_t)parity * g->cap_rows;
-		P.done[r] = reinterpret_cast<int*>(b + g->off_done) + parity;
 		P.out[r] = reinterpret_cast<float*>(b + g->off_out);
+	}
+	P.poison = reinterpret_cast<int*>(g->base + g->off_state);
+	P.wait_ns = g->wait_ns;
+	P.drop_arrivals = 0;
+	if (g->drop_next > 0)
+	{
+		P.drop_arrivals = 1;
+		--g->drop_next;
 	}
 	++g->calls;
 	return NNCU_OK;
