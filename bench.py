@@ -4,26 +4,28 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl nncu|reference] [--workload cfgN]
 
 Workloads (synthetic seeded data, no dataset involved):
- cfg2 (default; the config the metric is quoted on) Gemma-3-1B-shaped
-      26-layer decode: 4 query heads, 1 KV head of 256, every 6th layer
-      global (theta 1e6, 4097 keys), the rest sliding (window 512, theta
-      1e4, a 768-row ring), per-head Q/K RMSNorm with gains ~1+N(0,0.1), fp32
-      K/V holding 4096 positions, the new token at 4096. N GPUs: replicas.
+ cfg4 (default: the largest configuration that fits one GPU) Gemma-3-4B-shaped
+      batched verify: 34 layers (5:1 local window 1024 / global), 8/4 heads
+      of 256, 16 sequences at 32768 verifying 4 draft tokens, fp16 K/V, per-head
+      Q/K RMSNorm. N GPUs: the (sequence, KV head) units sharded, no exchange
+      (strong scaling).
  cfg1 Llama-3.2-1B-shaped single-layer decode: 32/8 heads of 64, 1024 cached
       keys (pre-rotated, NORM RoPE theta 5e5), fp32. N GPUs: replicas.
+ cfg2 Gemma-3-1B-shaped 26-layer decode: 4 query heads, 1 KV head of 256,
+      every 6th layer global (theta 1e6, 4097 keys), the rest sliding (window
+      512, theta 1e4, a 768-row ring), per-head Q/K RMSNorm, fp32 K/V holding
+      4096 positions, the new token at 4096. N GPUs: replicas.
  cfg3 Qwen3-4B-shaped causal prefill of one layer: 32/8 heads of 128, 2048
       tokens, Q/K RMSNorm, NEOX theta 1e6, bf16 cache. Metric: TFLOP/s.
- cfg4 Gemma-3-4B-shaped batched verify: 34 layers (5:1 local window 1024 /
-      global), 8/4 heads of 256, 16 sequences at 32768 verifying 4 draft
-      tokens, fp16 K/V. N GPUs: the (sequence, KV head) units sharded, no
-      exchange (strong scaling).
  cfg5 Llama-3.2-1B-shaped long-context decode: 32/8 heads of 64, 131072
       cached fp16 keys, one new token. N GPUs: the keys split in 256-aligned
-      runs, partials merged over NVLink inside the kernel (strong scaling).
+      runs, partials merged over NVLink (strong scaling).
 
-One step = one call of the library for the whole workload (all layers and
-sequences): nncu_attention_batch_dev, or nncu_attention_split_dev (cfg5 on
-N > 1 GPUs).
+One step = one decode (or verify, or prefill) step of the workload in the
+drop-in's call pattern: one library call per layer, in layer order (layer
+l + 1's inputs come from layer l's output in a real model), each call
+holding every sequence of that layer -- nncu_attention_batch_dev, or
+nncu_attention_split_dev for cfg5 on N > 1 GPUs.
 
 Reported:
  value     the metric of the whole job (all ranks): algorithmic bytes (K/V of
@@ -31,14 +33,19 @@ Reported:
            (4 * n_head * head_dim per query-key pair) / device time of K steps
            (CUDA events, max over ranks). Inputs stay in HBM; steps rotate over
            R replicas of the workload's caches where one is smaller than L2.
- e2e       the same metric through the host-pointer calls: host fp32 inputs
-           copied up and outputs copied down inside every timed step.
+ e2e       the same metric through the host-pointer call (nncu_attention_batch,
+           one synchronous call per layer): host fp32 inputs copied up and
+           outputs copied down inside every timed step.
  roofline  the attention kernel's achieved GB/s (TFLOP/s for cfg3) = its
            algorithmic work per launch / its mean launch time (CUDA events
-           recorded by the library's phase profiler around the launch),
+           recorded by the library's phase profiler around each launch),
            against MEASURED_PEAKS.json.
+ fused_layers  for reference only: every layer of a step in ONE call (a
+           launch no real decode step can make, since the layers depend on
+           each other through the projections).
  cpu_baseline  the reference's own CPU kernels (oracle/_ref) on the host's
-           cores, a bounded sample of the same workload.
+           cores, a bounded sample of the same workload, at all cores and at
+           the reference's default of min(8, cores) threads.
 With --impl reference only the reference's CPU path runs (rank 0).
 """
 from __future__ import annotations
@@ -141,7 +148,7 @@ def cfg2():
 
 def cfg3():
     return Workload("cfg3", "Qwen3-4B-shaped causal prefill of one layer, 2048 tokens, bf16 K/V",
-                    [Layer(32, 8, 128, 0, 1e6, True)], n_seqs=1, pos=0, n_tok=2048, kv_type=0, dtype="f32",
+                    [Layer(32, 8, 128, 0, 1e6, True)], n_seqs=1, pos=0, n_tok=2048, kv_type=0, dtype="bf16",
                     replicas=1, metric="flops", seed=2)
 
 
@@ -319,7 +326,7 @@ def run_product(args, w: Workload, rank: int, world: int, local_rank: int):
 
     # device-resident inputs, one set per replica (distinct memory, same values)
     host = []  # per (seq, layer): the host copies for the e2e leg
-    dev_jobs, keep = [], []
+    dev_jobs, layer_jobs, keep = [], [], []
     rows_out = sum(w.n_tok * L.n_head for L in layers) * nsq
     for r in range(R):
         jobs = []
@@ -340,6 +347,9 @@ def run_product(args, w: Workload, rank: int, world: int, local_rank: int):
                 jobs.append(N.job(li, p, t["q"], t["k"], t["v"], None if split else out, seq=r * nsq + s))
                 keep.append((t, out))
         dev_jobs.append((N.AttnJob * len(jobs))(*jobs))
+        # the drop-in's pattern: one call per layer, every sequence of the layer in it
+        layer_jobs.append([(N.AttnJob * nsq)(*[jobs[s * len(layers) + li] for s in range(nsq)])
+                           for li in range(len(layers))])
     stream = torch.cuda.Stream(device=dev)
     dist = None
     if world > 1:
@@ -347,6 +357,13 @@ def run_product(args, w: Workload, rank: int, world: int, local_rank: int):
     grp = N.SplitGroup(rank, world, max_rows=rows_out, head_dim=layers[0].D, device=local_rank) if split else None
 
     def step(i):
+        for arr in layer_jobs[i % R]:  # layer by layer, in order
+            if grp:
+                grp.attention(kv, arr, share.key_lo, share.key_hi, stream)
+            else:
+                kv.attention_batch_dev(arr, stream)
+
+    def fused_step(i):  # every layer in one call: not a pattern a real decode step allows
         if grp:
             grp.attention(kv, dev_jobs[i % R], share.key_lo, share.key_hi, stream)
         else:
@@ -417,6 +434,29 @@ def run_product(args, w: Workload, rank: int, world: int, local_rank: int):
                      "peak_source": peaks["source"], "us_per_launch": round(core_us, 3),
                      "attn_rope_us_per_launch": round(1e3 * rope["ms"] / max(rope["calls"], 1), 3)})
 
+    # ---- for reference: the same steps with every layer in one call ----
+    fused = None
+    if len(layers) > 1:
+        for i in range(args.warmup):
+            fused_step(i)
+        kv.sync(stream)
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for i in range(args.steps):
+            fused_step(i)
+        ev1.record(stream)
+        kv.sync(stream)
+        fms = ev0.elapsed_time(ev1)
+        if dist:
+            tm = torch.tensor([fms], device=dev)
+            dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+            fms = float(tm.item())
+        fused = {"value": round(w.rate(job_work, fms / args.steps * 1e-3), 3), "unit": w.unit,
+                 "ms_per_step": round(fms / args.steps, 5),
+                 "note": "all layers of a step in one launch; not the drop-in's call pattern"}
+
     # ---- e2e: host fp32 inputs up and outputs down inside every step ----
     e2e = run_e2e(args, w, N, kv, layers, share, host, grp, stream, dist, dev)
     e2e["value"] = round(w.rate(job_work, e2e.pop("seconds_per_step")), 3)
@@ -437,7 +477,10 @@ def run_product(args, w: Workload, rank: int, world: int, local_rank: int):
                                    "keys": f"keys split / {world}, merge over NVLink"}[w.shard]
                    if world > 1 else "single GPU"},
         "roofline": roofline, "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks,
+        "calls_per_step": len(layers),
     }
+    if fused:
+        line["fused_layers"] = fused
     if w.metric != "flops":
         line["hbm_frac"] = round(value / world / peaks["hbm_gbs"], 4)
     if dist:
@@ -461,20 +504,22 @@ def run_e2e(args, w: Workload, N, kv, layers, share: Share, host, grp, stream, d
     rows_out = sum(w.n_tok * L.n_head for L in layers) * nsq
     d2h = rows_out * layers[0].D * 4
     if grp is None:
-        jobs, outs = [], []
-        for s in range(nsq):
-            for li, L in enumerate(layers):
+        per_layer, outs = [], []
+        for li, L in enumerate(layers):
+            jobs = []
+            for s in range(nsq):
                 d = host[s * nl + li]
                 out = np.empty((w.n_tok, L.n_head * L.D), np.float32)
                 p = params_for(N, w, L, d["qg"], d["kg"])
                 jobs.append(N.job(li, p, d["q"], d["k"], d["v"], out, seq=s))
                 outs.append(out)
-
-        arr = (N.AttnJob * len(jobs))(*jobs)  # the job table a caller keeps; its host buffers change per step
+            # the job table a caller keeps; its host buffers change per step
+            per_layer.append((N.AttnJob * len(jobs))(*jobs))
 
         def one():
-            kv.attention_batch(arr)
-        api = "nncu_attention_batch (host pointers)"
+            for arr in per_layer:  # layer by layer: each call returns with its outputs in host memory
+                kv.attention_batch(arr)
+        api = "nncu_attention_batch (host pointers), one synchronous call per layer"
     else:
         pinned, devs, jobs = [], [], []
         for s in range(nsq):
@@ -544,6 +589,11 @@ def profiled_traffic(workload: str):
 
 
 # ---- the reference's CPU path ------------------------------------------------------------------
+
+def default_threads() -> int:
+    """The reference's default thread count: min(8, CPUs) (nnc.h:100-104)."""
+    return min(8, os.cpu_count() or 1)
+
 
 def cpu_reference(w: Workload, budget_s: float, threads: int | None):
     """The reference's own kernels (oracle/_ref), parallel through its pool,
@@ -616,7 +666,7 @@ def main(argv=None) -> int:
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["nncu", "reference"], default="nncu")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
@@ -632,13 +682,16 @@ def main(argv=None) -> int:
             return 0
         budget = max(5.0, min(60.0, args.cpu_seconds))
         rate, cores, kind, sample, s_per_step = cpu_reference(w, budget, None)
+        d_rate, d_cores, _, d_sample, _ = cpu_reference(w, budget / 2, default_threads())
         line = {"impl": "reference", "metric": w.metric_name, "value": round(rate, 4), "unit": w.unit,
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(1e3 * s_per_step, 4), "higher_is_better": True,
                 "scaling": "weak" if w.shard == "replicas" else "strong", "vs_baseline": None, "dtype": w.dtype,
                 "data": "synthetic", "config": {"workload": f"{w.name}: {w.title}", "work_per_step": int(w.work())},
                 "cpu_baseline": {"value": round(rate, 4), "unit": w.unit, "cores": cores, "kind": kind,
-                                 "sample": sample},
+                                 "sample": sample, "host_cpus": os.cpu_count(),
+                                 "at_default_threads": {"value": round(d_rate, 4), "cores": d_cores,
+                                                        "sample": d_sample}},
                 "e2e": {"value": round(rate, 4), "unit": w.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
         return 0
@@ -654,8 +707,11 @@ def main(argv=None) -> int:
     line = run_product(args, w, rank, world, local_rank)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, cores, kind, sample, _ = cpu_reference(w, args.cpu_seconds, None)
+        d_rate, d_cores, _, d_sample, _ = cpu_reference(w, args.cpu_seconds / 2, default_threads())
         line["cpu_baseline"] = {"value": round(rate, 4), "unit": w.unit, "cores": cores, "kind": kind,
-                                "sample": sample}
+                                "sample": sample, "host_cpus": os.cpu_count(),
+                                "at_default_threads": {"value": round(d_rate, 4), "cores": d_cores,
+                                                       "sample": d_sample}}
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

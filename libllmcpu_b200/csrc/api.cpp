@@ -57,7 +57,7 @@ int nncu::set_error(int status, const char* msg)
 	return fail(status, "%s", msg);
 }
 
-// Every pointer a kernel bulk-copies from (q rows, the gains, the frequency
+// Every (q rows, the gains, the frequency
 // factors, the new k and v rows, the cache) or writes with 16-byte stores
 // (the output) must be 16-byte aligned; a misaligned one would fault the GPU
 // instead of failing the call, so it is refused here, before any launch.
@@ -225,6 +225,8 @@ struct PerfScope
 	}
 };
 } // namespace
+
+void nncu::note_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
 // ---- the cache object ---------------------------------------------------------------
 

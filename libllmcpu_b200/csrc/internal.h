@@ -175,6 +175,8 @@ struct JobPointers
 	const void* v_cache;
 };
 int check_alignment(const JobPointers& p, int job, const char* what);
+// Count kernels launched outside api.cpp (nncu_launch_count).
+void note_launches(int n);
 
 // Launchers (implemented in the .cu files). Each returns a cudaError_t value.
 int launch_prep(const DecodePlan& plan, void* stream);

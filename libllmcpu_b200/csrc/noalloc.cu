@@ -247,10 +247,12 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	P.err = reinterpret_cast<int*>(scratch + OFF_ERR);
 	int e = P.fused ? 0 : launch_prep(P, st); // K2 appends itself when it can
 	if (e) return set_cuda_error(e, "K1 (norm, RoPE, append) launch");
+	if (!P.fused) note_launches(1);
 	if (P.n_ctas > 0)
 	{
 		e = launch_decode(P, st);
 		if (e) return set_cuda_error(e, "K2 (attention) launch");
+		note_launches(1);
 	}
 	return NNCU_OK;
 }

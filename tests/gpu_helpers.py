@@ -26,11 +26,26 @@ def make_cache(N, case: S.Case):
     return kv
 
 
-def run_product(N, case: S.Case, kv=None, batch: bool = False):
+def run_product(N, case: S.Case, kv=None, batch: bool = False, per_layer: bool = False):
     """Every layer of every sequence through the product, in the checker's
     order. batch=True submits all layers of a sequence in one
-    nncu_attention_batch call (only for cases without shared K/V)."""
+    nncu_attention_batch call (only for cases without shared K/V);
+    per_layer=True submits each layer once for all sequences (the drop-in's
+    call pattern for a batch of sequences)."""
     kv = kv or make_cache(N, case)
+    if per_layer:
+        outs = [[None] * len(case.layers) for _ in range(case.n_seqs)]
+        for li in range(len(case.layers)):
+            jobs = []
+            for s in range(case.n_seqs):
+                inp = case.inputs[s][li]
+                p = N.params(**case.params_dict(li, s))
+                out = np.empty((case.n_tok, p.n_head * p.head_dim), np.float32)
+                jobs.append(N.job(li, p, np.ascontiguousarray(inp.q), np.ascontiguousarray(inp.k),
+                                  np.ascontiguousarray(inp.v), out, seq=s))
+                outs[s][li] = out
+            kv.attention_batch(jobs)
+        return outs, kv
     outs = []
     for s in range(case.n_seqs):
         row = []

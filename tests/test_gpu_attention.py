@@ -20,9 +20,9 @@ pytestmark = pytest.mark.gpu
 GOLDEN = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "golden.npz"))
 
 
-def check_case(N, case, tight=None, batch=False):
+def check_case(N, case, tight=None, batch=False, per_layer=False):
     want, caches = S.run_checker(case, "oracle")
-    got, kv = run_product(N, case, batch=batch)
+    got, kv = run_product(N, case, batch=batch, per_layer=per_layer)
     if tight is None:
         tight = case.kv_type == O.KV_F32
     for s in range(case.n_seqs):
@@ -74,6 +74,19 @@ def test_cfg4_verify_f16(nncu):
            LayerSpec(8, 4, 256, window=0, freq_base=1e6, qk_norm=True)]
     case = S.build_case(3, g34, n_ctx=4096, n_tok=4, pos0=[2000, 3100, 4092], kv_type=O.KV_F16)
     check_case(nncu, case)
+
+
+def test_cfg4_verify_f16_full_context(nncu):
+    """BASELINE config 4 at its real context: 32768 cached fp16 keys per
+    sequence, 4 draft tokens at 32768..32771 (a 4-query causal block), 8
+    query heads on 4 KV heads of 256, Q/K RMSNorm; one window-1024 layer (a
+    1280-row ring) and one global layer; 2 of the 16 sequences, each layer
+    submitted once for both sequences as the benchmark does."""
+    g34 = [LayerSpec(8, 4, 256, window=1024, freq_base=1e4, qk_norm=True),
+           LayerSpec(8, 4, 256, window=0, freq_base=1e6, qk_norm=True)]
+    case = S.build_case(3, g34, n_ctx=32772, n_tok=4, pos0=[32768, 32768], kv_type=O.KV_F16)
+    assert case.rows == [1280, 32772]
+    check_case(nncu, case, per_layer=True)
 
 
 def test_cfg5_long_f16_reduced(nncu):
@@ -256,3 +269,46 @@ def test_errors_are_statuses(nncu):
     assert out.shape == (1, 256) and np.all(out == 0.0)
     del q, k
     kv.close()
+
+
+def test_misaligned_pointers_are_refused(nncu, torch_cuda):
+    """Every pointer the kernels bulk-copy from or write with 16-byte stores
+    is checked on the host: a misaligned k, out or cache (each inside a
+    buffer large enough for the call) fails with NNCU_ERR_INVALID_ARGUMENT
+    and nothing is launched."""
+    N, torch = nncu, torch_cuda
+    D, n_head, n_kv = 256, 4, 1
+    kv = N.KVCache([(n_kv, D, 0, 0)], n_ctx=512, n_batch=1, kv_type=O.KV_F32)
+    pad = 4  # floats: 16 bytes of room for a 4-byte offset
+
+    def buf(n):
+        return torch.zeros(n + pad, device="cuda")
+
+    q, k, v, out = buf(n_head * D), buf(n_kv * D), buf(n_kv * D), buf(n_head * D)
+    p = N.params(n_tok=1, pos0=100, n_head=n_head, n_kv=n_kv, head_dim=D)
+    good = dict(q=q.data_ptr(), k=k.data_ptr(), v=v.data_ptr(), out=out.data_ptr())
+    torch.cuda.synchronize()
+    for name in ("k", "out", "q", "v"):
+        ptrs = dict(good)
+        ptrs[name] += 4  # one float past a 16-byte boundary, still inside its buffer
+        before = N.launch_count()
+        with pytest.raises(N.NnncError) as e:
+            kv.attention_batch_dev([N.job(0, p, ptrs["q"], ptrs["k"], ptrs["v"], ptrs["out"])])
+        assert e.value.status == N.ERR_INVALID_ARGUMENT and name in str(e.value), str(e.value)
+        assert N.launch_count() == before
+    kv.attention_batch_dev([N.job(0, p, good["q"], good["k"], good["v"], good["out"])])  # and the aligned call runs
+    kv.sync()
+    kv.close()
+    # a caller-owned cache (the no-allocation call) whose base is off by 4 bytes
+    rows = 512
+    k_cache = torch.zeros(n_kv * rows * D + pad, device="cuda")
+    v_cache = torch.zeros(n_kv * rows * D + pad, device="cuda")
+    for which in ("k_cache", "v_cache"):
+        kc = k_cache.data_ptr() + (4 if which == "k_cache" else 0)
+        vc = v_cache.data_ptr() + (4 if which == "v_cache" else 0)
+        before = N.launch_count()
+        with pytest.raises(N.NnncError) as e:
+            N.attention_noalloc(p, good["q"], good["k"], good["v"], good["out"], kc, vc, O.KV_F32, rows)
+        assert e.value.status == N.ERR_INVALID_ARGUMENT and which in str(e.value), str(e.value)
+        assert N.launch_count() == before
+    torch.cuda.synchronize()

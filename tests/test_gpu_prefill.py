@@ -23,8 +23,8 @@ pytestmark = pytest.mark.gpu
 TOL_BF16_ABS, TOL_BF16_REL = 2e-2, 1e-2
 
 
-def check_prefill(N, case):
-    want, caches = S.run_checker(case, "oracle")
+def check_prefill(N, case, which="oracle"):
+    want, caches = S.run_checker(case, which)
     got, kv = run_product(N, case)
     errs = []
     for s in range(case.n_seqs):
@@ -47,6 +47,20 @@ def test_prefill_qwen3_shape(nncu):
     L = [LayerSpec(32, 8, 128, freq_base=1e6, qk_norm=True)]
     case = S.build_case(2, L, n_ctx=1024, n_tok=1024, pos0=0, kv_type=O.KV_BF16)
     check_prefill(nncu, case)
+
+
+def test_prefill_config3_full(nncu):
+    """BASELINE config 3 at its full size: one Qwen3-4B-shaped layer, 2048
+    tokens, 32 query heads on 8 KV heads of 128, Q/K RMSNorm, NEOX theta 1e6,
+    bf16 cache. The checker is the reference's own compiled kernels where
+    they were built (they take a second on the host's cores; the C
+    restatement takes about a minute and stands in where they were not)."""
+    L = [LayerSpec(32, 8, 128, freq_base=1e6, qk_norm=True)]
+    case = S.build_case(2, L, n_ctx=2048, n_tok=2048, pos0=0, kv_type=O.KV_BF16)
+    which = "ref" if O.ref() is not None else "oracle"
+    (e_abs, e_rel), = check_prefill(nncu, case, which)
+    print(f"config 3 prefill vs {which}: max-abs {e_abs:.3e}, rel-L2 {e_rel:.3e} "
+          f"(bf16 tolerance {TOL_BF16_ABS:g} / {TOL_BF16_REL:g})")
 
 
 @pytest.mark.parametrize("n_tok,pos0", [(128, 0), (300, 0), (257, 200), (640, 129)])
