@@ -167,6 +167,14 @@ int nncu_kv_plan(const nncu_layer_desc* layers, int32_t n_layer, const nncu_kv_p
                  nncu_kv_layer_info* per_layer, int32_t* max_rewind, size_t* bytes);
 int nncu_kv_create(const nncu_layer_desc* layers, int32_t n_layer, const nncu_kv_params* params, nncu_kv** out);
 void nncu_kv_free(nncu_kv* kv);
+/* Decode and verify on a 16-bit (f16, bf16) cache with three or more query
+ * rows per KV head (grouped heads x new tokens) and head_dim 64, 128 or 256
+ * run on the tensor cores by default (tcgen05; q and the softmax weights
+ * split into high and low 16-bit halves, so the products keep fp32
+ * accuracy). enabled = 0 keeps those launches on the CUDA-core kernel, as
+ * f32 caches and one- or two-row launches always are. No reference
+ * counterpart (the reference has one CPU kernel). */
+int nncu_kv_set_tensor_cores(nncu_kv* kv, int enabled);
 int nncu_kv_layer(const nncu_kv* kv, int32_t layer, nncu_kv_layer_info* out);
 int nncu_kv_get_state(const nncu_kv* kv, int32_t seq, nncu_kv_state* out);
 /* model_kv_rewind: pos in [0, cur_pos]; refused (NNCU_ERR_INVALID_ARGUMENT,

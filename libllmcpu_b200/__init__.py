@@ -55,7 +55,7 @@ EXPORTS = [
     "nncu_perf_read", "nncu_perf_report", "nncu_launch_count", "nncu_attention_noalloc", "nncu_group_create",
     "nncu_group_handle", "nncu_group_open", "nncu_group_output", "nncu_group_copy_output", "nncu_group_free",
     "nncu_attention_split_dev", "nncu_group_set_timeout", "nncu_group_reset", "nncu_group_inject_drop",
-    "nncu_noalloc_check",
+    "nncu_noalloc_check", "nncu_kv_set_tensor_cores",
 ]
 GROUP_HANDLE_BYTES = 64
 
@@ -205,6 +205,7 @@ def lib() -> C.CDLL:
     L.nncu_group_reset.argtypes = [vp]
     L.nncu_group_inject_drop.argtypes = [vp, i32]
     L.nncu_noalloc_check.argtypes = [vp]
+    L.nncu_kv_set_tensor_cores.argtypes = [vp, C.c_int]
     _lib = L
     return L
 
@@ -300,6 +301,11 @@ class KVCache:
     @property
     def handle(self):
         return self._h
+
+    def set_tensor_cores(self, enabled: bool) -> None:
+        """Decode / verify of several rows per KV head on a 16-bit cache on the
+        tensor cores (the default) or on the CUDA-core kernel."""
+        _check(lib().nncu_kv_set_tensor_cores(self._h, int(enabled)))
 
     def layer_info(self, layer: int) -> KVLayerInfo:
         info = KVLayerInfo()

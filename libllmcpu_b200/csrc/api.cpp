@@ -238,6 +238,7 @@ struct Buffer
 	size_t seq_bytes = 0;
 	void* k = nullptr;
 	void* v = nullptr;
+	void* tmaps = nullptr; // the tensor-core kernel's maps over k and v (device memory, made on first use)
 };
 
 struct nncu_kv
@@ -280,6 +281,7 @@ struct nncu_kv
 	std::vector<DevJob> jobs_tmp;
 	std::vector<CtaStart> starts_tmp;
 	int counters_n = 0;
+	bool no_tc = false; // keep 16-bit multi-row launches on the CUDA-core kernel (nncu_kv_set_option)
 
 	~nncu_kv()
 	{
@@ -289,6 +291,7 @@ struct nncu_kv
 		{
 			if (b.k) cudaFree(b.k);
 			if (b.v) cudaFree(b.v);
+			if (b.tmaps) cudaFree(b.tmaps);
 		}
 		for (auto& kv : rope_tables) cudaFree(kv.second);
 		if (err_dev) cudaFree(err_dev);
@@ -601,6 +604,13 @@ extern "C" int nncu_kv_create(const nncu_layer_desc* layers, int32_t n_layer, co
 
 extern "C" void nncu_kv_free(nncu_kv* kv) { delete kv; }
 
+extern "C" int nncu_kv_set_tensor_cores(nncu_kv* kv, int enabled)
+{
+	if (!kv) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL cache");
+	kv->no_tc = enabled == 0;
+	return NNCU_OK;
+}
+
 extern "C" int nncu_kv_layer(const nncu_kv* kv, int32_t layer, nncu_kv_layer_info* out)
 {
 	if (!kv || !out) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL argument");
@@ -795,6 +805,32 @@ int check_conflicts(const nncu_kv* kv, const nncu_attn_job* jobs, int n)
 	return NNCU_OK;
 }
 
+// The tensor maps of buffer `bi` for the tensor-core decode kernel, made
+// once: [n_seq * n_kv planes][rows][head_dim] over its K and its V. They are
+// never rewritten, so the kernels may cache them.
+int buffer_tmaps(nncu_kv* kv, int bi, int D, int n_kv, const void** out)
+{
+	Buffer& b = kv->bufs[bi];
+	if (!b.tmaps)
+	{
+		alignas(64) unsigned char h[2 * TENSOR_MAP_BYTES];
+		int e = tc_make_maps(h, h + TENSOR_MAP_BYTES, b.k, b.v, kv->kv_type, D, b.rows_alloc,
+		                     (long long)kv->n_seq * n_kv);
+		if (e) return cuda_fail((cudaError_t)e, "tensor maps of the cache");
+		void* dmem = nullptr;
+		CU(cudaMalloc(&dmem, sizeof h), "tensor maps");
+		cudaError_t ce = cudaMemcpy(dmem, h, sizeof h, cudaMemcpyHostToDevice);
+		if (ce != cudaSuccess)
+		{
+			cudaFree(dmem);
+			return cuda_fail(ce, "tensor maps upload");
+		}
+		b.tmaps = dmem;
+	}
+	*out = b.tmaps;
+	return NNCU_OK;
+}
+
 // Turn one public job into a DevJob (device pointers already resolved).
 void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 {
@@ -831,6 +867,25 @@ void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 	d.softcap = p.softcap;
 	d.key_lo = 0;
 	d.key_hi = INT_MAX;
+	d.plane0 = j.seq * p.n_kv;
+}
+
+// The tensor maps of every job that the tensor-core decode kernel could take
+// (16-bit cache, head_dim 64, 128 or 256).
+int attach_tmaps(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub)
+{
+	if (kv->kv_type == KV_F32) return NNCU_OK;
+	for (size_t i = 0; i < jobs.size(); ++i)
+	{
+		const int D = jobs[i].D;
+		if (D != 64 && D != 128 && D != 256) continue;
+		const void* maps = nullptr;
+		int rc = buffer_tmaps(kv, kv->kv_buf[pub[i].layer], D, pub[i].p.n_kv, &maps);
+		if (rc != NNCU_OK) return rc;
+		jobs[i].tmap_k = maps;
+		jobs[i].tmap_v = static_cast<const char*>(maps) + TENSOR_MAP_BYTES;
+	}
+	return NNCU_OK;
 }
 
 // Launch K1 and K2 for jobs whose DevJob pointers are all device pointers,
@@ -888,6 +943,11 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 		int rc = rope_table(kv, pub[i].p.freq_base, pub[i].p.n_rot, &jobs[i].rope_inv);
 		if (rc != NNCU_OK) return rc;
 	}
+	if (!group)
+	{
+		int rc = attach_tmaps(kv, jobs, pub);
+		if (rc != NNCU_OK) return rc;
+	}
 	// Every job of one launch shares head_dim (the kernels are specialised on it).
 	for (int i = 1; i < n; ++i)
 		if (jobs[i].D != jobs[0].D)
@@ -923,9 +983,18 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 			return NNCU_OK;
 		}
 	}
+	// several query rows per KV head on a 16-bit cache: the tensor-core kernel
+	int rows_needed = 1;
+	bool maps = true;
+	for (int i = 0; i < n; ++i)
+	{
+		rows_needed = std::max(rows_needed, (jobs[i].n_head / jobs[i].n_kv) * jobs[i].n_tok);
+		maps = maps && jobs[i].tmap_k != nullptr;
+	}
+	const int tc = !group && maps && !kv->no_tc ? tc_rows(jobs[0].D, kv->kv_type, rows_needed) : 0;
 	DecodePlan P{};
 	kv->starts_tmp.resize((size_t)kv->num_sms);
-	int rc = plan_launch(jobs.data(), n, kv->kv_type, kv->num_sms, P, kv->starts_tmp.data(), kv->num_sms);
+	int rc = plan_launch(jobs.data(), n, kv->kv_type, kv->num_sms, P, kv->starts_tmp.data(), kv->num_sms, true, tc);
 	if (rc != NNCU_OK) return rc;
 	P.err = kv->err_dev;
 	P.world = 1;
@@ -1044,7 +1113,7 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	if (e) return cuda_fail((cudaError_t)e, "K1 (norm, RoPE, append) launch");
 	{
 		PerfScope ps(NNCU_PERF_ATTN_CORE, core_bytes, st);
-		e = launch_decode(P, st, tab);
+		e = tc ? launch_decode_tc(P, nullptr, st) : launch_decode(P, st, tab);
 	}
 	if (e) return cuda_fail((cudaError_t)e, "K2 (attention) launch");
 	if (group)

@@ -68,6 +68,12 @@ struct alignas(16) DevJob
 	// query's span (the whole span unless the sequence is split over GPUs)
 	int key_lo, key_hi;
 	int out_row0;         // split over GPUs: the job's first row in the group's output
+	// the tensor-core decode kernel's view of the cache: tensor maps (CUtensorMap,
+	// in global memory) over this job's K and V buffers as [planes][rows][D],
+	// KV head h of this sequence at plane plane0 + h; NULL: the launch's own maps
+	const void* tmap_k;
+	const void* tmap_v;
+	int plane0;
 };
 static_assert(sizeof(DevJob) % 16 == 0, "DevJob is bulk-copied");
 
@@ -135,7 +141,20 @@ struct DecodePlan
 // per SM are cut finer for balance (more partial slots). Host code;
 // allocates nothing.
 int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, CtaStart* starts, int max_starts,
-                bool small_chunks = true);
+                bool small_chunks = true, int rows_fixed = 0);
+
+// The tensor-core decode kernel (k_decode_tc.cu): 16-bit caches, head_dim
+// 64, 128 or 256, several query rows per KV head (tc_rows(): 8 or 16 per
+// segment, 0 when the launch does not suit it). Launched after K1 (which
+// appends the new rows) as its programmatic dependent. `maps`: two
+// CUtensorMaps (K, V) for jobs whose tmap_k / tmap_v are NULL, or NULL.
+int tc_rows(int D, int kv_type, int rows_needed);
+int launch_decode_tc(const DecodePlan& plan, const void* maps, void* stream);
+// The tensor maps of a 16-bit cache buffer [planes][rows][D] in the kernel's
+// tile form (host side; 128 bytes each, 64-byte aligned).
+constexpr int TENSOR_MAP_BYTES = 128;
+int tc_make_maps(void* kmap, void* vmap, const void* k, const void* v, int kv_type, int D, long long rows,
+                 long long planes);
 
 // One causal prefill on the tensor cores (k_prefill.cu): bf16 cache, head_dim 128.
 struct PrefillPlan

@@ -34,6 +34,7 @@
 #include <math_constants.h>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace nncu
 {
@@ -58,89 +59,9 @@ constexpr int PF_SMEM = SM_BAR + 256 + 1024;    // + alignment slack
 constexpr int TMEM_COLS = 512;                  // S0, S1, O (128 columns each)
 constexpr float LAZY = 8.0f;                    // log2 headroom before the row maximum moves
 
-// tcgen05 instruction descriptors (kind::f16): fp32 accumulate, bf16 A and
-// B, M = 128, N = 128; A K-major; B K-major (Q K^T) or MN-major (P V).
-constexpr uint32_t idesc(bool b_mn_major)
-{
-	return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((128u >> 3) << 17) |
-	       ((128u >> 4) << 24);
-}
-
-// Shared memory matrix descriptor, 128-byte swizzle (layout type 2),
-// version 1: start address, leading and stride byte offsets (16-byte units).
-__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo)
-{
-	return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-	       ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t id, uint32_t acc)
-{
-	asm volatile(
-		"{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-		"tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-		"l"(adesc), "l"(bdesc), "r"(id), "r"(acc)
-		: "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar)
-{
-	asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-	             : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// 32 consecutive fp32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v)
-{
-	uint32_t r[32];
-	asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
-	             "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
-	             "[%32];"
-	             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-	               "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-	               "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
-	               "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
-	               "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-	             : "r"(taddr)
-	             : "memory");
-#pragma unroll
-	for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v)
-{
-	asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-	             "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, "
-	             "%31, %32};" ::"r"(taddr),
-	             "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-	             "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-	             "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-	             "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-	             "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-	             "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
-	             "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
-	             "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
-	             "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
-	             "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
-	             "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
-	             : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// One box of a 3-D tensor map (x along head_dim, y rows, z head) into shared
-// memory, completing on `bar`. x is 0 or 64: 128-byte aligned.
-__device__ __forceinline__ void tma3(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar)
-{
-	asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
-	             "%4}], [%5];" ::"r"(smem_u32(dst)),
-	             "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
-	             : "memory");
-}
+// tcgen05 instruction descriptors for the prefill: bf16 A and B, fp32
+// accumulate, M = 128, N = 128; A K-major; B K-major (Q K^T) or MN-major (P V).
+constexpr uint32_t idesc(bool b_mn_major) { return tc_idesc(128, 128, true, false, b_mn_major); }
 
 } // namespace
 
@@ -567,9 +488,17 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 // 64 x 128 x 1 box, 128-byte swizzled (the kernels' operand layout).
 int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads)
 {
-	const cuuint64_t dims[3] = {(cuuint64_t)PF_D, (cuuint64_t)rows, (cuuint64_t)heads};
-	const cuuint64_t strides[2] = {(cuuint64_t)PF_D * 2, (cuuint64_t)rows * PF_D * 2};
-	const cuuint32_t box[3] = {64, 128, 1};
+	return make_tensor_map(map, base, true, PF_D, rows, heads, 128);
+}
+
+} // namespace
+
+int make_tensor_map(CUtensorMap* map, const void* base, bool bf16, uint64_t D, uint64_t rows, uint64_t planes,
+                    uint32_t box_rows)
+{
+	const cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)rows, (cuuint64_t)planes};
+	const cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)rows * D * 2};
+	const cuuint32_t box[3] = {64, box_rows, 1};
 	const cuuint32_t estr[3] = {1, 1, 1};
 	// the driver's encoder, looked up through the runtime (the library loads
 	// without the driver library present, e.g. for its CPU-side checks)
@@ -586,13 +515,12 @@ int make_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads)
 			return (int)cudaErrorNotSupported;
 		encode = reinterpret_cast<Encode>(fn);
 	}
-	const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
-	                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-	                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+	const CUresult r = encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+	                          const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+	                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+	                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 	return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
-
-} // namespace
 
 bool prefill_supported(int D, int kv_type) { return D == PF_D && kv_type == KV_BF16; }
 

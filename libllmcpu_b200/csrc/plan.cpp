@@ -44,7 +44,7 @@ bool holds_new_rows(const DevJob& j, int tis, int len, int T)
 } // namespace
 
 int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, CtaStart* starts, int max_starts,
-                bool small_chunks)
+                bool small_chunks, int rows_fixed)
 {
 	const int D = jobs[0].D;
 	const int T = decode_tile_keys(D, kv_type);
@@ -56,6 +56,7 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 	}
 	int RM = 1;
 	while (RM < rows_needed && RM < decode_rows_max(D)) RM *= 2;
+	if (rows_fixed > 0) RM = rows_fixed; // the tensor-core kernel's row groups
 
 	// every job's tiles: the union of its tokens' spans (model_attn_span)
 	// within its key range
@@ -87,7 +88,7 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 	// every job's new tokens, every new position lies in its job's tiles, and
 	// the rows it bulk-copies are 16-byte aligned
 	auto aligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
-	int fused = max_tok <= decode_fuse_tokens(D, kv_type, RM);
+	int fused = rows_fixed == 0 && max_tok <= decode_fuse_tokens(D, kv_type, RM);
 	for (int i = 0; i < n && fused; ++i)
 	{
 		const DevJob& j = jobs[i];
