@@ -30,7 +30,10 @@ def both_kernels(N, case):
     for s in range(case.n_seqs):
         for li in range(len(case.layers)):
             assert_close(got_tc[s][li], want[s][li], f"tensor cores, seq {s} layer {li}")
-            assert_close(got_tc[s][li], got_cc[s][li], f"tensor cores vs CUDA cores, seq {s} layer {li}", 2e-5, 2e-5)
+            # bf16 halves keep 16 bits of q and of the weights (f16 halves 22):
+            # at scale 1.0 that moves a score by ~1e-4 against the CUDA cores' fp32
+            tol = 2e-5 if case.kv_type == O.KV_F16 else 2e-4
+            assert_close(got_tc[s][li], got_cc[s][li], f"tensor cores vs CUDA cores, seq {s} layer {li}", tol, tol)
     return got_tc
 
 
