@@ -669,6 +669,8 @@ def main(argv=None) -> int:
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="cfg4")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sequences", type=int, default=None,
+                    help="profiling aid: fewer sequences than the workload names (the line's config says so)")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
 
@@ -676,6 +678,9 @@ def main(argv=None) -> int:
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     w = WORKLOADS[args.workload]()
+    if args.sequences:
+        w.n_seqs = args.sequences
+        w.title += f" (reduced to {args.sequences} sequences)"
 
     if args.impl == "reference":
         if rank != 0:

@@ -149,6 +149,7 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 // appends the new rows) as its programmatic dependent. `maps`: two
 // CUtensorMaps (K, V) for jobs whose tmap_k / tmap_v are NULL, or NULL.
 int tc_rows(int D, int kv_type, int rows_needed);
+int tc_fuse_tokens(int D, int RM); // new tokens the tensor-core kernel appends itself (0: K1 must)
 int launch_decode_tc(const DecodePlan& plan, const void* maps, void* stream);
 // The tensor maps of a 16-bit cache buffer [planes][rows][D] in the kernel's
 // tile form (host side; 128 bytes each, 64-byte aligned).

@@ -36,10 +36,15 @@
 //    piece's end the row sums meet the same way and the piece gives the
 //    output, or a partial (o, m, l) merged in order by the segment's last
 //    piece (decode.cuh), as in k_decode.cu.
-// The new tokens' K/V rows are appended by K1 (k_prep.cu) first; this kernel
-// is its programmatic dependent and waits for it only before the tiles that
-// hold those rows. Every wait is bounded; a timed-out wait records an error
-// and the CTA steps through without waiting further.
+//  * warp 3 appends the new tokens' K/V rows when their raw rows fit the q
+//    slot (decode and short verify): the piece holding them normalises,
+//    rotates and narrows them, stores them to the cache (first row group),
+//    and writes them into the K and V stages of the tiles that hold them once
+//    those have landed, before the MMAs read the stages. Longer batches have
+//    K1 (k_prep.cu) append first; this kernel is then its programmatic
+//    dependent and waits for it only before the tiles that hold the new rows.
+// Every wait is bounded; a timed-out wait records an error and the CTA steps
+// through without waiting further.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -78,17 +83,25 @@ struct TcCfg
 	static constexpr int PPANEL = N * 128;          // one 64-key panel of the P operand
 	static constexpr int PBYTES = (T / 64) * PPANEL;
 	// the q slot (floats): descriptor and 4 info words, raw q rows, q gains,
-	// inverse frequencies, frequency factors
+	// inverse frequencies, frequency factors; when this kernel appends the new
+	// tokens itself, the k gains and the new tokens' raw k rows, then v rows
 	static constexpr int QHEAD = (int)(sizeof(DevJob) / 4) + 4;
 	static constexpr int QROWS = QHEAD;
 	static constexpr int QGAIN = QROWS + NR * D;
 	static constexpr int QINV = QGAIN + D;
 	static constexpr int QFF = QINV + D / 2;
-	static constexpr int SLOT = QFF + D / 2;
+	static constexpr int QKG = QFF + D / 2;
+	static constexpr int QNEW = QKG + D;
 	static constexpr int RED = 2 * NCW * NR;        // two buffers of per-warp row values
-	static constexpr int FIXED = QBYTES + 2 * PBYTES + SLOT * 4 + RED * 4 + 512;
-	static constexpr int FIT = (TC_SMEM_LIMIT - 1024 - FIXED) / (2 * TC_TILE);
-	static constexpr int STAGES = FIT < 4 ? FIT : 4;
+	static constexpr int FIXED0 = QBYTES + 2 * PBYTES + QNEW * 4 + RED * 4 + 512;
+	// three stages of K and V tiles where they fit, else two; then as many new
+	// tokens (up to 8) as what is left holds
+	static constexpr int LEFT3 = TC_SMEM_LIMIT - 1024 - 3 * 2 * TC_TILE - FIXED0;
+	static constexpr int STAGES = LEFT3 >= 0 ? 3 : 2;
+	static constexpr int LEFT = TC_SMEM_LIMIT - 1024 - STAGES * 2 * TC_TILE - FIXED0;
+	static constexpr int NT_FIT = LEFT / (2 * D * 4);
+	static constexpr int NT = NT_FIT > 8 ? 8 : NT_FIT; // (their narrowed rows stay in the append warp's registers)
+	static constexpr int SLOT = QNEW + 2 * NT * D;
 	static constexpr int OFF_K = 0;
 	static constexpr int OFF_V = STAGES * TC_TILE;
 	static constexpr int OFF_Q = 2 * STAGES * TC_TILE;
@@ -101,7 +114,7 @@ struct TcCfg
 	static constexpr int O_COLS = NPB * N;            // of one O buffer
 	static constexpr int TMEM_COLS = 2 * (S_COLS + O_COLS) <= 128 ? 128 : 256;
 	static_assert(2 * (S_COLS + O_COLS) <= 256, "TMEM columns");
-	static_assert(STAGES >= 2, "shared memory for two stages");
+	static_assert(LEFT >= 0, "shared memory for two stages");
 	static_assert(SMEM <= TC_SMEM_LIMIT, "shared memory");
 	static_assert(NR == 8 || NR == 16, "rows per segment");
 	static_assert(QBYTES % 1024 == 0 && PBYTES % 1024 == 0 && (SLOT * 4) % 16 == 0, "operand alignment");
@@ -215,11 +228,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 	uint64_t* o_full = p_full + 2;            // [2]
 	uint64_t* o_empty = o_full + 2;           // [2]
 	uint64_t* q_full = o_empty + 2;           // the slot holds a piece
-	uint64_t* q_empty = q_full + 1;           // the slot may be refilled
-	uint64_t* q_ready = q_empty + 1;          // the Q operand is written
+	uint64_t* q_empty = q_full + 1;           // the slot may be refilled (softmax warps and the append warp)
+	uint64_t* q_ready = q_empty + 1;          // the Q operand is written, the piece's patch range is known
 	uint64_t* mma_done = q_ready + 1;
-	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
-	volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 2); // [0] abort, [1] last piece, [2] piece tiles
+	uint64_t* k_patched = mma_done + 1;       // a tile's new K rows are in its stage
+	uint64_t* v_patched = k_patched + 1;      // a tile's new V rows are in its stage
+	uint64_t* k_land = v_patched + 1;         // a tile holding new rows has landed (the append warp waits,
+	uint64_t* v_land = k_land + 1;            // in order: a stage's own barrier may be phases ahead of it)
+	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(v_land + 1);
+	// [0] abort, [1] last piece, [2] the piece's tiles, [3] / [4] the first and
+	// last of its tiles (CTA-wide index) whose new rows this kernel patches in
+	volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 2);
 	CtaStart* s_start = reinterpret_cast<CtaStart*>(smem + C::OFF_BAR + 384);
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -242,12 +261,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			mbar_init(&o_empty[b], 32 * NCW);
 		}
 		mbar_init(q_full, 1);
-		mbar_init(q_empty, 1);
-		mbar_init(q_ready, 32 * NCW);
+		mbar_init(q_empty, 2);
+		mbar_init(q_ready, 32 * NCW + 1);
 		mbar_init(mma_done, 1);
-		flags[0] = 0;
-		flags[1] = 0;
-		flags[2] = 0;
+		mbar_init(k_patched, 1);
+		mbar_init(v_patched, 1);
+		mbar_init(k_land, 1);
+		mbar_init(v_land, 1);
+		for (int f = 0; f < 5; ++f) flags[f] = 0;
 		fence_barrier_init();
 	}
 	if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -268,38 +289,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			uint64_t* empty = is_k ? k_empty : v_empty;
 			unsigned char* ring = smem + (is_k ? C::OFF_K : C::OFF_V);
 			const CtaStart S = *s_start;
+			// the first tile goes out before the job is read, from the start record
+			// (tensor maps, first row, plane)
+			if (S.pre > 0)
+			{
+				const CUtensorMap* map = reinterpret_cast<const CUtensorMap*>(is_k ? S.k0 : S.v0);
+				mbar_arrive_expect_tx(&full[0], TC_TILE);
+#pragma unroll
+				for (int p = 0; p < C::KP; ++p) tma3(ring + p * C::PANEL, map, 64 * p, S.pad_[0], S.pad_[1], &full[0]);
+			}
 			Cursor cur;
 			cur.job = S.job;
 			cur.seg = S.seg;
 			cur.tis = S.tis;
 			cursor_load<false>(P.jobs, P.n_jobs, cur);
-			int i = 0, piece = 0;
+			int i = 0, piece = 0, landed = 0; // landed: tiles sent to the land barrier
 			bool waited = false;
 			for (int left = n_mine; left > 0 && !flags[0];)
 			{
 				const DevJob& J = P.jobs[cur.job];
 				const int n = min(min(cur.n_tiles - cur.tis, J.chunk - cur.tis % J.chunk), left);
 				const int h = cur.seg / J.n_rowgroups, rg = cur.seg % J.n_rowgroups;
+				const bool fresh = holds_new_rows(J, cur.tis, n, T);
 				if (is_k)
 				{
-					// the piece's descriptor, q rows, gains and RoPE tables, once the
-					// softmax warps are done with the previous piece's
+					// the piece's descriptor, q rows, gains and RoPE tables (and, when
+					// this kernel appends, the k gains and the new raw k, v rows of
+					// its KV head), once the previous piece is done with the slot
 					if (piece >= 1 && !mbar_wait_bounded(q_empty, (uint32_t)((piece - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
 					{
 						flags[0] = 1;
 						break;
 					}
+					const bool append = P.fused && fresh;
 					const int G = J.n_head / J.n_kv;
 					const int rows = seg_rows(J, rg, NR);
 					int* inf = reinterpret_cast<int*>(slot + C::QHEAD - 4);
 					inf[0] = n;
 					inf[1] = cur.tis;
 					inf[2] = cur.seg;
-					inf[3] = 0;
+					inf[3] = append;
 					const int half = J.n_rot / 2;
 					const uint32_t inv_bytes = (uint32_t)((half * 4 + 15) & ~15);
-					const uint32_t bytes = (uint32_t)(sizeof(DevJob) + rows * D * 4 + (J.q_gamma ? D * 4 : 0) +
-					                                  inv_bytes + (J.freq_factors ? half * 4 : 0));
+					const uint32_t bytes =
+						(uint32_t)(sizeof(DevJob) + rows * D * 4 + (J.q_gamma ? D * 4 : 0) + inv_bytes +
+					               (J.freq_factors ? half * 4 : 0) +
+					               (append ? (J.k_gamma ? D * 4 : 0) + 2 * J.n_tok * D * 4 : 0));
 					mbar_arrive_expect_tx(q_full, bytes); // also releases the info words above
 					bulk_g2s(slot, &J, (uint32_t)sizeof(DevJob), q_full);
 					if (J.q_gamma) bulk_g2s(slot + C::QGAIN, J.q_gamma, (uint32_t)(D * 4), q_full);
@@ -313,6 +348,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 						         (uint32_t)(run * D * 4), q_full);
 						r += run;
 					}
+					if (append)
+					{
+						if (J.k_gamma) bulk_g2s(slot + C::QKG, J.k_gamma, (uint32_t)(D * 4), q_full);
+						for (int t = 0; t < J.n_tok; ++t)
+						{
+							const size_t src = ((size_t)t * J.n_kv + h) * D;
+							bulk_g2s(slot + C::QNEW + t * D, J.k + src, (uint32_t)(D * 4), q_full);
+							bulk_g2s(slot + C::QNEW + (C::NT + t) * D, J.v + src, (uint32_t)(D * 4), q_full);
+						}
+					}
 				}
 				++piece;
 				const CUtensorMap* map = static_cast<const CUtensorMap*>(is_k ? J.tmap_k : J.tmap_v);
@@ -320,13 +365,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				const int plane = J.plane0 + h;
 				for (int k = 0; k < n; ++k, ++i)
 				{
-					// the rows K1 appends come from the preceding grid: wait for it
-					// before the tiles that hold them
-					if (!waited && holds_new_rows(J, cur.tis + k, 1, T))
+					// while K1 appends, the rows it writes come from the preceding grid:
+					// wait for it before the tiles that hold them
+					if (!P.fused && !waited && holds_new_rows(J, cur.tis + k, 1, T))
 					{
 						griddep_wait();
 						waited = true;
 					}
+					if (i < S.pre) continue; // issued at the start
 					const int s = i % STAGES;
 					if (i >= STAGES &&
 					    !mbar_wait_bounded(&empty[s], (uint32_t)(((i / STAGES) - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
@@ -337,9 +383,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 					if (flags[0]) break;
 					const int row0 = ((J.tile_lo + cur.tis + k) * T) % J.rows;
 					unsigned char* st = ring + s * TC_TILE;
-					mbar_arrive_expect_tx(&full[s], TC_TILE);
+					// a tile whose new rows the append warp writes lands on its own
+					// barrier; the stage's barrier still completes its phase (the MMAs
+					// wait for the patched tile instead)
+					uint64_t* bar = &full[s];
+					if (P.fused && holds_new_rows(J, cur.tis + k, 1, T))
+					{
+						mbar_arrive(&full[s]);
+						bar = is_k ? k_land : v_land;
+						++landed;
+					}
+					mbar_arrive_expect_tx(bar, TC_TILE);
 #pragma unroll
-					for (int p = 0; p < C::KP; ++p) tma3(st + p * C::PANEL, map, 64 * p, row0, plane, &full[s]);
+					for (int p = 0; p < C::KP; ++p) tma3(st + p * C::PANEL, map, 64 * p, row0, plane, bar);
 				}
 				left -= n;
 				cur.tis += n;
@@ -348,11 +404,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			if (flags[0])
 			{
 				// do not leave while a copy may still land in this CTA's shared memory
-				for (int k = max(0, i - STAGES); k < i; ++k)
+				for (int k = max(0, i - STAGES); k < max(i, S.pre); ++k)
 					mbar_wait_bounded(&full[k % STAGES], (uint32_t)((k / STAGES) & 1), nullptr, 0);
-				if (is_k) mbar_wait_bounded(q_full, (uint32_t)((piece - 1) & 1), nullptr, 0);
+				if (is_k && piece > 0) mbar_wait_bounded(q_full, (uint32_t)((piece - 1) & 1), nullptr, 0);
+				if (landed > 0) mbar_wait_bounded(is_k ? k_land : v_land, (uint32_t)((landed - 1) & 1), nullptr, 0);
 			}
 		}
+		__syncwarp(); // the whole warp meets the final barrier together
 	}
 	else if (warp == 1)
 	{
@@ -364,10 +422,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			const uint32_t kb0 = smem_u32(smem + C::OFF_K), vb0 = smem_u32(smem + C::OFF_V);
 			const uint32_t qa = smem_u32(smem + C::OFF_Q), pa0 = smem_u32(smem + C::OFF_P);
 			bool ok = true;
+			int patch_lo = -1, patch_hi = -2, kp = 0, vp = 0; // the piece's patched tiles; patches seen
 			auto issue_pv = [&](int j) -> bool {
 				const int s = j % STAGES, b = j & 1;
+				const bool patched = j >= patch_lo && j <= patch_hi;
 				if (!mbar_wait_bounded(&p_full[b], (uint32_t)((j >> 1) & 1), P.err, DEVERR_WAIT_FULL) ||
-				    !mbar_wait_bounded(&v_full[s], (uint32_t)((j / STAGES) & 1), P.err, DEVERR_WAIT_FULL) ||
+				    (patched ? !mbar_wait_bounded(v_patched, (uint32_t)(vp++ & 1), P.err, DEVERR_WAIT_FULL)
+				             : !mbar_wait_bounded(&v_full[s], (uint32_t)((j / STAGES) & 1), P.err, DEVERR_WAIT_FULL)) ||
 				    (j >= 2 && !mbar_wait_bounded(&o_empty[b], (uint32_t)(((j >> 1) - 1) & 1), P.err,
 				                                  DEVERR_WAIT_EMPTY)))
 					return false;
@@ -390,10 +451,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				ok = !flags[0] && mbar_wait_bounded(q_ready, (uint32_t)(piece & 1), P.err, DEVERR_WAIT_FULL);
 				if (!ok) break;
 				const int n = flags[2];
+				patch_lo = flags[3];
+				patch_hi = flags[4];
 				for (int k = 0; ok && k < n; ++k, ++i)
 				{
 					const int s = i % STAGES, b = i & 1;
-					ok = !flags[0] && mbar_wait_bounded(&k_full[s], (uint32_t)((i / STAGES) & 1), P.err, DEVERR_WAIT_FULL);
+					ok = !flags[0] &&
+					     (i >= patch_lo && i <= patch_hi
+					          ? mbar_wait_bounded(k_patched, (uint32_t)(kp++ & 1), P.err, DEVERR_WAIT_FULL)
+					          : mbar_wait_bounded(&k_full[s], (uint32_t)((i / STAGES) & 1), P.err, DEVERR_WAIT_FULL));
 					if (ok && i >= 2)
 						ok = mbar_wait_bounded(&s_empty[b], (uint32_t)(((i >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY);
 					if (!ok) break;
@@ -419,6 +485,135 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			mma_commit(mma_done);
 			mbar_wait_bounded(mma_done, 0, nullptr, 0);
 		}
+		__syncwarp(); // the whole warp meets the final barrier together
+	}
+	else if (warp == 3)
+	{
+		// ---- the append warp: for a piece holding the new tokens (when K1 does
+		// not run), their K/V rows through attention_forward's per-head steps
+		// (model.cpp:1616-1694: K RMSNorm with its gains and RoPE, Gemma 4's V
+		// norm), narrowed to the cache type, stored to the cache (first row
+		// group only), and written into the landed K and V stages of the tiles
+		// that hold them, in place of the rows TMA brought ----
+		int i = 0, nl = 0; // nl: patched tiles so far (the land barriers' phases)
+		for (int piece = 0; i < n_mine; ++piece)
+		{
+			bool ok = !flags[0] && mbar_wait_bounded(q_full, (uint32_t)(piece & 1), P.err, DEVERR_WAIT_FULL);
+			ok = __all_sync(0xffffffffu, ok);
+			if (!ok)
+			{
+				if (lane == 0)
+				{
+					flags[0] = 1;
+					mbar_arrive(q_ready);
+				}
+				break;
+			}
+			const DevJob& J = *reinterpret_cast<const DevJob*>(slot);
+			const int n_piece = info[0], tis0 = info[1], seg_local = info[2];
+			const bool append = info[3] != 0;
+			const int h = seg_local / J.n_rowgroups, rg = seg_local % J.n_rowgroups;
+			const int lo = max(J.pos0, J.key_lo), hi = min(J.pos0 + J.n_tok, J.key_hi); // positions appended
+			const int key0 = (J.tile_lo + tis0) * T;                                     // the piece's first key
+			int plo = -1, phi = -2;
+			if (append)
+			{
+				plo = i + max(0, (lo - key0) / T);
+				phi = i + min(n_piece - 1, (hi - 1 - key0) / T);
+			}
+			if (lane == 0)
+			{
+				flags[3] = plo;
+				flags[4] = phi;
+				mbar_arrive(q_ready); // after the softmax warps' writes of flags[2]: the MMA reads both
+			}
+			// the rows, narrowed, stay in this warp's registers (lane c holds 16-byte
+			// chunk c of each), so that the slot goes back to the producer at once
+			uint4 krow[C::NT], vrow[C::NT];
+			const int n_tok = J.n_tok, pos0 = J.pos0;
+			if (append)
+			{
+				// only the tiles holding the new rows need them (a piece's last,
+				// usually): let the softmax warps' q work go first, which the
+				// first tile waits for
+				if (!mbar_wait_bounded(q_ready, (uint32_t)(piece & 1), P.err, DEVERR_WAIT_FULL) && lane == 0) flags[0] = 1;
+				__syncwarp();
+				const float* ff = J.freq_factors ? slot + C::QFF : nullptr;
+#pragma unroll
+				for (int t = 0; t < C::NT; ++t)
+				{
+					if (t >= n_tok) break;
+					float* kb = slot + C::QNEW + t * D;
+					float* vb = slot + C::QNEW + (C::NT + t) * D;
+					prep_buf(kb, D, J.k_gamma ? slot + C::QKG : nullptr, false, J.eps, true, J.n_rot, J.rope_mode,
+					         (float)(pos0 + t) * J.rope_scale, slot + C::QINV, ff);
+					narrow_buf<KV>(kb, D);
+					prep_buf(vb, D, nullptr, J.v_rmsnorm != 0, J.eps, false, 0, 0, 0.0f, nullptr, nullptr);
+					narrow_buf<KV>(vb, D);
+					if (lane < D / 8)
+					{
+						krow[t] = reinterpret_cast<const uint4*>(kb)[lane];
+						vrow[t] = reinterpret_cast<const uint4*>(vb)[lane];
+					}
+				}
+			}
+			char* const Kc = J.K + (size_t)h * J.head_bytes;
+			char* const Vc = J.V + (size_t)h * J.head_bytes;
+			const int rows_c = J.rows;
+			__syncwarp();
+			if (lane == 0) mbar_arrive(q_empty); // done with the slot
+			if (append)
+			{
+				// the append loop (model.cpp:1662-1694): row pos % rows of the cache,
+				// by the first row group's piece holding the position
+#pragma unroll
+				for (int t = 0; t < C::NT; ++t)
+				{
+					if (t >= n_tok) break;
+					const int pos = pos0 + t;
+					if (rg == 0 && lane < D / 8 && pos >= lo && pos < hi && pos >= key0 && pos < key0 + n_piece * T)
+					{
+						const size_t off = (size_t)(pos % rows_c) * D * 2;
+						reinterpret_cast<uint4*>(Kc + off)[lane] = krow[t];
+						reinterpret_cast<uint4*>(Vc + off)[lane] = vrow[t];
+					}
+				}
+				// the tiles holding the new rows: once each landed, the rows in place
+				for (int pi = plo; pi <= phi; ++pi)
+				{
+					const int s = pi % STAGES;
+					const int tkey = key0 + (pi - i) * T; // the tile's first key
+					for (int which = 0; which < 2; ++which)
+					{
+						bool okp = !flags[0] && mbar_wait_bounded(which == 0 ? k_land : v_land, (uint32_t)(nl & 1),
+						                                          P.err, DEVERR_WAIT_FULL);
+						okp = __all_sync(0xffffffffu, okp);
+						if (okp)
+						{
+							unsigned char* stage = smem + (which == 0 ? C::OFF_K : C::OFF_V) + s * TC_TILE;
+#pragma unroll
+							for (int t = 0; t < C::NT; ++t)
+							{
+								if (t >= n_tok) break;
+								const int pos = pos0 + t;
+								if (pos < lo || pos >= hi || pos < tkey || pos >= tkey + T || lane >= D / 8) continue;
+								const int r = pos - tkey, c = lane;
+								*reinterpret_cast<uint4*>(stage + (c >> 3) * C::PANEL + r * 128 + (((c ^ r) & 7) << 4)) =
+									which == 0 ? krow[t] : vrow[t];
+							}
+						}
+						else if (lane == 0)
+							flags[0] = 1;
+						asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+						__syncwarp();
+						if (lane == 0) mbar_arrive(which == 0 ? k_patched : v_patched);
+					}
+					++nl;
+				}
+			}
+			i += n_piece;
+		}
+		__syncwarp();
 	}
 	else if (warp >= CW0)
 	{
@@ -740,8 +935,8 @@ int launch_tc(const DecodePlan& P, const void* maps, cudaStream_t st)
 		memcpy(&m, maps, sizeof m);
 	else
 		memset(&m, 0, sizeof m);
-	// a programmatic dependent of K1, which appends the new rows: it starts
-	// while K1 runs and waits for it before the tiles that hold them
+	// after K1 (which then appends the new rows) a programmatic dependent of
+	// it: it starts while K1 runs and waits for it before the tiles that hold them
 	cudaLaunchConfig_t cfg = {};
 	cfg.gridDim = dim3((unsigned)P.n_ctas);
 	cfg.blockDim = dim3(TC_THREADS);
@@ -751,7 +946,7 @@ int launch_tc(const DecodePlan& P, const void* maps, cudaStream_t st)
 	attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
 	attr[0].val.programmaticStreamSerializationAllowed = 1;
 	cfg.attrs = attr;
-	cfg.numAttrs = 1;
+	cfg.numAttrs = P.fused ? 0 : 1; // appending itself, it follows the stream's previous work in full
 	return (int)cudaLaunchKernelEx(&cfg, decode_tc_kernel<D, KV, NR>, P, m);
 }
 
@@ -768,6 +963,13 @@ int launch_tc_dims(const DecodePlan& P, const void* maps, cudaStream_t st)
 }
 
 } // namespace
+
+int tc_fuse_tokens(int D, int RM)
+{
+	if (RM == 8) return D == 64 ? TcCfg<64, 8>::NT : D == 128 ? TcCfg<128, 8>::NT : D == 256 ? TcCfg<256, 8>::NT : 0;
+	if (RM == 16) return D == 64 ? TcCfg<64, 16>::NT : D == 128 ? TcCfg<128, 16>::NT : D == 256 ? TcCfg<256, 16>::NT : 0;
+	return 0;
+}
 
 int tc_rows(int D, int kv_type, int rows_needed)
 {

@@ -172,6 +172,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			for (int jj = max(0, issued - 2); jj < issued; ++jj)
 				mbar_wait_bounded(&full[jj & 1], (uint32_t)((jj >> 1) & 1), nullptr, 0);
 		}
+		__syncwarp(); // the whole warp meets the final barrier together
 	}
 	else if (warp == 1)
 	{
@@ -220,6 +221,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			mma_commit(mma_done);
 			mbar_wait_bounded(mma_done, 0, nullptr, 0);
 		}
+		__syncwarp(); // the whole warp meets the final barrier together
 	}
 	else if (warp >= 4)
 	{

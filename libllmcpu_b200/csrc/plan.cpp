@@ -88,7 +88,7 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 	// every job's new tokens, every new position lies in its job's tiles, and
 	// the rows it bulk-copies are 16-byte aligned
 	auto aligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; };
-	int fused = rows_fixed == 0 && max_tok <= decode_fuse_tokens(D, kv_type, RM);
+	int fused = max_tok <= (rows_fixed ? tc_fuse_tokens(D, RM) : decode_fuse_tokens(D, kv_type, RM));
 	for (int i = 0; i < n && fused; ++i)
 	{
 		const DevJob& j = jobs[i];
@@ -180,6 +180,18 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 	{
 		CtaStart& S = starts[c];
 		const DevJob& j = jobs[S.job];
+		if (rows_fixed)
+		{
+			// the tensor-core kernel: its first tile by tensor map, row and plane,
+			// unless it holds new rows (it waits for K1, or lands for the append)
+			if (!j.tmap_k || holds_new_rows(j, S.tis, 1, T)) continue;
+			S.k0 = static_cast<const char*>(j.tmap_k);
+			S.v0 = static_cast<const char*>(j.tmap_v);
+			S.pad_[0] = (int)(((long long)(j.tile_lo + S.tis) * T) % j.rows);
+			S.pad_[1] = j.plane0 + S.seg / j.n_rowgroups;
+			S.pre = 1;
+			continue;
+		}
 		const int len = std::min({j.chunk - S.tis % j.chunk, j.n_tiles - S.tis, S.n_tiles});
 		if (!fused && holds_new_rows(j, S.tis, len, T)) continue;
 		const int h = S.seg / j.n_rowgroups;
