@@ -25,9 +25,9 @@
 //    and fills the q slot (job descriptor, raw q rows, gains, RoPE tables)
 //    of each piece; warp 2 streams the V tiles; each into its own ring;
 //  * warp 1 owns the TMEM allocation and, from one lane, issues the MMAs:
-//    S for tile i into one of two TMEM buffers, then O for tile i - 1 into
-//    one of two others, so the softmax of one tile overlaps the MMAs of the
-//    next;
+//    S for tile i + 1 into one of two TMEM buffers, then O for tile i into
+//    one of two others, so the next tile's scores are computed while this
+//    tile's softmax runs;
 //  * warps 4-7 (TMEM lanes 0-127) normalise and rotate the q rows, write the
 //    Q operand, and per tile: read S, scale, soft-cap, mask by each row's
 //    span, take the row maxima across the tile (warp shuffles, then shared
@@ -414,7 +414,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 	}
 	else if (warp == 1)
 	{
-		// ---- MMA issue: S_i = K_i Q^T, then O_{i-1} = V_{i-1}^T P_{i-1}^T ----
+		// ---- MMA issue: S_{i+1} = K_{i+1} Q^T, then O_i = V_i^T P_i^T ----
 		if (lane == 0 && n_mine > 0)
 		{
 			constexpr uint32_t ID_QK = tc_idesc(C::MQ, N, BF, false, false);
@@ -445,6 +445,35 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				mma_commit(&v_empty[s]);
 				return true;
 			};
+			// S_i = K_i Q^T into S[i % 2], once K_i has landed (or been patched)
+			// and the softmax warps have read what S[i % 2] held
+			auto issue_qk = [&](int i) -> bool {
+				const int s = i % STAGES, b = i & 1;
+				bool okq = !flags[0] &&
+				           (i >= patch_lo && i <= patch_hi
+				                ? mbar_wait_bounded(k_patched, (uint32_t)(kp++ & 1), P.err, DEVERR_WAIT_FULL)
+				                : mbar_wait_bounded(&k_full[s], (uint32_t)((i / STAGES) & 1), P.err, DEVERR_WAIT_FULL));
+				if (okq && i >= 2)
+					okq = mbar_wait_bounded(&s_empty[b], (uint32_t)(((i >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY);
+				if (!okq) return false;
+				tc_fence_after();
+				const uint32_t ka = kb0 + s * TC_TILE;
+				const uint32_t ts = tmem + b * C::S_COLS;
+#pragma unroll
+				for (int qb = 0; qb < C::NQB; ++qb)
+#pragma unroll
+					for (int kk = 0; kk < D / 16; ++kk)
+						mma_f16(ts + qb * N, sdesc(ka + (kk >> 2) * C::PANEL + qb * C::MQ * 128 + (kk & 3) * 32, 16, 1024),
+						        sdesc(qa + (kk >> 2) * C::QPANEL + (kk & 3) * 32, 16, 1024), ID_QK, kk > 0 ? 1u : 0u);
+				mma_commit(&s_full[b]);
+				mma_commit(&k_empty[s]);
+				return true;
+			};
+			// Within a piece S runs one tile ahead: S_{i+1} is issued before
+			// O_i, which waits for tile i's softmax, so the next tile's scores
+			// are ready when the softmax warps come for them. (Not across a
+			// piece's end: the next piece's Q is written only once this piece
+			// is done.)
 			int i = 0;
 			for (int piece = 0; ok && i < n_mine; ++piece)
 			{
@@ -453,32 +482,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				const int n = flags[2];
 				patch_lo = flags[3];
 				patch_hi = flags[4];
+				if (n > 0) ok = issue_qk(i);
 				for (int k = 0; ok && k < n; ++k, ++i)
 				{
-					const int s = i % STAGES, b = i & 1;
-					ok = !flags[0] &&
-					     (i >= patch_lo && i <= patch_hi
-					          ? mbar_wait_bounded(k_patched, (uint32_t)(kp++ & 1), P.err, DEVERR_WAIT_FULL)
-					          : mbar_wait_bounded(&k_full[s], (uint32_t)((i / STAGES) & 1), P.err, DEVERR_WAIT_FULL));
-					if (ok && i >= 2)
-						ok = mbar_wait_bounded(&s_empty[b], (uint32_t)(((i >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY);
-					if (!ok) break;
-					tc_fence_after();
-					const uint32_t ka = kb0 + s * TC_TILE;
-					const uint32_t ts = tmem + b * C::S_COLS;
-#pragma unroll
-					for (int qb = 0; qb < C::NQB; ++qb)
-#pragma unroll
-						for (int kk = 0; kk < D / 16; ++kk)
-							mma_f16(ts + qb * N,
-							        sdesc(ka + (kk >> 2) * C::PANEL + qb * C::MQ * 128 + (kk & 3) * 32, 16, 1024),
-							        sdesc(qa + (kk >> 2) * C::QPANEL + (kk & 3) * 32, 16, 1024), ID_QK,
-							        kk > 0 ? 1u : 0u);
-					mma_commit(&s_full[b]);
-					mma_commit(&k_empty[s]);
-					if (k > 0) ok = issue_pv(i - 1);
+					if (k + 1 < n) ok = issue_qk(i + 1);
+					if (ok) ok = issue_pv(i);
 				}
-				if (ok && n > 0) ok = issue_pv(i - 1);
 			}
 			if (!ok) flags[0] = 1;
 			// every MMA issued has completed before TMEM is freed
