@@ -333,6 +333,21 @@ __device__ __forceinline__ void named_sync(int id, int count)
 	asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// The same barrier, returning whether `pred` held on any of the threads: the
+// one answer every thread gets, so a decision to leave a loop of named
+// barriers is taken by all of them together (a flag read after a plain
+// barrier may change between two threads' reads).
+__device__ __forceinline__ bool named_sync_or(int id, int count, bool pred)
+{
+	uint32_t r;
+	asm volatile(
+		"{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+		: "=r"(r)
+		: "r"((uint32_t)pred), "r"(id), "r"(count)
+		: "memory");
+	return r != 0;
+}
+
 __device__ __forceinline__ float ex2(float x)
 {
 	float y;

@@ -719,10 +719,12 @@ __device__ __forceinline__ void decode_body(const DecodePlan& P, const unsigned 
 	for (int piece = 0; i < n_mine; ++piece)
 	{
 		const int sl = piece & 1;
-		if (!s_flags[0] && !mbar_wait_bounded(&qfull[sl], (uint32_t)((piece >> 1) & 1), P.err, DEVERR_WAIT_FULL))
+		const bool ok = !s_flags[0] && mbar_wait_bounded(&qfull[sl], (uint32_t)((piece >> 1) & 1), P.err, DEVERR_WAIT_FULL);
+		if (named_sync_or(1, NW * 32, !ok)) // every consumer takes the same decision
+		{
 			s_flags[0] = 1;
-		named_sync(1, NW * 32); // every warp has its answer: the decision below is uniform
-		if (s_flags[0]) break;
+			break;
+		}
 		const float* slot = qslot + sl * C::QSLOT_FLOATS;
 		const DevJob& J = *reinterpret_cast<const DevJob*>(slot);
 		const int* info = reinterpret_cast<const int*>(slot + C::QHEAD_FLOATS - 4);

@@ -59,9 +59,10 @@ namespace nncu
 namespace
 {
 
-constexpr int TC_THREADS = 256;   // 8 warps (roles above)
-constexpr int CW0 = 4;            // the first softmax warp; warps 4-7 reach TMEM lanes 0-127
-constexpr int NCW = 4;            // softmax warps
+constexpr int TC_THREADS = 384;   // 12 warps (roles above)
+constexpr int CW0 = 4;            // the first softmax warp; warps 4-7 and 8-11 each reach TMEM lanes 0-127
+constexpr int NCW = 4;            // warps per softmax group
+constexpr int NSG = 2;            // softmax groups: group g takes the tiles i with i % 2 == g
 constexpr int TC_SMEM_LIMIT = 232448;
 constexpr int TC_TILE = 32768;    // one tile's K (or V) rows in bytes
 constexpr float TC_LOG2E = 1.4426950408889634f;
@@ -92,7 +93,7 @@ struct TcCfg
 	static constexpr int QFF = QINV + D / 2;
 	static constexpr int QKG = QFF + D / 2;
 	static constexpr int QNEW = QKG + D;
-	static constexpr int RED = 2 * NCW * NR;        // two buffers of per-warp row values
+	static constexpr int RED = NSG * 2 * NCW * NR + 2 * NR; // per group two buffers of per-warp row values; m, l of group 1
 	static constexpr int FIXED0 = QBYTES + 2 * PBYTES + QNEW * 4 + RED * 4 + 512;
 	// three stages of K and V tiles where they fit, else two; then as many new
 	// tokens (up to 8) as what is left holds
@@ -112,8 +113,9 @@ struct TcCfg
 	static constexpr int SMEM = OFF_BAR + 512 + 1024; // + alignment slack
 	static constexpr int S_COLS = NQB * N;            // TMEM columns of one S buffer
 	static constexpr int O_COLS = NPB * N;            // of one O buffer
-	static constexpr int TMEM_COLS = 2 * (S_COLS + O_COLS) <= 128 ? 128 : 256;
-	static_assert(2 * (S_COLS + O_COLS) <= 256, "TMEM columns");
+	static constexpr int X_COLS = NPB * NR;           // group 1's o, handed to group 0 at a piece's end
+	static constexpr int TMEM_COLS = 2 * (S_COLS + O_COLS) + X_COLS <= 128 ? 128 : 256;
+	static_assert(2 * (S_COLS + O_COLS) + X_COLS <= 256, "TMEM columns");
 	static_assert(LEFT >= 0, "shared memory for two stages");
 	static_assert(SMEM <= TC_SMEM_LIMIT, "shared memory");
 	static_assert(NR == 8 || NR == 16, "rows per segment");
@@ -255,14 +257,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 		for (int b = 0; b < 2; ++b)
 		{
 			mbar_init(&s_full[b], 1);
-			mbar_init(&s_empty[b], 32 * NCW);
+			mbar_init(&s_empty[b], 32 * NCW); // buffer b belongs to softmax group b
 			mbar_init(&p_full[b], 32 * NCW);
 			mbar_init(&o_full[b], 1);
 			mbar_init(&o_empty[b], 32 * NCW);
 		}
 		mbar_init(q_full, 1);
 		mbar_init(q_empty, 2);
-		mbar_init(q_ready, 32 * NCW + 1);
+		mbar_init(q_ready, NSG * 32 * NCW + 1);
 		mbar_init(mma_done, 1);
 		mbar_init(k_patched, 1);
 		mbar_init(v_patched, 1);
@@ -626,11 +628,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 	}
 	else if (warp >= CW0)
 	{
-		// ---- softmax warps: TMEM lanes 32 cw .. 32 cw + 31 ----
-		const int cw = warp - CW0;
-		const int ctid = threadIdx.x - CW0 * 32; // 0 .. 127
+		// ---- two softmax groups: group g (warps 4 + 4g .. 7 + 4g) takes the
+		// tiles i with i % 2 == g and keeps its own online softmax state; warp
+		// cw of a group reaches TMEM lanes 32 cw .. 32 cw + 31 ----
+		const int g = (warp - CW0) / NCW;
+		const int cw = warp & 3;
+		const int gtid = threadIdx.x - CW0 * 32; // 0 .. 255 over both groups
+		const int ctid = gtid & (32 * NCW - 1);  // 0 .. 127 within the group
+		const int gbar = 2 + g;                  // the group's named barrier
 		const uint32_t lane_addr = (uint32_t)(32 * cw) << 16;
 		unsigned char* qop = smem + C::OFF_Q;
+		float* gred = red + g * 2 * NCW * NR;    // the group's two buffers of per-warp row values
+		float* ml1 = red + NSG * 2 * NCW * NR;   // group 1's m, then l, per row
 		// this thread's keys of a tile (per Q K^T block) and its head_dim
 		// columns of O (per P V block); -1: none (an M = 64 block fills half
 		// of each warp's lanes)
@@ -642,10 +651,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 		int i = 0;
 		for (int piece = 0; i < n_mine; ++piece)
 		{
-			bool ok = !flags[0] && mbar_wait_bounded(q_full, (uint32_t)(piece & 1), P.err, DEVERR_WAIT_FULL);
-			if (!ok) flags[0] = 1;
-			named_sync(1, 32 * NCW); // the decision below is uniform
-			if (flags[0]) break;
+			const bool ok = !flags[0] && mbar_wait_bounded(q_full, (uint32_t)(piece & 1), P.err, DEVERR_WAIT_FULL);
+			if (named_sync_or(1, NSG * 32 * NCW, !ok)) // every softmax thread takes the same decision
+			{
+				flags[0] = 1;
+				break;
+			}
 			const DevJob& J = *reinterpret_cast<const DevJob*>(slot);
 			const int n_piece = info[0], tis0 = info[1], seg_local = info[2];
 			const int G = J.n_head / J.n_kv;
@@ -654,13 +665,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			float* qs = slot + C::QROWS;
 			const float* ff = J.freq_factors ? slot + C::QFF : nullptr;
 			// attention_forward's per-head q work (model.cpp:1616-1660), a warp per row
-			for (int r = cw; r < rows; r += NCW)
+			for (int r = warp - CW0; r < rows; r += NSG * NCW)
 				prep_buf(qs + r * D, D, J.q_gamma ? slot + C::QGAIN : nullptr, false, J.eps, true, J.n_rot,
 				         J.rope_mode, (float)(J.pos0 + (rg * NR + r) / G) * J.rope_scale, slot + C::QINV, ff);
-			named_sync(1, 32 * NCW);
+			named_sync(1, NSG * 32 * NCW);
 			// the Q operand: row r's high half as operand row r, its low half as
 			// row NR + r; padding rows are zero
-			for (int idx = ctid; idx < NR * (D / 8); idx += 32 * NCW)
+			for (int idx = gtid; idx < NR * (D / 8); idx += NSG * 32 * NCW)
 			{
 				const int r = idx / (D / 8), c0 = (idx % (D / 8)) * 8;
 				uint16_t hi[8], lo[8];
@@ -695,16 +706,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			}
 			const bool softcap = J.softcap > 0.0f;
 			const float sl = softcap ? J.scale / J.softcap : J.scale * TC_LOG2E, cl = J.softcap * TC_LOG2E;
-			int key_base = (J.tile_lo + tis0) * T;
+			const int key_first = (J.tile_lo + tis0) * T;
 			// what the end of the piece needs from the slot
 			float* out = J.out;
 			const int n_head = J.n_head, n_tok = J.n_tok, seg = J.seg0 + seg_local, n_pieces = J.n_chunks;
 			const int part_slot = J.part0 + seg_local * J.n_chunks + tis0 / J.chunk;
 			const int part_first = J.part0 + seg_local * J.n_chunks;
-			if (ctid == 0) flags[2] = n_piece;
+			if (gtid == 0) flags[2] = n_piece;
 			asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); // the Q operand, for the MMAs
-			named_sync(1, 32 * NCW);
-			if (ctid == 0) mbar_arrive(q_empty); // the slot is no longer read
+			named_sync(1, NSG * 32 * NCW);
+			if (gtid == 0) mbar_arrive(q_empty); // the slot is no longer read
 			tc_fence_before();
 			mbar_arrive(q_ready);
 
@@ -718,8 +729,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 #pragma unroll
 				for (int mb = 0; mb < C::NPB; ++mb) o[mb][r] = 0.0f;
 			}
-			// O of tile j (in TMEM once its P V is done) into o, after the running
-			// maximum's correction of the tiles before it
+			// O of this group's tile j (in TMEM once its P V is done) into o, after
+			// the running maximum's correction of the group's tiles before it
 			auto fold_o = [&](int j) {
 				const int b = j & 1;
 				bool okf = !flags[0] && mbar_wait_bounded(&o_full[b], (uint32_t)((j >> 1) & 1), P.err, DEVERR_WAIT_FULL);
@@ -744,10 +755,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 					for (int r = 0; r < NR; ++r) o[mb][r] = fmaf(o[mb][r], alpha_prev[r], c[mb][r] + c[mb][NR + r]);
 			};
 
-			for (int k = 0; k < n_piece; ++k, ++i)
+			int jprev = -1; // the group's previous tile, whose O is folded after this tile's P
+			for (int k = g; k < n_piece; k += NSG)
 			{
-				const int b = i & 1;
-				bool okt = !flags[0] && mbar_wait_bounded(&s_full[b], (uint32_t)((i >> 1) & 1), P.err, DEVERR_WAIT_FULL);
+				const int ti = i + k; // this tile's CTA-wide index: its S, P and O buffers are ti % 2
+				const int b = ti & 1;
+				bool okt = !flags[0] && mbar_wait_bounded(&s_full[b], (uint32_t)((ti >> 1) & 1), P.err, DEVERR_WAIT_FULL);
 				okt = __all_sync(0xffffffffu, okt);
 				if (!okt) flags[0] = 1;
 				float s[C::NQB][NR];
@@ -773,6 +786,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				tc_fence_before();
 				mbar_arrive(&s_empty[b]);
 				// scores in log2 units, soft-capped where asked, masked by each row's span
+				const int key_base = key_first + k * T;
 				float tmax[NR];
 #pragma unroll
 				for (int r = 0; r < NR; ++r) tmax[r] = -CUDART_INF_F;
@@ -789,13 +803,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 						tmax[r] = fmaxf(tmax[r], x);
 					}
 				}
-				// the tile's row maxima: across the warp, then across the four warps
-				float* rb = red + (i & 1) * NCW * NR;
+				// the tile's row maxima: across the warp, then across the group's four warps
+				float* rb = gred + ((ti >> 1) & 1) * NCW * NR;
 				{
 					const float wm = warp_rows<NR, true>(tmax, lane);
 					if ((lane & (32 / NR - 1)) == 0) rb[cw * NR + lane / (32 / NR)] = wm;
 				}
-				named_sync(1, 32 * NCW);
+				named_sync(gbar, 32 * NCW);
 				float alpha[NR], mref[NR];
 #pragma unroll
 				for (int r = 0; r < NR; ++r)
@@ -809,8 +823,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 					mref[r] = (mn == -CUDART_INF_F ? 0.0f : mn) - P_SHIFT;
 				}
 				// the weights 2^8 exp2(s - m) as high and low halves into P (operand
-				// row r, and NR + r), once the P V that last read this buffer is done
-				// (its O was folded in the previous step)
+				// row r, and NR + r), once the P V that last read this buffer (the
+				// group's previous tile) is done: its O was folded in the last step
 				unsigned char* pb = smem + C::OFF_P + b * C::PBYTES;
 #pragma unroll
 				for (int qb = 0; qb < C::NQB; ++qb)
@@ -837,21 +851,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 				tc_fence_before();
 				mbar_arrive(&p_full[b]);
-				if (k > 0) fold_o(i - 1);
+				if (jprev >= 0) fold_o(jprev);
 #pragma unroll
 				for (int r = 0; r < NR; ++r) alpha_prev[r] = alpha[r];
-				key_base += T;
+				jprev = ti;
 			}
-			if (n_piece > 0) fold_o(i - 1);
+			if (jprev >= 0) fold_o(jprev);
+			i += n_piece;
 
-			// ---- the piece's end: the row sums, then the output or a partial ----
-			float* rs = red + ((i & 1) ^ 1) * NCW * NR; // the buffer the last tile's maxima did not use
+			// ---- the piece's end: each group's row sums; group 1 hands its (m, l, o)
+			// to group 0 (o through TMEM, lanes as O's), which merges them
+			// (nnc_attn_merge's formula) and gives the output or a partial ----
+			// not the buffer of the group's last tile (its maxima may still be read)
+			float* rs = gred + (jprev >= 0 ? ((jprev + 2) >> 1) & 1 : 0) * NCW * NR;
 			{
 				const float ws = warp_rows<NR, false>(lp, lane);
 				if ((lane & (32 / NR - 1)) == 0) rs[cw * NR + lane / (32 / NR)] = ws;
 			}
-			named_sync(1, 32 * NCW);
-			float L[NR], M[NR];
+			named_sync(gbar, 32 * NCW);
+			float L[NR];
 #pragma unroll
 			for (int r = 0; r < NR; ++r)
 			{
@@ -859,60 +877,103 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 #pragma unroll
 				for (int w = 1; w < NCW; ++w) l += rs[w * NR + r];
 				L[r] = l;
-				M[r] = m[r] == -CUDART_INF_F ? -CUDART_INF_F : m[r] - P_SHIFT;
 			}
-			const int rows_valid = G * n_tok - rg * NR;
-			auto out_row = [&](int R) -> float* {
-				const int gr = rg * NR + R;
-				return out + ((size_t)(gr / G) * n_head + (size_t)h * G + gr % G) * D;
-			};
-			if (n_pieces == 1)
+			const uint32_t xaddr = tmem + lane_addr + 2 * C::S_COLS + 2 * C::O_COLS;
+			if (g == 1)
 			{
+				float flat[C::X_COLS];
 #pragma unroll
 				for (int mb = 0; mb < C::NPB; ++mb)
-					if (dx[mb] >= 0)
 #pragma unroll
-						for (int r = 0; r < NR; ++r)
-							if (r < rows_valid) out_row(r)[dx[mb]] = L[r] > 0.0f ? o[mb][r] / L[r] : 0.0f;
-			}
-			else
-			{
-				float* part = P.parts + (size_t)part_slot * NR * PW;
-#pragma unroll
-				for (int mb = 0; mb < C::NPB; ++mb)
-					if (dx[mb] >= 0)
-#pragma unroll
-						for (int r = 0; r < NR; ++r) part[r * PW + dx[mb]] = o[mb][r];
+					for (int r = 0; r < NR; ++r) flat[mb * NR + r] = o[mb][r];
+				tmem_st<C::X_COLS>(xaddr, flat);
+				tmem_wait_st();
 				if (ctid < NR)
 				{
 #pragma unroll
 					for (int r = 0; r < NR; ++r)
-						if (r == ctid) *reinterpret_cast<float2*>(part + r * PW + D) = make_float2(M[r], L[r]);
+						if (r == ctid)
+						{
+							ml1[r] = m[r];
+							ml1[NR + r] = L[r];
+						}
 				}
-				named_sync(1, 32 * NCW);
-				if (ctid == 0)
-				{
-					const int prev = atomic_add_acq_rel(&P.counters[seg], 1);
-					flags[1] = prev == n_pieces - 1;
-				}
-				named_sync(1, 32 * NCW);
-				if (flags[1])
-				{
-					// the segment's last piece: fold the pieces in order
-					// (nnc_attn_merge), then divide (nnc_attn_finish)
-					merge_pieces<D, NR>(P.parts + (size_t)part_first * NR * PW, (size_t)NR * PW, n_pieces, rows_valid,
-					                    ctid, 32 * NCW, [&](int R, int d, float4 acc, float Mx, float Lx) {
-						                    const float inv = Lx > 0.0f ? 1.0f / Lx : 0.0f;
-						                    acc.x *= inv;
-						                    acc.y *= inv;
-						                    acc.z *= inv;
-						                    acc.w *= inv;
-						                    *reinterpret_cast<float4*>(out_row(R) + d) = acc;
-					                    });
-					if (ctid == 0) P.counters[seg] = 0; // ready for the next launch
-				}
+				tc_fence_before();
 			}
-			named_sync(1, 32 * NCW); // the reduction buffers are free again
+			named_sync(1, NSG * 32 * NCW);
+			if (g == 0)
+			{
+				tc_fence_after();
+				float x1[C::X_COLS];
+				tmem_ld<C::X_COLS>(xaddr, x1);
+				tmem_wait_ld();
+				float M[NR];
+#pragma unroll
+				for (int r = 0; r < NR; ++r)
+				{
+					const float m1 = ml1[r], l1 = ml1[NR + r];
+					const float mx = fmaxf(m[r], m1);
+					const float c0 = m[r] == -CUDART_INF_F ? 0.0f : ex2(m[r] - mx);
+					const float c1 = m1 == -CUDART_INF_F ? 0.0f : ex2(m1 - mx);
+#pragma unroll
+					for (int mb = 0; mb < C::NPB; ++mb) o[mb][r] = fmaf(o[mb][r], c0, x1[mb * NR + r] * c1);
+					L[r] = fmaf(L[r], c0, l1 * c1);
+					M[r] = mx == -CUDART_INF_F ? -CUDART_INF_F : mx - P_SHIFT;
+				}
+				const int rows_valid = G * n_tok - rg * NR;
+				auto out_row = [&](int R) -> float* {
+					const int gr = rg * NR + R;
+					return out + ((size_t)(gr / G) * n_head + (size_t)h * G + gr % G) * D;
+				};
+				if (n_pieces == 1)
+				{
+#pragma unroll
+					for (int mb = 0; mb < C::NPB; ++mb)
+						if (dx[mb] >= 0)
+#pragma unroll
+							for (int r = 0; r < NR; ++r)
+								if (r < rows_valid) out_row(r)[dx[mb]] = L[r] > 0.0f ? o[mb][r] / L[r] : 0.0f;
+				}
+				else
+				{
+					float* part = P.parts + (size_t)part_slot * NR * PW;
+#pragma unroll
+					for (int mb = 0; mb < C::NPB; ++mb)
+						if (dx[mb] >= 0)
+#pragma unroll
+							for (int r = 0; r < NR; ++r) part[r * PW + dx[mb]] = o[mb][r];
+					if (ctid < NR)
+					{
+#pragma unroll
+						for (int r = 0; r < NR; ++r)
+							if (r == ctid) *reinterpret_cast<float2*>(part + r * PW + D) = make_float2(M[r], L[r]);
+					}
+					named_sync(gbar, 32 * NCW);
+					if (ctid == 0)
+					{
+						const int prev = atomic_add_acq_rel(&P.counters[seg], 1);
+						flags[1] = prev == n_pieces - 1;
+					}
+					named_sync(gbar, 32 * NCW);
+					if (flags[1])
+					{
+						// the segment's last piece: fold the pieces in order
+						// (nnc_attn_merge), then divide (nnc_attn_finish)
+						merge_pieces<D, NR>(P.parts + (size_t)part_first * NR * PW, (size_t)NR * PW, n_pieces, rows_valid,
+						                    ctid, 32 * NCW, [&](int R, int d, float4 acc, float Mx, float Lx) {
+							                    const float inv = Lx > 0.0f ? 1.0f / Lx : 0.0f;
+							                    acc.x *= inv;
+							                    acc.y *= inv;
+							                    acc.z *= inv;
+							                    acc.w *= inv;
+							                    *reinterpret_cast<float4*>(out_row(R) + d) = acc;
+						                    });
+						if (ctid == 0) P.counters[seg] = 0; // ready for the next launch
+					}
+				}
+				tc_fence_before();
+			}
+			named_sync(1, NSG * 32 * NCW); // the reduction buffers and the hand-over columns are free again
 		}
 	}
 	tc_fence_before();

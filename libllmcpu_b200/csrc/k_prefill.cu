@@ -246,8 +246,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 		{
 			const int s = jj & 1;
 			if (ok) ok = !flags[0] && mbar_wait_bounded(&s_full[s], (uint32_t)((jj >> 1) & 1), P.err, DEVERR_WAIT_FULL);
-			ok = __all_sync(0xffffffffu, ok);
-			if (!ok) break;
+			ok = __all_sync(0xffffffffu, ok); // (the warps on these lanes leave together, at the barrier below)
 			tc_fence_after();
 			float x[PF_CW];
 			tmem_ld32(TS[s] + lane_off + col0, x);
@@ -278,7 +277,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl;
 			float* mxs = red + s * PF_NH * 128;
 			mxs[hf * 128 + r] = mx;
-			named_sync(2 + wq, 32 * PF_NH); // the warps on these TMEM lanes
+			// the warps on these TMEM lanes; a timed-out wait in any of them ends
+			// the loop for all of them
+			if (named_sync_or(2 + wq, 32 * PF_NH, !ok))
+			{
+				ok = false;
+				break;
+			}
 #pragma unroll
 			for (int o = 1; o < PF_NH; ++o) mx = fmaxf(mx, mxs[((hf + o) % PF_NH) * 128 + r]);
 			// the row's reference maximum moves only when a score exceeds it by
@@ -304,10 +309,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			if (jj > 0)
 			{
 				ok = mbar_wait_bounded(pv_done, (uint32_t)((jj - 1) & 1), P.err, DEVERR_WAIT_FULL);
-				ok = __all_sync(0xffffffffu, ok);
-				if (!ok) break;
+				ok = __all_sync(0xffffffffu, ok); // (a failure ends the loop at the next barrier)
 				tc_fence_after();
-				if (__any_sync(0xffffffffu, rescale))
+				if (ok && __any_sync(0xffffffffu, rescale))
 				{
 					float o[32];
 					tmem_ld32(TO + lane_off + col0, o);

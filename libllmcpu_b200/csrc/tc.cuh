@@ -82,6 +82,43 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v)
 	             : "memory");
 }
 
+// 8, 16 or 32 consecutive fp32 columns into this thread's TMEM lane.
+template <int N>
+__device__ __forceinline__ void tmem_st(uint32_t taddr, const float* v)
+{
+	static_assert(N == 8 || N == 16 || N == 32, "8, 16 or 32 columns");
+	if constexpr (N == 32)
+		tmem_st32(taddr, v);
+	else if constexpr (N == 8)
+		asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+		             "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+		             "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+		             "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+		             : "memory");
+	else
+		asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+		             "%12, %13, %14, %15, %16};" ::"r"(taddr),
+		             "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+		             "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+		             "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+		             "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+		             "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+		             "r"(__float_as_uint(v[15]))
+		             : "memory");
+}
+
+// 8 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v)
+{
+	uint32_t r[8];
+	asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+	             : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+	             : "r"(taddr)
+	             : "memory");
+#pragma unroll
+	for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -111,12 +148,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v)
 	for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// N (16 or 32) consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v);
+
+// N (8, 16 or 32) consecutive fp32 columns of this thread's TMEM lane.
 template <int N>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, float* v)
 {
-	static_assert(N == 16 || N == 32, "16 or 32 columns");
-	if constexpr (N == 16)
+	static_assert(N == 8 || N == 16 || N == 32, "8, 16 or 32 columns");
+	if constexpr (N == 8)
+		tmem_ld8(taddr, v);
+	else if constexpr (N == 16)
 		tmem_ld16(taddr, v);
 	else
 		tmem_ld32(taddr, v);
