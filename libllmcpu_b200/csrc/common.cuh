@@ -283,6 +283,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
 	return ok != 0;
 }
 
+// Whether phase `parity` of `bar` has completed, without waiting (test_wait
+// never suspends the thread, unlike try_wait): for a loop that polls several
+// barriers in turn.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity)
+{
+	uint32_t ok;
+	asm volatile(
+		"{\n\t.reg .pred p;\n\t"
+		"mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+		"selp.u32 %0, 1, 0, p;\n\t}"
+		: "=r"(ok)
+		: "r"(smem_u32(bar)), "r"(parity)
+		: "memory");
+	return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns()
 {
 	uint64_t t;

@@ -114,8 +114,13 @@ struct TcCfg
 	static constexpr int S_COLS = NQB * N;            // TMEM columns of one S buffer
 	static constexpr int O_COLS = NPB * N;            // of one O buffer
 	static constexpr int X_COLS = NPB * NR;           // group 1's o, handed to group 0 at a piece's end
-	static constexpr int TMEM_COLS = 2 * (S_COLS + O_COLS) + X_COLS <= 128 ? 128 : 256;
-	static_assert(2 * (S_COLS + O_COLS) + X_COLS <= 256, "TMEM columns");
+	// S buffers: four where TMEM holds them (S runs three tiles ahead of P V), else two
+	static constexpr int NSB = 4 * S_COLS + 2 * O_COLS + X_COLS <= 256 ? 4 : 2;
+	static constexpr int SA = NSB - 1;                // tiles S runs ahead
+	static constexpr int O_BASE = NSB * S_COLS;       // first column of the O buffers
+	static constexpr int X_BASE = O_BASE + 2 * O_COLS;
+	static constexpr int TMEM_COLS = X_BASE + X_COLS <= 128 ? 128 : 256;
+	static_assert(X_BASE + X_COLS <= 256, "TMEM columns");
 	static_assert(LEFT >= 0, "shared memory for two stages");
 	static_assert(SMEM <= TC_SMEM_LIMIT, "shared memory");
 	static_assert(NR == 8 || NR == 16, "rows per segment");
@@ -224,9 +229,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 	uint64_t* k_empty = k_full + STAGES;      // [STAGES]
 	uint64_t* v_full = k_empty + STAGES;      // [STAGES]
 	uint64_t* v_empty = v_full + STAGES;      // [STAGES]
-	uint64_t* s_full = v_empty + STAGES;      // [2]
-	uint64_t* s_empty = s_full + 2;           // [2]
-	uint64_t* p_full = s_empty + 2;           // [2]
+	uint64_t* s_full = v_empty + STAGES;      // [NSB]
+	uint64_t* s_empty = s_full + C::NSB;      // [NSB]
+	uint64_t* p_full = s_empty + C::NSB;      // [2]
 	uint64_t* o_full = p_full + 2;            // [2]
 	uint64_t* o_empty = o_full + 2;           // [2]
 	uint64_t* q_full = o_empty + 2;           // the slot holds a piece
@@ -254,11 +259,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			mbar_init(&v_full[s], 1);
 			mbar_init(&v_empty[s], 1);
 		}
-		for (int b = 0; b < 2; ++b)
+		for (int b = 0; b < C::NSB; ++b)
 		{
 			mbar_init(&s_full[b], 1);
-			mbar_init(&s_empty[b], 32 * NCW); // buffer b belongs to softmax group b
-			mbar_init(&p_full[b], 32 * NCW);
+			mbar_init(&s_empty[b], 32 * NCW); // tile i's S is read by softmax group i % 2
+		}
+		for (int b = 0; b < 2; ++b)
+		{
+			mbar_init(&p_full[b], 32 * NCW); // P and O buffer b belong to softmax group b
 			mbar_init(&o_full[b], 1);
 			mbar_init(&o_empty[b], 32 * NCW);
 		}
@@ -425,39 +433,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			const uint32_t qa = smem_u32(smem + C::OFF_Q), pa0 = smem_u32(smem + C::OFF_P);
 			bool ok = true;
 			int patch_lo = -1, patch_hi = -2, kp = 0, vp = 0; // the piece's patched tiles; patches seen
-			auto issue_pv = [&](int j) -> bool {
-				const int s = j % STAGES, b = j & 1;
-				const bool patched = j >= patch_lo && j <= patch_hi;
-				if (!mbar_wait_bounded(&p_full[b], (uint32_t)((j >> 1) & 1), P.err, DEVERR_WAIT_FULL) ||
-				    (patched ? !mbar_wait_bounded(v_patched, (uint32_t)(vp++ & 1), P.err, DEVERR_WAIT_FULL)
-				             : !mbar_wait_bounded(&v_full[s], (uint32_t)((j / STAGES) & 1), P.err, DEVERR_WAIT_FULL)) ||
-				    (j >= 2 && !mbar_wait_bounded(&o_empty[b], (uint32_t)(((j >> 1) - 1) & 1), P.err,
-				                                  DEVERR_WAIT_EMPTY)))
-					return false;
-				tc_fence_after();
-				const uint32_t va = vb0 + s * TC_TILE, pa = pa0 + b * C::PBYTES;
-				const uint32_t to = tmem + 2 * C::S_COLS + b * C::O_COLS;
-#pragma unroll
-				for (int mb = 0; mb < C::NPB; ++mb)
-#pragma unroll
-					for (int kk = 0; kk < T / 16; ++kk)
-						mma_f16(to + mb * N, sdesc(va + mb * 2 * C::PANEL + kk * 2048, C::PANEL, 1024),
-						        sdesc(pa + (kk >> 2) * C::PPANEL + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0 ? 1u : 0u);
-				mma_commit(&o_full[b]);
-				mma_commit(&v_empty[s]);
-				return true;
+			// whether tile j's K (or V) is in its stage: landed, or patched by the append warp
+			auto k_ready = [&](int j) {
+				return j >= patch_lo && j <= patch_hi ? mbar_test(k_patched, (uint32_t)(kp & 1))
+				                                      : mbar_test(&k_full[j % STAGES], (uint32_t)((j / STAGES) & 1));
 			};
-			// S_i = K_i Q^T into S[i % 2], once K_i has landed (or been patched)
-			// and the softmax warps have read what S[i % 2] held
-			auto issue_qk = [&](int i) -> bool {
-				const int s = i % STAGES, b = i & 1;
-				bool okq = !flags[0] &&
-				           (i >= patch_lo && i <= patch_hi
-				                ? mbar_wait_bounded(k_patched, (uint32_t)(kp++ & 1), P.err, DEVERR_WAIT_FULL)
-				                : mbar_wait_bounded(&k_full[s], (uint32_t)((i / STAGES) & 1), P.err, DEVERR_WAIT_FULL));
-				if (okq && i >= 2)
-					okq = mbar_wait_bounded(&s_empty[b], (uint32_t)(((i >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY);
-				if (!okq) return false;
+			auto v_ready = [&](int j) {
+				return j >= patch_lo && j <= patch_hi ? mbar_test(v_patched, (uint32_t)(vp & 1))
+				                                      : mbar_test(&v_full[j % STAGES], (uint32_t)((j / STAGES) & 1));
+			};
+			// S_j = K_j Q^T into S buffer j % NSB
+			auto issue_qk = [&](int j) {
+				const int s = j % STAGES, b = j % C::NSB;
+				if (j >= patch_lo && j <= patch_hi) ++kp;
 				tc_fence_after();
 				const uint32_t ka = kb0 + s * TC_TILE;
 				const uint32_t ts = tmem + b * C::S_COLS;
@@ -469,13 +457,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 						        sdesc(qa + (kk >> 2) * C::QPANEL + (kk & 3) * 32, 16, 1024), ID_QK, kk > 0 ? 1u : 0u);
 				mma_commit(&s_full[b]);
 				mma_commit(&k_empty[s]);
-				return true;
 			};
-			// Within a piece S runs one tile ahead: S_{i+1} is issued before
-			// O_i, which waits for tile i's softmax, so the next tile's scores
-			// are ready when the softmax warps come for them. (Not across a
-			// piece's end: the next piece's Q is written only once this piece
-			// is done.)
+			// O_j = V_j^T P_j^T into O buffer j % 2
+			auto issue_pv = [&](int j) {
+				const int s = j % STAGES, b = j & 1;
+				if (j >= patch_lo && j <= patch_hi) ++vp;
+				tc_fence_after();
+				const uint32_t va = vb0 + s * TC_TILE, pa = pa0 + b * C::PBYTES;
+				const uint32_t to = tmem + C::O_BASE + b * C::O_COLS;
+#pragma unroll
+				for (int mb = 0; mb < C::NPB; ++mb)
+#pragma unroll
+					for (int kk = 0; kk < T / 16; ++kk)
+						mma_f16(to + mb * N, sdesc(va + mb * 2 * C::PANEL + kk * 2048, C::PANEL, 1024),
+						        sdesc(pa + (kk >> 2) * C::PPANEL + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0 ? 1u : 0u);
+				mma_commit(&o_full[b]);
+				mma_commit(&v_empty[s]);
+			};
+			// Within a piece, whichever is ready first: the next S (its K landed,
+			// its buffer read by the softmax; up to NSB - 1 tiles ahead of the
+			// softmax) or the next O (its P written, its V landed, its buffer
+			// folded). Not across a piece's end: the next piece's Q is written
+			// only once this piece is done. A wait without progress gives up after
+			// the bounded-wait limit.
 			int i = 0;
 			for (int piece = 0; ok && i < n_mine; ++piece)
 			{
@@ -484,12 +488,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				const int n = flags[2];
 				patch_lo = flags[3];
 				patch_hi = flags[4];
-				if (n > 0) ok = issue_qk(i);
-				for (int k = 0; ok && k < n; ++k, ++i)
+				const int end = i + n;
+				int nq = i, np = i;
+				uint64_t t_prog = globaltimer_ns();
+				for (uint32_t spin = 0; np < end; ++spin)
 				{
-					if (k + 1 < n) ok = issue_qk(i + 1);
-					if (ok) ok = issue_pv(i);
+					bool did = false;
+					if (nq < end && nq < np + C::NSB && k_ready(nq) &&
+					    (nq < C::NSB || mbar_test(&s_empty[nq % C::NSB], (uint32_t)(((nq / C::NSB) - 1) & 1))))
+					{
+						issue_qk(nq++);
+						did = true;
+					}
+					if (np < nq && mbar_test(&p_full[np & 1], (uint32_t)((np >> 1) & 1)) && v_ready(np) &&
+					    (np < 2 || mbar_test(&o_empty[np & 1], (uint32_t)(((np >> 1) - 1) & 1))))
+					{
+						issue_pv(np++);
+						did = true;
+					}
+					if (did)
+						t_prog = globaltimer_ns();
+					else if ((spin & 255u) == 255u && (flags[0] || globaltimer_ns() - t_prog > WAIT_LIMIT_NS))
+					{
+						if (!flags[0]) atomicCAS(P.err, 0, DEVERR_WAIT_FULL);
+						ok = false;
+						break;
+					}
 				}
+				i = end;
 			}
 			if (!ok) flags[0] = 1;
 			// every MMA issued has completed before TMEM is freed
@@ -745,7 +771,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				float c[C::NPB][N];
 #pragma unroll
 				for (int mb = 0; mb < C::NPB; ++mb)
-					tmem_ld<N>(tmem + lane_addr + 2 * C::S_COLS + b * C::O_COLS + mb * N, c[mb]);
+					tmem_ld<N>(tmem + lane_addr + C::O_BASE + b * C::O_COLS + mb * N, c[mb]);
 				tmem_wait_ld();
 				tc_fence_before();
 				mbar_arrive(&o_empty[b]);
@@ -758,9 +784,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			int jprev = -1; // the group's previous tile, whose O is folded after this tile's P
 			for (int k = g; k < n_piece; k += NSG)
 			{
-				const int ti = i + k; // this tile's CTA-wide index: its S, P and O buffers are ti % 2
-				const int b = ti & 1;
-				bool okt = !flags[0] && mbar_wait_bounded(&s_full[b], (uint32_t)((ti >> 1) & 1), P.err, DEVERR_WAIT_FULL);
+				const int ti = i + k; // this tile's CTA-wide index: its S buffer is ti % NSB, P and O ti % 2
+				const int b = ti & 1, sb = ti % C::NSB;
+				bool okt = !flags[0] && mbar_wait_bounded(&s_full[sb], (uint32_t)((ti / C::NSB) & 1), P.err, DEVERR_WAIT_FULL);
 				okt = __all_sync(0xffffffffu, okt);
 				if (!okt) flags[0] = 1;
 				float s[C::NQB][NR];
@@ -769,7 +795,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 					tc_fence_after();
 					float c[C::NQB][N];
 #pragma unroll
-					for (int qb = 0; qb < C::NQB; ++qb) tmem_ld<N>(tmem + lane_addr + b * C::S_COLS + qb * N, c[qb]);
+					for (int qb = 0; qb < C::NQB; ++qb) tmem_ld<N>(tmem + lane_addr + sb * C::S_COLS + qb * N, c[qb]);
 					tmem_wait_ld();
 #pragma unroll
 					for (int qb = 0; qb < C::NQB; ++qb)
@@ -784,7 +810,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 						for (int r = 0; r < NR; ++r) s[qb][r] = 0.0f;
 				}
 				tc_fence_before();
-				mbar_arrive(&s_empty[b]);
+				mbar_arrive(&s_empty[sb]);
 				// scores in log2 units, soft-capped where asked, masked by each row's span
 				const int key_base = key_first + k * T;
 				float tmax[NR];
@@ -822,9 +848,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 					m[r] = mn;
 					mref[r] = (mn == -CUDART_INF_F ? 0.0f : mn) - P_SHIFT;
 				}
-				// the weights 2^8 exp2(s - m) as high and low halves into P (operand
-				// row r, and NR + r), once the P V that last read this buffer (the
-				// group's previous tile) is done: its O was folded in the last step
+				// the group's previous tile's O (its P V also read this P buffer
+				// last), then the weights 2^8 exp2(s - m) as high and low halves into
+				// P (operand row r, and NR + r)
+				if (jprev >= 0) fold_o(jprev);
+#pragma unroll
+				for (int r = 0; r < NR; ++r) alpha_prev[r] = alpha[r];
+				jprev = ti;
 				unsigned char* pb = smem + C::OFF_P + b * C::PBYTES;
 #pragma unroll
 				for (int qb = 0; qb < C::NQB; ++qb)
@@ -851,10 +881,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 				tc_fence_before();
 				mbar_arrive(&p_full[b]);
-				if (jprev >= 0) fold_o(jprev);
-#pragma unroll
-				for (int r = 0; r < NR; ++r) alpha_prev[r] = alpha[r];
-				jprev = ti;
 			}
 			if (jprev >= 0) fold_o(jprev);
 			i += n_piece;
@@ -878,7 +904,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				for (int w = 1; w < NCW; ++w) l += rs[w * NR + r];
 				L[r] = l;
 			}
-			const uint32_t xaddr = tmem + lane_addr + 2 * C::S_COLS + 2 * C::O_COLS;
+			const uint32_t xaddr = tmem + lane_addr + C::X_BASE;
 			if (g == 1)
 			{
 				float flat[C::X_COLS];
