@@ -208,6 +208,10 @@ typedef struct nncu_attn_params
 	int32_t v_rmsnorm;            /* Gemma 4: RMS-normalise V rows, no gamma */
 	float eps, scale, softcap;    /* softcap > 0: cap*tanh(s/cap) on scaled scores */
 	int32_t causal, window, reuse_kv; /* reuse_kv: read another layer's cache, append nothing */
+	/* Qwen3.5's output gate (model.cpp:1759-1760, nnc_mul_sigmoid_f32): the
+	 * attention output is multiplied, element by element, by sigmoid(gate);
+	 * gate is [n_tok][n_head*head_dim] like the output, or NULL (no gate). */
+	const float* gate;
 } nncu_attn_params;
 
 /* The drop-in call for attention_forward: q [n_tok][n_head*head_dim] and

@@ -80,6 +80,7 @@ class AttnParams(C.Structure):
         ("v_rmsnorm", C.c_int32),
         ("eps", C.c_float), ("scale", C.c_float), ("softcap", C.c_float),
         ("causal", C.c_int32), ("window", C.c_int32), ("reuse_kv", C.c_int32),
+        ("gate", C.c_void_p),
     ]
 
 
@@ -235,11 +236,11 @@ def attn_span(causal: bool, window: int, pos: int, n_seq: int) -> tuple[int, int
 
 def params(**kw) -> AttnParams:
     """An nncu_attn_params with the reference's defaults filled in. Array
-    arguments (freq_factors, q_gamma, k_gamma) may be numpy arrays (host
+    arguments (freq_factors, q_gamma, k_gamma, gate) may be numpy arrays (host
     calls) or device pointers / tensors (device calls)."""
     d = dict(n_tok=1, pos0=0, n_seq=None, n_head=1, n_kv=1, head_dim=64, n_rot=None, rope_mode=ROPE_NEOX,
              freq_base=10000.0, rope_scale=1.0, freq_factors=None, q_gamma=None, k_gamma=None, v_rmsnorm=0,
-             eps=1e-6, scale=None, softcap=0.0, causal=1, window=0, reuse_kv=0)
+             eps=1e-6, scale=None, softcap=0.0, causal=1, window=0, reuse_kv=0, gate=None)
     d.update(kw)
     if d["n_seq"] is None:
         d["n_seq"] = d["pos0"] + d["n_tok"]
@@ -250,7 +251,7 @@ def params(**kw) -> AttnParams:
     p = AttnParams()
     keep = {}
     for k, v in d.items():
-        if k in ("freq_factors", "q_gamma", "k_gamma"):
+        if k in ("freq_factors", "q_gamma", "k_gamma", "gate"):
             if isinstance(v, np.ndarray):
                 v = np.ascontiguousarray(v, np.float32)
                 keep[k] = v

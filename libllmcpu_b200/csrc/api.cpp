@@ -845,6 +845,7 @@ void fill_devjob(nncu_kv* kv, const nncu_attn_job& j, DevJob& d)
 	d.q_gamma = p.q_gamma;
 	d.k_gamma = p.k_gamma;
 	d.freq_factors = p.freq_factors;
+	d.gate = p.gate;
 	d.K = static_cast<char*>(b.k) + (size_t)j.seq * b.seq_bytes;
 	d.V = static_cast<char*>(b.v) + (size_t)j.seq * b.seq_bytes;
 	d.head_bytes = (long long)b.rows_alloc * p.head_dim * es;
@@ -1230,7 +1231,9 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 	if (!kv || !jobs || n_jobs <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "no jobs");
 	// Stage every input in one pinned block, copy it up in one transfer, run,
 	// and bring every output back in one transfer.
-	std::vector<size_t> in_off(n_jobs * 6), out_off(n_jobs);
+	// per job: q, k, v, the q and k gains, the frequency factors, the gate
+	constexpr int NIN = 7;
+	std::vector<size_t> in_off(n_jobs * NIN), out_off(n_jobs);
 	size_t in_bytes = 0, out_bytes = 0;
 	for (int i = 0; i < n_jobs; ++i)
 	{
@@ -1240,11 +1243,12 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 		if (!jobs[i].q || !jobs[i].out || (!p.reuse_kv && (!jobs[i].k || !jobs[i].v)))
 			return fail(NNCU_ERR_INVALID_ARGUMENT, "job %d: NULL input or output", i);
 		const size_t qn = (size_t)p.n_tok * p.n_head * p.head_dim, kn = (size_t)p.n_tok * p.n_kv * p.head_dim;
-		const size_t sizes[6] = {qn, p.reuse_kv ? 0 : kn, p.reuse_kv ? 0 : kn, p.q_gamma ? (size_t)p.head_dim : 0,
-		                         p.k_gamma ? (size_t)p.head_dim : 0, p.freq_factors ? (size_t)p.n_rot / 2 : 0};
-		for (int s = 0; s < 6; ++s)
+		const size_t sizes[NIN] = {qn, p.reuse_kv ? 0 : kn, p.reuse_kv ? 0 : kn, p.q_gamma ? (size_t)p.head_dim : 0,
+		                           p.k_gamma ? (size_t)p.head_dim : 0, p.freq_factors ? (size_t)p.n_rot / 2 : 0,
+		                           p.gate ? qn : 0};
+		for (int s = 0; s < NIN; ++s)
 		{
-			in_off[i * 6 + s] = in_bytes;
+			in_off[i * NIN + s] = in_bytes;
 			in_bytes += fbytes(sizes[s]);
 		}
 		out_off[i] = out_bytes;
@@ -1268,14 +1272,15 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 	{
 		const nncu_attn_params& p = jobs[i].p;
 		const size_t qn = (size_t)p.n_tok * p.n_head * p.head_dim, kn = (size_t)p.n_tok * p.n_kv * p.head_dim;
-		const float* srcs[6] = {jobs[i].q, jobs[i].k, jobs[i].v, p.q_gamma, p.k_gamma, p.freq_factors};
-		const size_t sizes[6] = {qn, p.reuse_kv ? 0 : kn, p.reuse_kv ? 0 : kn, p.q_gamma ? (size_t)p.head_dim : 0,
-		                         p.k_gamma ? (size_t)p.head_dim : 0, p.freq_factors ? (size_t)p.n_rot / 2 : 0};
-		const float* dptr[6];
-		for (int s = 0; s < 6; ++s)
+		const float* srcs[NIN] = {jobs[i].q, jobs[i].k, jobs[i].v, p.q_gamma, p.k_gamma, p.freq_factors, p.gate};
+		const size_t sizes[NIN] = {qn, p.reuse_kv ? 0 : kn, p.reuse_kv ? 0 : kn, p.q_gamma ? (size_t)p.head_dim : 0,
+		                           p.k_gamma ? (size_t)p.head_dim : 0, p.freq_factors ? (size_t)p.n_rot / 2 : 0,
+		                           p.gate ? qn : 0};
+		const float* dptr[NIN];
+		for (int s = 0; s < NIN; ++s)
 		{
-			dptr[s] = sizes[s] ? reinterpret_cast<const float*>(ds + in_off[i * 6 + s]) : nullptr;
-			if (sizes[s]) std::memcpy(hs + in_off[i * 6 + s], srcs[s], sizes[s] * sizeof(float));
+			dptr[s] = sizes[s] ? reinterpret_cast<const float*>(ds + in_off[i * NIN + s]) : nullptr;
+			if (sizes[s]) std::memcpy(hs + in_off[i * NIN + s], srcs[s], sizes[s] * sizeof(float));
 		}
 		dj[i].q = dptr[0];
 		dj[i].k = dptr[1];
@@ -1283,6 +1288,7 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 		dj[i].p.q_gamma = dptr[3];
 		dj[i].p.k_gamma = dptr[4];
 		dj[i].p.freq_factors = dptr[5];
+		dj[i].p.gate = dptr[6];
 		dj[i].out = reinterpret_cast<float*>(ds + out_base + out_off[i]);
 	}
 	kv->jobs_tmp.resize(n_jobs);

@@ -371,6 +371,19 @@ __device__ __forceinline__ float ex2(float x)
 	return y;
 }
 
+// Qwen3.5's output gate (model.cpp:1759-1760, nnc_mul_sigmoid_f32): an
+// attention output element times sigmoid(g), as y / (1 + exp(-g)).
+__device__ __forceinline__ float gated(float y, const float* gate, size_t i)
+{
+	return gate ? y / (1.0f + expf(-gate[i])) : y;
+}
+__device__ __forceinline__ float4 gated4(float4 y, const float* gate, size_t i)
+{
+	if (!gate) return y;
+	return make_float4(y.x / (1.0f + expf(-gate[i])), y.y / (1.0f + expf(-gate[i + 1])),
+	                   y.z / (1.0f + expf(-gate[i + 2])), y.w / (1.0f + expf(-gate[i + 3])));
+}
+
 // The keys [first, last] the query at `pos` sees (model.cpp:2300-2316).
 __device__ __forceinline__ void span_of(int causal, int window, int pos, int n_seq, int& first, int& last)
 {

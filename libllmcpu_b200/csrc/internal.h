@@ -74,6 +74,7 @@ struct alignas(16) DevJob
 	const void* tmap_k;
 	const void* tmap_v;
 	int plane0;
+	const float* gate;    // [n_tok][n_head*D] or null: the output times sigmoid(gate) (Qwen3.5)
 };
 static_assert(sizeof(DevJob) % 16 == 0, "DevJob is bulk-copied");
 
@@ -163,6 +164,7 @@ struct PrefillPlan
 	int n_tok, pos0, n_seq, n_head, n_kv, window, q_tiles;
 	float scale, log2e, softcap;
 	float* out; // [n_tok][n_head * 128]
+	const float* gate; // like out, or null
 	int* err;   // device error word
 };
 bool prefill_supported(int D, int kv_type);

@@ -334,6 +334,7 @@ __device__ __forceinline__ void decode_body(const DecodePlan& P, const unsigned 
 	struct PieceEnd
 	{
 		float* out;
+		const float* gate;
 		int n_head, G, h, rg, n_tok, seg, n_pieces, part, chunk, out_row0;
 	} pe;
 
@@ -420,6 +421,7 @@ __device__ __forceinline__ void decode_body(const DecodePlan& P, const unsigned 
 		else
 			first_v = 0, last_v = -1; // a padding row sees nothing
 		pe.out = J.out;
+		pe.gate = J.gate;
 		pe.n_head = J.n_head;
 		pe.G = G;
 		pe.h = h;
@@ -589,10 +591,12 @@ __device__ __forceinline__ void decode_body(const DecodePlan& P, const unsigned 
 		const int rows_valid = G * n_tok - rg * RM;
 		// where row R of this segment goes: the output (t, head) row, and, split,
 		// the segment's partial slot in GPU g's receive block of this rank
-		auto out_row = [&](float* base_out, int R) -> float* {
+		// the offset of row R of this segment in the job's output (and gate)
+		auto row_off = [&](int R) -> size_t {
 			const int gr = rg * RM + R;
-			return base_out + ((size_t)(gr / G) * n_head + (size_t)h * G + gr % G) * D;
+			return ((size_t)(gr / G) * n_head + (size_t)h * G + gr % G) * D;
 		};
+		auto out_row = [&](float* base_out, int R) -> float* { return base_out + row_off(R); };
 		auto recv_row = [&](int g, int rank, int R) {
 			return P.recv[g] + (size_t)rank * P.recv_stride + ((size_t)seg * RM + R) * PW;
 		};
@@ -629,7 +633,7 @@ __device__ __forceinline__ void decode_body(const DecodePlan& P, const unsigned 
 			}
 			if (single && !split)
 			{
-				if (R < rows_valid) out_row(pe.out, R)[d] = L > 0.0f ? acc / L : 0.0f;
+				if (R < rows_valid) out_row(pe.out, R)[d] = gated(L > 0.0f ? acc / L : 0.0f, pe.gate, row_off(R) + d);
 			}
 			else if (single)
 			{
@@ -679,7 +683,8 @@ __device__ __forceinline__ void decode_body(const DecodePlan& P, const unsigned 
 						                    acc.y *= inv;
 						                    acc.z *= inv;
 						                    acc.w *= inv;
-						                    *reinterpret_cast<float4*>(out_row(pe.out, R) + d) = acc;
+						                    *reinterpret_cast<float4*>(out_row(pe.out, R) + d) =
+							                    gated4(acc, pe.gate, row_off(R) + d);
 					                    });
 				else
 					merge_pieces<D, RM>(base, (size_t)RM * PW, n_pieces, rows_valid, ctid, NW * 32,
@@ -954,7 +959,8 @@ __global__ void split_merge_kernel(const DecodePlan P)
 			L = fmaf(__ldcg(pr + D + 1), c, L);
 		}
 		const int gr = rg * RM + R;
-		out[((size_t)(gr / G) * J.n_head + (size_t)h * G + gr % G) * D + d] = acc * (L > 0.0f ? 1.0f / L : 0.0f);
+		const size_t oi = ((size_t)(gr / G) * J.n_head + (size_t)h * G + gr % G) * D + d;
+		out[oi] = gated(acc * (L > 0.0f ? 1.0f / L : 0.0f), J.gate, oi);
 	}
 	__syncthreads();
 	if (threadIdx.x == 0) atomicExch(P.arrive[P.rank] + seg, 0); // ready for this parity's next call

@@ -735,6 +735,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			const int key_first = (J.tile_lo + tis0) * T;
 			// what the end of the piece needs from the slot
 			float* out = J.out;
+			const float* gate = J.gate;
 			const int n_head = J.n_head, n_tok = J.n_tok, seg = J.seg0 + seg_local, n_pieces = J.n_chunks;
 			const int part_slot = J.part0 + seg_local * J.n_chunks + tis0 / J.chunk;
 			const int part_first = J.part0 + seg_local * J.n_chunks;
@@ -947,10 +948,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 					M[r] = mx == -CUDART_INF_F ? -CUDART_INF_F : mx - P_SHIFT;
 				}
 				const int rows_valid = G * n_tok - rg * NR;
-				auto out_row = [&](int R) -> float* {
+				auto row_off = [&](int R) -> size_t {
 					const int gr = rg * NR + R;
-					return out + ((size_t)(gr / G) * n_head + (size_t)h * G + gr % G) * D;
+					return ((size_t)(gr / G) * n_head + (size_t)h * G + gr % G) * D;
 				};
+				auto out_row = [&](int R) -> float* { return out + row_off(R); };
 				if (n_pieces == 1)
 				{
 #pragma unroll
@@ -958,7 +960,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 						if (dx[mb] >= 0)
 #pragma unroll
 							for (int r = 0; r < NR; ++r)
-								if (r < rows_valid) out_row(r)[dx[mb]] = L[r] > 0.0f ? o[mb][r] / L[r] : 0.0f;
+								if (r < rows_valid)
+									out_row(r)[dx[mb]] = gated(L[r] > 0.0f ? o[mb][r] / L[r] : 0.0f, gate, row_off(r) + dx[mb]);
 				}
 				else
 				{
@@ -992,7 +995,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 							                    acc.y *= inv;
 							                    acc.z *= inv;
 							                    acc.w *= inv;
-							                    *reinterpret_cast<float4*>(out_row(R) + d) = acc;
+							                    *reinterpret_cast<float4*>(out_row(R) + d) = gated4(acc, gate, row_off(R) + d);
 						                    });
 						if (ctid == 0) P.counters[seg] = 0; // ready for the next launch
 					}

@@ -352,11 +352,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			tmem_wait_ld();
 			if (q0 + r < P.n_tok)
 			{
-				float* orow = P.out + ((size_t)(q0 + r) * P.n_head + h) * PF_D + col0;
+				const size_t orow0 = ((size_t)(q0 + r) * P.n_head + h) * PF_D + col0;
+				float* orow = P.out + orow0;
 #pragma unroll
 				for (int i = 0; i < 32; i += 4)
 					*reinterpret_cast<float4*>(orow + i) =
-						make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+						gated4(make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv), P.gate, orow0 + i);
 			}
 		}
 	}
@@ -572,6 +573,7 @@ int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream)
 	P.log2e = 1.4426950408889634f;
 	P.softcap = j.softcap;
 	P.out = j.out;
+	P.gate = j.gate;
 	P.err = err;
 	prefill_kernel<<<(unsigned)(P.q_tiles * j.n_head), PF_THREADS, PF_SMEM, st>>>(qmap, kmap, vmap, P);
 	return (int)cudaGetLastError();

@@ -165,6 +165,7 @@ extern "C" int nncu_attention_noalloc(const nncu_attn_params* p, const float* q,
 	j.q_gamma = p->q_gamma;
 	j.k_gamma = p->k_gamma;
 	j.freq_factors = p->freq_factors;
+	j.gate = p->gate;
 	j.rope_inv = reinterpret_cast<const float*>(scratch + off_rope);
 	j.K = static_cast<char*>(k_cache);
 	j.V = static_cast<char*>(v_cache);

@@ -367,5 +367,10 @@ int orc_attention_forward(const orc_attn_params* p, float* q, float* k, float* v
 			}
 		}
 	}
-	return orc_attend(p, q, Kc, Vc, kv_type, rows, out);
+	const int rc = orc_attend(p, q, Kc, Vc, kv_type, rows, out);
+	/* Qwen3.5 scales each head's output by its gate (model.cpp:1759-1760):
+	 * y /= 1 + exp(-g), the scalar form of nnc_mul_sigmoid_f32 (nn_ops.cpp:1731-1742) */
+	if (rc == 0 && p->gate)
+		for (size_t i = 0; i < (size_t)p->n_tok * q_dim; ++i) out[i] /= 1.0f + expf(-p->gate[i]);
+	return rc;
 }

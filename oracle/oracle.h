@@ -73,6 +73,7 @@ typedef struct orc_attn_params
 	int32_t v_rmsnorm;              /* Gemma 4: plain RMSNorm of V rows */
 	float eps, scale, softcap;
 	int32_t causal, window, reuse_kv;
+	const float* gate;              /* [n_tok][n_head*head_dim] or NULL: Qwen3.5 output gate */
 } orc_attn_params;
 
 /* q [n_tok][n_head*head_dim], k/v [n_tok][n_kv*head_dim] are modified in

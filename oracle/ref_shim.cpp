@@ -264,7 +264,10 @@ int ref_attention_forward(const orc_attn_params* p, float* q, float* k, float* v
 				std::memcpy(static_cast<float*>(Vc) + row, vt, kv_dim * sizeof(float));
 			}
 		}
-	return ref_attend(p, q, Kc, Vc, kv_type, rows, out);
+	const int rc = ref_attend(p, q, Kc, Vc, kv_type, rows, out);
+	// Qwen3.5's gate, the reference's own kernel (model.cpp:1759-1760)
+	if (rc == 0 && p->gate) nnc_mul_sigmoid_f32(out, p->gate, static_cast<size_t>(p->n_tok) * q_dim);
+	return rc;
 }
 
 } // extern "C"

@@ -5,7 +5,8 @@ call gets (q, k, v projections of n_tok new tokens, Q/K norm gains) and the
 cache contents it attends over (the K/V rows of the positions before pos0).
 Inputs come from the reference tests' generator -- std::mt19937(seed) through
 std::normal_distribution<float> -- drawn per sequence, per layer, in this
-order: q, k, v, q_gamma, k_gamma, then the past K rows, then the past V rows.
+order: q, k, v, q_gamma, k_gamma, then the past K rows, then the past V rows,
+then (Qwen3.5 layers only) the output gate.
 Past keys are optionally rotated at their own positions first, as the
 reference's own append would have left them.
 
@@ -38,6 +39,7 @@ class LayerSpec:
     v_rmsnorm: bool = False
     scale: float | None = None
     kv_layer: int | None = None  # another layer whose cache this one reads (None: its own)
+    gated: bool = False          # Qwen3.5: the output multiplied by sigmoid(gate)
 
 
 @dc.dataclass
@@ -50,6 +52,7 @@ class LayerInputs:
     past_k: np.ndarray         # [n_keep, n_kv*D] fp32 values of positions keep0 .. pos0-1
     past_v: np.ndarray
     keep0: int                 # first past position still held by the buffer
+    gate: np.ndarray | None = None  # [n_tok, n_head*D] (Qwen3.5), drawn last
 
 
 @dc.dataclass
@@ -78,7 +81,7 @@ class Case:
                  v_rmsnorm=int(L.v_rmsnorm), eps=1e-6,
                  scale=L.scale if L.scale is not None else 1.0 / float(np.sqrt(L.head_dim)),
                  softcap=L.softcap, causal=int(self.causal), window=L.window,
-                 reuse_kv=int(L.kv_layer is not None and L.kv_layer != layer))
+                 reuse_kv=int(L.kv_layer is not None and L.kv_layer != layer), gate=inp.gate)
         if not self.causal:
             d["n_seq"] = self.n_ctx
         return d
@@ -141,7 +144,9 @@ def build_case(seed: int, layers: list[LayerSpec], n_ctx: int, n_tok: int, pos0,
                 for t in range(n_keep):
                     pk[t] = rope(pk[t], L.n_kv, D, n_rot, float(keep0 + t) * L.rope_scale, L.freq_base,
                                  L.rope_mode, L.freq_factors)
-            per.append(LayerInputs(q, k, v, qg, kg, pk, pv, keep0))
+            # the gate comes after everything else, so ungated cases draw what they always drew
+            gate = rng.normal(n_tok * L.n_head * D, 0.0, 2.0).reshape(n_tok, L.n_head * D) if L.gated else None
+            per.append(LayerInputs(q, k, v, qg, kg, pk, pv, keep0, gate))
         inputs.append(per)
     return Case(layers, n_ctx, n_batch, n_tok, pos0, kv_type, causal, inputs, rows)
 

@@ -56,6 +56,12 @@ def all_cases() -> dict:
     c["bidirectional_f32"] = S.build_case(
         6, [LayerSpec(4, 2, 64, window=64, qk_norm=True), LayerSpec(4, 2, 64, window=0, qk_norm=True)],
         n_ctx=96, n_tok=96, pos0=0, kv_type=O.KV_F32, causal=False)
+    # Qwen3.5's gated attention: the output times sigmoid(gate), per element
+    # (model.cpp:1759-1760); partial rotation (64 of 256), Q/K norm, theta 1e7,
+    # a 3-token verify block
+    c["qwen35_gated_bf16"] = S.build_case(
+        8, [LayerSpec(8, 2, 256, freq_base=1e7, n_rot=64, qk_norm=True, gated=True)], n_ctx=900, n_tok=3,
+        pos0=800, kv_type=O.KV_BF16)
     # a layer reading the cache an earlier layer appended to (Gemma 3n / 4 shared K/V)
     c["reuse_kv_bf16"] = S.build_case(
         7, [LayerSpec(8, 2, 128, freq_base=1e6), LayerSpec(8, 2, 128, freq_base=1e6, kv_layer=0)],
@@ -67,7 +73,7 @@ def inputs_digest(case) -> str:
     h = hashlib.sha256()
     for per in case.inputs:
         for inp in per:
-            for a in (inp.q, inp.k, inp.v, inp.q_gamma, inp.k_gamma, inp.past_k, inp.past_v):
+            for a in (inp.q, inp.k, inp.v, inp.q_gamma, inp.k_gamma, inp.past_k, inp.past_v, inp.gate):
                 if a is not None:
                     h.update(np.ascontiguousarray(a, np.float32).tobytes())
     return h.hexdigest()

@@ -89,6 +89,15 @@ def test_cfg4_verify_f16_full_context(nncu):
     check_case(nncu, case, per_layer=True)
 
 
+def test_gate_cuda_cores_f32(nncu):
+    # the output gate in the CUDA-core kernel's direct write and in its merge of pieces
+    L = [LayerSpec(4, 1, 256, freq_base=1e6, qk_norm=True, gated=True)]
+    case = S.build_case(1500, L, n_ctx=6000, n_tok=1, pos0=5000, kv_type=O.KV_F32, n_batch=1)
+    check_case(nncu, case)
+    case = S.build_case(1501, L, n_ctx=300, n_tok=1, pos0=200, kv_type=O.KV_F32, n_batch=1)
+    check_case(nncu, case)
+
+
 def test_cfg5_long_f16_reduced(nncu):
     case = S.build_case(4, [LayerSpec(32, 8, 64, freq_base=5e5, rope_mode=O.ROPE_NORM)], n_ctx=16384 + 16,
                         n_tok=1, pos0=16384, kv_type=O.KV_F16)

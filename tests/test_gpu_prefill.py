@@ -78,3 +78,11 @@ def test_prefill_window_softcap_norm_rope(nncu):
     case = S.build_case(31, L, n_ctx=700, n_tok=500, pos0=0, kv_type=O.KV_BF16, n_batch=512)
     assert case.rows[0] >= 700  # not a ring: the tensor-core path takes it
     check_prefill(nncu, case)
+
+
+def test_prefill_qwen35_gate(nncu):
+    # the output gate applied in the tensor-core prefill's output write
+    L = [LayerSpec(8, 2, 128, freq_base=1e7, n_rot=64, qk_norm=True, gated=True)]
+    case = S.build_case(33, L, n_ctx=384, n_tok=384, pos0=0, kv_type=O.KV_BF16)
+    check_prefill(nncu, case)
+

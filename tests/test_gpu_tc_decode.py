@@ -69,3 +69,14 @@ def test_tc_long_chunks(nncu):
     case = S.build_case(1300, [LayerSpec(32, 8, 64, freq_base=5e5, rope_mode=O.ROPE_NORM)], n_ctx=40000, n_tok=1,
                         pos0=39990, kv_type=O.KV_F16)
     both_kernels(nncu, case)
+
+
+@pytest.mark.parametrize("kv_type", [O.KV_F16, O.KV_BF16])
+def test_tc_qwen35_gate(nncu, kv_type):
+    # Qwen3.5's output gate (model.cpp:1759-1760) on both kernels: a verify
+    # block, partial rotation, Q/K norm
+    L = [LayerSpec(8, 2, 256, freq_base=1e7, n_rot=64, qk_norm=True, gated=True),
+         LayerSpec(8, 2, 256, window=300, freq_base=1e7, n_rot=64, qk_norm=True, gated=True)]
+    case = S.build_case(1400, L, n_ctx=2200, n_tok=2, pos0=[2100, 700], kv_type=kv_type)
+    both_kernels(nncu, case)
+
