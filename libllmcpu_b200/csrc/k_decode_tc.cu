@@ -19,30 +19,33 @@
 // and V are exact in their own type). The weights are formed as
 // 2^8 exp2(s - m) so that their low halves stay in the normal range.
 //
-// Roles (8 warps):
+// Roles (12 warps):
 //  * warp 0 streams the K tiles with TMA (128-byte-swizzled 64-column
 //    panels, a tensor map over the cache buffer [planes][rows][head_dim])
 //    and fills the q slot (job descriptor, raw q rows, gains, RoPE tables)
 //    of each piece; warp 2 streams the V tiles; each into its own ring;
-//  * warp 1 owns the TMEM allocation and, from one lane, issues the MMAs:
-//    S for tile i + 1 into one of two TMEM buffers, then O for tile i into
-//    one of two others, so the next tile's scores are computed while this
-//    tile's softmax runs;
-//  * warps 4-7 (TMEM lanes 0-127) normalise and rotate the q rows, write the
-//    Q operand, and per tile: read S, scale, soft-cap, mask by each row's
-//    span, take the row maxima across the tile (warp shuffles, then shared
-//    memory), write P, and fold the previous tile's O into registers with
-//    the running maximum's correction (online softmax in base 2). At a
-//    piece's end the row sums meet the same way and the piece gives the
-//    output, or a partial (o, m, l) merged in order by the segment's last
-//    piece (decode.cuh), as in k_decode.cu.
+//  * warp 1 owns the TMEM allocation and, from one lane, issues the MMAs,
+//    polling for whichever is ready first: the next S (into one of four TMEM
+//    buffers, up to three tiles ahead of the softmax) or the next O (into
+//    one of two);
 //  * warp 3 appends the new tokens' K/V rows when their raw rows fit the q
 //    slot (decode and short verify): the piece holding them normalises,
 //    rotates and narrows them, stores them to the cache (first row group),
 //    and writes them into the K and V stages of the tiles that hold them once
 //    those have landed, before the MMAs read the stages. Longer batches have
 //    K1 (k_prep.cu) append first; this kernel is then its programmatic
-//    dependent and waits for it only before the tiles that hold the new rows.
+//    dependent and waits for it only before the tiles that hold the new rows;
+//  * warps 4-7 and 8-11 are two softmax groups (each reaching TMEM lanes
+//    0-127): together they normalise and rotate the q rows and write the Q
+//    operand; then group g takes the tiles i with i % 2 == g, keeping its own
+//    online softmax state: read S, scale, soft-cap, mask by each row's span,
+//    take the row maxima across the tile (warp shuffles, then the group's
+//    warps through shared memory), fold the group's previous O into
+//    registers with the running maximum's correction (base 2), write P. At a
+//    piece's end group 1 hands its (m, l, o) to group 0 through TMEM and
+//    shared memory; group 0 merges them and writes the output, or a partial
+//    (o, m, l) merged in order by the segment's last piece (decode.cuh), as
+//    in k_decode.cu.
 // Every wait is bounded; a timed-out wait records an error and the CTA steps
 // through without waiting further.
 #include <cuda.h>
