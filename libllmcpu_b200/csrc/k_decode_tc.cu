@@ -434,6 +434,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			constexpr uint32_t ID_PV = tc_idesc(C::MP, N, BF, true, false);
 			const uint32_t kb0 = smem_u32(smem + C::OFF_K), vb0 = smem_u32(smem + C::OFF_V);
 			const uint32_t qa = smem_u32(smem + C::OFF_Q), pa0 = smem_u32(smem + C::OFF_P);
+			// descriptors of the rings' first stages, of Q and of the first P
+			// buffer (shared memory stays below 256 KB, so adding an offset to the
+			// 14-bit start-address field never carries out of it)
+			const uint64_t adesc_k0 = sdesc(kb0, 16, 1024), adesc_v0 = sdesc(vb0, C::PANEL, 1024);
+			const uint64_t bdesc_q = sdesc(qa, 16, 1024), bdesc_p0 = sdesc(pa0, 16, 1024);
 			bool ok = true;
 			int patch_lo = -1, patch_hi = -2, kp = 0, vp = 0; // the piece's patched tiles; patches seen
 			// whether tile j's K (or V) is in its stage: landed, or patched by the append warp
@@ -450,14 +455,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				const int s = j % STAGES, b = j % C::NSB;
 				if (j >= patch_lo && j <= patch_hi) ++kp;
 				tc_fence_after();
-				const uint32_t ka = kb0 + s * TC_TILE;
 				const uint32_t ts = tmem + b * C::S_COLS;
+				// the descriptors of the stage and of Q once; each MMA adds its
+				// offset (in 16-byte units) to the start-address field
+				const uint64_t ad = adesc_k0 + (uint64_t)((s * TC_TILE) >> 4);
 #pragma unroll
 				for (int qb = 0; qb < C::NQB; ++qb)
 #pragma unroll
 					for (int kk = 0; kk < D / 16; ++kk)
-						mma_f16(ts + qb * N, sdesc(ka + (kk >> 2) * C::PANEL + qb * C::MQ * 128 + (kk & 3) * 32, 16, 1024),
-						        sdesc(qa + (kk >> 2) * C::QPANEL + (kk & 3) * 32, 16, 1024), ID_QK, kk > 0 ? 1u : 0u);
+						mma_f16(ts + qb * N, ad + (uint64_t)(((kk >> 2) * C::PANEL + qb * C::MQ * 128 + (kk & 3) * 32) >> 4),
+						        bdesc_q + (uint64_t)(((kk >> 2) * C::QPANEL + (kk & 3) * 32) >> 4), ID_QK, kk > 0 ? 1u : 0u);
 				mma_commit(&s_full[b]);
 				mma_commit(&k_empty[s]);
 			};
@@ -466,14 +473,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				const int s = j % STAGES, b = j & 1;
 				if (j >= patch_lo && j <= patch_hi) ++vp;
 				tc_fence_after();
-				const uint32_t va = vb0 + s * TC_TILE, pa = pa0 + b * C::PBYTES;
 				const uint32_t to = tmem + C::O_BASE + b * C::O_COLS;
+				const uint64_t ad = adesc_v0 + (uint64_t)((s * TC_TILE) >> 4);
+				const uint64_t bd = bdesc_p0 + (uint64_t)((b * C::PBYTES) >> 4);
 #pragma unroll
 				for (int mb = 0; mb < C::NPB; ++mb)
 #pragma unroll
 					for (int kk = 0; kk < T / 16; ++kk)
-						mma_f16(to + mb * N, sdesc(va + mb * 2 * C::PANEL + kk * 2048, C::PANEL, 1024),
-						        sdesc(pa + (kk >> 2) * C::PPANEL + (kk & 3) * 32, 16, 1024), ID_PV, kk > 0 ? 1u : 0u);
+						mma_f16(to + mb * N, ad + (uint64_t)((mb * 2 * C::PANEL + kk * 2048) >> 4),
+						        bd + (uint64_t)(((kk >> 2) * C::PPANEL + (kk & 3) * 32) >> 4), ID_PV, kk > 0 ? 1u : 0u);
 				mma_commit(&o_full[b]);
 				mma_commit(&v_empty[s]);
 			};
