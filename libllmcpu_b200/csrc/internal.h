@@ -161,7 +161,7 @@ int tc_make_maps(void* kmap, void* vmap, const void* k, const void* v, int kv_ty
 // One causal prefill on the tensor cores (k_prefill.cu): bf16 cache, head_dim 128.
 struct PrefillPlan
 {
-	int n_tok, pos0, n_seq, n_head, n_kv, window, q_tiles;
+	int n_tok, pos0, n_seq, n_head, n_kv, window, q_pairs; // q_pairs: CTAs per head (256 query rows each)
 	float scale, log2e, softcap;
 	float* out; // [n_tok][n_head * 128]
 	const float* gate; // like out, or null

@@ -4,23 +4,34 @@
 // nnc_attn_block / nnc_attn_merge / nnc_attn_finish, model.cpp:1251-1319,
 // nn_ops.cpp:351-499): every query row of a long batch attends over its
 // causal span. Here, for bf16 caches and head_dim 128, the two products run
-// on the 5th-generation tensor cores: one CTA takes 128 query rows of one
-// query head and walks the key tiles of its span, 128 keys at a time:
+// on the 5th-generation tensor cores. One CTA takes 256 query rows of one
+// query head as two Q tiles, A and B, of 128 rows, and walks the key tiles of
+// their spans, 128 keys at a time; each key tile is loaded once for both:
 //
-//   S = Q K^T      tcgen05.mma, M 128 x N 128 x K 128, bf16 in, fp32 in TMEM
-//   P = softmax    4 warps, one query row per thread, read from TMEM
-//   O += P V       tcgen05.mma, P (bf16) from shared memory, O in TMEM
+//   S = Q K^T      tcgen05.mma, M 128 x N 128 x K head_dim, 16-bit in, fp32 in TMEM
+//   P = softmax    one warpgroup per Q tile, one query row per thread (TMEM lane)
+//   O += P V       tcgen05.mma, P (16-bit) from TMEM over its own S, V from
+//                  shared memory, O in TMEM
 //
-// Roles: warps 0 and 2 issue the TMA loads (Q once and the K tiles; the V
-// tiles), each into its own 2-stage ring, K free again as soon as its S is
-// done; warp 1 owns the TMEM allocation and, from one lane, issues the MMAs
-// (S into two TMEM buffers in turn, so the next tile's S is computed while
-// this tile's softmax runs); warps 4 on do the softmax, PF_NH threads per
-// query row (the row maximum exchanged through shared memory),
-// keep O in scale and write the output. Online softmax in base 2 with a
-// lazily moved maximum: a row's reference maximum moves (and O and l are
-// rescaled) only when a new score exceeds it by more than 2^8, so O is rarely
-// touched; the result is the same softmax, divided by the same l.
+// Roles: warp 0 issues the TMA loads of the two Q tiles and of the K tiles,
+// warp 2 those of the V tiles, each into its own 2-stage ring; warp 1 owns
+// the TMEM allocation (S_A, S_B, O_A, O_B: 512 columns at head_dim 128) and,
+// from one lane, issues the MMAs in the order PV_A(t), S_A(t+1), PV_B(t),
+// S_B(t+1), so that the softmax of one Q tile runs while the tensor core
+// works on the other's products; warps 4-7 and 8-11 do the softmax of A and
+// of B: a thread reads its row of S from TMEM, masks it by the row's span,
+// writes its probabilities back as 16-bit pairs over the first 64 columns of
+// the same S (the A operand of P V; the next S into those columns is issued
+// after that P V, and tcgen05.mma operations of one thread execute in
+// order), keeps O in scale and writes the output row. Online softmax in base
+// 2 with a lazily moved maximum: a row's reference maximum moves (and O and
+// l are rescaled) only when a new score exceeds it by more than 2^8, so O is
+// rarely touched; the result is the same softmax, divided by the same l.
+// After a row's first keys, a tile's exponentials are taken against the
+// row's held maximum while the tile's own maximum is found on the way (no
+// separate pass over the scores); a row whose scores passed the held maximum
+// by more than 2^8 moves it and writes its P again. The first warpgroup
+// hands registers to the two softmax warpgroups (setmaxnreg).
 //
 // Operands in shared memory use the 128-byte swizzled K-major layout TMA
 // writes (8-row atoms of 1 KB), described to tcgen05.mma by shared memory
@@ -41,64 +52,146 @@ namespace nncu
 namespace
 {
 
-constexpr int PF_BM = 128;                      // query rows per CTA
-constexpr int PF_BN = 128;                      // keys per tile
-constexpr int PF_D = 128;                       // head_dim
-constexpr int PF_NH = 4;                        // softmax threads per query row (32 columns each)
-constexpr int PF_CW = PF_BN / PF_NH;            // columns per softmax thread
-constexpr int PF_THREADS = 128 + 128 * PF_NH;   // warps 0-3: TMA, MMA; then the softmax warps
-constexpr int PANEL = 128 * 128;                // 128 rows x 64 bf16: one 128-byte-swizzled panel
-constexpr int TILE = 2 * PANEL;                 // 128 rows x 128 bf16
-constexpr int SM_Q = 0;                         // Q tile
-constexpr int SM_K = SM_Q + TILE;               // [2] K tiles
-constexpr int SM_V = SM_K + 2 * TILE;           // [2] V tiles
-constexpr int SM_P = SM_V + 2 * TILE;           // P tile
-constexpr int SM_RED = SM_P + TILE;             // [2 tiles][PF_NH parts][128 rows] row maxima, then [PF_NH][128] row sums
-constexpr int SM_BAR = SM_RED + 3 * PF_NH * 128 * 4; // barriers, TMEM address
-constexpr int PF_SMEM = SM_BAR + 256 + 1024;    // + alignment slack
-constexpr int TMEM_COLS = 512;                  // S0, S1, O (128 columns each)
-constexpr float LAZY = 8.0f;                    // log2 headroom before the row maximum moves
+constexpr int PF_BM = 128;          // query rows per Q tile; a CTA takes two (A, B)
+constexpr int PF_BN = 128;          // keys per tile
+constexpr int PF_D = 128;           // head_dim of the prep kernel's rows
+constexpr int PF_THREADS = 384;     // warps 0-3: loads, MMA; 4-7: softmax of A; 8-11: softmax of B
+constexpr float LAZY = 8.0f;        // log2 headroom before a row's reference maximum moves
 
-// tcgen05 instruction descriptors for the prefill: bf16 A and B, fp32
-// accumulate, M = 128, N = 128; A K-major; B K-major (Q K^T) or MN-major (P V).
-constexpr uint32_t idesc(bool b_mn_major) { return tc_idesc(128, 128, true, false, b_mn_major); }
-
-} // namespace
-
-namespace
+// Shared memory and TMEM of the prefill for head_dim D (64 or 128).
+template <int D>
+struct PfLayout
 {
+	static constexpr int PANEL = 128 * 128;       // 128 rows x 64 16-bit elements, 128-byte swizzled
+	static constexpr int TILE = (D / 64) * PANEL; // 128 rows x D
+	static constexpr int SM_Q = 0;                // [2] Q tiles
+	static constexpr int SM_K = SM_Q + 2 * TILE;  // [2] K stages
+	static constexpr int SM_V = SM_K + 2 * TILE;  // [2] V stages
+	static constexpr int SM_BAR = SM_V + 2 * TILE;
+	static constexpr int SMEM = SM_BAR + 256 + 1024; // + alignment slack
+	// TMEM columns: S of tile X at 128 X (its P, 16-bit pairs, in the first
+	// 64 of them), O of tile X at 256 + D X
+	static constexpr uint32_t T_S = 0, T_O = 256, COLS = 512;
+};
 
+// Eight tcgen05.mma of one product in one asm block (one predicate set-up,
+// the descriptors advanced inside), so the issuing thread spends about two
+// instructions per MMA.
+// S = Q K^T over head_dim 128: A and B K-major; K step k advances both
+// descriptors by (k >> 2) panels + (k & 3) x 32 bytes (16-byte units).
+template <uint32_t PANEL16>
+__device__ __forceinline__ void mma8_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t id)
+{
+	asm volatile(
+		"{\n\t.reg .pred p0, p1;\n\t.reg .b64 a, b;\n\t"
+		"setp.ne.b32 p0, 0, 0;\n\tsetp.eq.b32 p1, 0, 0;\n\t"
+		"tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p0;\n\t"
+		"add.s64 a, %1, 2;\n\tadd.s64 b, %2, 2;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
+		"add.s64 a, %1, 4;\n\tadd.s64 b, %2, 4;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
+		"add.s64 a, %1, 6;\n\tadd.s64 b, %2, 6;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
+		"add.s64 a, %1, %4;\n\tadd.s64 b, %2, %4;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
+		"add.s64 a, %1, %5;\n\tadd.s64 b, %2, %5;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
+		"add.s64 a, %1, %6;\n\tadd.s64 b, %2, %6;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
+		"add.s64 a, %1, %7;\n\tadd.s64 b, %2, %7;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t}"
+		::"r"(d), "l"(a), "l"(b), "r"(id), "n"(PANEL16), "n"(PANEL16 + 2), "n"(PANEL16 + 4), "n"(PANEL16 + 6)
+		: "memory");
+}
+
+// O (+)= P V over a 128-key tile: A = P from TMEM (8 columns per K step of
+// 16 keys), B = V MN-major (2048 bytes per K step); `acc` = 0 starts O afresh.
+__device__ __forceinline__ void mma8_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc)
+{
+	asm volatile(
+		"{\n\t.reg .pred p0, p1;\n\t.reg .b64 b;\n\t.reg .b32 a;\n\t"
+		"setp.ne.b32 p0, %4, 0;\n\tsetp.eq.b32 p1, 0, 0;\n\t"
+		"tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p0;\n\t"
+		"add.s32 a, %1, 8;\n\tadd.s64 b, %2, 128;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
+		"add.s32 a, %1, 16;\n\tadd.s64 b, %2, 256;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
+		"add.s32 a, %1, 24;\n\tadd.s64 b, %2, 384;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
+		"add.s32 a, %1, 32;\n\tadd.s64 b, %2, 512;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
+		"add.s32 a, %1, 40;\n\tadd.s64 b, %2, 640;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
+		"add.s32 a, %1, 48;\n\tadd.s64 b, %2, 768;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
+		"add.s32 a, %1, 56;\n\tadd.s64 b, %2, 896;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t}"
+		::"r"(d), "r"(a), "l"(b), "r"(id), "r"(acc)
+		: "memory");
+}
+
+// 16 consecutive 32-bit columns into this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* v)
+{
+	asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+	             "%12, %13, %14, %15, %16};" ::"r"(taddr),
+	             "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+	             "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+	             : "memory");
+}
+
+// Two non-negative floats to bf16, packed (lo in the low half), rounded to
+// nearest with ties away from zero (an exact tie needs the low 16 bits to be
+// 0x8000: a bias below 2^-16 of an ulp), on the integer pipe: bf16 keeps the
+// exponent, so this is the float's top half after the carry.
+__device__ __forceinline__ uint32_t pack_p_bf16(float lo, float hi)
+{
+	const uint32_t a = __float_as_uint(lo) + 0x8000u, b = __float_as_uint(hi) + 0x8000u;
+	uint32_t r;
+	asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(r) : "r"(a), "r"(b));
+	return r;
+}
+__device__ __forceinline__ uint32_t pack_p_f16(float lo, float hi)
+{
+	__half2 h = __floats2half2_rn(lo, hi);
+	return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int D, bool BF16>
 __global__ void __launch_bounds__(PF_THREADS, 1)
 	prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const PrefillPlan P)
 {
+	static_assert(D == 128, "the MMA blocks walk head_dim 128 in eight K steps");
+	using L = PfLayout<D>;
 	extern __shared__ unsigned char smem_raw[];
 	unsigned char* smem =
 		reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-	uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
+	uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::SM_BAR);
 	uint64_t* q_full = bars + 0;
 	uint64_t* k_full = bars + 1;   // [2]
-	uint64_t* k_empty = bars + 3;  // [2]: K_j no longer needed once S_j is done
+	uint64_t* k_empty = bars + 3;  // [2]: a K stage is free once the S of both Q tiles are done
 	uint64_t* v_full = bars + 5;   // [2]
-	uint64_t* v_empty = bars + 7;  // [2]: V_j no longer needed once P_j V_j is done
-	uint64_t* s_full = bars + 9;   // [2]
-	uint64_t* s_empty = bars + 11; // [2]
-	uint64_t* p_full = bars + 13;
-	uint64_t* pv_done = bars + 14;
-	uint64_t* mma_done = bars + 16;
-	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
-	volatile int* flags = reinterpret_cast<volatile int*>(bars + 18); // [0] abort
+	uint64_t* v_empty = bars + 7;  // [2]: a V stage is free once both P V are done
+	uint64_t* s_full = bars + 9;   // [2 Q tiles]
+	uint64_t* p_full = bars + 11;  // [2 Q tiles]: P in TMEM (and O rescaled)
+	uint64_t* o_done = bars + 13;  // [2 Q tiles]: the tile's last P V has completed
+	uint64_t* mma_done = bars + 15; // every MMA issued has completed
+	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+	volatile int* flags = reinterpret_cast<volatile int*>(bars + 17); // [0] abort
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-	// the heaviest query tiles (the longest causal spans) go first
+	// the heaviest pairs of query tiles (the longest causal spans) go first;
+	// neighbouring CTAs are the query heads of one KV head (its K, V in L2)
 	const int h = blockIdx.x % P.n_head;
-	const int qt = P.q_tiles - 1 - blockIdx.x / P.n_head;
-	const int q0 = qt * PF_BM;
-	const int qlo = P.pos0 + q0, qhi = P.pos0 + min(P.n_tok, q0 + PF_BM) - 1;
-	const int klo = (P.window > 0 && qlo + 1 > P.window) ? qlo + 1 - P.window : 0;
-	const int khi = min(qhi, P.n_seq - 1);
-	const int j_lo = klo / PF_BN, n_tiles = khi / PF_BN - j_lo + 1;
+	const int q0 = (P.q_pairs - 1 - (int)blockIdx.x / P.n_head) * (2 * PF_BM);
 	const int hk = h / (P.n_head / P.n_kv);
+	// each Q tile's key tiles [lo, hi] (the union of its rows' spans); a tile
+	// past the batch is absent (lo > hi)
+	int lo[2], hi[2];
+#pragma unroll
+	for (int X = 0; X < 2; ++X)
+	{
+		const int r0 = q0 + X * PF_BM;
+		lo[X] = 1;
+		hi[X] = 0;
+		if (r0 < P.n_tok)
+		{
+			const int qlo = P.pos0 + r0, qhi = P.pos0 + min(P.n_tok, r0 + PF_BM) - 1;
+			const int klo = (P.window > 0 && qlo + 1 > P.window) ? qlo + 1 - P.window : 0;
+			lo[X] = klo / PF_BN;
+			hi[X] = min(qhi, P.n_seq - 1) / PF_BN;
+		}
+	}
+	// the tiles streamed: from A's first to the last of either (contiguous:
+	// B's first row directly follows A's last)
+	const int u_lo = lo[0], n_u = max(hi[0], hi[1]) - u_lo + 1;
 
 	if (threadIdx.x == 0)
 	{
@@ -110,254 +203,304 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			mbar_init(&v_full[s], 1);
 			mbar_init(&v_empty[s], 1);
 			mbar_init(&s_full[s], 1);
-			mbar_init(&s_empty[s], 128 * PF_NH);
+			mbar_init(&p_full[s], 128);
+			mbar_init(&o_done[s], 1);
 		}
-		mbar_init(p_full, 128 * PF_NH);
-		mbar_init(pv_done, 1);
 		mbar_init(mma_done, 1);
 		flags[0] = 0;
 		fence_barrier_init();
 	}
-	if (warp == 1)
-	{
-		asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-		             "r"(TMEM_COLS)
-		             : "memory");
-		asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-	}
+	if (warp == 1) tmem_alloc(tmem_slot, L::COLS);
 	tc_fence_before();
 	__syncthreads();
 	tc_fence_after();
 	const uint32_t tmem = *tmem_slot;
-	const uint32_t TS[2] = {tmem, tmem + 128};
-	const uint32_t TO = tmem + 256;
 
-	if (warp == 0 || warp == 2)
+	// registers from the load and MMA warps to the softmax warpgroups: the
+	// launch gives every thread 168 (384 x 168 = 64,512); after this the
+	// first warpgroup holds 96 and the two softmax warpgroups 200 each
+	// (128 x 96 + 256 x 200 = 63,488, within the launch's), so a softmax
+	// thread keeps its row of 128 scores and the exponentials' inputs in
+	// registers
+	if (warp < 4)
 	{
-		// ---- TMA: warp 0 Q once, then the K tiles; warp 2 the V tiles; each
-		// through its own 2-stage ring (K is free again as soon as S is done) ----
-		if (lane == 0)
+		asm volatile("setmaxnreg.dec.sync.aligned.u32 96;" ::: "memory");
+		if (warp == 0 || warp == 2)
 		{
-			const bool is_k = warp == 0;
-			const CUtensorMap* map = is_k ? &kmap : &vmap;
-			uint64_t* full = is_k ? k_full : v_full;
-			uint64_t* empty = is_k ? k_empty : v_empty;
-			unsigned char* ring = smem + (is_k ? SM_K : SM_V);
-			if (is_k)
+			// ---- TMA: warp 0 the Q tiles once, then the K tiles; warp 2 the V
+			// tiles; each through its own 2-stage ring ----
+			if (lane == 0)
 			{
-				mbar_arrive_expect_tx(q_full, TILE);
-				tma3(smem + SM_Q, &qmap, 0, q0, h, q_full);
-				tma3(smem + SM_Q + PANEL, &qmap, 64, q0, h, q_full);
-			}
-			int issued = 0;
-			for (int jj = 0; jj < n_tiles; ++jj)
-			{
-				const int s = jj & 1;
-				if (jj >= 2 &&
-				    !mbar_wait_bounded(&empty[s], (uint32_t)(((jj >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
+				const bool is_k = warp == 0;
+				const CUtensorMap* map = is_k ? &kmap : &vmap;
+				uint64_t* full = is_k ? k_full : v_full;
+				uint64_t* empty = is_k ? k_empty : v_empty;
+				unsigned char* ring = smem + (is_k ? L::SM_K : L::SM_V);
+				if (is_k)
 				{
-					flags[0] = 1;
-					break;
+					const int nq = lo[1] <= hi[1] ? 2 : 1;
+					mbar_arrive_expect_tx(q_full, nq * L::TILE);
+					for (int X = 0; X < nq; ++X)
+						for (int p = 0; p < D / 64; ++p)
+							tma3(smem + L::SM_Q + X * L::TILE + p * L::PANEL, &qmap, 64 * p, q0 + X * PF_BM, h, q_full);
 				}
-				if (flags[0]) break;
-				unsigned char* t = ring + s * TILE;
-				const int key0 = (j_lo + jj) * PF_BN;
-				mbar_arrive_expect_tx(&full[s], TILE);
-				tma3(t, map, 0, key0, hk, &full[s]);
-				tma3(t + PANEL, map, 64, key0, hk, &full[s]);
-				issued = jj + 1;
+				int issued = 0;
+				for (int u = 0; u < n_u; ++u)
+				{
+					const int s = u & 1;
+					if (u >= 2 &&
+					    !mbar_wait_bounded(&empty[s], (uint32_t)(((u >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
+					{
+						flags[0] = 1;
+						break;
+					}
+					if (flags[0]) break;
+					unsigned char* t = ring + s * L::TILE;
+					const int key0 = (u_lo + u) * PF_BN;
+					mbar_arrive_expect_tx(&full[s], L::TILE);
+					for (int p = 0; p < D / 64; ++p) tma3(t + p * L::PANEL, map, 64 * p, key0, hk, &full[s]);
+					issued = u + 1;
+				}
+				// on an abort, do not leave while a copy may still land here
+				if (is_k) mbar_wait_bounded(q_full, 0, nullptr, 0);
+				for (int u = max(0, issued - 2); u < issued; ++u)
+					mbar_wait_bounded(&full[u & 1], (uint32_t)((u >> 1) & 1), nullptr, 0);
 			}
-			// on an abort, do not leave while a copy may still land here
-			if (is_k) mbar_wait_bounded(q_full, 0, nullptr, 0);
-			for (int jj = max(0, issued - 2); jj < issued; ++jj)
-				mbar_wait_bounded(&full[jj & 1], (uint32_t)((jj >> 1) & 1), nullptr, 0);
+			__syncwarp(); // the whole warp meets the final barrier together
 		}
-		__syncwarp(); // the whole warp meets the final barrier together
-	}
-	else if (warp == 1)
-	{
-		// ---- MMA issue: S_j = Q K_j^T into S[j % 2], then O += P_{j-1} V_{j-1} ----
-		if (lane == 0)
+		else if (warp == 1)
 		{
-			constexpr uint32_t ID_QK = idesc(false), ID_PV = idesc(true);
-			const uint32_t qa = smem_u32(smem + SM_Q), pa0 = smem_u32(smem + SM_P);
-			bool ok = mbar_wait_bounded(q_full, 0, P.err, DEVERR_WAIT_FULL);
-			auto issue_pv = [&](int jj) -> bool {
-				if (!mbar_wait_bounded(p_full, (uint32_t)(jj & 1), P.err, DEVERR_WAIT_FULL) ||
-				    !mbar_wait_bounded(&v_full[jj & 1], (uint32_t)((jj >> 1) & 1), P.err, DEVERR_WAIT_FULL))
-					return false;
-				tc_fence_after();
-				const uint32_t va = smem_u32(smem + SM_V + (jj & 1) * TILE);
-				const uint32_t pa = pa0;
-#pragma unroll
-				for (int k = 0; k < PF_BN / 16; ++k)
-					mma_f16(TO, sdesc(pa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024), sdesc(va + k * 2048, PANEL, 1024),
-					        ID_PV, (jj > 0 || k > 0) ? 1u : 0u);
-				mma_commit(pv_done);
-				mma_commit(&v_empty[jj & 1]);
-				return true;
-			};
-			int jj = 0;
-			for (; ok && jj < n_tiles; ++jj)
+			// ---- MMA issue, in the order PV_A(t), S_A(t+1), PV_B(t), S_B(t+1):
+			// each Q tile's softmax of tile t+1 overlaps the other tile's MMAs ----
+			if (lane == 0)
 			{
-				const int s = jj & 1;
-				ok = !flags[0] && mbar_wait_bounded(&k_full[s], (uint32_t)((jj >> 1) & 1), P.err, DEVERR_WAIT_FULL);
-				if (ok && jj >= 2)
-					ok = mbar_wait_bounded(&s_empty[s], (uint32_t)(((jj >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY);
-				if (!ok) break;
-				tc_fence_after();
-				const uint32_t ka = smem_u32(smem + SM_K + s * TILE);
-#pragma unroll
-				for (int k = 0; k < PF_D / 16; ++k)
-					mma_f16(TS[s], sdesc(qa + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024),
-					        sdesc(ka + (k >> 2) * PANEL + (k & 3) * 32, 16, 1024), ID_QK, k > 0 ? 1u : 0u);
-				mma_commit(&s_full[s]);
-				mma_commit(&k_empty[s]);
-				if (jj >= 1) ok = issue_pv(jj - 1);
+				constexpr uint32_t ID_QK = tc_idesc(128, 128, BF16, false, false);
+				constexpr uint32_t ID_PV = tc_idesc(128, D, BF16, false, true);
+				// the operands' shared memory descriptors, formed once: a Q tile,
+				// a K or V stage and a K step are constant offsets (16-byte units)
+				// from these
+				constexpr uint64_t TILE16 = L::TILE >> 4, PANEL16 = L::PANEL >> 4;
+				const uint64_t dq = sdesc(smem_u32(smem + L::SM_Q), 16, 1024);
+				const uint64_t dk = sdesc(smem_u32(smem + L::SM_K), 16, 1024);
+				const uint64_t dv = sdesc(smem_u32(smem + L::SM_V), L::PANEL, 1024);
+				auto has = [&](int X, int t) { return X ? (t >= lo[1] && t <= hi[1]) : (t >= lo[0] && t <= hi[0]); };
+				auto issue_s = [&](int X, int u) {
+					mma8_ss<(uint32_t)PANEL16>(tmem + L::T_S + 128 * X, dq + (uint64_t)X * TILE16,
+					                           dk + (uint64_t)(u & 1) * TILE16, ID_QK);
+					mma_commit(&s_full[X]);
+				};
+				int np[2] = {0, 0}; // P consumed per Q tile (the phase of p_full)
+				bool ok = mbar_wait_bounded(q_full, 0, P.err, DEVERR_WAIT_FULL);
+				if (ok) ok = !flags[0] && mbar_wait_bounded(&k_full[0], 0, P.err, DEVERR_WAIT_FULL);
+				if (ok)
+				{
+					tc_fence_after();
+					for (int X = 0; X < 2; ++X)
+						if (has(X, u_lo)) issue_s(X, 0);
+					mma_commit(&k_empty[0]);
+				}
+				for (int u = 0; ok && u < n_u; ++u)
+				{
+					const int t = u_lo + u, s = u & 1;
+					ok = !flags[0] && mbar_wait_bounded(&v_full[s], (uint32_t)((u >> 1) & 1), P.err, DEVERR_WAIT_FULL);
+					const bool next = u + 1 < n_u;
+					bool k_ready = false;
+					for (int X = 0; ok && X < 2; ++X)
+					{
+						if (has(X, t))
+						{
+							ok = !flags[0] &&
+							     mbar_wait_bounded(&p_full[X], (uint32_t)(np[X] & 1), P.err, DEVERR_WAIT_FULL);
+							if (!ok) break;
+							tc_fence_after();
+							mma8_ts(tmem + L::T_O + D * X, tmem + L::T_S + 128 * X, dv + (uint64_t)s * TILE16, ID_PV,
+							        np[X] > 0 ? 1u : 0u);
+							++np[X];
+							if (t == (X ? hi[1] : hi[0])) mma_commit(&o_done[X]);
+						}
+						if (next && has(X, t + 1))
+						{
+							if (!k_ready)
+							{
+								ok = !flags[0] && mbar_wait_bounded(&k_full[(u + 1) & 1],
+								                                    (uint32_t)(((u + 1) >> 1) & 1), P.err,
+								                                    DEVERR_WAIT_FULL);
+								if (!ok) break;
+								tc_fence_after();
+								k_ready = true;
+							}
+							issue_s(X, u + 1);
+						}
+					}
+					if (!ok) break;
+					mma_commit(&v_empty[s]);
+					if (next)
+					{
+						if (!k_ready) // (every streamed tile belongs to a Q tile; kept for the ring's phases)
+							ok = mbar_wait_bounded(&k_full[(u + 1) & 1], (uint32_t)(((u + 1) >> 1) & 1), P.err,
+							                       DEVERR_WAIT_FULL);
+						mma_commit(&k_empty[(u + 1) & 1]);
+					}
+				}
+				if (!ok) flags[0] = 1;
+				// every MMA issued has completed before TMEM is freed
+				mma_commit(mma_done);
+				mbar_wait_bounded(mma_done, 0, nullptr, 0);
 			}
-			if (ok && n_tiles > 0) ok = issue_pv(n_tiles - 1);
-			if (!ok) flags[0] = 1;
-			// every MMA issued has completed before TMEM is freed
-			mma_commit(mma_done);
-			mbar_wait_bounded(mma_done, 0, nullptr, 0);
+			__syncwarp(); // the whole warp meets the final barrier together
 		}
-		__syncwarp(); // the whole warp meets the final barrier together
 	}
-	else if (warp >= 4)
+	else
 	{
-		// ---- softmax, O in scale, output: PF_NH threads per query row (warp
-		// 4 + 4 part + lane group takes columns [32 part, 32 part + 32); a warp
-		// reaches TMEM lanes 32 (warp % 4) .. +31), the row maximum shared
-		// through shared memory by the warps on the same lanes ----
-		const int wq = warp & 3;
-		const int hf = (warp >> 2) - 1; // column part
+		asm volatile("setmaxnreg.inc.sync.aligned.u32 200;" ::: "memory");
+		// ---- softmax of Q tile X, one query row per thread (TMEM lane r),
+		// O kept in scale, then the output ----
+		const int X = (warp - 4) >> 2, wq = warp & 3;
 		const int r = wq * 32 + lane;
 		const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-		const uint32_t col0 = (uint32_t)(hf * PF_CW);
-		const int qp = P.pos0 + q0 + r;
+		const uint32_t ts = tmem + L::T_S + 128 * X + lane_off, to = tmem + L::T_O + D * X + lane_off;
+		const int row = q0 + X * PF_BM + r;
+		const int qp = P.pos0 + row;
 		const int kf = (P.window > 0 && qp + 1 > P.window) ? qp + 1 - P.window : 0;
 		const int kl = min(qp, P.n_seq - 1);
-		float* red = reinterpret_cast<float*>(smem + SM_RED); // maxima [2][PF_NH][128], then sums [PF_NH][128]
 		float m_used = -CUDART_INF_F, l = 0.0f;
 		bool ok = true;
-		// this thread's 32 columns: 4 chunks of 8 in its row of panel hf / 2
-		unsigned char* prow = smem + SM_P + (hf >> 1) * PANEL + r * 128;
-		for (int jj = 0; jj < n_tiles; ++jj)
+		int n = 0;
+		const int t_lo = X ? lo[1] : lo[0], t_hi = X ? hi[1] : hi[0];
+		for (int t = t_lo; t <= t_hi; ++t, ++n)
 		{
-			const int s = jj & 1;
-			if (ok) ok = !flags[0] && mbar_wait_bounded(&s_full[s], (uint32_t)((jj >> 1) & 1), P.err, DEVERR_WAIT_FULL);
-			ok = __all_sync(0xffffffffu, ok); // (the warps on these lanes leave together, at the barrier below)
+			ok = ok && !flags[0] && mbar_wait_bounded(&s_full[X], (uint32_t)(n & 1), P.err, DEVERR_WAIT_FULL);
+			if (!__all_sync(0xffffffffu, ok))
+			{
+				ok = false;
+				break;
+			}
 			tc_fence_after();
-			float x[PF_CW];
-			tmem_ld32(TS[s] + lane_off + col0, x);
+			float x[PF_BN];
+#pragma unroll
+			for (int c = 0; c < PF_BN; c += 32) tmem_ld32(ts + c, x + c);
 			tmem_wait_ld();
-			tc_fence_before();
-			mbar_arrive(&s_empty[s]);
-			const int key0 = (j_lo + jj) * PF_BN + hf * PF_CW;
 			// scores in log2 units: sl * s, folded into the exponentials' FMA
 			// (sl > 0 keeps the maximum's place); with a soft-cap, capped first
-			// in their own loop (a select would evaluate tanh for every score)
 			float sl = P.scale * P.log2e;
 			if (P.softcap > 0.0f)
 			{
 				const float cs = P.scale / P.softcap, cl = P.softcap * P.log2e;
 #pragma unroll
-				for (int c = 0; c < PF_CW; ++c) x[c] = tanhf(x[c] * cs) * cl;
+				for (int c = 0; c < PF_BN; ++c) x[c] = tanhf(x[c] * cs) * cl;
 				sl = 1.0f;
 			}
-			if (key0 < kf || key0 + PF_CW - 1 > kl)
+			const int key0 = t * PF_BN;
+			if (key0 < kf || key0 + PF_BN - 1 > kl)
 			{
 #pragma unroll
-				for (int c = 0; c < PF_CW; ++c)
+				for (int c = 0; c < PF_BN; ++c)
 					if (key0 + c < kf || key0 + c > kl) x[c] = -CUDART_INF_F;
 			}
-			float mq[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F}; // four chains
+			// P into the first 64 columns of S as 16-bit pairs (S is in
+			// registers), p = 2^(x sl + nm); with `track`, the largest exponent
+			// x sl + nm is returned
+			float ls[4];
+			auto write_p = [&](float nm, bool track) -> float {
+				float mq[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
 #pragma unroll
-			for (int c = 0; c < PF_CW; ++c) mq[c & 3] = fmaxf(mq[c & 3], x[c]);
-			float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl;
-			float* mxs = red + s * PF_NH * 128;
-			mxs[hf * 128 + r] = mx;
-			// the warps on these TMEM lanes; a timed-out wait in any of them ends
-			// the loop for all of them
-			if (named_sync_or(2 + wq, 32 * PF_NH, !ok))
-			{
-				ok = false;
-				break;
-			}
+				for (int i = 0; i < 4; ++i) ls[i] = 0.0f;
 #pragma unroll
-			for (int o = 1; o < PF_NH; ++o) mx = fmaxf(mx, mxs[((hf + o) % PF_NH) * 128 + r]);
+				for (int c0 = 0; c0 < PF_BN; c0 += 32)
+				{
+					uint32_t pk[16];
+#pragma unroll
+					for (int c = 0; c < 32; c += 2)
+					{
+						const float e0 = fmaf(x[c0 + c], sl, nm), e1 = fmaf(x[c0 + c + 1], sl, nm);
+						if (track)
+						{
+							mq[(c >> 1) & 3] = fmaxf(mq[(c >> 1) & 3], e0);
+							mq[(c >> 1) & 3] = fmaxf(mq[(c >> 1) & 3], e1);
+						}
+						const float p0 = ex2(e0), p1 = ex2(e1); // masked (-inf): 0
+						ls[(c >> 1) & 3] += p0 + p1;
+						pk[c >> 1] = BF16 ? pack_p_bf16(p0, p1) : pack_p_f16(p0, p1);
+					}
+					tmem_st16u(ts + c0 / 2, pk);
+				}
+				return fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+			};
 			// the row's reference maximum moves only when a score exceeds it by
 			// more than 2^LAZY; then O (in TMEM) and l are rescaled
-			const bool move = mx > m_used + LAZY;
-			const float m_new = move ? mx : m_used;
-			const float alpha = (move && m_used != -CUDART_INF_F) ? ex2(m_used - m_new) : 1.0f;
-			const bool rescale = move && m_used != -CUDART_INF_F;
-			const float m_ref = m_new == -CUDART_INF_F ? 0.0f : m_new; // a row with no key yet: all p are 0
-			// the weights and their bf16 pairs, in registers first, then into the
-			// P tile once the previous P V has read it
-			uint32_t pk[PF_CW / 2];
-			float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-			const float nm = -m_ref;
+			float m_new = m_used;
+			bool rescale = false;
+			if (__any_sync(0xffffffffu, m_used == -CUDART_INF_F))
+			{
+				// a row without a reference maximum yet (its first keys): the
+				// tile's maximum first, then the exponentials
+				float mq[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
 #pragma unroll
-			for (int c = 0; c < PF_CW; c += 2)
-			{
-				const float p0 = ex2(fmaf(x[c], sl, nm)), p1 = ex2(fmaf(x[c + 1], sl, nm)); // masked (-inf): 0
-				ls[(c >> 1) & 3] += p0 + p1;
-				__nv_bfloat162 b2 = __floats2bfloat162_rn(p0, p1);
-				pk[c >> 1] = *reinterpret_cast<uint32_t*>(&b2);
+				for (int c = 0; c < PF_BN; ++c) mq[c & 3] = fmaxf(mq[c & 3], x[c]);
+				const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl;
+				const bool move = mx > m_used + LAZY;
+				rescale = move && m_used != -CUDART_INF_F;
+				m_new = move ? mx : m_used;
+				write_p(m_new == -CUDART_INF_F ? 0.0f : -m_new, false); // no key yet: every p is 0
 			}
-			if (jj > 0)
+			else
 			{
-				ok = mbar_wait_bounded(pv_done, (uint32_t)((jj - 1) & 1), P.err, DEVERR_WAIT_FULL);
-				ok = __all_sync(0xffffffffu, ok); // (a failure ends the loop at the next barrier)
-				tc_fence_after();
-				if (ok && __any_sync(0xffffffffu, rescale))
+				// the usual tile: the exponentials against the held maximum, the
+				// tile's own maximum found on the way (no separate pass over the
+				// scores); a row whose scores passed the held maximum by more
+				// than 2^LAZY moves it and writes its P again (rare after a row's
+				// first tiles)
+				const float top = write_p(-m_used, true);
+				const bool move = top > LAZY;
+				if (__any_sync(0xffffffffu, move))
+				{
+					rescale = move;
+					m_new = move ? m_used + top : m_used;
+					write_p(-m_new, false);
+				}
+			}
+			const float alpha = rescale ? ex2(m_used - m_new) : 1.0f;
+			// O holds every P V before this tile's (their S came first)
+			if (__any_sync(0xffffffffu, rescale))
+			{
+#pragma unroll
+				for (int c = 0; c < D; c += 32)
 				{
 					float o[32];
-					tmem_ld32(TO + lane_off + col0, o);
+					tmem_ld32(to + c, o);
 					tmem_wait_ld();
 #pragma unroll
 					for (int i = 0; i < 32; ++i) o[i] *= alpha;
-					tmem_st32(TO + lane_off + col0, o);
-					tmem_wait_st();
+					tmem_st32(to + c, o);
 				}
 			}
-#pragma unroll
-			for (int c4 = 0; c4 < PF_CW / 8; ++c4)
-			{
-				const int chunk = ((hf & 1) * (PF_CW / 8) + c4) ^ (r & 7);
-				*reinterpret_cast<uint4*>(prow + chunk * 16) =
-					make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]);
-			}
+			tmem_wait_st();
 			l = fmaf(l, alpha, (ls[0] + ls[1]) + (ls[2] + ls[3]));
 			m_used = m_new;
-			asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 			tc_fence_before();
-			mbar_arrive(p_full);
+			mbar_arrive(&p_full[X]);
 		}
-		// the output: O / l, once the last P V is done (l: the parts' sums)
-		if (ok && n_tiles > 0) ok = mbar_wait_bounded(pv_done, (uint32_t)((n_tiles - 1) & 1), P.err, DEVERR_WAIT_FULL);
-		ok = __all_sync(0xffffffffu, ok);
-		float* sums = red + 2 * PF_NH * 128;
-		sums[hf * 128 + r] = l;
-		named_sync(2 + wq, 32 * PF_NH);
-#pragma unroll
-		for (int o = 1; o < PF_NH; ++o) l += sums[((hf + o) % PF_NH) * 128 + r];
-		if (ok)
+		// the output: O / l once the tile's last P V is done
+		if (ok && n > 0) ok = !flags[0] && mbar_wait_bounded(&o_done[X], 0, P.err, DEVERR_WAIT_FULL);
+		if (__all_sync(0xffffffffu, ok) && n > 0)
 		{
 			tc_fence_after();
 			const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-			float o[32];
-			tmem_ld32(TO + lane_off + col0, o);
-			tmem_wait_ld();
-			if (q0 + r < P.n_tok)
-			{
-				const size_t orow0 = ((size_t)(q0 + r) * P.n_head + h) * PF_D + col0;
-				float* orow = P.out + orow0;
+			const size_t orow0 = ((size_t)row * P.n_head + h) * D;
 #pragma unroll
-				for (int i = 0; i < 32; i += 4)
-					*reinterpret_cast<float4*>(orow + i) =
-						gated4(make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv), P.gate, orow0 + i);
+			for (int c = 0; c < D; c += 32)
+			{
+				float o[32];
+				tmem_ld32(to + c, o);
+				tmem_wait_ld();
+				if (row < P.n_tok)
+				{
+					float* orow = P.out + orow0 + c;
+#pragma unroll
+					for (int i = 0; i < 32; i += 4)
+						*reinterpret_cast<float4*>(orow + i) = gated4(
+							make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv), P.gate, orow0 + c + i);
+				}
 			}
 		}
 	}
@@ -366,7 +509,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 	if (warp == 1)
 	{
 		tc_fence_after();
-		asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+		tmem_dealloc(tmem, L::COLS);
 	}
 }
 
@@ -555,9 +698,11 @@ int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream)
 	int dev = 0;
 	cudaGetDevice(&dev);
 	if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
+	auto kernel = prefill_kernel<PF_D, true>;
+	constexpr int smem = PfLayout<PF_D>::SMEM;
 	if (!configured[dev])
 	{
-		ce = cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
+		ce = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 		if (ce != cudaSuccess) return (int)ce;
 		configured[dev] = true;
 	}
@@ -568,14 +713,14 @@ int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream)
 	P.n_head = j.n_head;
 	P.n_kv = j.n_kv;
 	P.window = j.window;
-	P.q_tiles = (j.n_tok + PF_BM - 1) / PF_BM;
+	P.q_pairs = (j.n_tok + 2 * PF_BM - 1) / (2 * PF_BM);
 	P.scale = j.scale;
 	P.log2e = 1.4426950408889634f;
 	P.softcap = j.softcap;
 	P.out = j.out;
 	P.gate = j.gate;
 	P.err = err;
-	prefill_kernel<<<(unsigned)(P.q_tiles * j.n_head), PF_THREADS, PF_SMEM, st>>>(qmap, kmap, vmap, P);
+	kernel<<<(unsigned)(P.q_pairs * j.n_head), PF_THREADS, smem, st>>>(qmap, kmap, vmap, P);
 	return (int)cudaGetLastError();
 }
 
