@@ -491,11 +491,20 @@ def run_product(args, w: Workload, rank: int, world: int, local_rank: int):
     return line
 
 
+def _placed(carve, x):
+    """x copied into a fresh view of the arena that `carve` cuts."""
+    v = carve(x.size).reshape(x.shape)
+    v[...] = x
+    return v
+
+
 def run_e2e(args, w: Workload, N, kv, layers, share: Share, host, grp, stream, dist, dev):
-    """The same steps through the host-pointer path: nncu_attention_batch
-    (host fp32 inputs, copied up and the outputs down inside the call), or, for
-    a split, pinned host inputs copied up, the split call, and the merged
-    output copied down. Wall clock of the synchronous steps, max over ranks."""
+    """The same steps through the host-pointer path: nncu_attention_batch with
+    host fp32 buffers (views of one arena the caller registered once with
+    nncu_host_register: the call gathers the inputs up and scatters the outputs
+    down through the GPU's mapping of that memory), or, for a split, pinned
+    host inputs copied up, the split call, and the merged output copied down.
+    Wall clock of the synchronous steps, max over ranks."""
     import torch
 
     nsq, nl = len(share.seqs), len(layers)
@@ -504,22 +513,41 @@ def run_e2e(args, w: Workload, N, kv, layers, share: Share, host, grp, stream, d
     rows_out = sum(w.n_tok * L.n_head for L in layers) * nsq
     d2h = rows_out * layers[0].D * 4
     if grp is None:
+        # every host buffer a view of one arena, 16-byte aligned (registration
+        # pins whole pages, so small buffers share one registered range)
+        sizes = [x.size for d in host for x in d.values()]
+        sizes += [w.n_tok * L.n_head * L.D for _ in range(nsq) for L in layers]
+        arena = np.zeros(sum((n + 3) // 4 * 4 for n in sizes) + 4, np.float32)
+        off = (-arena.ctypes.data // 4) % 4
+
+        def carve(n):
+            nonlocal off
+            v = arena[off:off + n]
+            off += (n + 3) // 4 * 4
+            return v
+
+        host = [{k: _placed(carve, x) for k, x in d.items()} for d in host]
         per_layer, outs = [], []
         for li, L in enumerate(layers):
             jobs = []
             for s in range(nsq):
                 d = host[s * nl + li]
-                out = np.empty((w.n_tok, L.n_head * L.D), np.float32)
+                out = carve(w.n_tok * L.n_head * L.D).reshape(w.n_tok, L.n_head * L.D)
                 p = params_for(N, w, L, d["qg"], d["kg"])
                 jobs.append(N.job(li, p, d["q"], d["k"], d["v"], out, seq=s))
                 outs.append(out)
             # the job table a caller keeps; its host buffers change per step
             per_layer.append((N.AttnJob * len(jobs))(*jobs))
+        # the caller's host buffers live as long as its session: pinned once
+        # (nncu_host_register), so each call reads its inputs and writes its
+        # outputs through the GPU's mapping of that memory
+        N.host_register(arena)
 
         def one():
             for arr in per_layer:  # layer by layer: each call returns with its outputs in host memory
                 kv.attention_batch(arr)
-        api = "nncu_attention_batch (host pointers), one synchronous call per layer"
+        api = ("nncu_attention_batch (host pointers, one arena registered once with nncu_host_register), "
+               "one synchronous call per layer")
     else:
         pinned, devs, jobs = [], [], []
         for s in range(nsq):
@@ -562,6 +590,8 @@ def run_e2e(args, w: Workload, N, kv, layers, share: Share, host, grp, stream, d
         te = torch.tensor([t], device=dev)
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
         t = float(te.item())
+    if grp is None:
+        N.host_unregister(arena)
     return {"unit": w.unit, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "ms_per_step": round(1e3 * t / args.steps, 4), "api": api, "seconds_per_step": t / args.steps}
 

@@ -242,6 +242,22 @@ typedef struct nncu_attn_job
 } nncu_attn_job;
 
 int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs);
+
+/* Pin [p, p + bytes) of the caller's host memory for the host-pointer calls
+ * (cudaHostRegister, mapped and portable). A call of nncu_attention /
+ * nncu_attention_batch whose every host buffer (q, k, v, the gains, the
+ * frequency factors, the gate and out) lies inside registered ranges, with
+ * 128 KiB or more moved in all, has one kernel read its inputs through the
+ * GPU's mapping of that memory and another write its outputs back, instead
+ * of copying them through the library's pinned staging block on the host
+ * (the host copies of a verify step of a batch take longer than its kernels).
+ * No counterpart in libnnc, which holds its activations in ordinary host
+ * memory; the drop-in would register the session's scratch buffers, which
+ * live as long as the session. Ranges may not overlap (registration pins
+ * whole pages: keep small buffers inside one registered arena); unregister a
+ * range (by its start) before its memory is freed. */
+int nncu_host_register(void* p, size_t bytes);
+int nncu_host_unregister(void* p);
 int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs, void* stream);
 
 /* One layer's decode / verify attention that allocates nothing: the same

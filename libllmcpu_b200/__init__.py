@@ -29,7 +29,7 @@ import os
 import numpy as np
 
 __all__ = [
-    "NnncError", "lib", "LIB_PATH", "KV_BF16", "KV_F32", "KV_F16", "ROPE_NEOX", "ROPE_NORM",
+    "NnncError", "lib", "LIB_PATH", "host_register", "host_unregister", "KV_BF16", "KV_F32", "KV_F16", "ROPE_NEOX", "ROPE_NORM",
     "ATTN_BLOCK", "AttnParams", "AttnJob", "LayerDesc", "KVCache", "kv_plan", "job", "attn_span", "params",
     "attn_block_dev", "attn_merge_dev", "attn_finish_dev", "rmsnorm_gamma_multi_dev", "rmsnorm_dev",
     "rope_dev", "softcap_dev", "EXPORTS",
@@ -55,7 +55,7 @@ EXPORTS = [
     "nncu_perf_read", "nncu_perf_report", "nncu_launch_count", "nncu_attention_noalloc", "nncu_group_create",
     "nncu_group_handle", "nncu_group_open", "nncu_group_output", "nncu_group_copy_output", "nncu_group_free",
     "nncu_attention_split_dev", "nncu_group_set_timeout", "nncu_group_reset", "nncu_group_inject_drop",
-    "nncu_noalloc_check", "nncu_kv_set_tensor_cores",
+    "nncu_noalloc_check", "nncu_kv_set_tensor_cores", "nncu_host_register", "nncu_host_unregister",
 ]
 GROUP_HANDLE_BYTES = 64
 
@@ -141,6 +141,18 @@ def launch_count() -> int:
     return int(lib().nncu_launch_count())
 
 
+def host_register(arr) -> None:
+    """Pin a host numpy array for the host-pointer calls (nncu_host_register):
+    a call whose host buffers are all registered moves them with kernels
+    through the GPU's mapping of the memory instead of staging copies. Keep
+    the array alive until host_unregister(arr)."""
+    _check(lib().nncu_host_register(C.c_void_p(arr.ctypes.data), C.c_size_t(arr.nbytes)))
+
+
+def host_unregister(arr) -> None:
+    _check(lib().nncu_host_unregister(C.c_void_p(arr.ctypes.data)))
+
+
 _lib = None
 
 
@@ -184,6 +196,8 @@ def lib() -> C.CDLL:
     L.nncu_attention.argtypes = [vp, i32, i32, C.POINTER(AttnParams), vp, vp, vp, vp]
     L.nncu_attention_batch.argtypes = [vp, C.POINTER(AttnJob), i32]
     L.nncu_attention_batch_dev.argtypes = [vp, C.POINTER(AttnJob), i32, vp]
+    L.nncu_host_register.argtypes = [vp, sz]
+    L.nncu_host_unregister.argtypes = [vp]
     L.nncu_sync.argtypes = [vp, vp]
     L.nncu_perf_enable.argtypes = [C.c_int]
     L.nncu_perf_enable.restype = None

@@ -167,6 +167,32 @@ struct HostBuf
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// ---- registered host buffers (nncu_host_register) ----------------------------
+// Ranges of host memory the caller pinned through the library, keyed by
+// their start: a synchronous call whose every host buffer lies inside them
+// moves its inputs and outputs with kernels reading and writing the
+// device's mapping of that memory, instead of host copies through staging.
+struct Registered
+{
+	size_t bytes;
+	char* dev; // the device's address of the range's first byte
+};
+std::mutex g_reg_mu;
+std::map<uintptr_t, Registered> g_reg;
+
+// The device address of [p, p + bytes) if it lies inside one registered
+// range; nullptr otherwise.
+void* mapped(const void* p, size_t bytes)
+{
+	const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+	std::lock_guard<std::mutex> g(g_reg_mu);
+	auto it = g_reg.upper_bound(a);
+	if (it == g_reg.begin()) return nullptr;
+	--it;
+	if (a + bytes > it->first + it->second.bytes) return nullptr;
+	return it->second.dev + (a - it->first);
+}
+
 
 // ---- the phase profiler (nnc_perf_*, runtime.h:147-195, on CUDA events) ----
 std::atomic<uint64_t> g_launches{0};
@@ -933,7 +959,24 @@ struct Staged
 	char* dev;
 	size_t lead; // bytes before the table (16-byte aligned), uploaded with it
 	size_t cap;  // room for the table
+	size_t done; // bytes at the start already uploaded on the launching stream
 };
+
+// A synchronous call's inputs of at least this many bytes go up in groups
+// of about this size, each group's upload overlapping the host copy of the
+// next.
+constexpr size_t STAGE_GROUP_BYTES = 512 << 10;
+// A synchronous call moves its data with the copy kernels (registered host
+// buffers) only from this many bytes in and out: below it, two more launches
+// cost more than the host copies they replace.
+constexpr size_t MAP_MIN_BYTES = 128 << 10;
+
+// The rest of the staged inputs, [done, end), up on `st`.
+cudaError_t staged_upload(const Staged* sg, size_t end, cudaStream_t st)
+{
+	if (end <= sg->done) return cudaSuccess;
+	return cudaMemcpyAsync(sg->dev + sg->done, sg->host + sg->done, end - sg->done, cudaMemcpyHostToDevice, st);
+}
 
 int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, cudaStream_t st,
              nncu_group* group = nullptr, const Staged* staged = nullptr)
@@ -976,8 +1019,7 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 		n = keep;
 		if (n == 0)
 		{
-			if (staged)
-				CU(cudaMemcpyAsync(staged->dev, staged->host, staged->lead, cudaMemcpyHostToDevice, st), "input upload");
+			if (staged) CU(staged_upload(staged, staged->lead, st), "input upload");
 			CU(cudaEventRecord(kv->done, st), "completion event");
 			kv->last_stream = st;
 			kv->any_call = true;
@@ -1040,15 +1082,13 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	{
 		std::memcpy(staged->host + staged->lead, jobs.data(), (size_t)n * sizeof(DevJob));
 		std::memcpy(staged->host + staged->lead + jb, kv->starts_tmp.data(), sb);
-		CU(cudaMemcpyAsync(staged->dev, staged->host, staged->lead + jb + sb, cudaMemcpyHostToDevice, st),
-		   "input and job table upload");
+		CU(staged_upload(staged, staged->lead + jb + sb, st), "input and job table upload");
 		P.jobs = reinterpret_cast<const DevJob*>(staged->dev + staged->lead);
 		P.cta_start = reinterpret_cast<const CtaStart*>(staged->dev + staged->lead + jb);
 	}
 	else
 	{
-		if (staged)
-			CU(cudaMemcpyAsync(staged->dev, staged->host, staged->lead, cudaMemcpyHostToDevice, st), "input upload");
+		if (staged) CU(staged_upload(staged, staged->lead, st), "input upload");
 		auto& slot = kv->slots[kv->slot_next];
 		used = &slot;
 		kv->slot_next = (kv->slot_next + 1) % nncu_kv::JOB_SLOTS;
@@ -1226,6 +1266,42 @@ extern "C" int nncu_attention_split_dev(nncu_kv* kv, nncu_group* group, const nn
 	return run_jobs(kv, kv->jobs_tmp, jobs, static_cast<cudaStream_t>(stream), group);
 }
 
+extern "C" int nncu_host_register(void* p, size_t bytes)
+{
+	if (!p || !bytes) return fail(NNCU_ERR_INVALID_ARGUMENT, "nothing to register");
+	const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+	{
+		std::lock_guard<std::mutex> g(g_reg_mu);
+		auto it = g_reg.upper_bound(a + bytes - 1);
+		if (it != g_reg.begin() && std::prev(it)->first + std::prev(it)->second.bytes > a)
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "host range %p+%zu overlaps a registered one", p, bytes);
+	}
+	cudaError_t e = cudaHostRegister(p, bytes, cudaHostRegisterMapped | cudaHostRegisterPortable);
+	if (e != cudaSuccess) return cuda_fail(e, "cudaHostRegister");
+	void* dev = nullptr;
+	e = cudaHostGetDevicePointer(&dev, p, 0);
+	if (e != cudaSuccess)
+	{
+		cudaHostUnregister(p);
+		return cuda_fail(e, "cudaHostGetDevicePointer");
+	}
+	std::lock_guard<std::mutex> g(g_reg_mu);
+	g_reg[a] = Registered{bytes, static_cast<char*>(dev)};
+	return NNCU_OK;
+}
+
+extern "C" int nncu_host_unregister(void* p)
+{
+	{
+		std::lock_guard<std::mutex> g(g_reg_mu);
+		auto it = g_reg.find(reinterpret_cast<uintptr_t>(p));
+		if (it == g_reg.end()) return fail(NNCU_ERR_INVALID_ARGUMENT, "%p was not registered", p);
+		g_reg.erase(it);
+	}
+	CU(cudaHostUnregister(p), "cudaHostUnregister");
+	return NNCU_OK;
+}
+
 extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs)
 {
 	if (!kv || !jobs || n_jobs <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "no jobs");
@@ -1268,6 +1344,39 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 	char* hs = static_cast<char*>(kv->stage_host.p);
 	char* ds = static_cast<char*>(kv->stage_dev.p);
 	std::vector<nncu_attn_job> dj(jobs, jobs + n_jobs);
+	// Every host buffer registered (and enough bytes to pay for two more
+	// launches): a kernel gathers the inputs through the device's mapping of
+	// the caller's memory and another scatters the outputs back; no host copy.
+	CopyList gather, scatter;
+	gather.n = scatter.n = 0;
+	bool use_map = in_bytes + out_bytes >= MAP_MIN_BYTES;
+	for (int i = 0; i < n_jobs && use_map; ++i)
+	{
+		const nncu_attn_params& p = jobs[i].p;
+		const size_t qn = (size_t)p.n_tok * p.n_head * p.head_dim, kn = (size_t)p.n_tok * p.n_kv * p.head_dim;
+		const float* srcs[NIN] = {jobs[i].q, jobs[i].k, jobs[i].v, p.q_gamma, p.k_gamma, p.freq_factors, p.gate};
+		const size_t sizes[NIN] = {qn, p.reuse_kv ? 0 : kn, p.reuse_kv ? 0 : kn, p.q_gamma ? (size_t)p.head_dim : 0,
+		                           p.k_gamma ? (size_t)p.head_dim : 0, p.freq_factors ? (size_t)p.n_rot / 2 : 0,
+		                           p.gate ? qn : 0};
+		for (int s = 0; s < NIN && use_map; ++s)
+		{
+			if (!sizes[s]) continue;
+			const void* src = mapped(srcs[s], sizes[s] * sizeof(float));
+			use_map = src && gather.n < COPY_LIST_MAX;
+			if (use_map) gather.e[gather.n++] = {src, ds + in_off[i * NIN + s], sizes[s] * sizeof(float)};
+		}
+		void* dst = use_map ? mapped(jobs[i].out, qn * sizeof(float)) : nullptr;
+		use_map = dst && scatter.n < COPY_LIST_MAX;
+		if (use_map) scatter.e[scatter.n++] = {ds + out_base + out_off[i], dst, qn * sizeof(float)};
+	}
+	struct CopyTask
+	{
+		void* dst;
+		const void* src;
+		size_t bytes;
+	};
+	std::vector<CopyTask> ins;
+	ins.reserve((size_t)n_jobs * NIN);
 	for (int i = 0; i < n_jobs; ++i)
 	{
 		const nncu_attn_params& p = jobs[i].p;
@@ -1280,7 +1389,7 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 		for (int s = 0; s < NIN; ++s)
 		{
 			dptr[s] = sizes[s] ? reinterpret_cast<const float*>(ds + in_off[i * NIN + s]) : nullptr;
-			if (sizes[s]) std::memcpy(hs + in_off[i * NIN + s], srcs[s], sizes[s] * sizeof(float));
+			if (sizes[s]) ins.push_back({hs + in_off[i * NIN + s], srcs[s], sizes[s] * sizeof(float)});
 		}
 		dj[i].q = dptr[0];
 		dj[i].k = dptr[1];
@@ -1298,21 +1407,52 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 		fill_devjob(kv, dj[i], kv->jobs_tmp[i]);
 		prefill = prefill || prefill_eligible(kv, kv->jobs_tmp[i], dj[i]);
 	}
-	if (prefill) CU(cudaMemcpyAsync(ds, hs, in_bytes, cudaMemcpyHostToDevice, kv->stream), "input upload");
-	const Staged staged{hs, ds, in_bytes, table_cap};
+	// Into the pinned block: a large batch goes up in a few groups, each
+	// group's upload overlapping the next group's host copy; a small one goes
+	// up with the job table in one transfer.
+	size_t uploaded = 0;
+	if (use_map)
+	{
+		CU((cudaError_t)launch_copy_list(gather, kv->stream), "input gather");
+		uploaded = in_bytes;
+	}
+	else if (prefill || in_bytes >= STAGE_GROUP_BYTES)
+	{
+		size_t first = 0, group_end = 0;
+		for (size_t t = 0; t < ins.size(); ++t)
+		{
+			const size_t end = static_cast<char*>(ins[t].dst) - hs + ins[t].bytes;
+			if (end - group_end < STAGE_GROUP_BYTES && t + 1 < ins.size()) continue;
+			for (size_t c = first; c <= t; ++c) std::memcpy(ins[c].dst, ins[c].src, ins[c].bytes);
+			const size_t up_to = t + 1 < ins.size() ? end : in_bytes;
+			CU(cudaMemcpyAsync(ds + uploaded, hs + uploaded, up_to - uploaded, cudaMemcpyHostToDevice, kv->stream),
+			   "input upload");
+			uploaded = group_end = up_to;
+			first = t + 1;
+		}
+	}
+	else
+		for (const CopyTask& c : ins) std::memcpy(c.dst, c.src, c.bytes);
+	const Staged staged{hs, ds, in_bytes, table_cap, uploaded};
 	int rc = run_jobs(kv, kv->jobs_tmp, dj.data(), kv->stream, nullptr, prefill ? nullptr : &staged);
 	if (rc != NNCU_OK) return rc;
-	CU(cudaMemcpyAsync(hs + out_base, ds + out_base, out_bytes, cudaMemcpyDeviceToHost, kv->stream), "output download");
+	if (use_map)
+		CU((cudaError_t)launch_copy_list(scatter, kv->stream), "output scatter");
+	else
+		CU(cudaMemcpyAsync(hs + out_base, ds + out_base, out_bytes, cudaMemcpyDeviceToHost, kv->stream),
+		   "output download");
 	int* err_h = reinterpret_cast<int*>(hs + out_base + out_bytes);
 	CU(cudaMemcpyAsync(err_h, kv->err_dev, sizeof(int), cudaMemcpyDeviceToHost, kv->stream), "error word");
 	CU(cudaStreamSynchronize(kv->stream), "attention");
 	rc = device_error_status(kv, *err_h);
 	if (rc != NNCU_OK) return rc;
-	for (int i = 0; i < n_jobs; ++i)
-	{
-		const nncu_attn_params& p = jobs[i].p;
-		std::memcpy(jobs[i].out, hs + out_base + out_off[i], (size_t)p.n_tok * p.n_head * p.head_dim * sizeof(float));
-	}
+	if (!use_map)
+		for (int i = 0; i < n_jobs; ++i)
+		{
+			const nncu_attn_params& p = jobs[i].p;
+			std::memcpy(jobs[i].out, hs + out_base + out_off[i],
+			            (size_t)p.n_tok * p.n_head * p.head_dim * sizeof(float));
+		}
 	return NNCU_OK;
 }
 

@@ -175,6 +175,24 @@ int launch_prefill_prep(const DevJob& j, void* qbuf, void* stream);
 // The attention of every row over its causal span into j.out (after the prep).
 int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream);
 
+// A list of copies done by one kernel launch (k_prep.cu): each entry's
+// bytes from src to dst, either side device memory or the device's mapping
+// of registered (pinned) host memory. At most COPY_LIST_MAX entries travel as
+// the launch's parameter.
+struct CopyEntry
+{
+	const void* src;
+	void* dst;
+	uint64_t bytes;
+};
+constexpr int COPY_LIST_MAX = 160;
+struct CopyList
+{
+	int n;
+	CopyEntry e[COPY_LIST_MAX];
+};
+int launch_copy_list(const CopyList& l, void* stream);
+
 // Record a failure for nncu_last_error() (api.cpp); return `status`.
 int set_error(int status, const char* msg);
 int set_cuda_error(int cuda_status, const char* what);

@@ -170,4 +170,44 @@ int launch_softcap(float* y, const float* x, size_t n, float cap, void* stream)
 	return (int)cudaGetLastError();
 }
 
+// One CTA per entry of a copy list: 16-byte loads and stores where both
+// addresses are 16-byte aligned, 4-byte ones otherwise (every buffer here
+// holds floats). Reads or writes through the mapping of registered host
+// memory cross PCIe; each thread keeps four loads in flight.
+__global__ void __launch_bounds__(256) copy_list_kernel(const __grid_constant__ CopyList L)
+{
+	const CopyEntry e = L.e[blockIdx.x];
+	const bool wide = ((reinterpret_cast<uintptr_t>(e.src) | reinterpret_cast<uintptr_t>(e.dst)) & 15u) == 0;
+	size_t done = 0;
+	if (wide)
+	{
+		const uint4* s = static_cast<const uint4*>(e.src);
+		uint4* d = static_cast<uint4*>(e.dst);
+		const size_t n = e.bytes / 16;
+		size_t i = threadIdx.x;
+		for (; i + 3 * 256 < n; i += 4 * 256)
+		{
+			const uint4 a = s[i], b = s[i + 256], c = s[i + 512], f = s[i + 768];
+			d[i] = a;
+			d[i + 256] = b;
+			d[i + 512] = c;
+			d[i + 768] = f;
+		}
+		for (; i < n; i += 256) d[i] = s[i];
+		done = n * 16;
+	}
+	const uint32_t* s4 = static_cast<const uint32_t*>(e.src);
+	uint32_t* d4 = static_cast<uint32_t*>(e.dst);
+	for (size_t i = done / 4 + threadIdx.x; i < e.bytes / 4; i += 256) d4[i] = s4[i];
+}
+
+int launch_copy_list(const CopyList& l, void* stream)
+{
+	if (l.n <= 0) return 0;
+	if (l.n > COPY_LIST_MAX) return (int)cudaErrorInvalidValue;
+	copy_list_kernel<<<(unsigned)l.n, 256, 0, static_cast<cudaStream_t>(stream)>>>(l);
+	note_launches(1);
+	return (int)cudaGetLastError();
+}
+
 } // namespace nncu
