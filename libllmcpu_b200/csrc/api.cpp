@@ -1363,11 +1363,11 @@ extern "C" int nncu_attention_batch(nncu_kv* kv, const nncu_attn_job* jobs, int3
 			if (!sizes[s]) continue;
 			const void* src = mapped(srcs[s], sizes[s] * sizeof(float));
 			use_map = src && gather.n < COPY_LIST_MAX;
-			if (use_map) gather.e[gather.n++] = {src, ds + in_off[i * NIN + s], sizes[s] * sizeof(float)};
+			if (use_map) gather.e[gather.n++] = {src, ds + in_off[i * NIN + s], sizes[s] * sizeof(float), 0};
 		}
 		void* dst = use_map ? mapped(jobs[i].out, qn * sizeof(float)) : nullptr;
 		use_map = dst && scatter.n < COPY_LIST_MAX;
-		if (use_map) scatter.e[scatter.n++] = {ds + out_base + out_off[i], dst, qn * sizeof(float)};
+		if (use_map) scatter.e[scatter.n++] = {ds + out_base + out_off[i], dst, qn * sizeof(float), 0};
 	}
 	struct CopyTask
 	{

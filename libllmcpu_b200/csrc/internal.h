@@ -177,21 +177,24 @@ int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream);
 
 // A list of copies done by one kernel launch (k_prep.cu): each entry's
 // bytes from src to dst, either side device memory or the device's mapping
-// of registered (pinned) host memory. At most COPY_LIST_MAX entries travel as
-// the launch's parameter.
+// of registered (pinned) host memory, cut into COPY_CHUNK pieces, one CTA
+// each (cta0: the entry's first CTA, filled in by launch_copy_list). At most
+// COPY_LIST_MAX entries travel as the launch's parameter.
 struct CopyEntry
 {
 	const void* src;
 	void* dst;
 	uint64_t bytes;
+	uint32_t cta0;
 };
-constexpr int COPY_LIST_MAX = 160;
+constexpr int COPY_LIST_MAX = 120; // 8 + 120 x 32 bytes of parameter
+constexpr uint64_t COPY_CHUNK = 64 << 10;
 struct CopyList
 {
 	int n;
 	CopyEntry e[COPY_LIST_MAX];
 };
-int launch_copy_list(const CopyList& l, void* stream);
+int launch_copy_list(CopyList& l, void* stream);
 
 // Record a failure for nncu_last_error() (api.cpp); return `status`.
 int set_error(int status, const char* msg);

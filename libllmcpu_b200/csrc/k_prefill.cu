@@ -538,15 +538,19 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 		const int u = task - n_head;
 		return u < n_kv ? j.k + ((size_t)t * n_kv + u) * PF_D : j.v + ((size_t)t * n_kv + (u - n_kv)) * PF_D;
 	};
-	// a head vector in registers, element lane + 32 i in v[i]; the warp's
-	// next vector is loaded while this one is worked on
-	float v[PF_D / 32], vn[PF_D / 32];
+	// head vectors in registers, element lane + 32 i in v[i]; a warp issues
+	// the loads of all its vectors of a round (up to PREP_PER_WARP) before
+	// working on the first, so their latencies overlap
 	auto load = [&](float* dst, int task) {
 		const float* src = src_of(task);
 #pragma unroll
 		for (int i = 0; i < PF_D / 32; ++i) dst[i] = src[lane + 32 * i];
 	};
-	if (warp < n_tasks) load(v, warp);
+	constexpr int PREP_PER_WARP = 8;
+	float vv[PREP_PER_WARP][PF_D / 32];
+#pragma unroll
+	for (int r = 0; r < PREP_PER_WARP; ++r)
+		if (warp + 8 * r < n_tasks) load(vv[r], warp + 8 * r);
 	const float rpos = (float)pos * j.rope_scale;
 	for (int i = threadIdx.x; i < PF_D; i += blockDim.x)
 	{
@@ -564,9 +568,7 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 	// multiple of 32; NORM pairs e and e ^ 1: neighbouring lanes
 	const bool neox = j.rope_mode == 0;
 	const int row = pos % j.rows;
-	for (int task = warp; task < n_tasks; task += 8)
-	{
-		if (task + 8 < n_tasks) load(vn, task + 8);
+	auto process = [&](float* v, int task) {
 		const bool is_q = task < n_head, is_k = !is_q && task - n_head < n_kv;
 		const float* gamma = is_q ? (j.q_gamma ? s_qg : nullptr) : (is_k && j.k_gamma ? s_kg : nullptr);
 		const bool plain = !is_q && !is_k && j.v_rmsnorm;
@@ -626,11 +628,17 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 		// rounded to bf16 on the integer pipe (the conversion instruction would
 		// queue on the transcendental unit)
 #pragma unroll
-		for (int i = 0; i < PF_D / 32; ++i)
-		{
-			reinterpret_cast<uint16_t*>(dst)[lane + 32 * i] = (uint16_t)bf16_rne_bits(v[i]);
-			v[i] = vn[i];
-		}
+		for (int i = 0; i < PF_D / 32; ++i) reinterpret_cast<uint16_t*>(dst)[lane + 32 * i] = (uint16_t)bf16_rne_bits(v[i]);
+	};
+	for (int base = 0; base < n_tasks; base += 8 * PREP_PER_WARP)
+	{
+		if (base > 0)
+#pragma unroll
+			for (int r = 0; r < PREP_PER_WARP; ++r)
+				if (base + warp + 8 * r < n_tasks) load(vv[r], base + warp + 8 * r);
+#pragma unroll
+		for (int r = 0; r < PREP_PER_WARP; ++r)
+			if (base + warp + 8 * r < n_tasks) process(vv[r], base + warp + 8 * r);
 	}
 }
 

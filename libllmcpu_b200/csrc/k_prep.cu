@@ -170,13 +170,19 @@ int launch_softcap(float* y, const float* x, size_t n, float cap, void* stream)
 	return (int)cudaGetLastError();
 }
 
-// One CTA per entry of a copy list: 16-byte loads and stores where both
-// addresses are 16-byte aligned, 4-byte ones otherwise (every buffer here
-// holds floats). Reads or writes through the mapping of registered host
-// memory cross PCIe; each thread keeps four loads in flight.
+// One CTA per COPY_CHUNK piece of a copy list's entries: 16-byte loads and
+// stores where both addresses are 16-byte aligned, 4-byte ones otherwise
+// (every buffer here holds floats). Reads or writes through the mapping of
+// registered host memory cross PCIe; each thread keeps four loads in flight.
 __global__ void __launch_bounds__(256) copy_list_kernel(const __grid_constant__ CopyList L)
 {
-	const CopyEntry e = L.e[blockIdx.x];
+	int k = 0; // the entry whose pieces hold this CTA (entries in order of cta0)
+	while (k + 1 < L.n && L.e[k + 1].cta0 <= blockIdx.x) ++k;
+	CopyEntry e = L.e[k];
+	const uint64_t off = (uint64_t)(blockIdx.x - e.cta0) * COPY_CHUNK;
+	e.src = static_cast<const char*>(e.src) + off;
+	e.dst = static_cast<char*>(e.dst) + off;
+	e.bytes = e.bytes - off < COPY_CHUNK ? e.bytes - off : COPY_CHUNK;
 	const bool wide = ((reinterpret_cast<uintptr_t>(e.src) | reinterpret_cast<uintptr_t>(e.dst)) & 15u) == 0;
 	size_t done = 0;
 	if (wide)
@@ -201,11 +207,19 @@ __global__ void __launch_bounds__(256) copy_list_kernel(const __grid_constant__ 
 	for (size_t i = done / 4 + threadIdx.x; i < e.bytes / 4; i += 256) d4[i] = s4[i];
 }
 
-int launch_copy_list(const CopyList& l, void* stream)
+int launch_copy_list(CopyList& l, void* stream)
 {
 	if (l.n <= 0) return 0;
 	if (l.n > COPY_LIST_MAX) return (int)cudaErrorInvalidValue;
-	copy_list_kernel<<<(unsigned)l.n, 256, 0, static_cast<cudaStream_t>(stream)>>>(l);
+	uint64_t ctas = 0;
+	for (int i = 0; i < l.n; ++i)
+	{
+		l.e[i].cta0 = (uint32_t)ctas;
+		ctas += (l.e[i].bytes + COPY_CHUNK - 1) / COPY_CHUNK;
+	}
+	if (ctas == 0) return 0;
+	if (ctas > 0x7fffffffu) return (int)cudaErrorInvalidValue;
+	copy_list_kernel<<<(unsigned)ctas, 256, 0, static_cast<cudaStream_t>(stream)>>>(l);
 	note_launches(1);
 	return (int)cudaGetLastError();
 }
