@@ -526,7 +526,7 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 {
 	using T = typename KV::T;
 	static_assert(sizeof(T) == 2, "the prefill's cache and q rows are bf16");
-	__shared__ float s_qg[PF_D], s_kg[PF_D], s_cs[PF_D / 2], s_sn[PF_D / 2];
+	__shared__ __align__(16) float s_qg[PF_D], s_kg[PF_D], s_cs[PF_D / 2], s_sn[PF_D / 2];
 	const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	const int half = j.n_rot / 2;
 	const int pos = j.pos0 + t;
@@ -538,16 +538,19 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 		const int u = task - n_head;
 		return u < n_kv ? j.k + ((size_t)t * n_kv + u) * PF_D : j.v + ((size_t)t * n_kv + (u - n_kv)) * PF_D;
 	};
-	// head vectors in registers, element lane + 32 i in v[i]; a warp issues
-	// the loads of all its vectors of a round (up to PREP_PER_WARP) before
-	// working on the first, so their latencies overlap
+	// head vectors in registers, elements 4 lane .. 4 lane + 3 in v[0..3]
+	// (one 16-byte load per lane); a warp issues the loads of all its vectors
+	// of a round (up to PREP_PER_WARP) before working on the first, so their
+	// latencies overlap
 	auto load = [&](float* dst, int task) {
-		const float* src = src_of(task);
-#pragma unroll
-		for (int i = 0; i < PF_D / 32; ++i) dst[i] = src[lane + 32 * i];
+		const float4 x = reinterpret_cast<const float4*>(src_of(task))[lane];
+		dst[0] = x.x;
+		dst[1] = x.y;
+		dst[2] = x.z;
+		dst[3] = x.w;
 	};
 	constexpr int PREP_PER_WARP = 8;
-	float vv[PREP_PER_WARP][PF_D / 32];
+	float vv[PREP_PER_WARP][4];
 #pragma unroll
 	for (int r = 0; r < PREP_PER_WARP; ++r)
 		if (warp + 8 * r < n_tasks) load(vv[r], warp + 8 * r);
@@ -564,10 +567,12 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 		}
 	}
 	__syncthreads();
-	// NEOX pairs elements e and e + n_rot/2: the same lane when n_rot/2 is a
-	// multiple of 32; NORM pairs e and e ^ 1: neighbouring lanes
+	// NEOX pairs elements e and e + n_rot/2 (n_rot/2 is 32 or 64, checked on
+	// the host): the partner sits in lane ^ 8 or lane ^ 16 at the same place
+	// of its four; NORM pairs e and e ^ 1: within a lane's four
 	const bool neox = j.rope_mode == 0;
 	const int row = pos % j.rows;
+	const int partner = half == 64 ? 16 : 8;
 	auto process = [&](float* v, int task) {
 		const bool is_q = task < n_head, is_k = !is_q && task - n_head < n_kv;
 		const float* gamma = is_q ? (j.q_gamma ? s_qg : nullptr) : (is_k && j.k_gamma ? s_kg : nullptr);
@@ -575,45 +580,53 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 		if (gamma || plain)
 		{
 			// RMSNorm as rms_scale does: squares in fp32, the scale in double
-			float ss = 0.0f;
-#pragma unroll
-			for (int i = 0; i < PF_D / 32; ++i) ss = fmaf(v[i], v[i], ss);
+			float ss = v[0] * v[0];
+			ss = fmaf(v[1], v[1], ss);
+			ss = fmaf(v[2], v[2], ss);
+			ss = fmaf(v[3], v[3], ss);
 			ss = warp_sum(ss);
 			const double mean = gamma ? (double)ss * (double)(1.0f / (float)PF_D) : (double)ss / (double)PF_D;
 			const float sc = (float)(1.0 / sqrt(mean + (double)j.eps));
+			if (gamma)
+			{
+				const float4 g = reinterpret_cast<const float4*>(gamma)[lane];
+				v[0] = v[0] * sc * g.x;
+				v[1] = v[1] * sc * g.y;
+				v[2] = v[2] * sc * g.z;
+				v[3] = v[3] * sc * g.w;
+			}
+			else
 #pragma unroll
-			for (int i = 0; i < PF_D / 32; ++i) v[i] = gamma ? v[i] * sc * gamma[lane + 32 * i] : v[i] * sc;
+				for (int i = 0; i < 4; ++i) v[i] *= sc;
 		}
 		if ((is_q || is_k) && half > 0)
 		{
 			if (neox)
 			{
-				// half is 32 or 64 here (a multiple of 32, checked on the host)
-				auto rot = [&](float& a_, float& b_, int e) {
-					const float a = a_, b = b_;
-					a_ = s_cs[e] * a - s_sn[e] * b;
-					b_ = s_sn[e] * a + s_cs[e] * b;
-				};
-				if (half == 64)
-				{
-					rot(v[0], v[2], lane);
-					rot(v[1], v[3], lane + 32);
-				}
-				else
-					rot(v[0], v[1], lane);
-			}
-			else
-			{
+				float o[4];
 #pragma unroll
-				for (int i = 0; i < PF_D / 32; ++i)
+				for (int i = 0; i < 4; ++i) o[i] = __shfl_xor_sync(0xffffffffu, v[i], partner);
+				const int e = 4 * lane; // this lane's first element
+				if (e < 2 * half)
 				{
-					const int e = lane + 32 * i;
-					const float other = __shfl_xor_sync(0xffffffffu, v[i], 1);
-					if (e < j.n_rot)
-					{
-						const float cs = s_cs[e >> 1], sn = s_sn[e >> 1];
-						v[i] = (lane & 1) ? sn * other + cs * v[i] : cs * v[i] - sn * other;
-					}
+					const bool first = (lane & partner) == 0; // holds e of the pair (e, e + half)
+					const float4 cs = reinterpret_cast<const float4*>(s_cs)[lane & (partner - 1)];
+					const float4 sn = reinterpret_cast<const float4*>(s_sn)[lane & (partner - 1)];
+					const float c[4] = {cs.x, cs.y, cs.z, cs.w}, n[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+					for (int i = 0; i < 4; ++i) v[i] = first ? c[i] * v[i] - n[i] * o[i] : n[i] * o[i] + c[i] * v[i];
+				}
+			}
+			else if (4 * lane < j.n_rot)
+			{
+				const float2 cs = reinterpret_cast<const float2*>(s_cs)[lane], sn = reinterpret_cast<const float2*>(s_sn)[lane];
+				const float a0 = v[0], b0 = v[1], a1 = v[2], b1 = v[3];
+				v[0] = cs.x * a0 - sn.x * b0;
+				v[1] = sn.x * a0 + cs.x * b0;
+				if (4 * lane + 2 < j.n_rot)
+				{
+					v[2] = cs.y * a1 - sn.y * b1;
+					v[3] = sn.y * a1 + cs.y * b1;
 				}
 			}
 		}
@@ -625,10 +638,10 @@ __global__ void __launch_bounds__(256) prefill_prep_kernel(const __grid_constant
 			const int h = is_k ? task - n_head : task - n_head - n_kv;
 			dst = reinterpret_cast<T*>((is_k ? j.K : j.V) + (size_t)h * j.head_bytes) + (size_t)row * PF_D;
 		}
-		// rounded to bf16 on the integer pipe (the conversion instruction would
-		// queue on the transcendental unit)
-#pragma unroll
-		for (int i = 0; i < PF_D / 32; ++i) reinterpret_cast<uint16_t*>(dst)[lane + 32 * i] = (uint16_t)bf16_rne_bits(v[i]);
+		// four bf16 (round to nearest even) in one 8-byte store
+		const __nv_bfloat162 lo = __floats2bfloat162_rn(v[0], v[1]), hi = __floats2bfloat162_rn(v[2], v[3]);
+		reinterpret_cast<uint2*>(dst)[lane] =
+			make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
 	};
 	for (int base = 0; base < n_tasks; base += 8 * PREP_PER_WARP)
 	{
