@@ -430,7 +430,18 @@ def run_product(args, w: Workload, rank: int, world: int, local_rank: int):
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": profiled_traffic(w.name),
                     "bytes_per_launch": int(core_bytes)}
-    roofline.update({"kernel": "decode_kernel (K2+K3: split-KV attention, merge, fused append)",
+    # which kernel the library launches for this workload: the tensor-core
+    # prefill, the tensor-core decode (16-bit cache, 3+ query rows per KV head,
+    # not split), or the CUDA-core decode
+    L0 = layers[0]
+    rows = (L0.n_head // L0.n_kv) * w.n_tok
+    if w.metric == "flops":
+        kernel = "prefill_kernel (tcgen05 Q K^T and P V, TMEM softmax), after prefill_prep_kernel"
+    elif w.kv_type in (0, 2) and rows >= 3 and not split:
+        kernel = "decode_tc_kernel (tcgen05 K Q^T and V^T P^T, split-KV merge, fused append)"
+    else:
+        kernel = "decode_kernel (CUDA cores: split-KV attention, merge, fused append)"
+    roofline.update({"kernel": kernel,
                      "peak_source": peaks["source"], "us_per_launch": round(core_us, 3),
                      "attn_rope_us_per_launch": round(1e3 * rope["ms"] / max(rope["calls"], 1), 3)})
 
