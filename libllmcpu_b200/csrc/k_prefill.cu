@@ -6,27 +6,27 @@
 // causal span. Here, for bf16 caches and head_dim 128, the two products run
 // on the 5th-generation tensor cores. One CTA takes 256 query rows of one
 // query head as two Q tiles, A and B, of 128 rows, and walks the key tiles of
-// their spans, 128 keys at a time; each key tile is loaded once for both:
+// their spans, 64 keys at a time; each key tile is loaded once for both:
 //
-//   S = Q K^T      tcgen05.mma, M 128 x N 128 x K head_dim, 16-bit in, fp32 in TMEM
+//   S = Q K^T      tcgen05.mma, M 128 x N 64 x K 128, bf16 in, fp32 in TMEM
 //   P = softmax    one warpgroup per Q tile, one query row per thread (TMEM lane)
-//   O += P V       tcgen05.mma, P (16-bit) from TMEM over its own S, V from
-//                  shared memory, O in TMEM
+//   O += P V       tcgen05.mma, M 128 x N 128 x K 64, P (bf16) from TMEM over
+//                  its own S, V from shared memory, O in TMEM
 //
 // Roles: warp 0 issues the TMA loads of the two Q tiles and of the K tiles,
-// warp 2 those of the V tiles, each into its own 2-stage ring; warp 1 owns
-// the TMEM allocation (S_A, S_B, O_A, O_B: 512 columns at head_dim 128) and,
-// from one lane, issues the MMAs in the order PV_A(t), S_A(t+1), PV_B(t),
-// S_B(t+1), so that the softmax of one Q tile runs while the tensor core
-// works on the other's products; warps 4-7 and 8-11 do the softmax of A and
-// of B: a thread reads its row of S from TMEM, masks it by the row's span,
-// writes its probabilities back as 16-bit pairs over the first 64 columns of
-// the same S (the A operand of P V; the next S into those columns is issued
-// after that P V, and tcgen05.mma operations of one thread execute in
-// order), keeps O in scale and writes the output row. Online softmax in base
-// 2 with a lazily moved maximum: a row's reference maximum moves (and O and
-// l are rescaled) only when a new score exceeds it by more than 2^8, so O is
-// rarely touched; the result is the same softmax, divided by the same l.
+// warp 2 those of the V tiles, each into its own 4-stage ring; warp 1 owns
+// the TMEM allocation (per Q tile two S buffers of 64 columns and O of 128:
+// 512 columns) and, from one lane, issues the MMAs from descriptors formed
+// once. Each Q tile's S of key tile t + 2 goes into the buffer of tile t
+// right after P_t V_t (tcgen05 MMAs of one thread execute in order), so the
+// softmax of tile t + 1 runs while P_t V_t and S_{t+2} are computed. Warps
+// 4-7 and 8-11 do the softmax of A and of B: a thread reads its row of S
+// from TMEM, masks it by the row's span, writes its probabilities back as
+// 16-bit pairs over the first 32 columns of the same S buffer (the A operand
+// of P V), keeps O in scale and writes the output row. Online softmax in
+// base 2 with a lazily moved maximum: a row's reference maximum moves (and O
+// and l are rescaled) only when a new score exceeds it by more than 2^8, so O
+// is rarely touched; the result is the same softmax, divided by the same l.
 // After a row's first keys, a tile's exponentials are taken against the
 // row's held maximum while the tile's own maximum is found on the way (no
 // separate pass over the scores); a row whose scores passed the held maximum
@@ -53,34 +53,35 @@ namespace
 {
 
 constexpr int PF_BM = 128;          // query rows per Q tile; a CTA takes two (A, B)
-constexpr int PF_BN = 128;          // keys per tile
-constexpr int PF_D = 128;           // head_dim of the prep kernel's rows
+constexpr int PF_BN = 64;           // keys per tile
+constexpr int PF_D = 128;           // head_dim
+constexpr int PF_STAGES = 4;        // K and V ring depth
 constexpr int PF_THREADS = 384;     // warps 0-3: loads, MMA; 4-7: softmax of A; 8-11: softmax of B
 constexpr float LAZY = 8.0f;        // log2 headroom before a row's reference maximum moves
 
-// Shared memory and TMEM of the prefill for head_dim D (64 or 128).
-template <int D>
+// Shared memory and TMEM of the prefill (head_dim 128).
 struct PfLayout
 {
-	static constexpr int PANEL = 128 * 128;       // 128 rows x 64 16-bit elements, 128-byte swizzled
-	static constexpr int TILE = (D / 64) * PANEL; // 128 rows x D
-	static constexpr int SM_Q = 0;                // [2] Q tiles
-	static constexpr int SM_K = SM_Q + 2 * TILE;  // [2] K stages
-	static constexpr int SM_V = SM_K + 2 * TILE;  // [2] V stages
-	static constexpr int SM_BAR = SM_V + 2 * TILE;
+	static constexpr int Q_PANEL = 128 * 128;       // 128 rows x 64 bf16, 128-byte swizzled
+	static constexpr int Q_TILE = 2 * Q_PANEL;      // 128 rows x 128
+	static constexpr int KV_PANEL = PF_BN * 128;    // 64 rows x 64 bf16
+	static constexpr int KV_TILE = 2 * KV_PANEL;    // 64 keys x 128
+	static constexpr int SM_Q = 0;                  // [2] Q tiles
+	static constexpr int SM_K = SM_Q + 2 * Q_TILE;  // [PF_STAGES] K stages
+	static constexpr int SM_V = SM_K + PF_STAGES * KV_TILE; // [PF_STAGES] V stages
+	static constexpr int SM_BAR = SM_V + PF_STAGES * KV_TILE;
 	static constexpr int SMEM = SM_BAR + 256 + 1024; // + alignment slack
-	// TMEM columns: S of tile X at 128 X (its P, 16-bit pairs, in the first
-	// 64 of them), O of tile X at 256 + D X
+	// TMEM columns: S of Q tile X, buffer b at 128 X + 64 b (its P, bf16
+	// pairs, in its first 32 columns); O of Q tile X at 256 + 128 X
 	static constexpr uint32_t T_S = 0, T_O = 256, COLS = 512;
 };
 
-// Eight tcgen05.mma of one product in one asm block (one predicate set-up,
-// the descriptors advanced inside), so the issuing thread spends about two
-// instructions per MMA.
-// S = Q K^T over head_dim 128: A and B K-major; K step k advances both
-// descriptors by (k >> 2) panels + (k & 3) x 32 bytes (16-byte units).
-template <uint32_t PANEL16>
-__device__ __forceinline__ void mma8_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t id)
+// S = Q K^T for one Q tile and one 64-key tile, eight K steps of 16 over
+// head_dim 128 in one asm block: A (Q) and B (K) K-major, 128-byte swizzled;
+// K step k advances each descriptor by (k >> 2) of its panels + (k & 3) x 32
+// bytes (16-byte units), from descriptors formed once.
+template <uint32_t AP, uint32_t BP>
+__device__ __forceinline__ void mma8_s(uint32_t d, uint64_t a, uint64_t b, uint32_t id)
 {
 	asm volatile(
 		"{\n\t.reg .pred p0, p1;\n\t.reg .b64 a, b;\n\t"
@@ -89,17 +90,18 @@ __device__ __forceinline__ void mma8_ss(uint32_t d, uint64_t a, uint64_t b, uint
 		"add.s64 a, %1, 2;\n\tadd.s64 b, %2, 2;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
 		"add.s64 a, %1, 4;\n\tadd.s64 b, %2, 4;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
 		"add.s64 a, %1, 6;\n\tadd.s64 b, %2, 6;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
-		"add.s64 a, %1, %4;\n\tadd.s64 b, %2, %4;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
-		"add.s64 a, %1, %5;\n\tadd.s64 b, %2, %5;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
-		"add.s64 a, %1, %6;\n\tadd.s64 b, %2, %6;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
-		"add.s64 a, %1, %7;\n\tadd.s64 b, %2, %7;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t}"
-		::"r"(d), "l"(a), "l"(b), "r"(id), "n"(PANEL16), "n"(PANEL16 + 2), "n"(PANEL16 + 4), "n"(PANEL16 + 6)
+		"add.s64 a, %1, %4;\n\tadd.s64 b, %2, %8;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
+		"add.s64 a, %1, %5;\n\tadd.s64 b, %2, %9;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
+		"add.s64 a, %1, %6;\n\tadd.s64 b, %2, %10;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t"
+		"add.s64 a, %1, %7;\n\tadd.s64 b, %2, %11;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], a, b, %3, p1;\n\t}"
+		::"r"(d), "l"(a), "l"(b), "r"(id), "n"(AP), "n"(AP + 2), "n"(AP + 4), "n"(AP + 6), "n"(BP), "n"(BP + 2),
+		"n"(BP + 4), "n"(BP + 6)
 		: "memory");
 }
 
-// O (+)= P V over a 128-key tile: A = P from TMEM (8 columns per K step of
-// 16 keys), B = V MN-major (2048 bytes per K step); `acc` = 0 starts O afresh.
-__device__ __forceinline__ void mma8_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc)
+// O (+)= P V over a 64-key tile: A = P from TMEM (8 columns per K step of 16
+// keys), B = V MN-major (2048 bytes per K step); `acc` = 0 starts O afresh.
+__device__ __forceinline__ void mma4_pv(uint32_t d, uint32_t a, uint64_t b, uint32_t id, uint32_t acc)
 {
 	asm volatile(
 		"{\n\t.reg .pred p0, p1;\n\t.reg .b64 b;\n\t.reg .b32 a;\n\t"
@@ -107,11 +109,7 @@ __device__ __forceinline__ void mma8_ts(uint32_t d, uint32_t a, uint64_t b, uint
 		"tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p0;\n\t"
 		"add.s32 a, %1, 8;\n\tadd.s64 b, %2, 128;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
 		"add.s32 a, %1, 16;\n\tadd.s64 b, %2, 256;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
-		"add.s32 a, %1, 24;\n\tadd.s64 b, %2, 384;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
-		"add.s32 a, %1, 32;\n\tadd.s64 b, %2, 512;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
-		"add.s32 a, %1, 40;\n\tadd.s64 b, %2, 640;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
-		"add.s32 a, %1, 48;\n\tadd.s64 b, %2, 768;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t"
-		"add.s32 a, %1, 56;\n\tadd.s64 b, %2, 896;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t}"
+		"add.s32 a, %1, 24;\n\tadd.s64 b, %2, 384;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [a], b, %3, p1;\n\t}"
 		::"r"(d), "r"(a), "l"(b), "r"(id), "r"(acc)
 		: "memory");
 }
@@ -143,28 +141,29 @@ __device__ __forceinline__ uint32_t pack_p_f16(float lo, float hi)
 	return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <int D, bool BF16>
+template <bool BF16>
 __global__ void __launch_bounds__(PF_THREADS, 1)
 	prefill_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const PrefillPlan P)
 {
-	static_assert(D == 128, "the MMA blocks walk head_dim 128 in eight K steps");
-	using L = PfLayout<D>;
+	using L = PfLayout;
+	constexpr int D = PF_D;
 	extern __shared__ unsigned char smem_raw[];
 	unsigned char* smem =
 		reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
 	uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::SM_BAR);
 	uint64_t* q_full = bars + 0;
-	uint64_t* k_full = bars + 1;   // [2]
-	uint64_t* k_empty = bars + 3;  // [2]: a K stage is free once the S of both Q tiles are done
-	uint64_t* v_full = bars + 5;   // [2]
-	uint64_t* v_empty = bars + 7;  // [2]: a V stage is free once both P V are done
-	uint64_t* s_full = bars + 9;   // [2 Q tiles]
-	uint64_t* p_full = bars + 11;  // [2 Q tiles]: P in TMEM (and O rescaled)
-	uint64_t* o_done = bars + 13;  // [2 Q tiles]: the tile's last P V has completed
-	uint64_t* mma_done = bars + 15; // every MMA issued has completed
-	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-	volatile int* flags = reinterpret_cast<volatile int*>(bars + 17); // [0] abort
+	uint64_t* k_full = bars + 1;    // [PF_STAGES]
+	uint64_t* k_empty = bars + 5;   // [PF_STAGES]: a K stage is free once the S of both Q tiles are done
+	uint64_t* v_full = bars + 9;    // [PF_STAGES]
+	uint64_t* v_empty = bars + 13;  // [PF_STAGES]: a V stage is free once both P V are done
+	uint64_t* s_full = bars + 17;   // [2 Q tiles][2 buffers]
+	uint64_t* p_full = bars + 21;   // [2 Q tiles][2 buffers]: P in TMEM (and O rescaled)
+	uint64_t* pv_done = bars + 25;  // [2 Q tiles]: one phase per P V of the tile (for a rescale of O)
+	uint64_t* mma_done = bars + 27; // every MMA issued has completed
+	uint64_t* o_done = bars + 28;   // [2 Q tiles]: the tile's last P V has completed (one phase)
+	uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 30);
+	volatile int* flags = reinterpret_cast<volatile int*>(bars + 31); // [0] abort
 
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	// the heaviest pairs of query tiles (the longest causal spans) go first;
@@ -172,8 +171,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 	const int h = blockIdx.x % P.n_head;
 	const int q0 = (P.q_pairs - 1 - (int)blockIdx.x / P.n_head) * (2 * PF_BM);
 	const int hk = h / (P.n_head / P.n_kv);
-	// each Q tile's key tiles [lo, hi] (the union of its rows' spans); a tile
-	// past the batch is absent (lo > hi)
+	// each Q tile's 64-key tiles [lo, hi] (the union of its rows' spans); a
+	// tile past the batch is absent (lo > hi)
 	int lo[2], hi[2];
 #pragma unroll
 	for (int X = 0; X < 2; ++X)
@@ -196,16 +195,22 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 	if (threadIdx.x == 0)
 	{
 		mbar_init(q_full, 1);
-		for (int s = 0; s < 2; ++s)
+		for (int s = 0; s < PF_STAGES; ++s)
 		{
 			mbar_init(&k_full[s], 1);
 			mbar_init(&k_empty[s], 1);
 			mbar_init(&v_full[s], 1);
 			mbar_init(&v_empty[s], 1);
-			mbar_init(&s_full[s], 1);
-			mbar_init(&p_full[s], 128);
-			mbar_init(&o_done[s], 1);
 		}
+		for (int i = 0; i < 4; ++i)
+		{
+			mbar_init(&s_full[i], 1);
+			mbar_init(&p_full[i], 128);
+		}
+		mbar_init(&pv_done[0], 1);
+		mbar_init(&pv_done[1], 1);
+		mbar_init(&o_done[0], 1);
+		mbar_init(&o_done[1], 1);
 		mbar_init(mma_done, 1);
 		flags[0] = 0;
 		fence_barrier_init();
@@ -216,19 +221,15 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 	tc_fence_after();
 	const uint32_t tmem = *tmem_slot;
 
-	// registers from the load and MMA warps to the softmax warpgroups: the
-	// launch gives every thread 168 (384 x 168 = 64,512); after this the
-	// first warpgroup holds 96 and the two softmax warpgroups 200 each
-	// (128 x 96 + 256 x 200 = 63,488, within the launch's), so a softmax
-	// thread keeps its row of 128 scores and the exponentials' inputs in
-	// registers
+	// registers from the load and MMA warps to the softmax warpgroups (the
+	// launch gives every thread 168; 128 x 96 + 256 x 200 = 63,488 of 64,512)
 	if (warp < 4)
 	{
 		asm volatile("setmaxnreg.dec.sync.aligned.u32 96;" ::: "memory");
 		if (warp == 0 || warp == 2)
 		{
 			// ---- TMA: warp 0 the Q tiles once, then the K tiles; warp 2 the V
-			// tiles; each through its own 2-stage ring ----
+			// tiles; each through its own PF_STAGES-deep ring ----
 			if (lane == 0)
 			{
 				const bool is_k = warp == 0;
@@ -239,107 +240,117 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 				if (is_k)
 				{
 					const int nq = lo[1] <= hi[1] ? 2 : 1;
-					mbar_arrive_expect_tx(q_full, nq * L::TILE);
+					mbar_arrive_expect_tx(q_full, nq * L::Q_TILE);
 					for (int X = 0; X < nq; ++X)
-						for (int p = 0; p < D / 64; ++p)
-							tma3(smem + L::SM_Q + X * L::TILE + p * L::PANEL, &qmap, 64 * p, q0 + X * PF_BM, h, q_full);
+						for (int p = 0; p < 2; ++p)
+							tma3(smem + L::SM_Q + X * L::Q_TILE + p * L::Q_PANEL, &qmap, 64 * p, q0 + X * PF_BM, h,
+							     q_full);
 				}
 				int issued = 0;
 				for (int u = 0; u < n_u; ++u)
 				{
-					const int s = u & 1;
-					if (u >= 2 &&
-					    !mbar_wait_bounded(&empty[s], (uint32_t)(((u >> 1) - 1) & 1), P.err, DEVERR_WAIT_EMPTY))
+					const int s = u % PF_STAGES;
+					if (u >= PF_STAGES && !mbar_wait_bounded(&empty[s], (uint32_t)(((u / PF_STAGES) - 1) & 1), P.err,
+					                                         DEVERR_WAIT_EMPTY))
 					{
 						flags[0] = 1;
 						break;
 					}
 					if (flags[0]) break;
-					unsigned char* t = ring + s * L::TILE;
+					unsigned char* t = ring + s * L::KV_TILE;
 					const int key0 = (u_lo + u) * PF_BN;
-					mbar_arrive_expect_tx(&full[s], L::TILE);
-					for (int p = 0; p < D / 64; ++p) tma3(t + p * L::PANEL, map, 64 * p, key0, hk, &full[s]);
+					mbar_arrive_expect_tx(&full[s], L::KV_TILE);
+					for (int p = 0; p < 2; ++p) tma3(t + p * L::KV_PANEL, map, 64 * p, key0, hk, &full[s]);
 					issued = u + 1;
 				}
 				// on an abort, do not leave while a copy may still land here
 				if (is_k) mbar_wait_bounded(q_full, 0, nullptr, 0);
-				for (int u = max(0, issued - 2); u < issued; ++u)
-					mbar_wait_bounded(&full[u & 1], (uint32_t)((u >> 1) & 1), nullptr, 0);
+				for (int u = max(0, issued - PF_STAGES); u < issued; ++u)
+					mbar_wait_bounded(&full[u % PF_STAGES], (uint32_t)((u / PF_STAGES) & 1), nullptr, 0);
 			}
 			__syncwarp(); // the whole warp meets the final barrier together
 		}
 		else if (warp == 1)
 		{
-			// ---- MMA issue, in the order PV_A(t), S_A(t+1), PV_B(t), S_B(t+1):
-			// each Q tile's softmax of tile t+1 overlaps the other tile's MMAs ----
+			// ---- MMA issue. Each Q tile has two S buffers: S of its tile
+			// t + 2 goes into the buffer of tile t right after P_t V_t (tcgen05
+			// MMAs of one thread execute in order), so the softmax of tile t + 1
+			// runs while P_t V_t and S_{t+2} are computed ----
 			if (lane == 0)
 			{
-				constexpr uint32_t ID_QK = tc_idesc(128, 128, BF16, false, false);
+				constexpr uint32_t ID_S = tc_idesc(128, PF_BN, BF16, false, false);
 				constexpr uint32_t ID_PV = tc_idesc(128, D, BF16, false, true);
-				// the operands' shared memory descriptors, formed once: a Q tile,
-				// a K or V stage and a K step are constant offsets (16-byte units)
-				// from these
-				constexpr uint64_t TILE16 = L::TILE >> 4, PANEL16 = L::PANEL >> 4;
+				// the operands' shared memory descriptors, formed once
 				const uint64_t dq = sdesc(smem_u32(smem + L::SM_Q), 16, 1024);
 				const uint64_t dk = sdesc(smem_u32(smem + L::SM_K), 16, 1024);
-				const uint64_t dv = sdesc(smem_u32(smem + L::SM_V), L::PANEL, 1024);
+				const uint64_t dv = sdesc(smem_u32(smem + L::SM_V), L::KV_PANEL, 1024);
 				auto has = [&](int X, int t) { return X ? (t >= lo[1] && t <= hi[1]) : (t >= lo[0] && t <= hi[0]); };
+				int ns[2] = {0, 0}, np[2] = {0, 0}; // S issued, P consumed, per Q tile
 				auto issue_s = [&](int X, int u) {
-					mma8_ss<(uint32_t)PANEL16>(tmem + L::T_S + 128 * X, dq + (uint64_t)X * TILE16,
-					                           dk + (uint64_t)(u & 1) * TILE16, ID_QK);
-					mma_commit(&s_full[X]);
+					const int b = ns[X] & 1;
+					mma8_s<(uint32_t)(L::Q_PANEL >> 4), (uint32_t)(L::KV_PANEL >> 4)>(
+						tmem + L::T_S + 128 * X + 64 * b, dq + (uint64_t)X * (L::Q_TILE >> 4),
+						dk + (uint64_t)(u % PF_STAGES) * (L::KV_TILE >> 4), ID_S);
+					mma_commit(&s_full[2 * X + b]);
+					++ns[X];
 				};
-				int np[2] = {0, 0}; // P consumed per Q tile (the phase of p_full)
 				bool ok = mbar_wait_bounded(q_full, 0, P.err, DEVERR_WAIT_FULL);
-				if (ok) ok = !flags[0] && mbar_wait_bounded(&k_full[0], 0, P.err, DEVERR_WAIT_FULL);
-				if (ok)
+				for (int u = 0; ok && u < min(2, n_u); ++u)
 				{
+					ok = !flags[0] && mbar_wait_bounded(&k_full[u % PF_STAGES], (uint32_t)((u / PF_STAGES) & 1), P.err,
+					                                    DEVERR_WAIT_FULL);
+					if (!ok) break;
 					tc_fence_after();
 					for (int X = 0; X < 2; ++X)
-						if (has(X, u_lo)) issue_s(X, 0);
-					mma_commit(&k_empty[0]);
+						if (has(X, u_lo + u)) issue_s(X, u);
+					mma_commit(&k_empty[u % PF_STAGES]);
 				}
 				for (int u = 0; ok && u < n_u; ++u)
 				{
-					const int t = u_lo + u, s = u & 1;
-					ok = !flags[0] && mbar_wait_bounded(&v_full[s], (uint32_t)((u >> 1) & 1), P.err, DEVERR_WAIT_FULL);
-					const bool next = u + 1 < n_u;
+					const int t = u_lo + u, s = u % PF_STAGES;
+					ok = !flags[0] && mbar_wait_bounded(&v_full[s], (uint32_t)((u / PF_STAGES) & 1), P.err,
+					                                    DEVERR_WAIT_FULL);
+					const bool ahead = u + 2 < n_u;
 					bool k_ready = false;
 					for (int X = 0; ok && X < 2; ++X)
 					{
 						if (has(X, t))
 						{
-							ok = !flags[0] &&
-							     mbar_wait_bounded(&p_full[X], (uint32_t)(np[X] & 1), P.err, DEVERR_WAIT_FULL);
+							const int b = np[X] & 1;
+							ok = !flags[0] && mbar_wait_bounded(&p_full[2 * X + b], (uint32_t)((np[X] >> 1) & 1), P.err,
+							                                    DEVERR_WAIT_FULL);
 							if (!ok) break;
 							tc_fence_after();
-							mma8_ts(tmem + L::T_O + D * X, tmem + L::T_S + 128 * X, dv + (uint64_t)s * TILE16, ID_PV,
-							        np[X] > 0 ? 1u : 0u);
-							++np[X];
+							mma4_pv(tmem + L::T_O + 128 * X, tmem + L::T_S + 128 * X + 64 * b,
+							        dv + (uint64_t)s * (L::KV_TILE >> 4), ID_PV, np[X] > 0 ? 1u : 0u);
+							mma_commit(&pv_done[X]);
 							if (t == (X ? hi[1] : hi[0])) mma_commit(&o_done[X]);
+							++np[X];
 						}
-						if (next && has(X, t + 1))
+						if (ahead && has(X, t + 2))
 						{
 							if (!k_ready)
 							{
-								ok = !flags[0] && mbar_wait_bounded(&k_full[(u + 1) & 1],
-								                                    (uint32_t)(((u + 1) >> 1) & 1), P.err,
+								const int u2 = u + 2;
+								ok = !flags[0] && mbar_wait_bounded(&k_full[u2 % PF_STAGES],
+								                                    (uint32_t)((u2 / PF_STAGES) & 1), P.err,
 								                                    DEVERR_WAIT_FULL);
 								if (!ok) break;
 								tc_fence_after();
 								k_ready = true;
 							}
-							issue_s(X, u + 1);
+							issue_s(X, u + 2);
 						}
 					}
 					if (!ok) break;
 					mma_commit(&v_empty[s]);
-					if (next)
+					if (ahead)
 					{
+						const int u2 = u + 2;
 						if (!k_ready) // (every streamed tile belongs to a Q tile; kept for the ring's phases)
-							ok = mbar_wait_bounded(&k_full[(u + 1) & 1], (uint32_t)(((u + 1) >> 1) & 1), P.err,
+							ok = mbar_wait_bounded(&k_full[u2 % PF_STAGES], (uint32_t)((u2 / PF_STAGES) & 1), P.err,
 							                       DEVERR_WAIT_FULL);
-						mma_commit(&k_empty[(u + 1) & 1]);
+						mma_commit(&k_empty[u2 % PF_STAGES]);
 					}
 				}
 				if (!ok) flags[0] = 1;
@@ -358,7 +369,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 		const int X = (warp - 4) >> 2, wq = warp & 3;
 		const int r = wq * 32 + lane;
 		const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
-		const uint32_t ts = tmem + L::T_S + 128 * X + lane_off, to = tmem + L::T_O + D * X + lane_off;
+		const uint32_t ts0 = tmem + L::T_S + 128 * X + lane_off, to = tmem + L::T_O + 128 * X + lane_off;
 		const int row = q0 + X * PF_BM + r;
 		const int qp = P.pos0 + row;
 		const int kf = (P.window > 0 && qp + 1 > P.window) ? qp + 1 - P.window : 0;
@@ -369,7 +380,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 		const int t_lo = X ? lo[1] : lo[0], t_hi = X ? hi[1] : hi[0];
 		for (int t = t_lo; t <= t_hi; ++t, ++n)
 		{
-			ok = ok && !flags[0] && mbar_wait_bounded(&s_full[X], (uint32_t)(n & 1), P.err, DEVERR_WAIT_FULL);
+			const int b = n & 1;
+			const uint32_t ts = ts0 + 64 * b;
+			ok = ok && !flags[0] &&
+			     mbar_wait_bounded(&s_full[2 * X + b], (uint32_t)((n >> 1) & 1), P.err, DEVERR_WAIT_FULL);
 			if (!__all_sync(0xffffffffu, ok))
 			{
 				ok = false;
@@ -377,8 +391,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			}
 			tc_fence_after();
 			float x[PF_BN];
-#pragma unroll
-			for (int c = 0; c < PF_BN; c += 32) tmem_ld32(ts + c, x + c);
+			tmem_ld32(ts, x);
+			tmem_ld32(ts + 32, x + 32);
 			tmem_wait_ld();
 			// scores in log2 units: sl * s, folded into the exponentials' FMA
 			// (sl > 0 keeps the maximum's place); with a soft-cap, capped first
@@ -397,9 +411,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 				for (int c = 0; c < PF_BN; ++c)
 					if (key0 + c < kf || key0 + c > kl) x[c] = -CUDART_INF_F;
 			}
-			// P into the first 64 columns of S as 16-bit pairs (S is in
-			// registers), p = 2^(x sl + nm); with `track`, the largest exponent
-			// x sl + nm is returned
+			// P into the first 32 columns of this S buffer as 16-bit pairs (S is
+			// in registers), p = 2^(x sl + nm); with `track`, the largest
+			// exponent x sl + nm is returned
 			float ls[4];
 			auto write_p = [&](float nm, bool track) -> float {
 				float mq[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
@@ -446,10 +460,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			else
 			{
 				// the usual tile: the exponentials against the held maximum, the
-				// tile's own maximum found on the way (no separate pass over the
-				// scores); a row whose scores passed the held maximum by more
-				// than 2^LAZY moves it and writes its P again (rare after a row's
-				// first tiles)
+				// tile's own maximum found on the way; a row whose scores passed
+				// the held maximum by more than 2^LAZY moves it and writes its P
+				// again (rare after a row's first tiles)
 				const float top = write_p(-m_used, true);
 				const bool move = top > LAZY;
 				if (__any_sync(0xffffffffu, move))
@@ -460,9 +473,20 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 				}
 			}
 			const float alpha = rescale ? ex2(m_used - m_new) : 1.0f;
-			// O holds every P V before this tile's (their S came first)
 			if (__any_sync(0xffffffffu, rescale))
 			{
+				// O must hold every P V before this tile's: wait for the last
+				// one (a row rescales only after its first tile, so n >= 1; S of
+				// this tile completed after P V of tile n - 2, so pv_done is at
+				// most one phase behind and its parity wait cannot alias)
+				bool done = !flags[0] && mbar_wait_bounded(&pv_done[X], (uint32_t)((n - 1) & 1), P.err,
+				                                          DEVERR_WAIT_FULL);
+				if (!__all_sync(0xffffffffu, done))
+				{
+					ok = false;
+					break;
+				}
+				tc_fence_after();
 #pragma unroll
 				for (int c = 0; c < D; c += 32)
 				{
@@ -478,9 +502,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 			l = fmaf(l, alpha, (ls[0] + ls[1]) + (ls[2] + ls[3]));
 			m_used = m_new;
 			tc_fence_before();
-			mbar_arrive(&p_full[X]);
+			mbar_arrive(&p_full[2 * X + b]);
 		}
-		// the output: O / l once the tile's last P V is done
+		// the output: O / l once the tile's last P V is done (its own barrier:
+		// the softmax may finish its last tile while the P V before it still
+		// runs, two phases of pv_done behind, where a parity wait would alias)
 		if (ok && n > 0) ok = !flags[0] && mbar_wait_bounded(&o_done[X], 0, P.err, DEVERR_WAIT_FULL);
 		if (__all_sync(0xffffffffu, ok) && n > 0)
 		{
@@ -711,16 +737,16 @@ int launch_prefill(const DevJob& j, void* qbuf, int* err, void* stream)
 	auto st = static_cast<cudaStream_t>(stream);
 	CUtensorMap qmap, kmap, vmap;
 	int e = make_map(&qmap, qbuf, (uint64_t)j.n_tok, (uint64_t)j.n_head);
-	if (!e) e = make_map(&kmap, j.K, (uint64_t)j.rows, (uint64_t)j.n_kv);
-	if (!e) e = make_map(&vmap, j.V, (uint64_t)j.rows, (uint64_t)j.n_kv);
+	if (!e) e = make_tensor_map(&kmap, j.K, true, PF_D, (uint64_t)j.rows, (uint64_t)j.n_kv, PF_BN);
+	if (!e) e = make_tensor_map(&vmap, j.V, true, PF_D, (uint64_t)j.rows, (uint64_t)j.n_kv, PF_BN);
 	if (e) return e;
 	cudaError_t ce;
 	static bool configured[64] = {};
 	int dev = 0;
 	cudaGetDevice(&dev);
 	if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-	auto kernel = prefill_kernel<PF_D, true>;
-	constexpr int smem = PfLayout<PF_D>::SMEM;
+	auto kernel = prefill_kernel<true>;
+	constexpr int smem = PfLayout::SMEM;
 	if (!configured[dev])
 	{
 		ce = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
