@@ -104,6 +104,34 @@ int nncu_rope_dev(float* x, uint32_t n_tok, uint32_t n_heads, uint32_t head_dim,
 /* nnc_softcap_f32 (nn_ops.h:312). */
 int nncu_softcap_dev(float* y, const float* x, size_t n, float cap, void* stream);
 
+/* ---- the projections' gemvs (src/libnnc/nn_ops.h:89-170), device pointers --
+ * n_batch vectors of cols floats x_stride apart in X, n_batch outputs of rows
+ * floats y_stride apart in Y (n_batch 1 is the single-vector call); fp32
+ * accumulation, asynchronous on `stream`. */
+/* nnc_gemv_bf16w_f32x_batch (nn_ops.h:155-157): W BF16 [rows][cols]. */
+int nncu_gemv_bf16w_f32x_batch_dev(const void* W, const float* X, size_t x_stride, float* Y, size_t y_stride,
+                                   uint32_t rows, uint32_t cols, uint32_t n_batch, void* stream);
+/* nnc_gemv_q8_0_f32x_batch (nn_ops.h:159-162): qs int8 [rows][cols] (16-byte
+ * aligned), scales BF16 [rows][cols / 32]; cols a multiple of 32. */
+int nncu_gemv_q8_0_f32x_batch_dev(const int8_t* qs, const uint16_t* scales, const float* X, size_t x_stride,
+                                  float* Y, size_t y_stride, uint32_t rows, uint32_t cols, uint32_t n_batch,
+                                  void* stream);
+/* nnc_gemv_q4_s_f32x_batch (nn_ops.h:166-170): qs packed nibbles [rows][cols
+ * / 2] (16-byte aligned; byte k of a 32-block holds element k low and k + 16
+ * high), scales and biases BF16 [rows][cols / 32], XSUM the vectors' block
+ * sums (nncu_block_sums_dev) xsum_stride apart; cols a multiple of 32. */
+int nncu_gemv_q4_s_f32x_batch_dev(const uint8_t* qs, const uint16_t* scales, const uint16_t* biases,
+                                  const float* X, size_t x_stride, const float* XSUM, size_t xsum_stride, float* Y,
+                                  size_t y_stride, uint32_t rows, uint32_t cols, uint32_t n_batch, void* stream);
+/* nnc_block_sums_f32 (nn_ops.h:142): out[b] = sum of x[32 b .. 32 b + 31]. */
+int nncu_block_sums_dev(const float* x, float* out, size_t n, void* stream);
+/* nnc_gemv_bf16w_argmax_f32x (nn_ops.h:98-115), the greedy lm_head: writes to
+ * *out_index (device) the first index of the largest y[r] = W[r] . x without
+ * writing y; `scratch` is 8 bytes of device memory the call uses (cleared on
+ * the stream first), so calls sharing one scratch must not overlap. */
+int nncu_gemv_bf16w_argmax_dev(const void* W, const float* x, uint32_t rows, uint32_t cols,
+                               unsigned long long* scratch, int32_t* out_index, void* stream);
+
 /* ---- the HBM K/V cache ------------------------------------------------------
  * Replaces model_kv_buffer / model_kv_cache storage (model.h:231-326),
  * model_kv_init (model.cpp:1891-2040) and model_kv_rewind (model.cpp:

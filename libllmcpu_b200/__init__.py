@@ -32,7 +32,8 @@ __all__ = [
     "NnncError", "lib", "LIB_PATH", "host_register", "host_unregister", "KV_BF16", "KV_F32", "KV_F16", "ROPE_NEOX", "ROPE_NORM",
     "ATTN_BLOCK", "AttnParams", "AttnJob", "LayerDesc", "KVCache", "kv_plan", "job", "attn_span", "params",
     "attn_block_dev", "attn_merge_dev", "attn_finish_dev", "rmsnorm_gamma_multi_dev", "rmsnorm_dev",
-    "rope_dev", "softcap_dev", "EXPORTS",
+    "rope_dev", "softcap_dev", "gemv_bf16w_dev", "gemv_q8_0_dev", "gemv_q4_s_dev", "block_sums_dev",
+    "gemv_bf16w_argmax_dev", "EXPORTS",
 ]
 
 PKG = os.path.dirname(os.path.abspath(__file__))
@@ -56,6 +57,8 @@ EXPORTS = [
     "nncu_group_handle", "nncu_group_open", "nncu_group_output", "nncu_group_copy_output", "nncu_group_free",
     "nncu_attention_split_dev", "nncu_group_set_timeout", "nncu_group_reset", "nncu_group_inject_drop",
     "nncu_noalloc_check", "nncu_kv_set_tensor_cores", "nncu_host_register", "nncu_host_unregister",
+    "nncu_gemv_bf16w_f32x_batch_dev", "nncu_gemv_q8_0_f32x_batch_dev", "nncu_gemv_q4_s_f32x_batch_dev",
+    "nncu_block_sums_dev", "nncu_gemv_bf16w_argmax_dev",
 ]
 GROUP_HANDLE_BYTES = 64
 
@@ -182,6 +185,12 @@ def lib() -> C.CDLL:
     L.nncu_rope_dev.argtypes = [vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int32, f, f, C.c_int, vp,
                                 vp]
     L.nncu_softcap_dev.argtypes = [vp, vp, sz, f, vp]
+    u32 = C.c_uint32
+    L.nncu_gemv_bf16w_f32x_batch_dev.argtypes = [vp, vp, sz, vp, sz, u32, u32, u32, vp]
+    L.nncu_gemv_q8_0_f32x_batch_dev.argtypes = [vp, vp, vp, sz, vp, sz, u32, u32, u32, vp]
+    L.nncu_gemv_q4_s_f32x_batch_dev.argtypes = [vp, vp, vp, vp, sz, vp, sz, vp, sz, u32, u32, u32, vp]
+    L.nncu_block_sums_dev.argtypes = [vp, vp, sz, vp]
+    L.nncu_gemv_bf16w_argmax_dev.argtypes = [vp, vp, u32, u32, vp, vp, vp]
     L.nncu_kv_plan.argtypes = [C.POINTER(LayerDesc), i32, C.POINTER(KVParams), C.POINTER(KVLayerInfo),
                                C.POINTER(i32), C.POINTER(sz)]
     L.nncu_kv_create.argtypes = [C.POINTER(LayerDesc), i32, C.POINTER(KVParams), C.POINTER(vp)]
@@ -443,6 +452,33 @@ def rope_dev(x, n_tok, n_heads, head_dim, n_rot, pos0, pos_scale, freq_base, mod
 
 def softcap_dev(y, x, n, cap, stream=None):
     _check(lib().nncu_softcap_dev(_ptr(y), _ptr(x), n, cap, _stream(stream)))
+
+
+def gemv_bf16w_dev(W, X, Y, rows, cols, n_batch=1, x_stride=None, y_stride=None, stream=None):
+    """nnc_gemv_bf16w_f32x_batch on device buffers (tensors or pointers)."""
+    _check(lib().nncu_gemv_bf16w_f32x_batch_dev(_ptr(W), _ptr(X), x_stride or cols, _ptr(Y), y_stride or rows, rows,
+                                                cols, n_batch, _stream(stream)))
+
+
+def gemv_q8_0_dev(qs, scales, X, Y, rows, cols, n_batch=1, x_stride=None, y_stride=None, stream=None):
+    _check(lib().nncu_gemv_q8_0_f32x_batch_dev(_ptr(qs), _ptr(scales), _ptr(X), x_stride or cols, _ptr(Y),
+                                               y_stride or rows, rows, cols, n_batch, _stream(stream)))
+
+
+def gemv_q4_s_dev(qs, scales, biases, X, XSUM, Y, rows, cols, n_batch=1, x_stride=None, xsum_stride=None,
+                  y_stride=None, stream=None):
+    _check(lib().nncu_gemv_q4_s_f32x_batch_dev(_ptr(qs), _ptr(scales), _ptr(biases), _ptr(X), x_stride or cols,
+                                               _ptr(XSUM), xsum_stride or cols // 32, _ptr(Y), y_stride or rows,
+                                               rows, cols, n_batch, _stream(stream)))
+
+
+def block_sums_dev(x, out, n, stream=None):
+    _check(lib().nncu_block_sums_dev(_ptr(x), _ptr(out), n, _stream(stream)))
+
+
+def gemv_bf16w_argmax_dev(W, x, rows, cols, scratch, out_index, stream=None):
+    _check(lib().nncu_gemv_bf16w_argmax_dev(_ptr(W), _ptr(x), rows, cols, _ptr(scratch), _ptr(out_index),
+                                            _stream(stream)))
 
 
 # ---- one sequence split over the GPUs of a node (nncu_group) ----------------------------------

@@ -1,0 +1,339 @@
+// k_gemv.cu -- the projections' gemvs on the device: libnnc's weight formats
+// (nn_ops.h:89-174) times fp32 activations, one vector or a batch of them.
+//
+//   BF16   y[r] = sum_k bf16(W[r, k]) x[k]                      (nnc_gemv_bf16w_f32x)
+//   Q8_0   y[r] = sum_b scale[r, b] sum_{k in b} q[r, k] x[k]   (nnc_gemv_q8_0_f32x)
+//   Q4_S   y[r] = sum_b scale[r, b] sum_{k in b} q[r, k] x[k]
+//                 + sum_b bias[r, b] xsum[b]                    (nnc_gemv_q4_s_f32x)
+//
+// with 32-element blocks b, int8 q for Q8_0, and for Q4_S unsigned nibbles,
+// byte k of a block holding element k (low nibble) and element k + 16 (high)
+// (nnc_quantize_f32_to_q4_s, nn_ops.cpp:1252-1288); scales and biases are
+// BF16, row-major [rows][cols / 32]. The batched forms (nn_ops.h:146-170)
+// take n_batch vectors x_stride floats apart and write n_batch outputs
+// y_stride floats apart. Also the streaming gemv + argmax of the greedy
+// lm_head (nnc_gemv_bf16w_argmax_f32x, nn_ops.h:98-115): the index of the
+// largest y[r], the first one on ties, without writing y.
+//
+// The work is the weight stream: one warp per row at a time, each lane
+// taking 16 bytes of the row per step (8 BF16 weights, 16 int8 weights, or
+// one whole Q4_S block), several steps' loads in flight, up to 8 vectors of
+// the batch per pass over the weights (a larger batch makes more passes).
+// fp32 accumulation; the sum order differs from the reference's 8-lane FMA
+// chains (tolerance: its own tests' 1e-3 x max(1, |y|)).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "nncu.h"
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace nncu
+{
+namespace
+{
+
+constexpr int GW_THREADS = 256;
+constexpr int GW_MAXNB = 8;
+
+struct GemvArgs
+{
+	const void* w;           // BF16 weights, Q8_0 or Q4_S quants
+	const uint16_t* scales;  // Q8_0, Q4_S: BF16 [rows][cols / 32]
+	const uint16_t* biases;  // Q4_S: BF16 [rows][cols / 32]
+	const float* X;
+	size_t x_stride;
+	const float* XSUM;       // Q4_S: the vectors' block sums, cols / 32 each
+	size_t xsum_stride;
+	float* Y;
+	size_t y_stride;
+	uint32_t rows, cols, n_batch;
+	unsigned long long* best; // argmax: the running (value, index) key
+};
+
+__device__ __forceinline__ float bf16f(uint32_t h) { return __uint_as_float(h << 16); }
+
+// One row's dot products with NB vectors (the lanes' partial sums, not yet reduced).
+template <int FMT, int NB>
+__device__ __forceinline__ void row_dots(const GemvArgs& a, uint32_t r, int lane, float (&acc)[NB])
+{
+#pragma unroll
+	for (int v = 0; v < NB; ++v) acc[v] = 0.0f;
+	const uint32_t cols = a.cols;
+	if (FMT == 0)
+	{
+		const uint16_t* row = static_cast<const uint16_t*>(a.w) + (size_t)r * cols;
+		const bool vec = (cols & 7u) == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15u) == 0;
+		uint32_t k0 = 0;
+		if (vec)
+		{
+			const uint4* row4 = reinterpret_cast<const uint4*>(row);
+			const uint32_t n8 = cols / 8;
+#pragma unroll 4
+			for (uint32_t i = lane; i < n8; i += 32)
+			{
+				const uint4 w4 = __ldg(row4 + i);
+				const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+				for (int v = 0; v < NB; ++v)
+				{
+					const float* x = a.X + (size_t)v * a.x_stride + (size_t)i * 8;
+					float s = acc[v];
+#pragma unroll
+					for (int j = 0; j < 4; ++j)
+					{
+						s = fmaf(bf16f(ww[j] & 0xFFFFu), __ldg(x + 2 * j), s);
+						s = fmaf(bf16f(ww[j] >> 16), __ldg(x + 2 * j + 1), s);
+					}
+					acc[v] = s;
+				}
+			}
+			k0 = n8 * 8;
+		}
+		for (uint32_t k = k0 + lane; k < cols; k += 32)
+		{
+			const float w = bf16f(row[k]);
+#pragma unroll
+			for (int v = 0; v < NB; ++v) acc[v] = fmaf(w, __ldg(a.X + (size_t)v * a.x_stride + k), acc[v]);
+		}
+	}
+	else if (FMT == 1)
+	{
+		// 16 int8 weights per lane step: half a block, one scale
+		const uint4* row4 = reinterpret_cast<const uint4*>(static_cast<const int8_t*>(a.w) + (size_t)r * cols);
+		const uint16_t* sc = a.scales + (size_t)r * (cols / 32);
+		const uint32_t n16 = cols / 16;
+#pragma unroll 4
+		for (uint32_t i = lane; i < n16; i += 32)
+		{
+			const uint4 q4 = __ldg(row4 + i);
+			const float s = bf16f(__ldg(sc + i / 2));
+			const uint32_t qq[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+			for (int v = 0; v < NB; ++v)
+			{
+				const float* x = a.X + (size_t)v * a.x_stride + (size_t)i * 16;
+				float d = 0.0f;
+#pragma unroll
+				for (int j = 0; j < 4; ++j)
+#pragma unroll
+					for (int b = 0; b < 4; ++b)
+						d = fmaf((float)(int8_t)(qq[j] >> (8 * b)), __ldg(x + 4 * j + b), d);
+				acc[v] = fmaf(s, d, acc[v]);
+			}
+		}
+	}
+	else
+	{
+		// one whole block (16 bytes, 32 nibbles) per lane step
+		const uint4* row4 = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.w) + (size_t)r * (cols / 2));
+		const uint32_t nb = cols / 32;
+		const uint16_t* sc = a.scales + (size_t)r * nb;
+		const uint16_t* bi = a.biases + (size_t)r * nb;
+#pragma unroll 2
+		for (uint32_t b = lane; b < nb; b += 32)
+		{
+			const uint4 q4 = __ldg(row4 + b);
+			const float s = bf16f(__ldg(sc + b)), bias = bf16f(__ldg(bi + b));
+			const uint32_t qq[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+			for (int v = 0; v < NB; ++v)
+			{
+				const float* x = a.X + (size_t)v * a.x_stride + (size_t)b * 32;
+				float d = 0.0f;
+#pragma unroll
+				for (int j = 0; j < 4; ++j)
+#pragma unroll
+					for (int t = 0; t < 4; ++t)
+					{
+						const uint32_t byte = (qq[j] >> (8 * t)) & 0xFFu; // byte k = 4 j + t
+						d = fmaf((float)(byte & 0x0Fu), __ldg(x + 4 * j + t), d);
+						d = fmaf((float)(byte >> 4), __ldg(x + 4 * j + t + 16), d);
+					}
+				acc[v] = fmaf(s, d, fmaf(bias, __ldg(a.XSUM + (size_t)v * a.xsum_stride + b), acc[v]));
+			}
+		}
+	}
+}
+
+template <int FMT, int NB>
+__global__ void __launch_bounds__(GW_THREADS) gemv_kernel(const GemvArgs a, uint32_t v0)
+{
+	const int lane = threadIdx.x & 31;
+	const uint32_t warps = gridDim.x * (GW_THREADS / 32);
+	GemvArgs b = a;
+	b.X = a.X + (size_t)v0 * a.x_stride;
+	if (FMT == 2) b.XSUM = a.XSUM + (size_t)v0 * a.xsum_stride;
+	for (uint32_t r = blockIdx.x * (GW_THREADS / 32) + (threadIdx.x >> 5); r < a.rows; r += warps)
+	{
+		float acc[NB];
+		row_dots<FMT, NB>(b, r, lane, acc);
+#pragma unroll
+		for (int v = 0; v < NB; ++v)
+		{
+			const float y = warp_sum(acc[v]);
+			if (lane == 0) a.Y[(size_t)(v0 + v) * a.y_stride + r] = y;
+		}
+	}
+}
+
+// A float's order as an unsigned key: larger floats, larger keys.
+__device__ __forceinline__ uint32_t order_key(float f)
+{
+	const uint32_t u = __float_as_uint(f);
+	return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Greedy lm_head: every warp keeps its best (value, first index) and the
+// CTA's best goes into one 64-bit atomic max: value key high, ~index low,
+// so the larger value wins and, on a tie, the smaller index.
+__global__ void __launch_bounds__(GW_THREADS) gemv_argmax_kernel(const GemvArgs a)
+{
+	__shared__ unsigned long long s_best[GW_THREADS / 32];
+	const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+	const uint32_t warps = gridDim.x * (GW_THREADS / 32);
+	unsigned long long best = 0;
+	for (uint32_t r = blockIdx.x * (GW_THREADS / 32) + warp; r < a.rows; r += warps)
+	{
+		float acc[1];
+		row_dots<0, 1>(a, r, lane, acc);
+		const float y = warp_sum(acc[0]);
+		if (y == y) // NaN never wins
+		{
+			const unsigned long long key = ((unsigned long long)order_key(y) << 32) | (0xFFFFFFFFu - r);
+			best = key > best ? key : best;
+		}
+	}
+	if (lane == 0) s_best[warp] = best;
+	__syncthreads();
+	if (threadIdx.x == 0)
+	{
+		for (int w = 1; w < GW_THREADS / 32; ++w) best = s_best[w] > best ? s_best[w] : best;
+		if (best) atomicMax(a.best, best);
+	}
+}
+
+__global__ void argmax_finish_kernel(const unsigned long long* best, int32_t* out)
+{
+	const unsigned long long b = *best;
+	*out = b ? (int32_t)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFu)) : -1;
+}
+
+// out[b] = sum of x[32 b .. 32 b + 31]: a warp per block.
+__global__ void block_sums_kernel(const float* x, float* out, size_t nb)
+{
+	const size_t b = (size_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+	if (b >= nb) return;
+	const float s = warp_sum(x[b * 32 + (threadIdx.x & 31)]);
+	if ((threadIdx.x & 31) == 0) out[b] = s;
+}
+
+int grid_for(uint32_t rows)
+{
+	int dev = 0, sms = 148;
+	cudaGetDevice(&dev);
+	cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+	const uint32_t want = (rows + GW_THREADS / 32 - 1) / (GW_THREADS / 32);
+	return (int)(want < (uint32_t)(sms * 8) ? want : (uint32_t)(sms * 8));
+}
+
+template <int FMT>
+int launch_gemv_fmt(const GemvArgs& a, cudaStream_t st)
+{
+	const int grid = grid_for(a.rows);
+	for (uint32_t v0 = 0; v0 < a.n_batch;)
+	{
+		const uint32_t left = a.n_batch - v0;
+		if (left >= 8)
+			gemv_kernel<FMT, 8><<<grid, GW_THREADS, 0, st>>>(a, v0), v0 += 8;
+		else if (left >= 4)
+			gemv_kernel<FMT, 4><<<grid, GW_THREADS, 0, st>>>(a, v0), v0 += 4;
+		else if (left >= 2)
+			gemv_kernel<FMT, 2><<<grid, GW_THREADS, 0, st>>>(a, v0), v0 += 2;
+		else
+			gemv_kernel<FMT, 1><<<grid, GW_THREADS, 0, st>>>(a, v0), v0 += 1;
+		note_launches(1);
+	}
+	return (int)cudaGetLastError();
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+} // namespace
+} // namespace nncu
+
+using namespace nncu;
+
+extern "C" int nncu_gemv_bf16w_f32x_batch_dev(const void* W, const float* X, size_t x_stride, float* Y,
+                                              size_t y_stride, uint32_t rows, uint32_t cols, uint32_t n_batch,
+                                              void* stream)
+{
+	if (rows == 0 || cols == 0 || n_batch == 0) return NNCU_OK;
+	if (!W || !X || !Y) return set_error(NNCU_ERR_INVALID_ARGUMENT, "gemv: NULL weights, input or output");
+	if (n_batch > 1 && (x_stride < cols || y_stride < rows))
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "gemv: strides shorter than a vector");
+	GemvArgs a{W, nullptr, nullptr, X, x_stride, nullptr, 0, Y, y_stride, rows, cols, n_batch, nullptr};
+	const int e = launch_gemv_fmt<0>(a, static_cast<cudaStream_t>(stream));
+	return e ? set_cuda_error(e, "gemv launch") : NNCU_OK;
+}
+
+extern "C" int nncu_gemv_q8_0_f32x_batch_dev(const int8_t* qs, const uint16_t* scales, const float* X,
+                                             size_t x_stride, float* Y, size_t y_stride, uint32_t rows,
+                                             uint32_t cols, uint32_t n_batch, void* stream)
+{
+	if (rows == 0 || cols == 0 || n_batch == 0) return NNCU_OK;
+	if (!qs || !scales || !X || !Y) return set_error(NNCU_ERR_INVALID_ARGUMENT, "gemv: NULL weights, input or output");
+	if (cols % 32) return set_error(NNCU_ERR_INVALID_ARGUMENT, "Q8_0 gemv: cols must be a multiple of 32");
+	if (!aligned16(qs)) return set_error(NNCU_ERR_INVALID_ARGUMENT, "Q8_0 gemv: quants must be 16-byte aligned");
+	if (n_batch > 1 && (x_stride < cols || y_stride < rows))
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "gemv: strides shorter than a vector");
+	GemvArgs a{qs, scales, nullptr, X, x_stride, nullptr, 0, Y, y_stride, rows, cols, n_batch, nullptr};
+	const int e = launch_gemv_fmt<1>(a, static_cast<cudaStream_t>(stream));
+	return e ? set_cuda_error(e, "gemv launch") : NNCU_OK;
+}
+
+extern "C" int nncu_gemv_q4_s_f32x_batch_dev(const uint8_t* qs, const uint16_t* scales, const uint16_t* biases,
+                                             const float* X, size_t x_stride, const float* XSUM, size_t xsum_stride,
+                                             float* Y, size_t y_stride, uint32_t rows, uint32_t cols,
+                                             uint32_t n_batch, void* stream)
+{
+	if (rows == 0 || cols == 0 || n_batch == 0) return NNCU_OK;
+	if (!qs || !scales || !biases || !X || !XSUM || !Y)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "gemv: NULL weights, input, block sums or output");
+	if (cols % 32) return set_error(NNCU_ERR_INVALID_ARGUMENT, "Q4_S gemv: cols must be a multiple of 32");
+	if (!aligned16(qs)) return set_error(NNCU_ERR_INVALID_ARGUMENT, "Q4_S gemv: quants must be 16-byte aligned");
+	if (n_batch > 1 && (x_stride < cols || y_stride < rows || xsum_stride < cols / 32))
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "gemv: strides shorter than a vector");
+	GemvArgs a{qs, scales, biases, X, x_stride, XSUM, xsum_stride, Y, y_stride, rows, cols, n_batch, nullptr};
+	const int e = launch_gemv_fmt<2>(a, static_cast<cudaStream_t>(stream));
+	return e ? set_cuda_error(e, "gemv launch") : NNCU_OK;
+}
+
+extern "C" int nncu_block_sums_dev(const float* x, float* out, size_t n, void* stream)
+{
+	if (n == 0 || n % 32) return set_error(NNCU_ERR_INVALID_ARGUMENT, "block sums: n must be a positive multiple of 32");
+	if (!x || !out) return set_error(NNCU_ERR_INVALID_ARGUMENT, "block sums: NULL input or output");
+	const size_t nb = n / 32;
+	block_sums_kernel<<<(unsigned)((nb + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, out, nb);
+	note_launches(1);
+	const int e = (int)cudaGetLastError();
+	return e ? set_cuda_error(e, "block sums launch") : NNCU_OK;
+}
+
+extern "C" int nncu_gemv_bf16w_argmax_dev(const void* W, const float* x, uint32_t rows, uint32_t cols,
+                                          unsigned long long* scratch, int32_t* out_index, void* stream)
+{
+	if (rows == 0 || cols == 0) return set_error(NNCU_ERR_INVALID_ARGUMENT, "argmax gemv: no rows or columns");
+	if (!W || !x || !scratch || !out_index)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "argmax gemv: NULL weights, input, scratch or output");
+	auto st = static_cast<cudaStream_t>(stream);
+	cudaError_t ce = cudaMemsetAsync(scratch, 0, sizeof(unsigned long long), st);
+	if (ce != cudaSuccess) return set_cuda_error((int)ce, "argmax scratch clear");
+	GemvArgs a{W, nullptr, nullptr, x, cols, nullptr, 0, nullptr, 0, rows, cols, 1, scratch};
+	gemv_argmax_kernel<<<grid_for(rows), GW_THREADS, 0, st>>>(a);
+	argmax_finish_kernel<<<1, 1, 0, st>>>(scratch, out_index);
+	note_launches(2);
+	const int e = (int)cudaGetLastError();
+	return e ? set_cuda_error(e, "argmax gemv launch") : NNCU_OK;
+}

@@ -109,6 +109,13 @@ def ref():
 
 def _declare(L, pfx: str) -> None:
     vp, sz, f, i = C.c_void_p, C.c_size_t, C.c_float, C.c_int
+    u32 = C.c_uint32
+    getattr(L, f"{pfx}_gemv_bf16w").argtypes = [vp, vp, sz, vp, sz, u32, u32, u32]
+    getattr(L, f"{pfx}_gemv_q8_0").argtypes = [vp, vp, vp, sz, vp, sz, u32, u32, u32]
+    getattr(L, f"{pfx}_gemv_q4_s").argtypes = [vp, vp, vp, vp, sz, vp, sz, vp, sz, u32, u32, u32]
+    getattr(L, f"{pfx}_block_sums").argtypes = [vp, vp, sz]
+    getattr(L, f"{pfx}_gemv_bf16w_argmax").argtypes = [vp, vp, u32, u32]
+    getattr(L, f"{pfx}_gemv_bf16w_argmax").restype = C.c_int
     getattr(L, f"{pfx}_attn_span").argtypes = [i, i, i, i, C.POINTER(C.c_int), C.POINTER(C.c_int)]
     getattr(L, f"{pfx}_rmsnorm_f32").argtypes = [vp, vp, sz, f]
     getattr(L, f"{pfx}_rmsnorm_gamma_multi_f32").argtypes = [vp, vp, sz, sz, vp, f]
@@ -326,3 +333,62 @@ orc_params = params
 def ring_rows(window: int, n_batch: int) -> int:
     """round_up(window + n_batch, 256) (model.cpp:1934)."""
     return int(lib().orc_ring_rows(int(window), int(n_batch)))
+
+
+# ---- the projections' gemvs (src/libnnc/nn_ops.h:89-170) ----------------------------------------
+
+def _gemv_lib(which: str):
+    L = lib() if which == "oracle" else ref()
+    return L, ("orc" if which == "oracle" else "ref")
+
+
+def gemv_bf16w(W_bits: np.ndarray, X: np.ndarray, which: str = "oracle") -> np.ndarray:
+    """Y[v] = W X[v] for BF16 weights W_bits [rows][cols] (uint16) and fp32 X [n_batch][cols]."""
+    L, p = _gemv_lib(which)
+    rows, cols = W_bits.shape
+    X = np.ascontiguousarray(X, np.float32).reshape(-1, cols)
+    Y = np.empty((X.shape[0], rows), np.float32)
+    getattr(L, f"{p}_gemv_bf16w")(ptr(np.ascontiguousarray(W_bits)), ptr(X), cols, ptr(Y), rows, rows, cols, X.shape[0])
+    return Y
+
+
+def gemv_q8_0(qs: np.ndarray, scales: np.ndarray, X: np.ndarray, which: str = "oracle") -> np.ndarray:
+    """Q8_0 split layout: qs int8 [rows][cols], scales BF16 [rows][cols / 32]."""
+    L, p = _gemv_lib(which)
+    rows, cols = qs.shape
+    X = np.ascontiguousarray(X, np.float32).reshape(-1, cols)
+    Y = np.empty((X.shape[0], rows), np.float32)
+    getattr(L, f"{p}_gemv_q8_0")(ptr(np.ascontiguousarray(qs)), ptr(np.ascontiguousarray(scales)), ptr(X), cols,
+                                 ptr(Y), rows, rows, cols, X.shape[0])
+    return Y
+
+
+def gemv_q4_s(qs: np.ndarray, scales: np.ndarray, biases: np.ndarray, X: np.ndarray, XSUM: np.ndarray,
+              which: str = "oracle") -> np.ndarray:
+    """Q4_S split layout: qs uint8 [rows][cols / 2] (byte k of a block: element k low, k + 16 high),
+    scales and biases BF16 [rows][cols / 32], XSUM the vectors' block sums [n_batch][cols / 32]."""
+    L, p = _gemv_lib(which)
+    rows, half = qs.shape
+    cols = 2 * half
+    X = np.ascontiguousarray(X, np.float32).reshape(-1, cols)
+    XSUM = np.ascontiguousarray(XSUM, np.float32).reshape(-1, cols // 32)
+    Y = np.empty((X.shape[0], rows), np.float32)
+    getattr(L, f"{p}_gemv_q4_s")(ptr(np.ascontiguousarray(qs)), ptr(np.ascontiguousarray(scales)),
+                                 ptr(np.ascontiguousarray(biases)), ptr(X), cols, ptr(XSUM), cols // 32, ptr(Y), rows,
+                                 rows, cols, X.shape[0])
+    return Y
+
+
+def block_sums(x: np.ndarray, which: str = "oracle") -> np.ndarray:
+    L, p = _gemv_lib(which)
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    out = np.empty(x.size // 32, np.float32)
+    getattr(L, f"{p}_block_sums")(ptr(x), ptr(out), x.size)
+    return out
+
+
+def gemv_bf16w_argmax(W_bits: np.ndarray, x: np.ndarray, which: str = "oracle") -> int:
+    L, p = _gemv_lib(which)
+    rows, cols = W_bits.shape
+    x = np.ascontiguousarray(x, np.float32).ravel()
+    return int(getattr(L, f"{p}_gemv_bf16w_argmax")(ptr(np.ascontiguousarray(W_bits)), ptr(x), rows, cols))

@@ -374,3 +374,92 @@ int orc_attention_forward(const orc_attn_params* p, float* q, float* k, float* v
 		for (size_t i = 0; i < (size_t)p->n_tok * q_dim; ++i) out[i] /= 1.0f + expf(-p->gate[i]);
 	return rc;
 }
+
+/* ---- the projections' gemvs (src/libnnc/nn_ops.h:89-170) ---- */
+
+void orc_gemv_bf16w(const uint16_t* W, const float* X, size_t x_stride, float* Y, size_t y_stride, uint32_t rows,
+                    uint32_t cols, uint32_t n_batch)
+{
+	for (uint32_t v = 0; v < n_batch; ++v)
+		for (uint32_t r = 0; r < rows; ++r)
+		{
+			const uint16_t* row = W + (size_t)r * cols;
+			const float* x = X + (size_t)v * x_stride;
+			double s = 0.0;
+			for (uint32_t k = 0; k < cols; ++k) s += (double)orc_bf16_to_f32(row[k]) * x[k];
+			Y[(size_t)v * y_stride + r] = (float)s;
+		}
+}
+
+void orc_gemv_q8_0(const int8_t* qs, const uint16_t* scales, const float* X, size_t x_stride, float* Y,
+                   size_t y_stride, uint32_t rows, uint32_t cols, uint32_t n_batch)
+{
+	const uint32_t nb = cols / 32;
+	for (uint32_t v = 0; v < n_batch; ++v)
+		for (uint32_t r = 0; r < rows; ++r)
+		{
+			const float* x = X + (size_t)v * x_stride;
+			double s = 0.0;
+			for (uint32_t b = 0; b < nb; ++b)
+			{
+				double d = 0.0;
+				for (uint32_t k = 0; k < 32; ++k) d += (double)qs[(size_t)r * cols + b * 32 + k] * x[b * 32 + k];
+				s += (double)orc_bf16_to_f32(scales[(size_t)r * nb + b]) * d;
+			}
+			Y[(size_t)v * y_stride + r] = (float)s;
+		}
+}
+
+void orc_gemv_q4_s(const uint8_t* qs, const uint16_t* scales, const uint16_t* biases, const float* X, size_t x_stride,
+                   const float* XSUM, size_t xsum_stride, float* Y, size_t y_stride, uint32_t rows, uint32_t cols,
+                   uint32_t n_batch)
+{
+	const uint32_t nb = cols / 32;
+	for (uint32_t v = 0; v < n_batch; ++v)
+		for (uint32_t r = 0; r < rows; ++r)
+		{
+			const float* x = X + (size_t)v * x_stride;
+			const float* xs = XSUM + (size_t)v * xsum_stride;
+			double s = 0.0;
+			for (uint32_t b = 0; b < nb; ++b)
+			{
+				const uint8_t* blk = qs + (size_t)r * (cols / 2) + b * 16;
+				double d = 0.0;
+				for (uint32_t k = 0; k < 16; ++k)
+				{
+					d += (double)(blk[k] & 0x0F) * x[b * 32 + k];
+					d += (double)(blk[k] >> 4) * x[b * 32 + k + 16];
+				}
+				s += (double)orc_bf16_to_f32(scales[(size_t)r * nb + b]) * d +
+				     (double)orc_bf16_to_f32(biases[(size_t)r * nb + b]) * xs[b];
+			}
+			Y[(size_t)v * y_stride + r] = (float)s;
+		}
+}
+
+void orc_block_sums(const float* x, float* out, size_t n)
+{
+	for (size_t b = 0; b < n / 32; ++b)
+	{
+		double s = 0.0;
+		for (size_t k = 0; k < 32; ++k) s += x[b * 32 + k];
+		out[b] = (float)s;
+	}
+}
+
+int orc_gemv_bf16w_argmax(const uint16_t* W, const float* x, uint32_t rows, uint32_t cols)
+{
+	int best = -1;
+	float bv = 0.0f;
+	for (uint32_t r = 0; r < rows; ++r)
+	{
+		float y;
+		orc_gemv_bf16w(W + (size_t)r * cols, x, cols, &y, 1, 1, cols, 1);
+		if (best < 0 || y > bv)
+		{
+			bv = y;
+			best = (int)r;
+		}
+	}
+	return best;
+}

@@ -87,6 +87,26 @@ int orc_attention_forward(const orc_attn_params* p, float* q, float* k, float* v
 int orc_attend(const orc_attn_params* p, const float* q, const void* Kc, const void* Vc, int kv_type,
                int rows, float* out);
 
+/* The projections' gemvs (src/libnnc/nn_ops.h:89-170), batched: n_batch
+ * vectors x_stride floats apart in, y_stride apart out; sums in double (the
+ * reference's own tests' scalar checks, tests.cpp:819-880). BF16 weights
+ * (nn_ops.cpp:1000-1047); Q8_0: int8 quants, BF16 scale per 32-block
+ * (nn_ops.cpp:1352-1377); Q4_S: nibbles, byte k of a block holding element k
+ * low and k + 16 high, BF16 scale and bias per block, the bias term through
+ * the vectors' block sums xsum (nn_ops.cpp:1252-1288, 1422-1446). */
+void orc_gemv_bf16w(const uint16_t* W, const float* X, size_t x_stride, float* Y, size_t y_stride, uint32_t rows,
+                    uint32_t cols, uint32_t n_batch);
+void orc_gemv_q8_0(const int8_t* qs, const uint16_t* scales, const float* X, size_t x_stride, float* Y,
+                   size_t y_stride, uint32_t rows, uint32_t cols, uint32_t n_batch);
+void orc_gemv_q4_s(const uint8_t* qs, const uint16_t* scales, const uint16_t* biases, const float* X, size_t x_stride,
+                   const float* XSUM, size_t xsum_stride, float* Y, size_t y_stride, uint32_t rows, uint32_t cols,
+                   uint32_t n_batch);
+/* nnc_block_sums_f32 (nn_ops.cpp:1305-1316). */
+void orc_block_sums(const float* x, float* out, size_t n);
+/* nnc_gemv_bf16w_argmax_f32x (nn_ops.cpp:1055-1197): the first index of the
+ * largest y[r]. */
+int orc_gemv_bf16w_argmax(const uint16_t* W, const float* x, uint32_t rows, uint32_t cols);
+
 /* Sliding-ring sizing of model_kv_init (src/libnnc/model.cpp:1934-1955). */
 int orc_ring_rows(int window, int n_batch);
 

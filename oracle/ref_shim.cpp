@@ -122,6 +122,33 @@ void ref_attn_span(int causal, int window, int pos, int n_seq, int* first, int* 
 
 uint16_t ref_f32_to_bf16(float f) { return nnc_f32_to_bf16(f); }
 
+// The projections' gemvs and their helpers, the reference's own (nn_ops.h:89-183).
+void ref_gemv_bf16w(const void* W, const float* X, size_t x_stride, float* Y, size_t y_stride, uint32_t rows,
+                    uint32_t cols, uint32_t n_batch)
+{
+	nnc_gemv_bf16w_f32x_batch(W, X, x_stride, Y, y_stride, rows, cols, n_batch);
+}
+void ref_gemv_q8_0(const int8_t* qs, const uint16_t* scales, const float* X, size_t x_stride, float* Y,
+                   size_t y_stride, uint32_t rows, uint32_t cols, uint32_t n_batch)
+{
+	nnc_gemv_q8_0_f32x_batch(qs, scales, X, x_stride, Y, y_stride, rows, cols, n_batch);
+}
+void ref_gemv_q4_s(const uint8_t* qs, const uint16_t* scales, const uint16_t* biases, const float* X, size_t x_stride,
+                   const float* XSUM, size_t xsum_stride, float* Y, size_t y_stride, uint32_t rows, uint32_t cols,
+                   uint32_t n_batch)
+{
+	nnc_gemv_q4_s_f32x_batch(qs, scales, biases, X, x_stride, XSUM, xsum_stride, Y, y_stride, rows, cols, n_batch);
+}
+void ref_block_sums(const float* x, float* out, size_t n) { nnc_block_sums_f32(x, out, n); }
+int ref_gemv_bf16w_argmax(const void* W, const float* x, uint32_t rows, uint32_t cols)
+{
+	return nnc_gemv_bf16w_argmax_f32x(W, x, rows, cols);
+}
+void ref_quantize_f32_to_q4_s(const float* src, uint8_t* qs, uint16_t* scales, uint16_t* biases, size_t n)
+{
+	nnc_quantize_f32_to_q4_s(src, qs, scales, biases, n);
+}
+
 void ref_rmsnorm_f32(float* y, const float* x, size_t n, float eps) { nnc_rmsnorm_f32(y, x, n, eps); }
 
 void ref_rmsnorm_gamma_multi_f32(float* y, const float* x, size_t n_groups, size_t dim, const float* gamma, float eps)

@@ -256,3 +256,58 @@ def test_restatement_vs_reference_scenarios(name):
             # values ~N(0,1), where RoPE's a*c - b*s may cancel)
             step, floor = (2.0 ** -7, 1e-2) if case.kv_type == O.KV_BF16 else (2.0 ** -20, 1.0)
             assert np.all(np.abs(ka - kb) <= step * np.maximum(np.abs(kb), floor)), (name, owner)
+
+
+# ---- the projections' gemvs: the restatement against the reference's own ----------------------
+
+GEMV_SHAPES = [(1, 32, 1), (8, 64, 1), (64, 128, 3), (256, 256, 2), (512, 512, 1), (1024, 2048, 4)]
+
+
+def _gemv_inputs(rows, cols, nb, seed):
+    rng = np.random.default_rng(seed)
+    W = O.f32_to_bf16_bits(rng.uniform(-1, 1, (rows, cols)).astype(np.float32))
+    X = rng.uniform(-1, 1, (nb, cols)).astype(np.float32)
+    qs8 = rng.integers(-128, 128, (rows, cols), dtype=np.int8)
+    sc = O.f32_to_bf16_bits((rng.random((rows, cols // 32)) * 0.02).astype(np.float32))
+    qs4 = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
+    bi = O.f32_to_bf16_bits((rng.uniform(-1, 1, (rows, cols // 32)) * 0.1).astype(np.float32))
+    return W, X, qs8, sc, qs4, bi
+
+
+def _close(got, want):
+    # the reference's own gemv tests: 1e-3 x max(1, |ref|) (tests.cpp:819-880)
+    return np.all(np.abs(got - want) <= 1e-3 * np.maximum(1.0, np.abs(want)))
+
+
+@needs_ref
+@pytest.mark.parametrize("rows,cols,nb", GEMV_SHAPES)
+def test_gemv_restatement_matches_reference(rows, cols, nb):
+    """nnc_gemv_{bf16w,q8_0,q4_s}_f32x_batch, nnc_block_sums_f32 and
+    nnc_gemv_bf16w_argmax_f32x (nn_ops.cpp:1000-1446), compiled from the
+    reference's sources, against the plain-C restatement on the shapes of the
+    reference's own gemv tests."""
+    W, X, qs8, sc, qs4, bi = _gemv_inputs(rows, cols, nb, rows * 7 + cols)
+    assert _close(O.gemv_bf16w(W, X), O.gemv_bf16w(W, X, "ref"))
+    assert _close(O.gemv_q8_0(qs8, sc, X), O.gemv_q8_0(qs8, sc, X, "ref"))
+    xs_ref = np.stack([O.block_sums(x, "ref") for x in X])
+    xs = np.stack([O.block_sums(x) for x in X])
+    assert np.allclose(xs, xs_ref, rtol=1e-5, atol=1e-5)
+    assert _close(O.gemv_q4_s(qs4, sc, bi, X, xs_ref), O.gemv_q4_s(qs4, sc, bi, X, xs_ref, "ref"))
+    assert O.gemv_bf16w_argmax(W, X[0]) == O.gemv_bf16w_argmax(W, X[0], "ref")
+
+
+def test_gemv_restatement_scalar_cases():
+    # hand-checkable: one row, one block
+    W = O.f32_to_bf16_bits(np.arange(32, dtype=np.float32))
+    x = np.ones(32, np.float32)
+    assert O.gemv_bf16w(W.reshape(1, 32), x)[0, 0] == sum(range(32))
+    qs = np.arange(-16, 16, dtype=np.int8).reshape(1, 32)
+    sc = O.f32_to_bf16_bits(np.array([[0.5]], np.float32))
+    assert O.gemv_q8_0(qs, sc, x)[0, 0] == 0.5 * sum(range(-16, 16))
+    q4 = np.array([[k | (15 - k) << 4 for k in range(16)]], np.uint8)  # element k: k, element k + 16: 15 - k
+    bi = O.f32_to_bf16_bits(np.array([[2.0]], np.float32))
+    xs = O.block_sums(x)
+    assert O.gemv_q4_s(q4, sc, bi, x, xs)[0, 0] == 0.5 * (sum(range(16)) + sum(15 - k for k in range(16))) + 2.0 * 32
+    # argmax: the first of equal maxima
+    W2 = O.f32_to_bf16_bits(np.array([[1.0] * 32, [2.0] * 32, [2.0] * 32], np.float32))
+    assert O.gemv_bf16w_argmax(W2, x) == 1
