@@ -54,17 +54,34 @@ struct GemvArgs
 
 __device__ __forceinline__ float bf16f(uint32_t h) { return __uint_as_float(h << 16); }
 
-// One row's dot products with NB vectors (the lanes' partial sums, not yet reduced).
+// Small unsigned integers to floats on the integer and FMA pipes (the
+// conversion instruction is a quarter-rate one): the byte permute builds the
+// bit pattern of 2^23 + n (n in [0, 255] in the low mantissa bits), then one
+// subtract of 2^23 leaves exactly n.
+__device__ __forceinline__ float byte_as_float(uint32_t word, uint32_t sel)
+{
+	uint32_t r;
+	asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(word), "r"(0x4B000000u), "r"(sel));
+	return __uint_as_float(r) - 8388608.0f;
+}
+// byte i of `word` (as 0..255) into the low byte, zeros above, then 0x4B at the top
+__device__ __forceinline__ uint32_t sel_byte(int i) { return 0x7440u | (uint32_t)i; }
+
+__device__ __forceinline__ float4 ldx4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// One row's dot products with NB vectors (the lanes' partial sums, not yet
+// reduced). X rows are read as float4 where the vectors are 16-byte aligned.
 template <int FMT, int NB>
 __device__ __forceinline__ void row_dots(const GemvArgs& a, uint32_t r, int lane, float (&acc)[NB])
 {
 #pragma unroll
 	for (int v = 0; v < NB; ++v) acc[v] = 0.0f;
 	const uint32_t cols = a.cols;
+	const bool x4 = (reinterpret_cast<uintptr_t>(a.X) & 15u) == 0 && (NB == 1 || (a.x_stride & 3u) == 0);
 	if (FMT == 0)
 	{
 		const uint16_t* row = static_cast<const uint16_t*>(a.w) + (size_t)r * cols;
-		const bool vec = (cols & 7u) == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15u) == 0;
+		const bool vec = x4 && (cols & 7u) == 0 && (reinterpret_cast<uintptr_t>(a.w) & 15u) == 0;
 		uint32_t k0 = 0;
 		if (vec)
 		{
@@ -74,18 +91,24 @@ __device__ __forceinline__ void row_dots(const GemvArgs& a, uint32_t r, int lane
 			for (uint32_t i = lane; i < n8; i += 32)
 			{
 				const uint4 w4 = __ldg(row4 + i);
-				const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+				const float w[8] = {__uint_as_float(w4.x << 16), __uint_as_float(w4.x & 0xFFFF0000u),
+				                    __uint_as_float(w4.y << 16), __uint_as_float(w4.y & 0xFFFF0000u),
+				                    __uint_as_float(w4.z << 16), __uint_as_float(w4.z & 0xFFFF0000u),
+				                    __uint_as_float(w4.w << 16), __uint_as_float(w4.w & 0xFFFF0000u)};
 #pragma unroll
 				for (int v = 0; v < NB; ++v)
 				{
 					const float* x = a.X + (size_t)v * a.x_stride + (size_t)i * 8;
+					const float4 xa = ldx4(x), xb = ldx4(x + 4);
 					float s = acc[v];
-#pragma unroll
-					for (int j = 0; j < 4; ++j)
-					{
-						s = fmaf(bf16f(ww[j] & 0xFFFFu), __ldg(x + 2 * j), s);
-						s = fmaf(bf16f(ww[j] >> 16), __ldg(x + 2 * j + 1), s);
-					}
+					s = fmaf(w[0], xa.x, s);
+					s = fmaf(w[1], xa.y, s);
+					s = fmaf(w[2], xa.z, s);
+					s = fmaf(w[3], xa.w, s);
+					s = fmaf(w[4], xb.x, s);
+					s = fmaf(w[5], xb.y, s);
+					s = fmaf(w[6], xb.z, s);
+					s = fmaf(w[7], xb.w, s);
 					acc[v] = s;
 				}
 			}
@@ -100,33 +123,51 @@ __device__ __forceinline__ void row_dots(const GemvArgs& a, uint32_t r, int lane
 	}
 	else if (FMT == 1)
 	{
-		// 16 int8 weights per lane step: half a block, one scale
+		// 16 int8 weights per lane step: half a block, one scale. A weight q
+		// is taken as (q + 128) - 128: the sign bit flipped makes it an
+		// unsigned byte, and the 128 comes off with the magic subtract
 		const uint4* row4 = reinterpret_cast<const uint4*>(static_cast<const int8_t*>(a.w) + (size_t)r * cols);
 		const uint16_t* sc = a.scales + (size_t)r * (cols / 32);
 		const uint32_t n16 = cols / 16;
-#pragma unroll 4
+#pragma unroll 2
 		for (uint32_t i = lane; i < n16; i += 32)
 		{
 			const uint4 q4 = __ldg(row4 + i);
 			const float s = bf16f(__ldg(sc + i / 2));
-			const uint32_t qq[4] = {q4.x, q4.y, q4.z, q4.w};
+			const uint32_t qq[4] = {q4.x ^ 0x80808080u, q4.y ^ 0x80808080u, q4.z ^ 0x80808080u, q4.w ^ 0x80808080u};
+			float w[16];
+#pragma unroll
+			for (int j = 0; j < 4; ++j)
+#pragma unroll
+				for (int t = 0; t < 4; ++t) w[4 * j + t] = byte_as_float(qq[j], sel_byte(t)) - 128.0f;
 #pragma unroll
 			for (int v = 0; v < NB; ++v)
 			{
 				const float* x = a.X + (size_t)v * a.x_stride + (size_t)i * 16;
 				float d = 0.0f;
+				if (x4)
+				{
 #pragma unroll
-				for (int j = 0; j < 4; ++j)
+					for (int j = 0; j < 4; ++j)
+					{
+						const float4 xv = ldx4(x + 4 * j);
+						d = fmaf(w[4 * j], xv.x, d);
+						d = fmaf(w[4 * j + 1], xv.y, d);
+						d = fmaf(w[4 * j + 2], xv.z, d);
+						d = fmaf(w[4 * j + 3], xv.w, d);
+					}
+				}
+				else
 #pragma unroll
-					for (int b = 0; b < 4; ++b)
-						d = fmaf((float)(int8_t)(qq[j] >> (8 * b)), __ldg(x + 4 * j + b), d);
+					for (int k = 0; k < 16; ++k) d = fmaf(w[k], __ldg(x + k), d);
 				acc[v] = fmaf(s, d, acc[v]);
 			}
 		}
 	}
 	else
 	{
-		// one whole block (16 bytes, 32 nibbles) per lane step
+		// one whole block (16 bytes, 32 nibbles) per lane step: byte k holds
+		// element k (low nibble) and element k + 16 (high)
 		const uint4* row4 = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.w) + (size_t)r * (cols / 2));
 		const uint32_t nb = cols / 32;
 		const uint16_t* sc = a.scales + (size_t)r * nb;
@@ -137,20 +178,38 @@ __device__ __forceinline__ void row_dots(const GemvArgs& a, uint32_t r, int lane
 			const uint4 q4 = __ldg(row4 + b);
 			const float s = bf16f(__ldg(sc + b)), bias = bf16f(__ldg(bi + b));
 			const uint32_t qq[4] = {q4.x, q4.y, q4.z, q4.w};
+			float w[32];
+#pragma unroll
+			for (int j = 0; j < 4; ++j)
+			{
+				const uint32_t lo = qq[j] & 0x0F0F0F0Fu, hi = (qq[j] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+				for (int t = 0; t < 4; ++t)
+				{
+					w[4 * j + t] = byte_as_float(lo, sel_byte(t));
+					w[16 + 4 * j + t] = byte_as_float(hi, sel_byte(t));
+				}
+			}
 #pragma unroll
 			for (int v = 0; v < NB; ++v)
 			{
 				const float* x = a.X + (size_t)v * a.x_stride + (size_t)b * 32;
 				float d = 0.0f;
+				if (x4)
+				{
 #pragma unroll
-				for (int j = 0; j < 4; ++j)
-#pragma unroll
-					for (int t = 0; t < 4; ++t)
+					for (int j = 0; j < 8; ++j)
 					{
-						const uint32_t byte = (qq[j] >> (8 * t)) & 0xFFu; // byte k = 4 j + t
-						d = fmaf((float)(byte & 0x0Fu), __ldg(x + 4 * j + t), d);
-						d = fmaf((float)(byte >> 4), __ldg(x + 4 * j + t + 16), d);
+						const float4 xv = ldx4(x + 4 * j);
+						d = fmaf(w[4 * j], xv.x, d);
+						d = fmaf(w[4 * j + 1], xv.y, d);
+						d = fmaf(w[4 * j + 2], xv.z, d);
+						d = fmaf(w[4 * j + 3], xv.w, d);
 					}
+				}
+				else
+#pragma unroll
+					for (int k = 0; k < 32; ++k) d = fmaf(w[k], __ldg(x + k), d);
 				acc[v] = fmaf(s, d, fmaf(bias, __ldg(a.XSUM + (size_t)v * a.xsum_stride + b), acc[v]));
 			}
 		}
