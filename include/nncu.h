@@ -288,6 +288,60 @@ int nncu_host_register(void* p, size_t bytes);
 int nncu_host_unregister(void* p);
 int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, int32_t n_jobs, void* stream);
 
+/* ---- attention_forward on the device (model.cpp:1559-1768) -----------------
+ * A weight matrix as the reference's gemv_batch (model.cpp:1181-1206) sees an
+ * nnc_tensor: `type` NNCU_W_BF16 (data BF16 [rows][cols]), NNCU_W_Q8_0 (data
+ * int8 quants [rows][cols], scales BF16 [rows][cols / 32]) or NNCU_W_Q4_S
+ * (data packed nibbles [rows][cols / 2], scales and biases BF16 [rows][cols /
+ * 32]); quants 16-byte aligned, cols a multiple of 32 for the quantised
+ * types. Device pointers. */
+enum
+{
+	NNCU_W_BF16 = 0,
+	NNCU_W_Q8_0 = 1,
+	NNCU_W_Q4_S = 2,
+};
+
+typedef struct nncu_weight
+{
+	int32_t type;
+	uint32_t rows, cols;
+	const void* data;
+	const uint16_t* scales;
+	const uint16_t* biases;
+} nncu_weight;
+
+/* One layer's attention weights (model_layer's attn_* tensors, model.h).
+ * q: rows n_head * head_dim, or 2 * n_head * head_dim when `gated` (Qwen3.5:
+ * each head's rows are its query, then its output gate). k, v: rows n_kv *
+ * head_dim; v.data NULL means V is the raw K projection (Gemma 4 global
+ * layers without v_proj). o: rows n_embd, cols n_head * head_dim. The q, k,
+ * v biases (Qwen2) are fp32 device vectors of the projections' output length
+ * or NULL. Every projection's cols is n_embd. */
+typedef struct nncu_attn_weights
+{
+	nncu_weight q, k, v, o;
+	const float* q_bias;
+	const float* k_bias;
+	const float* v_bias;
+	int32_t gated;
+} nncu_attn_weights;
+
+/* attention_forward for n_tok tokens of one sequence, on device pointers:
+ * x [n_tok][n_embd] are the normed hidden states (the reference's s.normed),
+ * y [n_tok][n_embd] receives the output projection. The q / k / v gemvs
+ * (with the gate split and the biases), the attention of
+ * nncu_attention_batch_dev (Q / K norms, RoPE, append, attend, the gate's
+ * sigmoid multiply), then the o gemv, all asynchronous on `stream`; k and v
+ * are not projected when p->reuse_kv. p->gate must be NULL: the gate comes
+ * from the q projection when w->gated. The pointer fields of `p` are device
+ * pointers. The q, k, v and attention rows live in a scratch array of the
+ * cache, grown (cudaMalloc) on a call that needs more than any before it;
+ * calls on one cache are ordered on the device whatever their streams. x and
+ * y must not overlap. */
+int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t seq, const nncu_attn_params* p,
+                               const nncu_attn_weights* w, const float* x, float* y, void* stream);
+
 /* One layer's decode / verify attention that allocates nothing: the same
  * K1 + K2 kernels as nncu_attention_batch_dev for one job, with every buffer
  * the caller's. No counterpart in the reference, whose CPU path never

@@ -33,7 +33,7 @@ __all__ = [
     "ATTN_BLOCK", "AttnParams", "AttnJob", "LayerDesc", "KVCache", "kv_plan", "job", "attn_span", "params",
     "attn_block_dev", "attn_merge_dev", "attn_finish_dev", "rmsnorm_gamma_multi_dev", "rmsnorm_dev",
     "rope_dev", "softcap_dev", "gemv_bf16w_dev", "gemv_q8_0_dev", "gemv_q4_s_dev", "block_sums_dev",
-    "gemv_bf16w_argmax_dev", "EXPORTS",
+    "gemv_bf16w_argmax_dev", "Weight", "AttnWeights", "weight", "W_BF16", "W_Q8_0", "W_Q4_S", "EXPORTS",
 ]
 
 PKG = os.path.dirname(os.path.abspath(__file__))
@@ -44,6 +44,7 @@ ROPE_NEOX, ROPE_NORM = 0, 1
 ATTN_BLOCK = 256
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_OUT_OF_MEMORY, ERR_CONTEXT_FULL = 0, 1, 2, 6, 7
 ERR_DEVICE, ERR_TIMEOUT = 20, 21
+W_BF16, W_Q8_0, W_Q4_S = 0, 1, 2
 
 # Every symbol include/nncu.h declares.
 EXPORTS = [
@@ -58,7 +59,7 @@ EXPORTS = [
     "nncu_attention_split_dev", "nncu_group_set_timeout", "nncu_group_reset", "nncu_group_inject_drop",
     "nncu_noalloc_check", "nncu_kv_set_tensor_cores", "nncu_host_register", "nncu_host_unregister",
     "nncu_gemv_bf16w_f32x_batch_dev", "nncu_gemv_q8_0_f32x_batch_dev", "nncu_gemv_q4_s_f32x_batch_dev",
-    "nncu_block_sums_dev", "nncu_gemv_bf16w_argmax_dev",
+    "nncu_block_sums_dev", "nncu_gemv_bf16w_argmax_dev", "nncu_attention_forward_dev",
 ]
 GROUP_HANDLE_BYTES = 64
 
@@ -92,6 +93,20 @@ class AttnJob(C.Structure):
 
     _fields_ = [("layer", C.c_int32), ("seq", C.c_int32), ("p", AttnParams),
                 ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("out", C.c_void_p)]
+
+
+class Weight(C.Structure):
+    """nncu_weight (include/nncu.h): one projection's device weights."""
+
+    _fields_ = [("type", C.c_int32), ("rows", C.c_uint32), ("cols", C.c_uint32),
+                ("data", C.c_void_p), ("scales", C.c_void_p), ("biases", C.c_void_p)]
+
+
+class AttnWeights(C.Structure):
+    """nncu_attn_weights (include/nncu.h): one layer's q, k, v, o projections."""
+
+    _fields_ = [("q", Weight), ("k", Weight), ("v", Weight), ("o", Weight),
+                ("q_bias", C.c_void_p), ("k_bias", C.c_void_p), ("v_bias", C.c_void_p), ("gated", C.c_int32)]
 
 
 class LayerDesc(C.Structure):
@@ -205,6 +220,8 @@ def lib() -> C.CDLL:
     L.nncu_attention.argtypes = [vp, i32, i32, C.POINTER(AttnParams), vp, vp, vp, vp]
     L.nncu_attention_batch.argtypes = [vp, C.POINTER(AttnJob), i32]
     L.nncu_attention_batch_dev.argtypes = [vp, C.POINTER(AttnJob), i32, vp]
+    L.nncu_attention_forward_dev.argtypes = [vp, i32, i32, C.POINTER(AttnParams), C.POINTER(AttnWeights), vp, vp,
+                                             vp]
     L.nncu_host_register.argtypes = [vp, sz]
     L.nncu_host_unregister.argtypes = [vp]
     L.nncu_sync.argtypes = [vp, vp]
@@ -388,6 +405,14 @@ class KVCache:
         arr = jobs if isinstance(jobs, C.Array) else (AttnJob * len(jobs))(*jobs)
         _check(lib().nncu_attention_batch_dev(self._h, arr, len(arr), _stream(stream)))
 
+    def attention_forward_dev(self, layer: int, p: AttnParams, w: AttnWeights, x, y, seq: int = 0,
+                              stream=None) -> None:
+        """nncu_attention_forward_dev: one layer's q / k / v projections,
+        attention and output projection for p.n_tok tokens of `seq`; x and y
+        are device arrays [n_tok][n_embd], asynchronous on `stream`."""
+        _check(lib().nncu_attention_forward_dev(self._h, layer, seq, C.byref(p), C.byref(w), _ptr(x), _ptr(y),
+                                                _stream(stream)))
+
     def sync(self, stream=None) -> None:
         """Wait for `stream` and report a kernel's timed-out wait."""
         _check(lib().nncu_sync(self._h, _stream(stream)))
@@ -404,6 +429,13 @@ def noalloc_check(stream=None) -> None:
     """nncu_noalloc_check: wait for `stream`; raise (ERR_TIMEOUT) if a no-allocation
     call on the current device timed out since the last check."""
     _check(lib().nncu_noalloc_check(_stream(stream)))
+
+
+def weight(kind: int, rows: int, cols: int, data, scales=None, biases=None) -> Weight:
+    """A Weight over device arrays (torch tensors or raw pointers)."""
+    w = Weight(int(kind), int(rows), int(cols), _ptr(data), _ptr(scales), _ptr(biases))
+    w._keep = (data, scales, biases)
+    return w
 
 
 def job(layer: int, p: AttnParams, q, k, v, out, seq: int = 0) -> AttnJob:

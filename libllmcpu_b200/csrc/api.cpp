@@ -283,6 +283,7 @@ struct nncu_kv
 	cudaStream_t stream = nullptr; // the host-pointer calls' stream
 	int* err_dev = nullptr;        // device error word (bounded waits)
 	DevBuf stage_dev, parts, counters, qbuf;
+	DevBuf fwd; // attention_forward's q / gate / k / v / attention rows and block sums
 	HostBuf stage_host;
 	// The job tables go up on their own stream through a ring of slots, so
 	// the upload of one call's table overlaps the previous call's kernels
@@ -330,6 +331,7 @@ struct nncu_kv
 		}
 		stage_dev.release();
 		qbuf.release();
+		fwd.release();
 		parts.release();
 		counters.release();
 		stage_host.release();
@@ -1071,9 +1073,10 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	nncu_kv::JobSlot* used = nullptr;
 	InlineTable tab_inline;
 	const InlineTable* tab = nullptr;
-	if (!group && !staged && P.fused && jb + sb <= (size_t)INLINE_TABLE_BYTES)
+	if (!group && !staged && !tc && P.fused && jb + sb <= (size_t)INLINE_TABLE_BYTES)
 	{
-		// small enough to travel with the launch: no upload, no events
+		// small enough to travel with the launch (the CUDA-core kernel takes an
+		// inline table; the tensor-core kernel reads P.jobs): no upload, no events
 		std::memcpy(tab_inline.b, jobs.data(), (size_t)n * sizeof(DevJob));
 		std::memcpy(tab_inline.b + jb, kv->starts_tmp.data(), sb);
 		tab = &tab_inline;
@@ -1228,6 +1231,87 @@ extern "C" int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, 
 	kv->jobs_tmp.resize(n_jobs);
 	for (int i = 0; i < n_jobs; ++i) fill_devjob(kv, jobs[i], kv->jobs_tmp[i]);
 	return run_jobs(kv, kv->jobs_tmp, jobs, static_cast<cudaStream_t>(stream));
+}
+
+// attention_forward (model.cpp:1559-1768) on the device: the reference's
+// sequence of gemv_batch calls, bias adds and the attention, with the
+// query / gate split and the biases folded into the q / k / v gemvs'
+// stores, and norms, RoPE, append, attend and the gate inside the attention
+// kernels of nncu_attention_batch_dev.
+extern "C" int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t seq, const nncu_attn_params* p,
+                                          const nncu_attn_weights* w, const float* x, float* y, void* stream)
+{
+	if (!kv || !p || !w || !x || !y) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL argument");
+	if (p->gate) return fail(NNCU_ERR_INVALID_ARGUMENT, "the gate comes from the q projection: p->gate must be NULL");
+	nncu_attn_job job{};
+	job.layer = layer;
+	job.seq = seq;
+	job.p = *p;
+	int rc = validate_job(kv, job);
+	if (rc != NNCU_OK) return rc;
+	const bool reuse = p->reuse_kv != 0, gated = w->gated != 0;
+	const uint32_t n_tok = (uint32_t)p->n_tok, hd = (uint32_t)p->head_dim;
+	const uint32_t q_dim = (uint32_t)p->n_head * hd, kv_dim = (uint32_t)p->n_kv * hd, n_embd = w->o.rows;
+	if (n_embd == 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "o: no rows");
+	rc = check_weight(w->q, (gated ? 2 : 1) * q_dim, n_embd, "q");
+	if (rc == NNCU_OK && !reuse) rc = check_weight(w->k, kv_dim, n_embd, "k");
+	if (rc == NNCU_OK && !reuse && w->v.data) rc = check_weight(w->v, kv_dim, n_embd, "v");
+	if (rc == NNCU_OK) rc = check_weight(w->o, n_embd, q_dim, "o");
+	if (rc != NNCU_OK) return rc;
+	const size_t io = (size_t)n_tok * n_embd * sizeof(float);
+	const char *xb = reinterpret_cast<const char*>(x), *yb = reinterpret_cast<const char*>(y);
+	if (xb < yb + io && yb < xb + io) return fail(NNCU_ERR_INVALID_ARGUMENT, "x and y overlap");
+
+	// V is the raw K projection without a v_proj; with a K bias it is a
+	// second, unbiased K gemv (the reference copies V before adding biases)
+	const bool v_own = !reuse && (w->v.data || w->k_bias);
+	const bool q4_in = w->q.type == NNCU_W_Q4_S ||
+	                   (!reuse && (w->k.type == NNCU_W_Q4_S || (w->v.data && w->v.type == NNCU_W_Q4_S)));
+	const bool q4_out = w->o.type == NNCU_W_Q4_S;
+	auto up64 = [](size_t n) { return (n + 63) & ~size_t(63); }; // 256-byte slots
+	const size_t n_q = up64((size_t)n_tok * q_dim), n_kv = up64((size_t)n_tok * kv_dim);
+	const size_t o_q = 0, o_g = o_q + n_q, o_k = o_g + (gated ? n_q : 0), o_v = o_k + (reuse ? 0 : n_kv);
+	const size_t o_a = o_v + (v_own ? n_kv : 0), o_xs = o_a + n_q;
+	const size_t o_as = o_xs + (q4_in ? up64((size_t)n_tok * (n_embd / 32)) : 0);
+	const size_t total = o_as + (q4_out ? up64((size_t)n_tok * (q_dim / 32)) : 0);
+
+	DeviceGuard g(kv->device);
+	cudaStream_t st = static_cast<cudaStream_t>(stream);
+	// the scratch is the cache's: wait for the previous call on another stream
+	if (kv->any_call && kv->last_stream != st)
+		CU(cudaStreamWaitEvent(st, kv->done, 0), "order after the previous call");
+	CU(kv->fwd.reserve(total * sizeof(float)), "attention_forward scratch");
+	float* f = static_cast<float*>(kv->fwd.p);
+	float *q = f + o_q, *gate = gated ? f + o_g : nullptr, *k = f + o_k, *v = v_own ? f + o_v : k, *attn = f + o_a;
+	float* xs = f + o_xs;
+	float* as = f + o_as;
+
+	int e = 0;
+	if (q4_in) e = launch_block_sums(x, xs, (size_t)n_tok * n_embd, st);
+	const size_t xss = n_embd / 32;
+	if (!e)
+		e = launch_projection(w->q, x, n_embd, xs, xss, q, q_dim, gate, gated ? hd : 0, w->q_bias, n_tok, st);
+	if (!e && !reuse) e = launch_projection(w->k, x, n_embd, xs, xss, k, kv_dim, nullptr, 0, w->k_bias, n_tok, st);
+	if (!e && v_own)
+		e = launch_projection(w->v.data ? w->v : w->k, x, n_embd, xs, xss, v, kv_dim, nullptr, 0,
+		                      w->v.data ? w->v_bias : nullptr, n_tok, st);
+	if (e) return cuda_fail((cudaError_t)e, "attention_forward projections");
+
+	job.p.gate = gate;
+	job.q = q;
+	job.k = reuse ? nullptr : k;
+	job.v = reuse ? nullptr : v;
+	job.out = attn;
+	rc = nncu_attention_batch_dev(kv, &job, 1, st);
+	if (rc != NNCU_OK) return rc;
+
+	if (q4_out) e = launch_block_sums(attn, as, (size_t)n_tok * q_dim, st);
+	if (!e) e = launch_projection(w->o, attn, q_dim, as, q_dim / 32, y, n_embd, nullptr, 0, nullptr, n_tok, st);
+	if (e) return cuda_fail((cudaError_t)e, "attention_forward output projection");
+	CU(cudaEventRecord(kv->done, st), "completion event");
+	kv->last_stream = st;
+	kv->any_call = true;
+	return NNCU_OK;
 }
 
 extern "C" int nncu_attention_split_dev(nncu_kv* kv, nncu_group* group, const nncu_attn_job* jobs, int32_t n_jobs,

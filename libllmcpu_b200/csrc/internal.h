@@ -8,7 +8,8 @@
 
 #include <vector_types.h>
 
-struct nncu_group; // split.cpp
+struct nncu_group;  // split.cpp
+struct nncu_weight; // nncu.h
 
 namespace nncu
 {
@@ -250,5 +251,14 @@ int launch_rmsnorm(float* y, const float* x, size_t n_groups, size_t dim, const 
 int launch_rope(float* x, uint32_t n_tok, uint32_t n_heads, uint32_t head_dim, uint32_t n_rot, int32_t pos0,
                 float pos_scale, const float* rope_inv, int mode, const float* freq_factors, void* stream);
 int launch_softcap(float* y, const float* x, size_t n, float cap, void* stream);
+
+// attention_forward's projections (k_gemv.cu): a weight's shape and pointers
+// checked against what the layer needs; one batched gemv with the optional
+// query / gate split and bias (GemvArgs); block sums for Q4_S weights.
+int check_weight(const nncu_weight& w, uint32_t rows, uint32_t cols, const char* name);
+int launch_projection(const nncu_weight& w, const float* X, size_t x_stride, const float* XSUM, size_t xsum_stride,
+                      float* Y, size_t y_stride, float* Y2, uint32_t split, const float* bias, uint32_t n_batch,
+                      void* stream);
+int launch_block_sums(const float* x, float* out, size_t n, void* stream);
 
 } // namespace nncu

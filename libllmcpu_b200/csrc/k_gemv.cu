@@ -24,6 +24,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdio>
+
 #include "nncu.h"
 
 #include "common.cuh"
@@ -50,6 +52,13 @@ struct GemvArgs
 	size_t y_stride;
 	uint32_t rows, cols, n_batch;
 	unsigned long long* best; // argmax: the running (value, index) key
+	// attention_forward's projections: `bias` (or NULL) added to each output;
+	// with split > 0, rows come in pairs of split-row halves per head (query,
+	// then gate): the first halves go to Y and the second to Y2, each
+	// [n_batch][rows / 2], and the bias applies to Y's only
+	const float* bias;
+	float* Y2;
+	uint32_t split;
 };
 
 __device__ __forceinline__ float bf16f(uint32_t h) { return __uint_as_float(h << 16); }
@@ -228,11 +237,21 @@ __global__ void __launch_bounds__(GW_THREADS) gemv_kernel(const GemvArgs a, uint
 	{
 		float acc[NB];
 		row_dots<FMT, NB>(b, r, lane, acc);
+		float* Y = a.Y;
+		uint32_t o = r;
+		if (a.split)
+		{
+			const uint32_t h = r / (2 * a.split), i = r - h * 2 * a.split;
+			Y = i < a.split ? a.Y : a.Y2;
+			o = h * a.split + (i < a.split ? i : i - a.split);
+		}
+		const float bias = (a.bias && Y == a.Y) ? __ldg(a.bias + o) : 0.0f;
 #pragma unroll
 		for (int v = 0; v < NB; ++v)
 		{
-			const float y = warp_sum(acc[v]);
-			if (lane == 0) a.Y[(size_t)(v0 + v) * a.y_stride + r] = y;
+			float y = warp_sum(acc[v]);
+			if (a.bias) y += bias; // the reference adds the bias to the stored float
+			if (lane == 0) Y[(size_t)(v0 + v) * a.y_stride + o] = y;
 		}
 	}
 }
@@ -320,6 +339,46 @@ int launch_gemv_fmt(const GemvArgs& a, cudaStream_t st)
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 } // namespace
+
+int check_weight(const nncu_weight& w, uint32_t rows, uint32_t cols, const char* name)
+{
+	char msg[160];
+	msg[0] = 0;
+	if (w.type < NNCU_W_BF16 || w.type > NNCU_W_Q4_S)
+		snprintf(msg, sizeof msg, "%s: unknown weight type %d", name, (int)w.type);
+	else if (w.rows != rows || w.cols != cols)
+		snprintf(msg, sizeof msg, "%s: %u x %u weights where %u x %u are needed", name, w.rows, w.cols, rows, cols);
+	else if (!w.data)
+		snprintf(msg, sizeof msg, "%s: NULL weights", name);
+	else if (w.type != NNCU_W_BF16 && (!w.scales || (w.type == NNCU_W_Q4_S && !w.biases)))
+		snprintf(msg, sizeof msg, "%s: NULL scales or biases", name);
+	else if (w.type != NNCU_W_BF16 && cols % 32)
+		snprintf(msg, sizeof msg, "%s: cols must be a multiple of 32", name);
+	else if (w.type != NNCU_W_BF16 && !aligned16(w.data))
+		snprintf(msg, sizeof msg, "%s: quants must be 16-byte aligned", name);
+	return msg[0] ? set_error(NNCU_ERR_INVALID_ARGUMENT, msg) : NNCU_OK;
+}
+
+int launch_projection(const nncu_weight& w, const float* X, size_t x_stride, const float* XSUM, size_t xsum_stride,
+                      float* Y, size_t y_stride, float* Y2, uint32_t split, const float* bias, uint32_t n_batch,
+                      void* stream)
+{
+	GemvArgs a{w.data, w.scales, w.biases, X, x_stride, XSUM, xsum_stride, Y, y_stride, w.rows, w.cols, n_batch,
+	           nullptr, bias, Y2, split};
+	const auto st = static_cast<cudaStream_t>(stream);
+	if (w.type == NNCU_W_Q8_0) return launch_gemv_fmt<1>(a, st);
+	if (w.type == NNCU_W_Q4_S) return launch_gemv_fmt<2>(a, st);
+	return launch_gemv_fmt<0>(a, st);
+}
+
+int launch_block_sums(const float* x, float* out, size_t n, void* stream)
+{
+	const size_t nb = n / 32;
+	block_sums_kernel<<<(unsigned)((nb + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, out, nb);
+	note_launches(1);
+	return (int)cudaGetLastError();
+}
+
 } // namespace nncu
 
 using namespace nncu;
@@ -373,10 +432,7 @@ extern "C" int nncu_block_sums_dev(const float* x, float* out, size_t n, void* s
 {
 	if (n == 0 || n % 32) return set_error(NNCU_ERR_INVALID_ARGUMENT, "block sums: n must be a positive multiple of 32");
 	if (!x || !out) return set_error(NNCU_ERR_INVALID_ARGUMENT, "block sums: NULL input or output");
-	const size_t nb = n / 32;
-	block_sums_kernel<<<(unsigned)((nb + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, out, nb);
-	note_launches(1);
-	const int e = (int)cudaGetLastError();
+	const int e = launch_block_sums(x, out, n, stream);
 	return e ? set_cuda_error(e, "block sums launch") : NNCU_OK;
 }
 

@@ -276,12 +276,15 @@ def test_registered_host_buffers_match_staging(nncu):
         N.host_unregister(arena)
 
 
-def test_device_pointer_batch_matches_host(nncu, torch_cuda):
+@pytest.mark.parametrize("kv_type,one_by_one", [(O.KV_F32, False), (O.KV_BF16, False), (O.KV_BF16, True)])
+def test_device_pointer_batch_matches_host(nncu, torch_cuda, kv_type, one_by_one):
+    # a bf16 cache with 4 query rows per KV head takes the tensor-core kernel;
+    # one job alone is a table small enough to travel inline with a launch
     torch = torch_cuda
     N = nncu
     layers = [LayerSpec(4, 1, 256, window=512, freq_base=1e4, qk_norm=True),
               LayerSpec(4, 1, 256, window=0, freq_base=1e6, qk_norm=True)]
-    case = S.build_case(700, layers, n_ctx=2048, n_tok=1, pos0=1500, kv_type=O.KV_F32, n_batch=1)
+    case = S.build_case(700, layers, n_ctx=2048, n_tok=1, pos0=1500, kv_type=kv_type, n_batch=1)
     want, kv_h = run_product(N, case)
     kv_h.close()
     kv = make_cache(N, case)
@@ -297,7 +300,11 @@ def test_device_pointer_batch_matches_host(nncu, torch_cuda):
         keep.append(t)
         outs.append(out)
     torch.cuda.synchronize()
-    kv.attention_batch_dev(jobs, st)
+    if one_by_one:
+        for j in jobs:
+            kv.attention_batch_dev([j], st)
+    else:
+        kv.attention_batch_dev(jobs, st)
     kv.sync(st)
     for li in range(2):
         assert np.array_equal(outs[li].cpu().numpy(), want[0][li])
