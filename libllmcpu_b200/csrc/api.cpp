@@ -1073,10 +1073,9 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	nncu_kv::JobSlot* used = nullptr;
 	InlineTable tab_inline;
 	const InlineTable* tab = nullptr;
-	if (!group && !staged && !tc && P.fused && jb + sb <= (size_t)INLINE_TABLE_BYTES)
+	if (!group && !staged && P.fused && jb + sb <= (size_t)INLINE_TABLE_BYTES)
 	{
-		// small enough to travel with the launch (the CUDA-core kernel takes an
-		// inline table; the tensor-core kernel reads P.jobs): no upload, no events
+		// small enough to travel with the launch: no upload, no events
 		std::memcpy(tab_inline.b, jobs.data(), (size_t)n * sizeof(DevJob));
 		std::memcpy(tab_inline.b + jb, kv->starts_tmp.data(), sb);
 		tab = &tab_inline;
@@ -1157,7 +1156,7 @@ int run_jobs(nncu_kv* kv, std::vector<DevJob>& jobs, const nncu_attn_job* pub, c
 	if (e) return cuda_fail((cudaError_t)e, "K1 (norm, RoPE, append) launch");
 	{
 		PerfScope ps(NNCU_PERF_ATTN_CORE, core_bytes, st);
-		e = tc ? launch_decode_tc(P, nullptr, st) : launch_decode(P, st, tab);
+		e = tc ? launch_decode_tc(P, nullptr, st, tab) : launch_decode(P, st, tab);
 	}
 	if (e) return cuda_fail((cudaError_t)e, "K2 (attention) launch");
 	if (group)

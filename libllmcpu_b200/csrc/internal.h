@@ -94,9 +94,11 @@ static_assert(sizeof(CtaStart) == 48, "CtaStart layout");
 
 // A small launch's job table (n DevJobs, then the CTA starts at the next
 // 16-byte boundary) passed by value as a kernel parameter, so the launch
-// needs no upload. Sized so that it and the DecodePlan stay within the
-// 4 KB of ordinary kernel parameters.
-constexpr int INLINE_TABLE_BYTES = 3712;
+// needs no upload and no cross-stream events. With the DecodePlan it makes
+// 12 KB of parameters (sm_70 and later take up to 32,764 bytes since CUDA
+// 12.1): one job on all 148 SMs (7.3 KB), or the 16 sequences of one layer
+// (10.9 KB).
+constexpr int INLINE_TABLE_BYTES = 12288 - 320;
 struct alignas(16) InlineTable
 {
 	unsigned char b[INLINE_TABLE_BYTES];
@@ -135,6 +137,7 @@ struct DecodePlan
 	unsigned long long wait_ns;  // the merge's bounded wait
 	int drop_arrivals;           // test injection: this rank's partials are stored but never counted
 };
+static_assert(sizeof(DecodePlan) + sizeof(InlineTable) <= 12288, "an inline launch's parameters: 12 KB");
 
 // Plan one launch over jobs[0, n) (their D, kv geometry, positions and
 // pointers filled): the row group size, every job's tiles, chunks and
@@ -152,7 +155,7 @@ int plan_launch(DevJob* jobs, int n, int kv_type, int num_sms, DecodePlan& P, Ct
 // CUtensorMaps (K, V) for jobs whose tmap_k / tmap_v are NULL, or NULL.
 int tc_rows(int D, int kv_type, int rows_needed);
 int tc_fuse_tokens(int D, int RM); // new tokens the tensor-core kernel appends itself (0: K1 must)
-int launch_decode_tc(const DecodePlan& plan, const void* maps, void* stream);
+int launch_decode_tc(const DecodePlan& plan, const void* maps, void* stream, const InlineTable* tab = nullptr);
 // The tensor maps of a 16-bit cache buffer [planes][rows][D] in the kernel's
 // tile form (host side; 128 bytes each, 64-byte aligned).
 constexpr int TENSOR_MAP_BYTES = 128;

@@ -214,8 +214,11 @@ __device__ __forceinline__ float warp_rows(const float (&v)[NR], int lane)
 	return cur[0];
 }
 
-template <int D, typename KV, int NR>
-__global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePlan P, const __grid_constant__ TcMaps maps)
+// The kernel's body. INL: the job table and the CTA starts are the bytes of
+// `tab` (a kernel parameter) instead of P.jobs / P.cta_start, and every job
+// carries its own tensor maps (`maps` is then NULL).
+template <int D, typename KV, int NR, bool INL>
+__device__ __forceinline__ void decode_tc_body(const DecodePlan& P, const TcMaps* maps, const unsigned char* tab)
 {
 	using C = TcCfg<D, NR>;
 	constexpr int T = C::T, N = C::N, PW = D + 4;
@@ -251,10 +254,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 	volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 2);
 	CtaStart* s_start = reinterpret_cast<CtaStart*>(smem + C::OFF_BAR + 384);
 
+	const DevJob* jobs = INL ? reinterpret_cast<const DevJob*>(tab) : P.jobs;
+	const CtaStart* starts =
+		INL ? reinterpret_cast<const CtaStart*>(tab + ((P.n_jobs * sizeof(DevJob) + 15) & ~size_t(15))) : P.cta_start;
 	const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 	if (threadIdx.x == 0)
 	{
-		*s_start = P.cta_start[blockIdx.x];
+		*s_start = starts[blockIdx.x];
 		for (int s = 0; s < STAGES; ++s)
 		{
 			mbar_init(&k_full[s], 1);
@@ -315,12 +321,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 			cur.job = S.job;
 			cur.seg = S.seg;
 			cur.tis = S.tis;
-			cursor_load<false>(P.jobs, P.n_jobs, cur);
+			cursor_load<INL>(jobs, P.n_jobs, cur);
 			int i = 0, piece = 0, landed = 0; // landed: tiles sent to the land barrier
 			bool waited = false;
 			for (int left = n_mine; left > 0 && !flags[0];)
 			{
-				const DevJob& J = P.jobs[cur.job];
+				const DevJob& J = jobs[cur.job];
 				const int n = min(min(cur.n_tiles - cur.tis, J.chunk - cur.tis % J.chunk), left);
 				const int h = cur.seg / J.n_rowgroups, rg = cur.seg % J.n_rowgroups;
 				const bool fresh = holds_new_rows(J, cur.tis, n, T);
@@ -348,8 +354,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 						(uint32_t)(sizeof(DevJob) + rows * D * 4 + (J.q_gamma ? D * 4 : 0) + inv_bytes +
 					               (J.freq_factors ? half * 4 : 0) +
 					               (append ? (J.k_gamma ? D * 4 : 0) + 2 * J.n_tok * D * 4 : 0));
-					mbar_arrive_expect_tx(q_full, bytes); // also releases the info words above
-					bulk_g2s(slot, &J, (uint32_t)sizeof(DevJob), q_full);
+					if constexpr (INL)
+					{
+						// from the parameters: plain copies (the bulk copy reads global memory only)
+#pragma unroll
+						for (int w = 0; w < (int)(sizeof(DevJob) / 16); ++w)
+							reinterpret_cast<uint4*>(slot)[w] = reinterpret_cast<const uint4*>(&J)[w];
+					}
+					// also releases the info words (and an inline descriptor) above
+					mbar_arrive_expect_tx(q_full, bytes - (INL ? (uint32_t)sizeof(DevJob) : 0u));
+					if constexpr (!INL) bulk_g2s(slot, &J, (uint32_t)sizeof(DevJob), q_full);
 					if (J.q_gamma) bulk_g2s(slot + C::QGAIN, J.q_gamma, (uint32_t)(D * 4), q_full);
 					if (inv_bytes) bulk_g2s(slot + C::QINV, J.rope_inv, inv_bytes, q_full);
 					if (J.freq_factors) bulk_g2s(slot + C::QFF, J.freq_factors, (uint32_t)(half * 4), q_full);
@@ -374,7 +388,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				}
 				++piece;
 				const CUtensorMap* map = static_cast<const CUtensorMap*>(is_k ? J.tmap_k : J.tmap_v);
-				if (!map) map = is_k ? &maps.k : &maps.v;
+				if (!map) map = is_k ? &maps->k : &maps->v; // an inline launch's jobs all carry maps
 				const int plane = J.plane0 + h;
 				for (int k = 0; k < n; ++k, ++i)
 				{
@@ -412,7 +426,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 				}
 				left -= n;
 				cur.tis += n;
-				if (cur.tis >= cur.n_tiles) cursor_next_segment<false>(P.jobs, P.n_jobs, cur);
+				if (cur.tis >= cur.n_tiles) cursor_next_segment<INL>(jobs, P.n_jobs, cur);
 			}
 			if (flags[0])
 			{
@@ -1026,19 +1040,36 @@ __global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePl
 }
 
 template <int D, typename KV, int NR>
-int launch_tc(const DecodePlan& P, const void* maps, cudaStream_t st)
+__global__ void __launch_bounds__(TC_THREADS, 1) decode_tc_kernel(const DecodePlan P, const __grid_constant__ TcMaps maps)
+{
+	decode_tc_body<D, KV, NR, false>(P, &maps, nullptr);
+}
+
+// A small launch: its job table and CTA starts come with the parameters.
+template <int D, typename KV, int NR>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+	decode_tc_kernel_inline(const DecodePlan P, const __grid_constant__ InlineTable tab)
+{
+	decode_tc_body<D, KV, NR, true>(P, nullptr, tab.b);
+}
+
+template <int D, typename KV, int NR>
+int launch_tc(const DecodePlan& P, const void* maps, const InlineTable* tab, cudaStream_t st)
 {
 	using C = TcCfg<D, NR>;
-	static bool configured[64] = {};
+	static bool configured[2][64] = {};
 	int dev = 0;
 	cudaGetDevice(&dev);
 	if (dev < 0 || dev >= 64) return (int)cudaErrorInvalidDevice;
-	if (!configured[dev])
+	if (tab && maps) return (int)cudaErrorInvalidValue; // an inline launch takes the jobs' own maps
+	if (!configured[tab != nullptr][dev])
 	{
 		const cudaError_t e =
-			cudaFuncSetAttribute(decode_tc_kernel<D, KV, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+			tab ? cudaFuncSetAttribute(decode_tc_kernel_inline<D, KV, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+			                           C::SMEM)
+			    : cudaFuncSetAttribute(decode_tc_kernel<D, KV, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
 		if (e != cudaSuccess) return (int)e;
-		configured[dev] = true;
+		configured[tab != nullptr][dev] = true;
 	}
 	TcMaps m;
 	if (maps)
@@ -1057,17 +1088,18 @@ int launch_tc(const DecodePlan& P, const void* maps, cudaStream_t st)
 	attr[0].val.programmaticStreamSerializationAllowed = 1;
 	cfg.attrs = attr;
 	cfg.numAttrs = P.fused ? 0 : 1; // appending itself, it follows the stream's previous work in full
+	if (tab) return (int)cudaLaunchKernelEx(&cfg, decode_tc_kernel_inline<D, KV, NR>, P, *tab);
 	return (int)cudaLaunchKernelEx(&cfg, decode_tc_kernel<D, KV, NR>, P, m);
 }
 
 template <typename KV, int NR>
-int launch_tc_dims(const DecodePlan& P, const void* maps, cudaStream_t st)
+int launch_tc_dims(const DecodePlan& P, const void* maps, const InlineTable* tab, cudaStream_t st)
 {
 	switch (P.D)
 	{
-	case 64: return launch_tc<64, KV, NR>(P, maps, st);
-	case 128: return launch_tc<128, KV, NR>(P, maps, st);
-	case 256: return launch_tc<256, KV, NR>(P, maps, st);
+	case 64: return launch_tc<64, KV, NR>(P, maps, tab, st);
+	case 128: return launch_tc<128, KV, NR>(P, maps, tab, st);
+	case 256: return launch_tc<256, KV, NR>(P, maps, tab, st);
 	default: return (int)cudaErrorInvalidValue;
 	}
 }
@@ -1089,15 +1121,16 @@ int tc_rows(int D, int kv_type, int rows_needed)
 	return rows_needed <= 8 ? 8 : 16;
 }
 
-int launch_decode_tc(const DecodePlan& P, const void* maps, void* stream)
+int launch_decode_tc(const DecodePlan& P, const void* maps, void* stream, const InlineTable* tab)
 {
 	if (P.n_ctas == 0) return 0;
 	auto st = static_cast<cudaStream_t>(stream);
 	if (P.RM != 8 && P.RM != 16) return (int)cudaErrorInvalidValue;
 	if (P.kv_type == KV_F16)
-		return P.RM == 8 ? launch_tc_dims<kv_f16, 8>(P, maps, st) : launch_tc_dims<kv_f16, 16>(P, maps, st);
+		return P.RM == 8 ? launch_tc_dims<kv_f16, 8>(P, maps, tab, st) : launch_tc_dims<kv_f16, 16>(P, maps, tab, st);
 	if (P.kv_type == KV_BF16)
-		return P.RM == 8 ? launch_tc_dims<kv_bf16, 8>(P, maps, st) : launch_tc_dims<kv_bf16, 16>(P, maps, st);
+		return P.RM == 8 ? launch_tc_dims<kv_bf16, 8>(P, maps, tab, st)
+		                 : launch_tc_dims<kv_bf16, 16>(P, maps, tab, st);
 	return (int)cudaErrorInvalidValue;
 }
 

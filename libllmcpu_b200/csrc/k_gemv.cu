@@ -309,9 +309,16 @@ __global__ void block_sums_kernel(const float* x, float* out, size_t nb)
 
 int grid_for(uint32_t rows)
 {
-	int dev = 0, sms = 148;
+	static int sm_count[64] = {}; // per device, looked up once
+	int dev = 0;
 	cudaGetDevice(&dev);
-	cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+	int sms = dev >= 0 && dev < 64 ? sm_count[dev] : 0;
+	if (sms <= 0)
+	{
+		sms = 148;
+		cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+		if (dev >= 0 && dev < 64) sm_count[dev] = sms;
+	}
 	const uint32_t want = (rows + GW_THREADS / 32 - 1) / (GW_THREADS / 32);
 	return (int)(want < (uint32_t)(sms * 8) ? want : (uint32_t)(sms * 8));
 }
