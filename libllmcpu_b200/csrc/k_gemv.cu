@@ -18,7 +18,10 @@
 // The work is the weight stream: one warp per row at a time, each lane
 // taking 16 bytes of the row per step (8 BF16 weights, 16 int8 weights, or
 // one whole Q4_S block), several steps' loads in flight, up to 8 vectors of
-// the batch per pass over the weights (a larger batch makes more passes).
+// the batch per pass over the weights (a larger batch makes more passes). A
+// single vector against a tall quantised matrix takes 2 to 8 rows per warp at
+// a time instead: the rows' quants of a step are in flight together and the
+// step's activations are read once for them.
 // fp32 accumulation; the sum order differs from the reference's 8-lane FMA
 // chains (tolerance: its own tests' 1e-3 x max(1, |y|)).
 #include <cuda_runtime.h>
@@ -225,6 +228,139 @@ __device__ __forceinline__ void row_dots(const GemvArgs& a, uint32_t r, int lane
 	}
 }
 
+// RR consecutive rows of one warp against one vector, quantised formats: at
+// each 16-byte step of a lane the RR rows' quants are loaded together (RR
+// loads in flight per lane), the step's activations once for all of them,
+// and each row's sum formed exactly as row_dots forms it. Rows past the end
+// read the last row again; the caller drops them.
+template <int FMT, int RR>
+__device__ __forceinline__ void rows_dot1(const GemvArgs& a, uint32_t r0, int lane, float (&acc)[RR])
+{
+#pragma unroll
+	for (int i = 0; i < RR; ++i) acc[i] = 0.0f;
+	const uint32_t cols = a.cols, nb = cols / 32;
+	const bool x4 = (reinterpret_cast<uintptr_t>(a.X) & 15u) == 0;
+	uint32_t rr_[RR];
+#pragma unroll
+	for (int i = 0; i < RR; ++i) rr_[i] = min(r0 + i, a.rows - 1);
+	if (FMT == 1)
+	{
+		const uint32_t n16 = cols / 16;
+		for (uint32_t i = lane; i < n16; i += 32)
+		{
+			uint4 q[RR];
+			float sc[RR];
+#pragma unroll
+			for (int k = 0; k < RR; ++k)
+			{
+				q[k] = __ldg(reinterpret_cast<const uint4*>(static_cast<const int8_t*>(a.w) + (size_t)rr_[k] * cols) + i);
+				sc[k] = bf16f(__ldg(a.scales + (size_t)rr_[k] * nb + i / 2));
+			}
+			float x[16];
+			const float* xp = a.X + (size_t)i * 16;
+			if (x4)
+			{
+#pragma unroll
+				for (int j = 0; j < 4; ++j)
+				{
+					const float4 xv = ldx4(xp + 4 * j);
+					x[4 * j] = xv.x;
+					x[4 * j + 1] = xv.y;
+					x[4 * j + 2] = xv.z;
+					x[4 * j + 3] = xv.w;
+				}
+			}
+			else
+#pragma unroll
+				for (int k = 0; k < 16; ++k) x[k] = __ldg(xp + k);
+#pragma unroll
+			for (int k = 0; k < RR; ++k)
+			{
+				const uint32_t qq[4] = {q[k].x ^ 0x80808080u, q[k].y ^ 0x80808080u, q[k].z ^ 0x80808080u,
+				                        q[k].w ^ 0x80808080u};
+				float d = 0.0f;
+#pragma unroll
+				for (int j = 0; j < 4; ++j)
+#pragma unroll
+					for (int t = 0; t < 4; ++t) d = fmaf(byte_as_float(qq[j], sel_byte(t)) - 128.0f, x[4 * j + t], d);
+				acc[k] = fmaf(sc[k], d, acc[k]);
+			}
+		}
+	}
+	else
+	{
+		for (uint32_t b = lane; b < nb; b += 32)
+		{
+			uint4 q[RR];
+			float sc[RR], bi[RR];
+#pragma unroll
+			for (int k = 0; k < RR; ++k)
+			{
+				q[k] = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.w) + (size_t)rr_[k] * (cols / 2)) + b);
+				sc[k] = bf16f(__ldg(a.scales + (size_t)rr_[k] * nb + b));
+				bi[k] = bf16f(__ldg(a.biases + (size_t)rr_[k] * nb + b));
+			}
+			const float xs = __ldg(a.XSUM + b);
+			float x[32];
+			const float* xp = a.X + (size_t)b * 32;
+			if (x4)
+			{
+#pragma unroll
+				for (int j = 0; j < 8; ++j)
+				{
+					const float4 xv = ldx4(xp + 4 * j);
+					x[4 * j] = xv.x;
+					x[4 * j + 1] = xv.y;
+					x[4 * j + 2] = xv.z;
+					x[4 * j + 3] = xv.w;
+				}
+			}
+			else
+#pragma unroll
+				for (int k = 0; k < 32; ++k) x[k] = __ldg(xp + k);
+#pragma unroll
+			for (int k = 0; k < RR; ++k)
+			{
+				const uint32_t qq[4] = {q[k].x, q[k].y, q[k].z, q[k].w};
+				float d = 0.0f;
+				// the order of row_dots: elements 0-15 (low nibbles) of j = 0..3, then 16-31 (high)
+#pragma unroll
+				for (int j = 0; j < 4; ++j)
+#pragma unroll
+					for (int t = 0; t < 4; ++t) d = fmaf(byte_as_float(qq[j] & 0x0F0F0F0Fu, sel_byte(t)), x[4 * j + t], d);
+#pragma unroll
+				for (int j = 0; j < 4; ++j)
+#pragma unroll
+					for (int t = 0; t < 4; ++t)
+						d = fmaf(byte_as_float((qq[j] >> 4) & 0x0F0F0F0Fu, sel_byte(t)), x[16 + 4 * j + t], d);
+				acc[k] = fmaf(sc[k], d, fmaf(bi[k], xs, acc[k]));
+			}
+		}
+	}
+}
+
+// Where output row r goes: Y or Y2 (the query / gate split) and its index,
+// with its bias (or 0).
+struct OutSlot
+{
+	float* Y;
+	uint32_t o;
+	float bias;
+};
+
+__device__ __forceinline__ OutSlot out_slot(const GemvArgs& a, uint32_t r)
+{
+	OutSlot s{a.Y, r, 0.0f};
+	if (a.split)
+	{
+		const uint32_t h = r / (2 * a.split), i = r - h * 2 * a.split;
+		s.Y = i < a.split ? a.Y : a.Y2;
+		s.o = h * a.split + (i < a.split ? i : i - a.split);
+	}
+	if (a.bias && s.Y == a.Y) s.bias = __ldg(a.bias + s.o);
+	return s;
+}
+
 template <int FMT, int NB>
 __global__ void __launch_bounds__(GW_THREADS) gemv_kernel(const GemvArgs a, uint32_t v0)
 {
@@ -237,21 +373,37 @@ __global__ void __launch_bounds__(GW_THREADS) gemv_kernel(const GemvArgs a, uint
 	{
 		float acc[NB];
 		row_dots<FMT, NB>(b, r, lane, acc);
-		float* Y = a.Y;
-		uint32_t o = r;
-		if (a.split)
-		{
-			const uint32_t h = r / (2 * a.split), i = r - h * 2 * a.split;
-			Y = i < a.split ? a.Y : a.Y2;
-			o = h * a.split + (i < a.split ? i : i - a.split);
-		}
-		const float bias = (a.bias && Y == a.Y) ? __ldg(a.bias + o) : 0.0f;
+		const OutSlot os = out_slot(a, r);
 #pragma unroll
 		for (int v = 0; v < NB; ++v)
 		{
 			float y = warp_sum(acc[v]);
-			if (a.bias) y += bias; // the reference adds the bias to the stored float
-			if (lane == 0) Y[(size_t)(v0 + v) * a.y_stride + o] = y;
+			if (a.bias) y += os.bias; // the reference adds the bias to the stored float
+			if (lane == 0) os.Y[(size_t)(v0 + v) * a.y_stride + os.o] = y;
+		}
+	}
+}
+
+// One vector against quantised weights: RR rows per warp at a time.
+template <int FMT, int RR>
+__global__ void __launch_bounds__(GW_THREADS) gemv_rows_kernel(const GemvArgs a)
+{
+	const int lane = threadIdx.x & 31;
+	const uint32_t warps = gridDim.x * (GW_THREADS / 32);
+	for (uint32_t r0 = (blockIdx.x * (GW_THREADS / 32) + (threadIdx.x >> 5)) * RR; r0 < a.rows; r0 += warps * RR)
+	{
+		float acc[RR];
+		rows_dot1<FMT, RR>(a, r0, lane, acc);
+#pragma unroll
+		for (int k = 0; k < RR; ++k)
+		{
+			const float y0 = warp_sum(acc[k]);
+			if (r0 + k < a.rows)
+			{
+				const OutSlot os = out_slot(a, r0 + k);
+				const float y = a.bias ? y0 + os.bias : y0;
+				if (lane == 0) os.Y[os.o] = y;
+			}
 		}
 	}
 }
@@ -326,6 +478,31 @@ int grid_for(uint32_t rows)
 template <int FMT>
 int launch_gemv_fmt(const GemvArgs& a, cudaStream_t st)
 {
+	if constexpr (FMT != 0)
+	{
+		// one vector: RR rows per warp (their quants in flight together) on
+		// matrices tall enough to keep every SM busy with RR rows per warp.
+		// Measured on a B200 (L2 flushed, one vector, cols 2560 and 4096):
+		// Q4_S best at 8 rows per warp from 12288 rows (65536 x 4096: 256 us at
+		// 1, 86 at 4, 64 at 8), at 4 from 2048; Q8_0 best at 4 from 12288
+		// (65536 x 4096: 174 us at 1, 91 at 4), at 2 from 8192 (10240 x 2560:
+		// 26.6 us at 1, 19.4 at 2), and at 1 row per warp below.
+		const uint32_t rows = a.rows;
+		const int rr = FMT == 2 ? (rows >= 12288 ? 8 : rows >= 2048 ? 4 : 1) : (rows >= 12288 ? 4 : rows >= 8192 ? 2 : 0);
+		if (a.n_batch == 1 && rr > 0)
+		{
+			if (rr == 8)
+				gemv_rows_kernel<FMT, 8><<<grid_for((rows + 7) / 8), GW_THREADS, 0, st>>>(a);
+			else if (rr == 4)
+				gemv_rows_kernel<FMT, 4><<<grid_for((rows + 3) / 4), GW_THREADS, 0, st>>>(a);
+			else if (rr == 2)
+				gemv_rows_kernel<FMT, 2><<<grid_for((rows + 1) / 2), GW_THREADS, 0, st>>>(a);
+			else
+				gemv_rows_kernel<FMT, 1><<<grid_for(rows), GW_THREADS, 0, st>>>(a);
+			note_launches(1);
+			return (int)cudaGetLastError();
+		}
+	}
 	const int grid = grid_for(a.rows);
 	for (uint32_t v0 = 0; v0 < a.n_batch;)
 	{

@@ -14,8 +14,10 @@ import oracle as O
 
 pytestmark = pytest.mark.gpu
 
+# the last three: one vector on tall matrices (Q4_S 4 and 8 rows per warp, Q8_0
+# 2 and 4), heights not a multiple of the rows per warp
 SHAPES = [(1, 32, 1), (8, 64, 1), (64, 128, 3), (256, 256, 2), (512, 512, 1), (1024, 2048, 4), (2560, 2048, 9),
-          (300, 96, 17)]
+          (300, 96, 17), (2050, 96, 1), (8195, 64, 1), (12301, 64, 1)]
 
 
 def _inputs(rows, cols, nb, seed):
