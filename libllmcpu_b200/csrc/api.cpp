@@ -1287,13 +1287,14 @@ extern "C" int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t se
 
 	int e = 0;
 	if (q4_in) e = launch_block_sums(x, xs, (size_t)n_tok * n_embd, st);
-	const size_t xss = n_embd / 32;
-	if (!e)
-		e = launch_projection(w->q, x, n_embd, xs, xss, q, q_dim, gate, gated ? hd : 0, w->q_bias, n_tok, st);
-	if (!e && !reuse) e = launch_projection(w->k, x, n_embd, xs, xss, k, kv_dim, nullptr, 0, w->k_bias, n_tok, st);
-	if (!e && v_own)
-		e = launch_projection(w->v.data ? w->v : w->k, x, n_embd, xs, xss, v, kv_dim, nullptr, 0,
-		                      w->v.data ? w->v_bias : nullptr, n_tok, st);
+	// q, k and v in one launch per weight format
+	Projection proj[3];
+	int n_proj = 0;
+	proj[n_proj++] = Projection{&w->q, q, q_dim, gate, gated ? hd : 0, w->q_bias};
+	if (!reuse) proj[n_proj++] = Projection{&w->k, k, kv_dim, nullptr, 0, w->k_bias};
+	if (v_own)
+		proj[n_proj++] = Projection{w->v.data ? &w->v : &w->k, v, kv_dim, nullptr, 0, w->v.data ? w->v_bias : nullptr};
+	if (!e) e = launch_projections(proj, n_proj, x, n_embd, xs, n_embd / 32, n_tok, st);
 	if (e) return cuda_fail((cudaError_t)e, "attention_forward projections");
 
 	job.p.gate = gate;
@@ -1305,7 +1306,8 @@ extern "C" int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t se
 	if (rc != NNCU_OK) return rc;
 
 	if (q4_out) e = launch_block_sums(attn, as, (size_t)n_tok * q_dim, st);
-	if (!e) e = launch_projection(w->o, attn, q_dim, as, q_dim / 32, y, n_embd, nullptr, 0, nullptr, n_tok, st);
+	const Projection po{&w->o, y, n_embd, nullptr, 0, nullptr};
+	if (!e) e = launch_projections(&po, 1, attn, q_dim, as, q_dim / 32, n_tok, st);
 	if (e) return cuda_fail((cudaError_t)e, "attention_forward output projection");
 	CU(cudaEventRecord(kv->done, st), "completion event");
 	kv->last_stream = st;

@@ -256,12 +256,21 @@ int launch_rope(float* x, uint32_t n_tok, uint32_t n_heads, uint32_t head_dim, u
 int launch_softcap(float* y, const float* x, size_t n, float cap, void* stream);
 
 // attention_forward's projections (k_gemv.cu): a weight's shape and pointers
-// checked against what the layer needs; one batched gemv with the optional
+// checked against what the layer needs; batched gemvs with the optional
 // query / gate split and bias (GemvArgs); block sums for Q4_S weights.
 int check_weight(const nncu_weight& w, uint32_t rows, uint32_t cols, const char* name);
-int launch_projection(const nncu_weight& w, const float* X, size_t x_stride, const float* XSUM, size_t xsum_stride,
-                      float* Y, size_t y_stride, float* Y2, uint32_t split, const float* bias, uint32_t n_batch,
-                      void* stream);
+struct Projection
+{
+	const nncu_weight* w;
+	float* Y;
+	size_t y_stride;
+	float* Y2;          // with split > 0: the second half-rows of each pair (the gate)
+	uint32_t split;
+	const float* bias;  // or NULL
+};
+// up to three projections of the same vectors, one launch per weight format
+int launch_projections(const Projection* p, int n, const float* X, size_t x_stride, const float* XSUM,
+                       size_t xsum_stride, uint32_t n_batch, void* stream);
 int launch_block_sums(const float* x, float* out, size_t n, void* stream);
 
 } // namespace nncu

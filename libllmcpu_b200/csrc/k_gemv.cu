@@ -361,9 +361,18 @@ __device__ __forceinline__ OutSlot out_slot(const GemvArgs& a, uint32_t r)
 	return s;
 }
 
-template <int FMT, int NB>
-__global__ void __launch_bounds__(GW_THREADS) gemv_kernel(const GemvArgs a, uint32_t v0)
+// Up to three matrices against the same vectors in one launch (a projection's
+// q, k and v): grid row y takes matrix y.
+constexpr int GW_MAXMAT = 3;
+struct GemvSet
 {
+	GemvArgs m[GW_MAXMAT];
+};
+
+template <int FMT, int NB>
+__global__ void __launch_bounds__(GW_THREADS) gemv_kernel(const __grid_constant__ GemvSet set, uint32_t v0)
+{
+	const GemvArgs& a = set.m[blockIdx.y];
 	const int lane = threadIdx.x & 31;
 	const uint32_t warps = gridDim.x * (GW_THREADS / 32);
 	GemvArgs b = a;
@@ -386,8 +395,9 @@ __global__ void __launch_bounds__(GW_THREADS) gemv_kernel(const GemvArgs a, uint
 
 // One vector against quantised weights: RR rows per warp at a time.
 template <int FMT, int RR>
-__global__ void __launch_bounds__(GW_THREADS) gemv_rows_kernel(const GemvArgs a)
+__global__ void __launch_bounds__(GW_THREADS) gemv_rows_kernel(const __grid_constant__ GemvSet set)
 {
+	const GemvArgs& a = set.m[blockIdx.y];
 	const int lane = threadIdx.x & 31;
 	const uint32_t warps = gridDim.x * (GW_THREADS / 32);
 	for (uint32_t r0 = (blockIdx.x * (GW_THREADS / 32) + (threadIdx.x >> 5)) * RR; r0 < a.rows; r0 += warps * RR)
@@ -475,9 +485,19 @@ int grid_for(uint32_t rows)
 	return (int)(want < (uint32_t)(sms * 8) ? want : (uint32_t)(sms * 8));
 }
 
+// n (1 to GW_MAXMAT) matrices of format FMT, the same vectors and n_batch;
+// grid rows beyond a shorter matrix's need return at once.
 template <int FMT>
-int launch_gemv_fmt(const GemvArgs& a, cudaStream_t st)
+int launch_gemv_fmt(const GemvArgs* mats, int n, cudaStream_t st)
 {
+	GemvSet set{};
+	uint32_t rows = 0;
+	for (int i = 0; i < n; ++i)
+	{
+		set.m[i] = mats[i];
+		rows = mats[i].rows > rows ? mats[i].rows : rows;
+	}
+	const uint32_t n_batch = mats[0].n_batch;
 	if constexpr (FMT != 0)
 	{
 		// one vector: RR rows per warp (their quants in flight together) on
@@ -487,34 +507,34 @@ int launch_gemv_fmt(const GemvArgs& a, cudaStream_t st)
 		// 1, 86 at 4, 64 at 8), at 4 from 2048; Q8_0 best at 4 from 12288
 		// (65536 x 4096: 174 us at 1, 91 at 4), at 2 from 8192 (10240 x 2560:
 		// 26.6 us at 1, 19.4 at 2), and at 1 row per warp below.
-		const uint32_t rows = a.rows;
 		const int rr = FMT == 2 ? (rows >= 12288 ? 8 : rows >= 2048 ? 4 : 1) : (rows >= 12288 ? 4 : rows >= 8192 ? 2 : 0);
-		if (a.n_batch == 1 && rr > 0)
+		if (n_batch == 1 && rr > 0)
 		{
+			const dim3 grid((unsigned)grid_for((rows + rr - 1) / rr), (unsigned)n);
 			if (rr == 8)
-				gemv_rows_kernel<FMT, 8><<<grid_for((rows + 7) / 8), GW_THREADS, 0, st>>>(a);
+				gemv_rows_kernel<FMT, 8><<<grid, GW_THREADS, 0, st>>>(set);
 			else if (rr == 4)
-				gemv_rows_kernel<FMT, 4><<<grid_for((rows + 3) / 4), GW_THREADS, 0, st>>>(a);
+				gemv_rows_kernel<FMT, 4><<<grid, GW_THREADS, 0, st>>>(set);
 			else if (rr == 2)
-				gemv_rows_kernel<FMT, 2><<<grid_for((rows + 1) / 2), GW_THREADS, 0, st>>>(a);
+				gemv_rows_kernel<FMT, 2><<<grid, GW_THREADS, 0, st>>>(set);
 			else
-				gemv_rows_kernel<FMT, 1><<<grid_for(rows), GW_THREADS, 0, st>>>(a);
+				gemv_rows_kernel<FMT, 1><<<grid, GW_THREADS, 0, st>>>(set);
 			note_launches(1);
 			return (int)cudaGetLastError();
 		}
 	}
-	const int grid = grid_for(a.rows);
-	for (uint32_t v0 = 0; v0 < a.n_batch;)
+	const dim3 grid((unsigned)grid_for(rows), (unsigned)n);
+	for (uint32_t v0 = 0; v0 < n_batch;)
 	{
-		const uint32_t left = a.n_batch - v0;
+		const uint32_t left = n_batch - v0;
 		if (left >= 8)
-			gemv_kernel<FMT, 8><<<grid, GW_THREADS, 0, st>>>(a, v0), v0 += 8;
+			gemv_kernel<FMT, 8><<<grid, GW_THREADS, 0, st>>>(set, v0), v0 += 8;
 		else if (left >= 4)
-			gemv_kernel<FMT, 4><<<grid, GW_THREADS, 0, st>>>(a, v0), v0 += 4;
+			gemv_kernel<FMT, 4><<<grid, GW_THREADS, 0, st>>>(set, v0), v0 += 4;
 		else if (left >= 2)
-			gemv_kernel<FMT, 2><<<grid, GW_THREADS, 0, st>>>(a, v0), v0 += 2;
+			gemv_kernel<FMT, 2><<<grid, GW_THREADS, 0, st>>>(set, v0), v0 += 2;
 		else
-			gemv_kernel<FMT, 1><<<grid, GW_THREADS, 0, st>>>(a, v0), v0 += 1;
+			gemv_kernel<FMT, 1><<<grid, GW_THREADS, 0, st>>>(set, v0), v0 += 1;
 		note_launches(1);
 	}
 	return (int)cudaGetLastError();
@@ -543,16 +563,30 @@ int check_weight(const nncu_weight& w, uint32_t rows, uint32_t cols, const char*
 	return msg[0] ? set_error(NNCU_ERR_INVALID_ARGUMENT, msg) : NNCU_OK;
 }
 
-int launch_projection(const nncu_weight& w, const float* X, size_t x_stride, const float* XSUM, size_t xsum_stride,
-                      float* Y, size_t y_stride, float* Y2, uint32_t split, const float* bias, uint32_t n_batch,
-                      void* stream)
+int launch_projections(const Projection* p, int n, const float* X, size_t x_stride, const float* XSUM,
+                       size_t xsum_stride, uint32_t n_batch, void* stream)
 {
-	GemvArgs a{w.data, w.scales, w.biases, X, x_stride, XSUM, xsum_stride, Y, y_stride, w.rows, w.cols, n_batch,
-	           nullptr, bias, Y2, split};
 	const auto st = static_cast<cudaStream_t>(stream);
-	if (w.type == NNCU_W_Q8_0) return launch_gemv_fmt<1>(a, st);
-	if (w.type == NNCU_W_Q4_S) return launch_gemv_fmt<2>(a, st);
-	return launch_gemv_fmt<0>(a, st);
+	// one launch per weight format present
+	for (int type = NNCU_W_BF16; type <= NNCU_W_Q4_S; ++type)
+	{
+		GemvArgs mats[GW_MAXMAT];
+		int k = 0;
+		for (int i = 0; i < n; ++i)
+		{
+			if (p[i].w->type != type) continue;
+			if (k == GW_MAXMAT) return (int)cudaErrorInvalidValue;
+			const nncu_weight& w = *p[i].w;
+			mats[k++] = GemvArgs{w.data, w.scales, w.biases, X, x_stride, XSUM, xsum_stride, p[i].Y, p[i].y_stride,
+			                     w.rows, w.cols, n_batch, nullptr, p[i].bias, p[i].Y2, p[i].split};
+		}
+		if (k == 0) continue;
+		const int e = type == NNCU_W_Q8_0 ? launch_gemv_fmt<1>(mats, k, st)
+		              : type == NNCU_W_Q4_S ? launch_gemv_fmt<2>(mats, k, st)
+		                                    : launch_gemv_fmt<0>(mats, k, st);
+		if (e) return e;
+	}
+	return 0;
 }
 
 int launch_block_sums(const float* x, float* out, size_t n, void* stream)
@@ -576,7 +610,7 @@ extern "C" int nncu_gemv_bf16w_f32x_batch_dev(const void* W, const float* X, siz
 	if (n_batch > 1 && (x_stride < cols || y_stride < rows))
 		return set_error(NNCU_ERR_INVALID_ARGUMENT, "gemv: strides shorter than a vector");
 	GemvArgs a{W, nullptr, nullptr, X, x_stride, nullptr, 0, Y, y_stride, rows, cols, n_batch, nullptr};
-	const int e = launch_gemv_fmt<0>(a, static_cast<cudaStream_t>(stream));
+	const int e = launch_gemv_fmt<0>(&a, 1, static_cast<cudaStream_t>(stream));
 	return e ? set_cuda_error(e, "gemv launch") : NNCU_OK;
 }
 
@@ -591,7 +625,7 @@ extern "C" int nncu_gemv_q8_0_f32x_batch_dev(const int8_t* qs, const uint16_t* s
 	if (n_batch > 1 && (x_stride < cols || y_stride < rows))
 		return set_error(NNCU_ERR_INVALID_ARGUMENT, "gemv: strides shorter than a vector");
 	GemvArgs a{qs, scales, nullptr, X, x_stride, nullptr, 0, Y, y_stride, rows, cols, n_batch, nullptr};
-	const int e = launch_gemv_fmt<1>(a, static_cast<cudaStream_t>(stream));
+	const int e = launch_gemv_fmt<1>(&a, 1, static_cast<cudaStream_t>(stream));
 	return e ? set_cuda_error(e, "gemv launch") : NNCU_OK;
 }
 
@@ -608,7 +642,7 @@ extern "C" int nncu_gemv_q4_s_f32x_batch_dev(const uint8_t* qs, const uint16_t* 
 	if (n_batch > 1 && (x_stride < cols || y_stride < rows || xsum_stride < cols / 32))
 		return set_error(NNCU_ERR_INVALID_ARGUMENT, "gemv: strides shorter than a vector");
 	GemvArgs a{qs, scales, biases, X, x_stride, XSUM, xsum_stride, Y, y_stride, rows, cols, n_batch, nullptr};
-	const int e = launch_gemv_fmt<2>(a, static_cast<cudaStream_t>(stream));
+	const int e = launch_gemv_fmt<2>(&a, 1, static_cast<cudaStream_t>(stream));
 	return e ? set_cuda_error(e, "gemv launch") : NNCU_OK;
 }
 
