@@ -6,8 +6,10 @@
  * in host vectors (model_kv_cache, src/libnnc/model.h:252-326). This library
  * replaces the part of attention_forward after the Q/K/V projections -- the
  * per-head Q/K RMSNorm, RoPE, the K/V append and the blocked attention
- * (model.cpp:1616-1757) -- and moves the K/V cache to HBM. The projections,
- * nnc.h and everything else in libnnc stay as they are.
+ * (model.cpp:1616-1757) -- and moves the K/V cache to HBM; on device memory it
+ * also runs the whole attention_forward with its projections
+ * (nncu_attention_forward_dev) and the verify logits with their argmax. nnc.h
+ * and everything else in libnnc stay as they are.
  *
  * Conventions, all of them libnnc's:
  *  - Every entry point returns an int holding an nnc_status value
@@ -341,6 +343,22 @@ typedef struct nncu_attn_weights
  * y must not overlap. */
 int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t seq, const nncu_attn_params* p,
                                const nncu_attn_weights* w, const float* x, float* y, void* stream);
+
+/* model_logits_batch (model.cpp:2198-2208): logits [n][lm_head->rows] of n
+ * hidden rows [n][lm_head->cols] (the verify rows of speculate, session.cpp:
+ * 545), then final_softcap > 0 applies cap * tanh(x / cap) to each
+ * (nnc_softcap_f32, nn_ops.cpp:1877-1882; the reference skips it for greedy
+ * verify). A Q4_S lm_head needs `xsum`, n * cols / 32 floats of scratch for
+ * the block sums (the reference's cache.sxsum). Device pointers,
+ * asynchronous on `stream`. */
+int nncu_logits_batch_dev(const nncu_weight* lm_head, const float* hidden, int32_t n, float* logits,
+                          float final_softcap, float* xsum, void* stream);
+
+/* Greedy verify's argmax of each of n_rows rows of n floats, x_stride apart
+ * (session.cpp:128-134, 552): out[r] = the first index of the largest value
+ * under >, so -0 and +0 tie, a NaN never replaces the best and a NaN in the
+ * first place is the answer. Device pointers, asynchronous on `stream`. */
+int nncu_argmax_rows_dev(const float* x, size_t x_stride, int32_t n_rows, uint32_t n, int32_t* out, void* stream);
 
 /* One layer's decode / verify attention that allocates nothing: the same
  * K1 + K2 kernels as nncu_attention_batch_dev for one job, with every buffer

@@ -33,7 +33,8 @@ __all__ = [
     "ATTN_BLOCK", "AttnParams", "AttnJob", "LayerDesc", "KVCache", "kv_plan", "job", "attn_span", "params",
     "attn_block_dev", "attn_merge_dev", "attn_finish_dev", "rmsnorm_gamma_multi_dev", "rmsnorm_dev",
     "rope_dev", "softcap_dev", "gemv_bf16w_dev", "gemv_q8_0_dev", "gemv_q4_s_dev", "block_sums_dev",
-    "gemv_bf16w_argmax_dev", "Weight", "AttnWeights", "weight", "W_BF16", "W_Q8_0", "W_Q4_S", "EXPORTS",
+    "gemv_bf16w_argmax_dev", "Weight", "AttnWeights", "weight", "W_BF16", "W_Q8_0", "W_Q4_S", "logits_batch_dev",
+    "argmax_rows_dev", "EXPORTS",
 ]
 
 PKG = os.path.dirname(os.path.abspath(__file__))
@@ -59,7 +60,8 @@ EXPORTS = [
     "nncu_attention_split_dev", "nncu_group_set_timeout", "nncu_group_reset", "nncu_group_inject_drop",
     "nncu_noalloc_check", "nncu_kv_set_tensor_cores", "nncu_host_register", "nncu_host_unregister",
     "nncu_gemv_bf16w_f32x_batch_dev", "nncu_gemv_q8_0_f32x_batch_dev", "nncu_gemv_q4_s_f32x_batch_dev",
-    "nncu_block_sums_dev", "nncu_gemv_bf16w_argmax_dev", "nncu_attention_forward_dev",
+    "nncu_block_sums_dev", "nncu_gemv_bf16w_argmax_dev", "nncu_attention_forward_dev", "nncu_logits_batch_dev",
+    "nncu_argmax_rows_dev",
 ]
 GROUP_HANDLE_BYTES = 64
 
@@ -222,6 +224,8 @@ def lib() -> C.CDLL:
     L.nncu_attention_batch_dev.argtypes = [vp, C.POINTER(AttnJob), i32, vp]
     L.nncu_attention_forward_dev.argtypes = [vp, i32, i32, C.POINTER(AttnParams), C.POINTER(AttnWeights), vp, vp,
                                              vp]
+    L.nncu_logits_batch_dev.argtypes = [C.POINTER(Weight), vp, i32, vp, f, vp, vp]
+    L.nncu_argmax_rows_dev.argtypes = [vp, sz, i32, C.c_uint32, vp, vp]
     L.nncu_host_register.argtypes = [vp, sz]
     L.nncu_host_unregister.argtypes = [vp]
     L.nncu_sync.argtypes = [vp, vp]
@@ -436,6 +440,19 @@ def weight(kind: int, rows: int, cols: int, data, scales=None, biases=None) -> W
     w = Weight(int(kind), int(rows), int(cols), _ptr(data), _ptr(scales), _ptr(biases))
     w._keep = (data, scales, biases)
     return w
+
+
+def logits_batch_dev(lm_head: Weight, hidden, n: int, logits, final_softcap: float = 0.0, xsum=None,
+                     stream=None) -> None:
+    """nncu_logits_batch_dev: model_logits_batch on the device."""
+    _check(lib().nncu_logits_batch_dev(C.byref(lm_head), _ptr(hidden), int(n), _ptr(logits), float(final_softcap),
+                                       _ptr(xsum), _stream(stream)))
+
+
+def argmax_rows_dev(x, n_rows: int, n: int, out, x_stride=None, stream=None) -> None:
+    """nncu_argmax_rows_dev: greedy verify's argmax of each row."""
+    _check(lib().nncu_argmax_rows_dev(_ptr(x), int(x_stride if x_stride is not None else n), int(n_rows), int(n),
+                                      _ptr(out), _stream(stream)))
 
 
 def job(layer: int, p: AttnParams, q, k, v, out, seq: int = 0) -> AttnJob:

@@ -454,6 +454,42 @@ __global__ void __launch_bounds__(GW_THREADS) gemv_argmax_kernel(const GemvArgs 
 	}
 }
 
+// Greedy verify's argmax of each logits row (session.cpp:128-134: the first
+// index of the largest value, compared with >): one CTA per row, a 64-bit
+// max of (value key, ~index) as above. -0 counts as +0 (equal under >); a NaN
+// never wins, and a NaN in the first place is the answer (nothing compares
+// greater than it).
+__global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* X, size_t x_stride, uint32_t n, int32_t* out)
+{
+	__shared__ unsigned long long s_best[32];
+	const float* x = X + (size_t)blockIdx.x * x_stride;
+	unsigned long long best = 0;
+	for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
+	{
+		float v = __ldg(x + i);
+		if (v == v)
+		{
+			if (v == 0.0f) v = 0.0f;
+			const unsigned long long key = ((unsigned long long)order_key(v) << 32) | (0xFFFFFFFFu - i);
+			best = key > best ? key : best;
+		}
+	}
+#pragma unroll
+	for (int o = 16; o > 0; o >>= 1)
+	{
+		const unsigned long long b = __shfl_xor_sync(0xffffffffu, best, o);
+		best = b > best ? b : best;
+	}
+	if ((threadIdx.x & 31) == 0) s_best[threadIdx.x >> 5] = best;
+	__syncthreads();
+	if (threadIdx.x == 0)
+	{
+		for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = s_best[w] > best ? s_best[w] : best;
+		const float x0 = __ldg(x);
+		out[blockIdx.x] = (x0 != x0 || !best) ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
+	}
+}
+
 __global__ void argmax_finish_kernel(const unsigned long long* best, int32_t* out)
 {
 	const unsigned long long b = *best;
@@ -669,4 +705,35 @@ extern "C" int nncu_gemv_bf16w_argmax_dev(const void* W, const float* x, uint32_
 	note_launches(2);
 	const int e = (int)cudaGetLastError();
 	return e ? set_cuda_error(e, "argmax gemv launch") : NNCU_OK;
+}
+
+extern "C" int nncu_logits_batch_dev(const nncu_weight* lm_head, const float* hidden, int32_t n, float* logits,
+                                     float final_softcap, float* xsum, void* stream)
+{
+	if (!lm_head || !hidden || !logits || n <= 0)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "logits: NULL argument or no rows");
+	const int rc = check_weight(*lm_head, lm_head->rows, lm_head->cols, "lm_head");
+	if (rc != NNCU_OK) return rc;
+	if (lm_head->type == NNCU_W_Q4_S && !xsum)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "logits: a Q4_S lm_head needs the block-sum scratch");
+	if (final_softcap < 0.0f || final_softcap != final_softcap)
+		return set_error(NNCU_ERR_INVALID_ARGUMENT, "logits: bad soft-cap");
+	const uint32_t cols = lm_head->cols, rows = lm_head->rows;
+	int e = 0;
+	if (lm_head->type == NNCU_W_Q4_S) e = launch_block_sums(hidden, xsum, (size_t)n * cols, stream);
+	const Projection pr{lm_head, logits, rows, nullptr, 0, nullptr};
+	if (!e) e = launch_projections(&pr, 1, hidden, cols, xsum, cols / 32, (uint32_t)n, stream);
+	if (!e && final_softcap > 0.0f) e = launch_softcap(logits, logits, (size_t)n * rows, final_softcap, stream);
+	return e ? set_cuda_error(e, "logits launch") : NNCU_OK;
+}
+
+extern "C" int nncu_argmax_rows_dev(const float* x, size_t x_stride, int32_t n_rows, uint32_t n, int32_t* out,
+                                    void* stream)
+{
+	if (!x || !out || n_rows <= 0 || n == 0) return set_error(NNCU_ERR_INVALID_ARGUMENT, "argmax: NULL argument or empty");
+	if (n_rows > 1 && x_stride < n) return set_error(NNCU_ERR_INVALID_ARGUMENT, "argmax: stride shorter than a row");
+	argmax_rows_kernel<<<(unsigned)n_rows, 1024, 0, static_cast<cudaStream_t>(stream)>>>(x, x_stride, n, out);
+	note_launches(1);
+	const int e = (int)cudaGetLastError();
+	return e ? set_cuda_error(e, "argmax launch") : NNCU_OK;
 }

@@ -74,6 +74,8 @@ def lib() -> C.CDLL:
             L.orc_rng_normal.argtypes = [C.c_void_p, _f32p, C.c_size_t, C.c_float, C.c_float]
             L.orc_rng_uniform.argtypes = [C.c_void_p, _f32p, C.c_size_t, C.c_float, C.c_float]
             L.orc_rng_free.argtypes = [C.c_void_p]
+            L.orc_argmax_rows.argtypes = [C.c_void_p, C.c_size_t, C.c_int, C.c_uint32, C.c_void_p]
+            L.orc_argmax_rows.restype = None
             L.orc_ring_rows.restype = C.c_int
             L.orc_ring_rows.argtypes = [C.c_int, C.c_int]
             L.orc_f32_to_bf16.restype = C.c_uint16
@@ -384,6 +386,16 @@ def block_sums(x: np.ndarray, which: str = "oracle") -> np.ndarray:
     x = np.ascontiguousarray(x, np.float32).ravel()
     out = np.empty(x.size // 32, np.float32)
     getattr(L, f"{p}_block_sums")(ptr(x), ptr(out), x.size)
+    return out
+
+
+def argmax_rows(X: np.ndarray) -> np.ndarray:
+    """session.cpp:128-134's argmax of each row of X (the checker's)."""
+    X = np.ascontiguousarray(X, np.float32)
+    if X.ndim == 1:
+        X = X[None, :]
+    out = np.zeros(X.shape[0], np.int32)
+    lib().orc_argmax_rows(ptr(X), X.shape[1], X.shape[0], X.shape[1], ptr(out))
     return out
 
 

@@ -447,6 +447,22 @@ void orc_block_sums(const float* x, float* out, size_t n)
 	}
 }
 
+/* Greedy verify's argmax of a logits row (session.cpp:128-134): the best
+ * index moves only to a value comparing greater, so the first maximum wins,
+ * -0 and +0 tie, a NaN never replaces the best and a NaN in the first place
+ * stays the answer. */
+void orc_argmax_rows(const float* x, size_t x_stride, int n_rows, uint32_t n, int32_t* out)
+{
+	for (int r = 0; r < n_rows; ++r)
+	{
+		const float* v = x + (size_t)r * x_stride;
+		int32_t best = 0;
+		for (uint32_t i = 1; i < n; ++i)
+			if (v[i] > v[best]) best = (int32_t)i;
+		out[r] = best;
+	}
+}
+
 int orc_gemv_bf16w_argmax(const uint16_t* W, const float* x, uint32_t rows, uint32_t cols)
 {
 	int best = -1;

@@ -106,6 +106,8 @@ void orc_block_sums(const float* x, float* out, size_t n);
 /* nnc_gemv_bf16w_argmax_f32x (nn_ops.cpp:1055-1197): the first index of the
  * largest y[r]. */
 int orc_gemv_bf16w_argmax(const uint16_t* W, const float* x, uint32_t rows, uint32_t cols);
+/* argmax of session.cpp:128-134 over each of n_rows rows of n floats. */
+void orc_argmax_rows(const float* x, size_t x_stride, int n_rows, uint32_t n, int32_t* out);
 
 /* Sliding-ring sizing of model_kv_init (src/libnnc/model.cpp:1934-1955). */
 int orc_ring_rows(int window, int n_batch);

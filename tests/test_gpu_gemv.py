@@ -108,3 +108,62 @@ def test_gemv_refusals(nncu, torch_cuda):
         N.gemv_q8_0_dev(buf, buf, buf, buf, 4, 48)  # cols not a multiple of 32
     with pytest.raises(N.NnncError):
         N.gemv_q4_s_dev(buf[1:], buf, buf, buf, buf, buf, 4, 64)  # misaligned quants
+
+
+def test_argmax_rows_match_the_checker(nncu, torch_cuda):
+    # session.cpp:128-134 on each row: ties, signed zeros, NaNs, infinities,
+    # and random rows of a Gemma-sized vocabulary
+    N, torch = nncu, torch_cuda
+    rng = np.random.default_rng(3)
+    n = 262144
+    X = rng.standard_normal((6, n)).astype(np.float32)
+    X[1, 77] = X[1, 9000] = 50.0                     # the first of two maxima
+    X[2, 0] = np.nan                                 # NaN first: index 0
+    X[3, :] = -0.0
+    X[3, 5] = 0.0                                    # -0 and +0 tie: index 0
+    X[4, 1000:2000] = np.nan
+    X[4, 1500] = 1e30                                # NaNs skipped around the max
+    X[5, :] = -np.inf                                # all -inf: index 0
+    out = torch.full((6,), -7, dtype=torch.int32, device="cuda")
+    N.argmax_rows_dev(torch.from_numpy(X).cuda(), 6, n, out)
+    torch.cuda.synchronize()
+    assert out.cpu().numpy().tolist() == O.argmax_rows(X).tolist()
+    # strided rows, a short length
+    Xp = np.zeros((3, 40), np.float32)
+    Xp[:, :33] = rng.standard_normal((3, 33))
+    Xp[:, 33:] = 1e9  # beyond each row's length
+    out3 = torch.zeros(3, dtype=torch.int32, device="cuda")
+    N.argmax_rows_dev(torch.from_numpy(Xp).cuda(), 3, 33, out3, x_stride=40)
+    torch.cuda.synchronize()
+    assert out3.cpu().numpy().tolist() == O.argmax_rows(np.ascontiguousarray(Xp[:, :33])).tolist()
+
+
+@pytest.mark.parametrize("kind", ["bf16", "q8_0", "q4_s"])
+def test_verify_logits_match_the_checker(nncu, torch_cuda, kind):
+    # model_logits_batch (model.cpp:2198-2208): the lm_head over the n + 1
+    # verify rows, then the final soft-cap (sampling) or none (greedy)
+    N, torch = nncu, torch_cuda
+    rows, cols, n = 5000, 640, 5
+    W, X, qs8, sc, qs4, bi = _inputs(rows, cols, n, 17)
+    d = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    if kind == "bf16":
+        w = N.weight(N.W_BF16, rows, cols, d(W.view(np.int16)))
+        want = O.gemv_bf16w(W, X)
+    elif kind == "q8_0":
+        w = N.weight(N.W_Q8_0, rows, cols, d(qs8), d(sc.view(np.int16)))
+        want = O.gemv_q8_0(qs8, sc, X)
+    else:
+        w = N.weight(N.W_Q4_S, rows, cols, d(qs4), d(sc.view(np.int16)), d(bi.view(np.int16)))
+        want = O.gemv_q4_s(qs4, sc, bi, X, np.stack([O.block_sums(x) for x in X]))
+    keep = w._keep
+    xs = torch.empty((n, cols // 32), device="cuda")
+    for cap in (0.0, 30.0):
+        logits = torch.full((n, rows), float("nan"), device="cuda")
+        N.logits_batch_dev(w, d(X), n, logits, cap, xs)
+        torch.cuda.synchronize()
+        ref = want if cap == 0.0 else O.softcap(want.ravel(), cap).reshape(want.shape)
+        _check(logits.cpu().numpy(), ref, f"{kind} logits, cap {cap}")
+    if kind == "q4_s":
+        with pytest.raises(N.NnncError, match="block-sum"):
+            N.logits_batch_dev(w, d(X), n, logits, 0.0, None)
+    del keep

@@ -311,3 +311,11 @@ def test_gemv_restatement_scalar_cases():
     # argmax: the first of equal maxima
     W2 = O.f32_to_bf16_bits(np.array([[1.0] * 32, [2.0] * 32, [2.0] * 32], np.float32))
     assert O.gemv_bf16w_argmax(W2, x) == 1
+
+
+def test_argmax_rows_known_answers():
+    # session.cpp:128-134: first maximum under >, -0 ties +0, NaN never
+    # replaces the best, a NaN in the first place stays the answer
+    x = np.array([[1, 3, 3, 2], [np.nan, 5, 6, 1], [-0.0, 0.0, -1, -2], [1, np.nan, 7, 7],
+                  [-np.inf, -np.inf, -np.inf, -np.inf], [0.5, 0.25, np.inf, 1]], np.float32)
+    assert O.argmax_rows(x).tolist() == [1, 0, 0, 2, 0, 2]
