@@ -265,3 +265,37 @@ def test_refusals(nncu, torch_cuda):
     with pytest.raises(N.NnncError, match="gate"):
         call(p=N.params(n_tok=1, pos0=1, n_head=4, n_kv=2, head_dim=64, gate=g.data_ptr()))
     kv.close()
+
+
+def test_second_sequence_of_a_shared_cache(nncu, torch_cuda):
+    # a cache of two sequences: the call on sequence 1 appends to and reads
+    # only its own rows
+    N, torch = nncu, torch_cuda
+    rng = np.random.default_rng(10)
+    n_embd, n_head, n_kv, hd, pos0 = 256, 4, 2, 64, 70
+    kv = N.KVCache([(n_kv, hd, 0, 0)], n_ctx=256, n_batch=16, n_seq=2, kv_type=O.KV_F32)
+    rows = kv.layer_info(0).rows
+    caches = []
+    for s in range(2):
+        pk = rng.standard_normal((pos0, n_kv * hd)).astype(np.float32)
+        pv = rng.standard_normal((pos0, n_kv * hd)).astype(np.float32)
+        kv.write_rows(0, 0, pk, pv, seq=s)
+        Kc = np.zeros((rows, n_kv * hd), np.float32)
+        Vc = np.zeros_like(Kc)
+        Kc[:pos0], Vc[:pos0] = pk, pv
+        caches.append((Kc, Vc))
+    ws = {k: W(rng, O_Q8, r, c, torch) for k, r, c in (("q", n_head * hd, n_embd), ("k", n_kv * hd, n_embd),
+                                                       ("v", n_kv * hd, n_embd), ("o", n_embd, n_head * hd))}
+    x = rng.standard_normal((2, n_embd)).astype(np.float32)
+    p_kw = dict(n_tok=2, pos0=pos0, n_head=n_head, n_kv=n_kv, head_dim=hd, freq_base=1e4)
+    want = _checker(p_kw, ws, x, caches[1][0], caches[1][1], O.KV_F32, rows)
+    w = N.AttnWeights(ws["q"].desc(N), ws["k"].desc(N), ws["v"].desc(N), ws["o"].desc(N), None, None, None, 0)
+    y = torch.empty((2, n_embd), device="cuda")
+    kv.attention_forward_dev(0, N.params(**p_kw), w, torch.from_numpy(x).cuda(), y, seq=1)
+    kv.sync()
+    _close(y.cpu().numpy(), want)
+    k1, _ = kv.read_rows(0, pos0, 2, seq=1)
+    k0, _ = kv.read_rows(0, pos0, 2, seq=0)
+    assert np.abs(k1 - caches[1][0][pos0:pos0 + 2]).max() < 1e-4  # appended to sequence 1
+    assert not np.any(k0)  # sequence 0 untouched past its rows
+    kv.close()
