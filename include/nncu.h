@@ -344,6 +344,16 @@ typedef struct nncu_attn_weights
 int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t seq, const nncu_attn_params* p,
                                const nncu_attn_weights* w, const float* x, float* y, void* stream);
 
+/* attention_forward for n_seqs sequences of one layer in one call (a serving
+ * batch): sequence seqs[i] takes params[i] (the layer's heads the same for
+ * all; n_tok, pos0, n_seq each its own) and its rows of x and y, the
+ * sequences' tokens one after another. The q / k / v / o gemvs run over all
+ * the tokens together (one pass over the weights for the batch), the
+ * attention is one job per sequence. A sequence may appear once. */
+int nncu_attention_forward_batch_dev(nncu_kv* kv, int32_t layer, int32_t n_seqs, const int32_t* seqs,
+                                     const nncu_attn_params* params, const nncu_attn_weights* w, const float* x,
+                                     float* y, void* stream);
+
 /* model_logits_batch (model.cpp:2198-2208): logits [n][lm_head->rows] of n
  * hidden rows [n][lm_head->cols] (the verify rows of speculate, session.cpp:
  * 545), then final_softcap > 0 applies cap * tanh(x / cap) to each

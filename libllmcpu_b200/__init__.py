@@ -61,6 +61,7 @@ EXPORTS = [
     "nncu_noalloc_check", "nncu_kv_set_tensor_cores", "nncu_host_register", "nncu_host_unregister",
     "nncu_gemv_bf16w_f32x_batch_dev", "nncu_gemv_q8_0_f32x_batch_dev", "nncu_gemv_q4_s_f32x_batch_dev",
     "nncu_block_sums_dev", "nncu_gemv_bf16w_argmax_dev", "nncu_attention_forward_dev", "nncu_logits_batch_dev",
+    "nncu_attention_forward_batch_dev",
     "nncu_argmax_rows_dev",
 ]
 GROUP_HANDLE_BYTES = 64
@@ -225,6 +226,8 @@ def lib() -> C.CDLL:
     L.nncu_attention_forward_dev.argtypes = [vp, i32, i32, C.POINTER(AttnParams), C.POINTER(AttnWeights), vp, vp,
                                              vp]
     L.nncu_logits_batch_dev.argtypes = [C.POINTER(Weight), vp, i32, vp, f, vp, vp]
+    L.nncu_attention_forward_batch_dev.argtypes = [vp, i32, i32, vp, C.POINTER(AttnParams), C.POINTER(AttnWeights),
+                                                   vp, vp, vp]
     L.nncu_argmax_rows_dev.argtypes = [vp, sz, i32, C.c_uint32, vp, vp]
     L.nncu_host_register.argtypes = [vp, sz]
     L.nncu_host_unregister.argtypes = [vp]
@@ -416,6 +419,15 @@ class KVCache:
         are device arrays [n_tok][n_embd], asynchronous on `stream`."""
         _check(lib().nncu_attention_forward_dev(self._h, layer, seq, C.byref(p), C.byref(w), _ptr(x), _ptr(y),
                                                 _stream(stream)))
+
+    def attention_forward_batch_dev(self, layer: int, seqs, ps, w: AttnWeights, x, y, stream=None) -> None:
+        """nncu_attention_forward_batch_dev: one layer for several sequences;
+        ps: one AttnParams per sequence; x, y: the sequences' token rows one
+        after another."""
+        sa = (C.c_int32 * len(seqs))(*[int(s_) for s_ in seqs])
+        pa = (AttnParams * len(ps))(*ps)
+        _check(lib().nncu_attention_forward_batch_dev(self._h, layer, len(seqs), C.cast(sa, C.c_void_p), pa,
+                                                      C.byref(w), _ptr(x), _ptr(y), _stream(stream)))
 
     def sync(self, stream=None) -> None:
         """Wait for `stream` and report a kernel's timed-out wait."""

@@ -284,6 +284,7 @@ struct nncu_kv
 	int* err_dev = nullptr;        // device error word (bounded waits)
 	DevBuf stage_dev, parts, counters, qbuf;
 	DevBuf fwd; // attention_forward's q / gate / k / v / attention rows and block sums
+	std::vector<nncu_attn_job> fwd_jobs;
 	HostBuf stage_host;
 	// The job tables go up on their own stream through a ring of slots, so
 	// the upload of one call's table overlaps the previous call's kernels
@@ -1232,27 +1233,41 @@ extern "C" int nncu_attention_batch_dev(nncu_kv* kv, const nncu_attn_job* jobs, 
 	return run_jobs(kv, kv->jobs_tmp, jobs, static_cast<cudaStream_t>(stream));
 }
 
-// attention_forward (model.cpp:1559-1768) on the device: the reference's
-// sequence of gemv_batch calls, bias adds and the attention, with the
-// query / gate split and the biases folded into the q / k / v gemvs'
-// stores, and norms, RoPE, append, attend and the gate inside the attention
-// kernels of nncu_attention_batch_dev.
-extern "C" int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t seq, const nncu_attn_params* p,
-                                          const nncu_attn_weights* w, const float* x, float* y, void* stream)
+namespace
 {
-	if (!kv || !p || !w || !x || !y) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL argument");
-	if (p->gate) return fail(NNCU_ERR_INVALID_ARGUMENT, "the gate comes from the q projection: p->gate must be NULL");
-	nncu_attn_job job{};
-	job.layer = layer;
-	job.seq = seq;
-	job.p = *p;
-	int rc = validate_job(kv, job);
-	if (rc != NNCU_OK) return rc;
-	const bool reuse = p->reuse_kv != 0, gated = w->gated != 0;
-	const uint32_t n_tok = (uint32_t)p->n_tok, hd = (uint32_t)p->head_dim;
-	const uint32_t q_dim = (uint32_t)p->n_head * hd, kv_dim = (uint32_t)p->n_kv * hd, n_embd = w->o.rows;
+
+// attention_forward for n sequences of one layer: x and y hold their tokens
+// one sequence after another; the gemvs run over all the tokens at once (one
+// pass over the weights for the whole batch), the attention takes one job per
+// sequence.
+int forward_impl(nncu_kv* kv, int32_t layer, int32_t n, const int32_t* seqs, const nncu_attn_params* ps,
+                 const nncu_attn_weights* w, const float* x, float* y, cudaStream_t st)
+{
+	if (!kv || !ps || !w || !x || !y || n <= 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL argument or no sequences");
+	const nncu_attn_params& p0 = ps[0];
+	std::vector<nncu_attn_job>& jobs = kv->fwd_jobs;
+	jobs.assign((size_t)n, nncu_attn_job{});
+	uint32_t n_tok = 0;
+	for (int i = 0; i < n; ++i)
+	{
+		const nncu_attn_params& p = ps[i];
+		if (p.gate) return fail(NNCU_ERR_INVALID_ARGUMENT, "the gate comes from the q projection: p->gate must be NULL");
+		if (p.n_head != p0.n_head || p.n_kv != p0.n_kv || p.head_dim != p0.head_dim || p.reuse_kv != p0.reuse_kv)
+			return fail(NNCU_ERR_INVALID_ARGUMENT, "sequence %d: the layer's heads differ from the first sequence's", i);
+		for (int j = 0; j < i; ++j)
+			if (seqs[j] == seqs[i]) return fail(NNCU_ERR_INVALID_ARGUMENT, "sequence %d appears twice", seqs[i]);
+		jobs[i].layer = layer;
+		jobs[i].seq = seqs[i];
+		jobs[i].p = p;
+		const int rc = validate_job(kv, jobs[i]);
+		if (rc != NNCU_OK) return rc;
+		n_tok += (uint32_t)p.n_tok;
+	}
+	const bool reuse = p0.reuse_kv != 0, gated = w->gated != 0;
+	const uint32_t hd = (uint32_t)p0.head_dim;
+	const uint32_t q_dim = (uint32_t)p0.n_head * hd, kv_dim = (uint32_t)p0.n_kv * hd, n_embd = w->o.rows;
 	if (n_embd == 0) return fail(NNCU_ERR_INVALID_ARGUMENT, "o: no rows");
-	rc = check_weight(w->q, (gated ? 2 : 1) * q_dim, n_embd, "q");
+	int rc = check_weight(w->q, (gated ? 2 : 1) * q_dim, n_embd, "q");
 	if (rc == NNCU_OK && !reuse) rc = check_weight(w->k, kv_dim, n_embd, "k");
 	if (rc == NNCU_OK && !reuse && w->v.data) rc = check_weight(w->v, kv_dim, n_embd, "v");
 	if (rc == NNCU_OK) rc = check_weight(w->o, n_embd, q_dim, "o");
@@ -1267,15 +1282,14 @@ extern "C" int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t se
 	const bool q4_in = w->q.type == NNCU_W_Q4_S ||
 	                   (!reuse && (w->k.type == NNCU_W_Q4_S || (w->v.data && w->v.type == NNCU_W_Q4_S)));
 	const bool q4_out = w->o.type == NNCU_W_Q4_S;
-	auto up64 = [](size_t n) { return (n + 63) & ~size_t(63); }; // 256-byte slots
-	const size_t n_q = up64((size_t)n_tok * q_dim), n_kv = up64((size_t)n_tok * kv_dim);
-	const size_t o_q = 0, o_g = o_q + n_q, o_k = o_g + (gated ? n_q : 0), o_v = o_k + (reuse ? 0 : n_kv);
-	const size_t o_a = o_v + (v_own ? n_kv : 0), o_xs = o_a + n_q;
+	auto up64 = [](size_t v) { return (v + 63) & ~size_t(63); }; // 256-byte slots
+	const size_t n_q = up64((size_t)n_tok * q_dim), n_kvr = up64((size_t)n_tok * kv_dim);
+	const size_t o_q = 0, o_g = o_q + n_q, o_k = o_g + (gated ? n_q : 0), o_v = o_k + (reuse ? 0 : n_kvr);
+	const size_t o_a = o_v + (v_own ? n_kvr : 0), o_xs = o_a + n_q;
 	const size_t o_as = o_xs + (q4_in ? up64((size_t)n_tok * (n_embd / 32)) : 0);
 	const size_t total = o_as + (q4_out ? up64((size_t)n_tok * (q_dim / 32)) : 0);
 
 	DeviceGuard g(kv->device);
-	cudaStream_t st = static_cast<cudaStream_t>(stream);
 	// the scratch is the cache's: wait for the previous call on another stream
 	if (kv->any_call && kv->last_stream != st)
 		CU(cudaStreamWaitEvent(st, kv->done, 0), "order after the previous call");
@@ -1297,12 +1311,18 @@ extern "C" int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t se
 	if (!e) e = launch_projections(proj, n_proj, x, n_embd, xs, n_embd / 32, n_tok, st);
 	if (e) return cuda_fail((cudaError_t)e, "attention_forward projections");
 
-	job.p.gate = gate;
-	job.q = q;
-	job.k = reuse ? nullptr : k;
-	job.v = reuse ? nullptr : v;
-	job.out = attn;
-	rc = nncu_attention_batch_dev(kv, &job, 1, st);
+	size_t row = 0; // the sequence's first token among all
+	for (int i = 0; i < n; ++i)
+	{
+		nncu_attn_job& j = jobs[i];
+		j.p.gate = gate ? gate + row * q_dim : nullptr;
+		j.q = q + row * q_dim;
+		j.k = reuse ? nullptr : k + row * kv_dim;
+		j.v = reuse ? nullptr : v + row * kv_dim;
+		j.out = attn + row * q_dim;
+		row += (size_t)j.p.n_tok;
+	}
+	rc = nncu_attention_batch_dev(kv, jobs.data(), n, st);
 	if (rc != NNCU_OK) return rc;
 
 	if (q4_out) e = launch_block_sums(attn, as, (size_t)n_tok * q_dim, st);
@@ -1313,6 +1333,27 @@ extern "C" int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t se
 	kv->last_stream = st;
 	kv->any_call = true;
 	return NNCU_OK;
+}
+
+} // namespace
+
+// attention_forward (model.cpp:1559-1768) on the device: the reference's
+// sequence of gemv_batch calls, bias adds and the attention, with the
+// query / gate split and the biases folded into the q / k / v gemvs'
+// stores, and norms, RoPE, append, attend and the gate inside the attention
+// kernels of nncu_attention_batch_dev.
+extern "C" int nncu_attention_forward_dev(nncu_kv* kv, int32_t layer, int32_t seq, const nncu_attn_params* p,
+                                          const nncu_attn_weights* w, const float* x, float* y, void* stream)
+{
+	return forward_impl(kv, layer, 1, &seq, p, w, x, y, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nncu_attention_forward_batch_dev(nncu_kv* kv, int32_t layer, int32_t n_seqs, const int32_t* seqs,
+                                                const nncu_attn_params* params, const nncu_attn_weights* w,
+                                                const float* x, float* y, void* stream)
+{
+	if (!seqs) return fail(NNCU_ERR_INVALID_ARGUMENT, "NULL sequence list");
+	return forward_impl(kv, layer, n_seqs, seqs, params, w, x, y, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int nncu_attention_split_dev(nncu_kv* kv, nncu_group* group, const nncu_attn_job* jobs, int32_t n_jobs,

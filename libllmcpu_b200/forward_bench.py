@@ -4,8 +4,9 @@ and a filled K/V cache:
 
     python -m libllmcpu_b200.forward_bench --model qwen3-8b --weights q4_s --context 4096 --calls 200
 
-Each call is one decode token (``--tokens`` for a verify block): the q/k/v
-gemvs, the attention over ``--context`` keys, the o gemv. L2 is flushed
+Each call is one decode token (``--tokens`` for a verify block; ``--seqs``
+sequences of the layer in one call): the q/k/v gemvs, the attention over
+``--context`` keys, the o gemv. L2 is flushed
 before every timed call (a 256 MB write) and each call is timed alone with
 CUDA events on the launching stream; one JSON line with the median. The
 weights are random bytes of the right layout (quants, BF16 scales and
@@ -71,6 +72,7 @@ def main(argv=None) -> int:
     ap.add_argument("--kv", choices=sorted(KVTYPES), default="bf16")
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--tokens", type=int, default=1)
+    ap.add_argument("--seqs", type=int, default=1, help="sequences of the layer in one call (a serving batch)")
     ap.add_argument("--calls", type=int, default=100)
     ap.add_argument("--gemv", default=None, help="ROWSxCOLS: time one single-vector gemv of this shape instead")
     a = ap.parse_args(argv)
@@ -105,24 +107,30 @@ def main(argv=None) -> int:
           "v": random_weight(torch, kind, kv_dim, n_embd, gen),
           "o": random_weight(torch, kind, n_embd, q_dim, gen)}
     kv_type = KVTYPES[a.kv]
-    kv = KVCache([(n_kv, hd, 0, 0)], n_ctx=a.context + a.tokens + 256, n_batch=max(16, a.tokens), kv_type=kv_type)
+    kv = KVCache([(n_kv, hd, 0, 0)], n_ctx=a.context + a.tokens + 256, n_batch=max(16, a.tokens), n_seq=a.seqs,
+                 kv_type=kv_type)
     el = {KV_F32: torch.float32, KV_BF16: torch.bfloat16, KV_F16: torch.float16}[kv_type]
-    for p0 in range(0, a.context, 4096):
-        n = min(4096, a.context - p0)
-        rows_k = torch.randn(n, kv_dim, generator=gen, device="cuda").to(el)
-        kv.write_rows(0, p0, rows_k, rows_k)
+    for s in range(a.seqs):
+        for p0 in range(0, a.context, 4096):
+            n = min(4096, a.context - p0)
+            rows_k = torch.randn(n, kv_dim, generator=gen, device="cuda").to(el)
+            kv.write_rows(0, p0, rows_k, rows_k, seq=s)
     w = AttnWeights(ws["q"], ws["k"], ws["v"], ws["o"], None, None, None, int(gated))
     p = params(n_tok=a.tokens, pos0=a.context, n_head=n_head, n_kv=n_kv, head_dim=hd, freq_base=1e6)
-    x = torch.randn(a.tokens, n_embd, device="cuda")
+    x = torch.randn(a.seqs * a.tokens, n_embd, device="cuda")
     y = torch.empty_like(x)
-    ts = _time(torch, lambda: kv.attention_forward_dev(0, p, w, x, y), a.calls, flush)
+    if a.seqs == 1:
+        ts = _time(torch, lambda: kv.attention_forward_dev(0, p, w, x, y), a.calls, flush)
+    else:
+        seqs, ps = list(range(a.seqs)), [p] * a.seqs
+        ts = _time(torch, lambda: kv.attention_forward_batch_dev(0, seqs, ps, w, x, y), a.calls, flush)
     kv.sync()
     kv.close()
     med = float(np.median(ts))
     wbytes = sum(int(t.numel() * t.element_size()) for wt in ws.values() for t in wt._keep if t is not None)
-    kvbytes = 2 * a.context * kv_dim * (4 if kv_type == KV_F32 else 2)
+    kvbytes = 2 * a.context * kv_dim * (4 if kv_type == KV_F32 else 2) * a.seqs
     print(json.dumps(dict(what="attention_forward", model=a.model, weights=a.weights, kv=a.kv, context=a.context,
-                          tokens=a.tokens, us=round(med, 2), weight_MB=round(wbytes / 1e6, 2),
+                          tokens=a.tokens, seqs=a.seqs, us=round(med, 2), weight_MB=round(wbytes / 1e6, 2),
                           kv_MB=round(kvbytes / 1e6, 2), GBs=round((wbytes + kvbytes) / med / 1e3, 1))))
     return 0
 

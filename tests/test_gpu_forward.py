@@ -299,3 +299,47 @@ def test_second_sequence_of_a_shared_cache(nncu, torch_cuda):
     assert np.abs(k1 - caches[1][0][pos0:pos0 + 2]).max() < 1e-4  # appended to sequence 1
     assert not np.any(k0)  # sequence 0 untouched past its rows
     kv.close()
+
+
+def test_batch_of_sequences_in_one_call(nncu, torch_cuda):
+    # nncu_attention_forward_batch_dev: three sequences of different lengths
+    # and positions through one gated Q4_S layer with Q/K norms; each against
+    # the checker's composition on its own cache
+    N, torch = nncu, torch_cuda
+    rng = np.random.default_rng(12)
+    n_embd, n_head, n_kv, hd = 512, 4, 2, 128
+    kv = N.KVCache([(n_kv, hd, 0, 0)], n_ctx=512, n_batch=16, n_seq=3, kv_type=O.KV_BF16)
+    rows = kv.layer_info(0).rows
+    seqs, toks, pos = [2, 0, 1], [4, 1, 2], [250, 100, 30]
+    qg = rng.uniform(0.5, 1.5, hd).astype(np.float32)
+    kg = rng.uniform(0.5, 1.5, hd).astype(np.float32)
+    ws = {"q": W(rng, O_Q4, 2 * n_head * hd, n_embd, torch), "k": W(rng, O_Q4, n_kv * hd, n_embd, torch),
+          "v": W(rng, O_Q4, n_kv * hd, n_embd, torch), "o": W(rng, O_Q4, n_embd, n_head * hd, torch)}
+    x = rng.standard_normal((sum(toks), n_embd)).astype(np.float32)
+    want, params = [], []
+    dqg, dkg = torch.from_numpy(qg).cuda(), torch.from_numpy(kg).cuda()
+    r0 = 0
+    for s, nt, p0 in zip(seqs, toks, pos):
+        pk = O.narrow(rng.standard_normal((p0, n_kv * hd)).astype(np.float32), O.KV_BF16)
+        pv = O.narrow(rng.standard_normal((p0, n_kv * hd)).astype(np.float32), O.KV_BF16)
+        kv.write_rows(0, 0, pk, pv, seq=s)
+        Kc = np.zeros((rows, n_kv * hd), np.uint16)
+        Vc = np.zeros_like(Kc)
+        Kc[:p0], Vc[:p0] = pk, pv
+        kw = dict(n_tok=nt, pos0=p0, n_head=n_head, n_kv=n_kv, head_dim=hd, freq_base=1e4)
+        want.append(_checker(dict(kw, q_gamma=qg, k_gamma=kg), ws, x[r0:r0 + nt], Kc, Vc, O.KV_BF16, rows,
+                             gated=True))
+        params.append(N.params(**kw, q_gamma=dqg.data_ptr(), k_gamma=dkg.data_ptr()))
+        r0 += nt
+    w = N.AttnWeights(ws["q"].desc(N), ws["k"].desc(N), ws["v"].desc(N), ws["o"].desc(N), None, None, None, 1)
+    y = torch.full((sum(toks), n_embd), float("nan"), device="cuda")
+    kv.attention_forward_batch_dev(0, seqs, params, w, torch.from_numpy(x).cuda(), y)
+    kv.sync()
+    got = y.cpu().numpy()
+    r0 = 0
+    for i, nt in enumerate(toks):
+        _close(got[r0:r0 + nt], want[i])
+        r0 += nt
+    with pytest.raises(N.NnncError, match="twice"):
+        kv.attention_forward_batch_dev(0, [0, 0], params[:2], w, torch.from_numpy(x[:2]).cuda(), y)
+    kv.close()
