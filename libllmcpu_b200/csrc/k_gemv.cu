@@ -543,19 +543,38 @@ int launch_gemv_fmt(const GemvArgs* mats, int n, cudaStream_t st)
 		// 1, 86 at 4, 64 at 8), at 4 from 2048; Q8_0 best at 4 from 12288
 		// (65536 x 4096: 174 us at 1, 91 at 4), at 2 from 8192 (10240 x 2560:
 		// 26.6 us at 1, 19.4 at 2), and at 1 row per warp below.
+		// Q4_S batches too, one vector per launch: the batched kernel's
+		// per-vector arithmetic (activation loads and FMAs for every row) costs
+		// more than re-reading the weights, which stay in L2 from the first
+		// vector (10240 x 2560: 4 vectors 103 us batched, 70.6 one by one; 16
+		// vectors 447 us against 284.7). Each row's sum is formed in the same
+		// order either way.
 		const int rr = FMT == 2 ? (rows >= 12288 ? 8 : rows >= 2048 ? 4 : 1) : (rows >= 12288 ? 4 : rows >= 8192 ? 2 : 0);
-		if (n_batch == 1 && rr > 0)
+		if ((n_batch == 1 || FMT == 2) && rr > 0)
 		{
 			const dim3 grid((unsigned)grid_for((rows + rr - 1) / rr), (unsigned)n);
-			if (rr == 8)
-				gemv_rows_kernel<FMT, 8><<<grid, GW_THREADS, 0, st>>>(set);
-			else if (rr == 4)
-				gemv_rows_kernel<FMT, 4><<<grid, GW_THREADS, 0, st>>>(set);
-			else if (rr == 2)
-				gemv_rows_kernel<FMT, 2><<<grid, GW_THREADS, 0, st>>>(set);
-			else
-				gemv_rows_kernel<FMT, 1><<<grid, GW_THREADS, 0, st>>>(set);
-			note_launches(1);
+			for (uint32_t v = 0; v < n_batch; ++v)
+			{
+				GemvSet one = set;
+				for (int i = 0; i < n; ++i)
+				{
+					GemvArgs& m = one.m[i];
+					m.X = mats[i].X + (size_t)v * mats[i].x_stride;
+					if (FMT == 2) m.XSUM = mats[i].XSUM + (size_t)v * mats[i].xsum_stride;
+					m.Y = mats[i].Y + (size_t)v * mats[i].y_stride;
+					if (m.Y2) m.Y2 = mats[i].Y2 + (size_t)v * mats[i].y_stride;
+					m.n_batch = 1;
+				}
+				if (rr == 8)
+					gemv_rows_kernel<FMT, 8><<<grid, GW_THREADS, 0, st>>>(one);
+				else if (rr == 4)
+					gemv_rows_kernel<FMT, 4><<<grid, GW_THREADS, 0, st>>>(one);
+				else if (rr == 2)
+					gemv_rows_kernel<FMT, 2><<<grid, GW_THREADS, 0, st>>>(one);
+				else
+					gemv_rows_kernel<FMT, 1><<<grid, GW_THREADS, 0, st>>>(one);
+				note_launches(1);
+			}
 			return (int)cudaGetLastError();
 		}
 	}
