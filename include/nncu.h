@@ -358,9 +358,9 @@ int nncu_attention_forward_batch_dev(nncu_kv* kv, int32_t layer, int32_t n_seqs,
  * hidden rows [n][lm_head->cols] (the verify rows of speculate, session.cpp:
  * 545), then final_softcap > 0 applies cap * tanh(x / cap) to each
  * (nnc_softcap_f32, nn_ops.cpp:1877-1882; the reference skips it for greedy
- * verify). A Q4_S lm_head needs `xsum`, n * cols / 32 floats of scratch for
- * the block sums (the reference's cache.sxsum). Device pointers,
- * asynchronous on `stream`. */
+ * verify). For a Q4_S lm_head `xsum` (n * cols / 32 floats, the reference's
+ * cache.sxsum) receives the block sums first; NULL lets the gemv form them
+ * itself. Device pointers, asynchronous on `stream`. */
 int nncu_logits_batch_dev(const nncu_weight* lm_head, const float* hidden, int32_t n, float* logits,
                           float final_softcap, float* xsum, void* stream);
 

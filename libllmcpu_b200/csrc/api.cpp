@@ -1279,9 +1279,12 @@ int forward_impl(nncu_kv* kv, int32_t layer, int32_t n, const int32_t* seqs, con
 	// V is the raw K projection without a v_proj; with a K bias it is a
 	// second, unbiased K gemv (the reference copies V before adding biases)
 	const bool v_own = !reuse && (w->v.data || w->k_bias);
-	const bool q4_in = w->q.type == NNCU_W_Q4_S ||
-	                   (!reuse && (w->k.type == NNCU_W_Q4_S || (w->v.data && w->v.type == NNCU_W_Q4_S)));
-	const bool q4_out = w->o.type == NNCU_W_Q4_S;
+	// Q4_S weights need the activations' block sums: one token's are formed
+	// inside the gemv (no launch); several tokens' once, by a block-sum launch
+	// (the gemv runs once per token and would form them every time)
+	const bool q4_in = n_tok > 1 && (w->q.type == NNCU_W_Q4_S ||
+	                                 (!reuse && (w->k.type == NNCU_W_Q4_S || (w->v.data && w->v.type == NNCU_W_Q4_S))));
+	const bool q4_out = n_tok > 1 && w->o.type == NNCU_W_Q4_S;
 	auto up64 = [](size_t v) { return (v + 63) & ~size_t(63); }; // 256-byte slots
 	const size_t n_q = up64((size_t)n_tok * q_dim), n_kvr = up64((size_t)n_tok * kv_dim);
 	const size_t o_q = 0, o_g = o_q + n_q, o_k = o_g + (gated ? n_q : 0), o_v = o_k + (reuse ? 0 : n_kvr);
@@ -1296,8 +1299,8 @@ int forward_impl(nncu_kv* kv, int32_t layer, int32_t n, const int32_t* seqs, con
 	CU(kv->fwd.reserve(total * sizeof(float)), "attention_forward scratch");
 	float* f = static_cast<float*>(kv->fwd.p);
 	float *q = f + o_q, *gate = gated ? f + o_g : nullptr, *k = f + o_k, *v = v_own ? f + o_v : k, *attn = f + o_a;
-	float* xs = f + o_xs;
-	float* as = f + o_as;
+	float* xs = q4_in ? f + o_xs : nullptr;
+	float* as = q4_out ? f + o_as : nullptr;
 
 	int e = 0;
 	if (q4_in) e = launch_block_sums(x, xs, (size_t)n_tok * n_embd, st);

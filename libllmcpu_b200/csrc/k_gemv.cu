@@ -300,7 +300,9 @@ __device__ __forceinline__ void rows_dot1(const GemvArgs& a, uint32_t r0, int la
 				sc[k] = bf16f(__ldg(a.scales + (size_t)rr_[k] * nb + b));
 				bi[k] = bf16f(__ldg(a.biases + (size_t)rr_[k] * nb + b));
 			}
-			const float xs = __ldg(a.XSUM + b);
+			// the block's activation sum: the caller's (nnc_block_sums_f32), or,
+			// without one, formed below from the 32 values once in registers
+			float xs = a.XSUM ? __ldg(a.XSUM + b) : 0.0f;
 			float x[32];
 			const float* xp = a.X + (size_t)b * 32;
 			if (x4)
@@ -318,6 +320,17 @@ __device__ __forceinline__ void rows_dot1(const GemvArgs& a, uint32_t r0, int la
 			else
 #pragma unroll
 				for (int k = 0; k < 32; ++k) x[k] = __ldg(xp + k);
+			if (!a.XSUM)
+			{
+				float t[16];
+#pragma unroll
+				for (int k = 0; k < 16; ++k) t[k] = x[k] + x[k + 16];
+#pragma unroll
+				for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+					for (int k = 0; k < w; ++k) t[k] += t[k + w];
+				xs = t[0];
+			}
 #pragma unroll
 			for (int k = 0; k < RR; ++k)
 			{
@@ -543,7 +556,8 @@ int launch_gemv_fmt(const GemvArgs* mats, int n, cudaStream_t st)
 		// 1, 86 at 4, 64 at 8), at 4 from 2048; Q8_0 best at 4 from 12288
 		// (65536 x 4096: 174 us at 1, 91 at 4), at 2 from 8192 (10240 x 2560:
 		// 26.6 us at 1, 19.4 at 2), and at 1 row per warp below.
-		// Q4_S batches too, one vector per launch: the batched kernel's
+		// Q4_S batches too, one vector per launch (this kernel alone forms
+		// the block sums itself when the caller passes none): the batched kernel's
 		// per-vector arithmetic (activation loads and FMAs for every row) costs
 		// more than re-reading the weights, which stay in L2 from the first
 		// vector (10240 x 2560: 4 vectors 103 us batched, 70.6 one by one; 16
@@ -560,7 +574,7 @@ int launch_gemv_fmt(const GemvArgs* mats, int n, cudaStream_t st)
 				{
 					GemvArgs& m = one.m[i];
 					m.X = mats[i].X + (size_t)v * mats[i].x_stride;
-					if (FMT == 2) m.XSUM = mats[i].XSUM + (size_t)v * mats[i].xsum_stride;
+					if (FMT == 2 && m.XSUM) m.XSUM = mats[i].XSUM + (size_t)v * mats[i].xsum_stride;
 					m.Y = mats[i].Y + (size_t)v * mats[i].y_stride;
 					if (m.Y2) m.Y2 = mats[i].Y2 + (size_t)v * mats[i].y_stride;
 					m.n_batch = 1;
@@ -733,15 +747,17 @@ extern "C" int nncu_logits_batch_dev(const nncu_weight* lm_head, const float* hi
 		return set_error(NNCU_ERR_INVALID_ARGUMENT, "logits: NULL argument or no rows");
 	const int rc = check_weight(*lm_head, lm_head->rows, lm_head->cols, "lm_head");
 	if (rc != NNCU_OK) return rc;
-	if (lm_head->type == NNCU_W_Q4_S && !xsum)
-		return set_error(NNCU_ERR_INVALID_ARGUMENT, "logits: a Q4_S lm_head needs the block-sum scratch");
 	if (final_softcap < 0.0f || final_softcap != final_softcap)
 		return set_error(NNCU_ERR_INVALID_ARGUMENT, "logits: bad soft-cap");
 	const uint32_t cols = lm_head->cols, rows = lm_head->rows;
+	// a Q4_S lm_head's block sums: the caller's scratch filled first, or
+	// (xsum NULL) formed inside the gemv
 	int e = 0;
-	if (lm_head->type == NNCU_W_Q4_S) e = launch_block_sums(hidden, xsum, (size_t)n * cols, stream);
+	if (lm_head->type == NNCU_W_Q4_S && xsum) e = launch_block_sums(hidden, xsum, (size_t)n * cols, stream);
 	const Projection pr{lm_head, logits, rows, nullptr, 0, nullptr};
-	if (!e) e = launch_projections(&pr, 1, hidden, cols, xsum, cols / 32, (uint32_t)n, stream);
+	if (!e)
+		e = launch_projections(&pr, 1, hidden, cols, lm_head->type == NNCU_W_Q4_S ? xsum : nullptr, cols / 32,
+		                       (uint32_t)n, stream);
 	if (!e && final_softcap > 0.0f) e = launch_softcap(logits, logits, (size_t)n * rows, final_softcap, stream);
 	return e ? set_cuda_error(e, "logits launch") : NNCU_OK;
 }
