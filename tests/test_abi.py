@@ -142,3 +142,17 @@ def test_no_gpu_means_a_loud_failure(L):
     x = np.zeros(64, np.float32)
     with pytest.raises(N.NnncError):
         N.rmsnorm_dev(x, x, 1, 64, 1e-6)  # host memory, no device: refused, not computed
+
+
+def test_forward_and_logits_refuse_bad_arguments_before_any_device_work(L):
+    # argument checks come first: NULL handles and pointers, empty batches,
+    # a gate passed in although the q projection makes it
+    vp = None
+    p = N.params(n_tok=1, pos0=0, n_head=4, n_kv=2, head_dim=64)
+    w = N.AttnWeights()
+    assert L.nncu_attention_forward_dev(vp, 0, 0, p, w, vp, vp, vp) == N.ERR_INVALID_ARGUMENT
+    assert L.nncu_attention_forward_batch_dev(vp, 0, 0, vp, p, w, vp, vp, vp) == N.ERR_INVALID_ARGUMENT
+    head = N.Weight(N.W_Q4_S, 64, 64, None, None, None)
+    assert L.nncu_logits_batch_dev(head, vp, 1, vp, 0.0, vp, vp) == N.ERR_INVALID_ARGUMENT
+    assert L.nncu_argmax_rows_dev(vp, 4, 1, 4, vp, vp) == N.ERR_INVALID_ARGUMENT
+    assert b"NULL" in L.nncu_last_error()
