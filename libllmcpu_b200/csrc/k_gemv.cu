@@ -592,6 +592,11 @@ int launch_gemv_fmt(const GemvArgs* mats, int n, cudaStream_t st)
 			return (int)cudaGetLastError();
 		}
 	}
+	// the batched kernel reads the caller's block sums (only the rows kernel
+	// forms them itself)
+	if (FMT == 2)
+		for (int i = 0; i < n; ++i)
+			if (!mats[i].XSUM) return (int)cudaErrorInvalidValue;
 	const dim3 grid((unsigned)grid_for(rows), (unsigned)n);
 	for (uint32_t v0 = 0; v0 < n_batch;)
 	{
