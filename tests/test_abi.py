@@ -156,3 +156,12 @@ def test_forward_and_logits_refuse_bad_arguments_before_any_device_work(L):
     assert L.nncu_logits_batch_dev(head, vp, 1, vp, 0.0, vp, vp) == N.ERR_INVALID_ARGUMENT
     assert L.nncu_argmax_rows_dev(vp, 4, 1, 4, vp, vp) == N.ERR_INVALID_ARGUMENT
     assert b"NULL" in L.nncu_last_error()
+
+
+def test_forward_bench_parses_its_arguments():
+    from libllmcpu_b200 import forward_bench
+
+    with pytest.raises(SystemExit) as e:
+        forward_bench.main(["--help"])
+    assert e.value.code == 0
+    assert set(forward_bench.MODELS) >= {"gemma3-4b", "qwen3-8b", "qwen3.5-4b", "llama3.2-1b"}
